@@ -1,0 +1,146 @@
+/* libvarda_b200 — the C ABI of the B200-native GraphTransformer backend.
+ *
+ * Drop-in replacement for the CUDA backend of varda.cpp (frazane/varda.cpp). Each entry point names
+ * the reference interface it replaces (file:line in the reference project). Plain pointers and sizes
+ * only; no C++ or torch types cross this boundary; no exception crosses it: every function returns
+ * a status (VB_OK = 0, else an error class below) and vb_last_error() gives the message of the
+ * calling thread's last failure.
+ *
+ * Ownership: the caller owns x and y (host or device buffers it passes in). The library owns every
+ * device weight, graph and activation buffer of a model; they are allocated by vb_load and freed by
+ * vb_free. After vb_prepare, the *_device entry points and vb_enqueue_predict only enqueue work on
+ * the given stream (no allocation, no synchronisation), so a caller may capture them in its own CUDA
+ * graph. At most one forward pass may be in flight per model.
+ */
+#ifndef VARDA_B200_H
+#define VARDA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status / error classes */
+#define VB_OK 0
+#define VB_ERR_INVALID_ARGUMENT 1
+#define VB_ERR_FORMAT 2      /* model file or config: missing/unconsumed tensor, bad shape, unknown kind */
+#define VB_ERR_CUDA 3
+#define VB_ERR_UNSUPPORTED 4
+#define VB_ERR_INTERNAL 5
+#define VB_ERR_TIMEOUT 6     /* a bounded device-side wait gave up */
+
+#define VB_PRECISION_FP32 0
+#define VB_PRECISION_FP16 1
+
+typedef struct vb_model vb_model;
+
+/* varda::Options (src/varda/varda.h:21-27). device is always CUDA here; num_threads is accepted
+ * and ignored (it configures the reference's CPU backend). */
+typedef struct {
+    int precision;      /* VB_PRECISION_FP32 | VB_PRECISION_FP16 */
+    int cuda_device;
+    int cuda_graph;     /* nonzero: capture the forward pass once, replay afterwards */
+    int num_threads;
+} vb_options;
+
+/* varda::ActivationHook (src/varda/varda.h:31-32): every contract activation once per predict_step,
+ * host fp32, contiguous, row-major with `shape` (ndim entries); valid only during the call. */
+typedef void (*vb_hook_fn)(const char* key, const float* data, const int64_t* shape, int ndim, void* user);
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* vb_last_error(void);
+
+/* varda::Model::load (src/varda/varda.h:39, model.cpp:23-78) + make_cuda_backend (backend.h:25-26):
+ * maps the safetensors file, parses and checks the config, uploads weights and graphs, allocates
+ * every activation buffer. Strict: fails unless every tensor of the file is consumed. */
+int vb_load(const char* path, const vb_options* opts, vb_model** out);
+
+/* Multi-GPU load: one process per GPU (rank of world), the graph partitioned by destination node.
+ * nccl_id: the 128-byte ncclUniqueId made by vb_nccl_unique_id on one rank and shared by the
+ * caller. No reference counterpart (the reference runs one GPU). */
+int vb_load_sharded(const char* path, const vb_options* opts, int rank, int world, const void* nccl_id,
+                    vb_model** out);
+int vb_nccl_unique_id(void* out128);
+
+/* delete the Model / Backend (the reference's destructors). */
+void vb_free(vb_model* m);
+
+/* varda::Model::predict_step (src/varda/varda.h:50, backend.h:16): host x (1, T_in, G, V_in) fp32 in
+ * physical units -> host y (1, T_out, 1, G, V_out). hook may be NULL. On a sharded model every rank
+ * passes the full x and writes only its own data rows of y (vb_data_range). */
+int vb_predict_step(vb_model* m, const float* x, float* y, vb_hook_fn hook, void* user);
+
+/* sizes: [T_in, G, V_in, T_out, V_out, H, C, n_proc]; input_numel = T_in G V_in, output_numel =
+ * T_out G V_out (cuda/cuda_backend.h:34-35). */
+int vb_sizes(const vb_model* m, int64_t out8[8]);
+int vb_data_range(const vb_model* m, int64_t* lo, int64_t* hi);
+
+/* varda::cuda::CudaBackend device entry points (src/varda/cuda/cuda_backend.h:38-69). Pointers are
+ * device pointers (fp32, contiguous); stream is a cudaStream_t (NULL = the legacy default stream). */
+int vb_normalise(vb_model* m, const float* x, float* xn, void* stream);            /* :38 */
+int vb_forward_normalised(vb_model* m, const float* xn, float* yn, void* stream);  /* :42 */
+int vb_denormalise(vb_model* m, const float* yn, float* y, void* stream);          /* :44 */
+int vb_predict_step_device(vb_model* m, const float* x, float* y, void* stream);   /* :46 */
+int vb_prepare(vb_model* m);                                                       /* :50 */
+int vb_use_high_priority_stream(vb_model* m);                                      /* :56 */
+float* vb_device_input(vb_model* m);                                               /* :66 */
+const float* vb_device_output(vb_model* m);                                        /* :67 */
+void* vb_stream(vb_model* m);                                                      /* :68 */
+int vb_enqueue_predict(vb_model* m);                                               /* :69 */
+int vb_device(const vb_model* m);                                                  /* :71 */
+size_t vb_weight_bytes(const vb_model* m);                                         /* :72 */
+size_t vb_activation_bytes(const vb_model* m);                                     /* :73 */
+int64_t vb_decoder_chunk_rows(const vb_model* m);                                  /* :74 */
+
+/* Synchronises the current device and reports (then clears) the error flag a bounded device wait
+ * sets when it gives up: VB_OK or VB_ERR_TIMEOUT. */
+int vb_check_device(void);
+
+/* Instrumentation, no reference counterpart (the reference profiles with external tools):
+ * vb_launch_count: kernel launches issued by this library in this process so far (eager launches and
+ * launches recorded into graph captures). vb_profile_forward: one eager forward pass on the model's
+ * internal buffers with a CUDA event pair around every launch; writes a JSON array of
+ * {"name", "ms", "flop", "bytes"} records (algorithmic FLOPs / compulsory bytes) into buf and returns
+ * the length it needs (call again with a larger buffer if that exceeds len). Synchronises. */
+int64_t vb_launch_count(void);
+int64_t vb_profile_forward(vb_model* m, char* buf, size_t len);
+
+/* ---------------------------------------------------------------- kernel-level entry points
+ * The reference's internal kernel interface (src/varda/cuda/kernels.h, graph.h, gemm.h), exported
+ * for unit tests and benchmarks. dtype: VB_PRECISION_FP32 (float) or VB_PRECISION_FP16 (__half
+ * storage, fp32 math). All enqueue on `stream`. */
+
+/* build_csr_by_dst (src/varda/graph.cpp:17-61), host memory: edge_index int64 [2, E], edge_attr
+ * float [E, A] -> row_ptr [n_dst + 1], src [E], edge_id [E], attr_csr [E, A]. Bit-exact. */
+int vb_build_csr(const int64_t* edge_index, int64_t E, const float* edge_attr, int A, int64_t n_src, int64_t n_dst,
+                 int32_t* row_ptr, int32_t* src, int32_t* edge_id, float* attr_csr);
+
+/* One 16-byte record per CSR slot {a0, a1, a2, src} as the attention kernel reads it (the reference's
+ * Engine::load_graph packing, backend_cuda.cu:323-348); host memory. round_fp16 rounds attributes. */
+int vb_pack_edges(const int32_t* src, const float* attr_csr, int A, int64_t E, int round_fp16, void* out16);
+
+/* cuda::attention<T> (src/varda/cuda/kernels.h:79-96): device pointers. edges = packed records,
+ * w_e = fp32 [4, C] (edge weight columns zero padded to 3, then the edge bias). */
+int vb_attention(int dtype, const int32_t* row_ptr, const void* edges, int64_t dst_lo, int64_t n_rows,
+                 const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, const void* xr, int64_t ldxr,
+                 void* out, int64_t ldo, const float* w_e, int C, int heads, int head_dim, void* stream);
+
+/* Gemm::linear (src/varda/cuda/gemm.h): y[M, N] = A[M, K] W[N, K]^T (+ bias), then epilogue
+ * 0 = none, 1 = GELU (gelu_tanh selects the tanh form), 2 = + residual R[M, N]. engine: 0 = auto
+ * (tensor cores for fp16), 1 = CUDA cores, 2 = tensor cores (fp16 only; fails if not applicable). */
+int vb_gemm(int dtype, int engine, const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* Y,
+            int64_t ldy, const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int epilogue, int gelu_tanh,
+            void* stream);
+
+/* layernorm / add_layernorm (src/varda/cuda/kernels.h:49-59); b may be NULL. */
+int vb_layernorm(int dtype, const void* x, int64_t ldx, const float* w, const float* b, void* y, int64_t ldy,
+                 int64_t rows, int C, float eps, void* stream);
+int vb_add_layernorm(int dtype, const void* a, const void* r, void* out1, const float* w, const float* b, void* ln,
+                     int64_t ld, int64_t rows, int C, float eps, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VARDA_B200_H */

@@ -1,0 +1,103 @@
+"""Generates the committed golden fixtures of tests/golden/ (run in a container that has the reference
+sources and oracle/_ref built; the fixtures then travel, the reference does not).
+
+1. synthetic_pin.json: for the reference's own synthetic models a-h (python/tests/synthetic.py of
+   varda.cpp, imported from the reference tree), the sha256 of the model file and the worst
+   rel_absmax of this repo's oracle restatement (oracle/oracle.py) against the reference's float64
+   goldens, per key.
+2. <name>.golden.npz for this repo's seeded models (varda_b200.synth: c0 and the t* parity models):
+   contract activations computed by the UNMODIFIED reference CPU backend (oracle/_ref/ref_dump,
+   compiled from the reference's sources), the model file's sha256, and the input's sha256.
+
+    python tests/golden/make_golden.py [--reference /root/reference] [--only NAME ...]
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(REPO, "varda.cpp_b200"))
+sys.path.insert(0, os.path.join(REPO, "oracle"))
+
+from varda_b200 import safetensors as st, synth  # noqa: E402
+import oracle  # noqa: E402
+
+MODELS = ["c0", "t128", "t256", "t512", "t768", "t1024", "t384i", "t2048"]
+# keys kept in the fixtures (the small ones; [H, C] / [G, C] keys only for small models)
+KEEP_ALWAYS = ["dec.out", "out.pre_bound", "out.norm", "out.y"]
+KEEP_SMALL = ["enc.out", "latent"]
+
+
+def pin_synthetic(ref_root, work):
+    spec = importlib.util.spec_from_file_location("ref_synthetic", os.path.join(ref_root, "python/tests/synthetic.py"))
+    syn = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(syn)
+    out = {}
+    for name in sorted(syn.CONFIGS):
+        syn.generate(name, work)
+        mp = os.path.join(work, f"{name}.model.safetensors")
+        gold, _ = oracle.read_safetensors(os.path.join(work, f"{name}.golden.safetensors"))
+        m = oracle.OracleModel(mp)
+        res = {}
+        m.predict_step(gold["in.x"], lambda k, a: res.__setitem__(k, oracle.rel_absmax(a, gold[k])))
+        out[name] = {"model_sha256": synth.sha256_file(mp), "rel_absmax": res,
+                     "worst": max(res.values()), "tolerance_fp32": 1e-5}
+        print(f"synthetic {name}: worst {out[name]['worst']:.3e}")
+    return out
+
+
+def ref_golden(name, work, ref_dump):
+    mp, xp = synth.generate(name, work)
+    dump = os.path.join(work, f"{name}.dump.safetensors")
+    r = subprocess.run([ref_dump, "--model", mp, "--input", xp, "--dump", dump, "--threads", "8"],
+                       capture_output=True, text=True, check=True)
+    acts, _ = st.read(dump)
+    keep = {k: np.array(acts[k], np.float32) for k in KEEP_ALWAYS}
+    for k in KEEP_SMALL:
+        if acts[k].size <= 300_000:
+            keep[k] = np.array(acts[k], np.float32)
+    # the oracle restatement against the reference, same inputs (printed, and checked by the tests)
+    x = st.read(xp)[0]["in.x"]
+    om = oracle.OracleModel(mp)
+    worst = {}
+    om.predict_step(x, lambda k, a: worst.__setitem__(k, oracle.rel_absmax(a, acts[k])))
+    keep["__model_sha256__"] = np.frombuffer(synth.sha256_file(mp).encode(), np.uint8)
+    keep["__input_sha256__"] = np.frombuffer(synth.sha256_file(xp).encode(), np.uint8)
+    np.savez_compressed(os.path.join(HERE, f"{name}.golden.npz"), **keep)
+    print(f"{name}: reference ref_dump {r.stdout.strip()} ; oracle vs reference worst {max(worst.values()):.3e}")
+    return {k: float(v) for k, v in worst.items()}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", nargs="*")
+    ap.add_argument("--skip-synthetic", action="store_true")
+    a = ap.parse_args()
+    ref_dump = os.path.join(REPO, "oracle", "_ref", "ref_dump")
+    if not os.path.exists(ref_dump):
+        subprocess.run(["make", "-C", os.path.join(REPO, "oracle"), f"REF={a.reference}"], check=True)
+    with tempfile.TemporaryDirectory() as work:
+        summary_path = os.path.join(HERE, "oracle_vs_reference.json")
+        summary = json.load(open(summary_path)) if os.path.exists(summary_path) else {}
+        if not a.skip_synthetic:
+            pin = pin_synthetic(a.reference, work)
+            with open(os.path.join(HERE, "synthetic_pin.json"), "w") as f:
+                json.dump(pin, f, indent=1, sort_keys=True)
+        for name in a.only or MODELS:
+            summary[name] = ref_golden(name, work, ref_dump)
+        with open(summary_path, "w") as f:
+            json.dump(summary, f, indent=1, sort_keys=True)
+
+
+if __name__ == "__main__":
+    main()

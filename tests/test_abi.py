@@ -1,0 +1,110 @@
+"""The C ABI boundary, on CPU: the library loads and exports every declared symbol, the host-side
+parts (CSR build, edge packing, strict model loading) behave like the reference's. No GPU."""
+import json
+import os
+import re
+
+import numpy as np
+import pytest
+
+import oracle
+import varda_b200 as vb
+from conftest import REPO
+from varda_b200 import safetensors as st
+
+HEADER = os.path.join(REPO, "include", "varda_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(vb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_functions()
+    assert len(names) >= 25
+    for n in names:
+        assert hasattr(vb.lib, n), f"{n} declared in include/varda_b200.h but not exported"
+
+
+def random_graph(rng, ns, nd, E):
+    return np.stack([rng.integers(0, ns, E), rng.integers(0, nd, E)]).astype(np.int64)
+
+
+@pytest.mark.parametrize("seed,ns,nd,E,A", [(0, 50, 40, 0, 3), (1, 300, 200, 5000, 3), (2, 7, 1000, 30000, 2),
+                                             (3, 10000, 97, 20000, 1)])
+def test_build_csr_bit_exact(seed, ns, nd, E, A):
+    rng = np.random.default_rng(seed)
+    ei = random_graph(rng, ns, nd, E)
+    ea = rng.normal(size=(E, A)).astype(np.float32)
+    got = vb.build_csr(ei, ea, ns, nd)
+    ref = oracle.build_csr(ei, ea, ns, nd)
+    for g, r in zip(got, ref):
+        assert g.dtype == r.dtype and np.array_equal(g, r)
+
+
+def test_build_csr_rejects_out_of_range():
+    ei = np.array([[0, 5], [0, 1]], np.int64)
+    with pytest.raises(vb.VardaError) as e:
+        vb.build_csr(ei, np.zeros((2, 3), np.float32), 5, 2)
+    assert e.value.code == 2 and "out of range" in str(e.value)
+
+
+def test_pack_edges_layout_and_rounding():
+    src = np.array([3, 0, 7], np.int32)
+    at = np.array([[0.1, 1.0 / 3, 2.0], [5.0, -1.5, 0.2], [1e-3, 7.7, -2.2]], np.float32)
+    p = vb.pack_edges(src, at[:, :2], round_fp16=False)
+    assert np.array_equal(p[:, :2], at[:, :2]) and np.all(p[:, 2] == 0)
+    assert np.array_equal(p[:, 3].view(np.int32), src)
+    p16 = vb.pack_edges(src, at, round_fp16=True)
+    assert np.array_equal(p16[:, :3], at.astype(np.float16).astype(np.float32))
+
+
+def _small_model(tmp_path, mutate=None, cfg_mutate=None):
+    from varda_b200 import synth
+    cfg, t, x = synth.config_test("t128")
+    if mutate:
+        mutate(t)
+    if cfg_mutate:
+        cfg_mutate(cfg)
+    p = str(tmp_path / "m.safetensors")
+    synth.write_model(p, cfg, t)
+    return p
+
+
+def _load_error(path):
+    with pytest.raises(vb.VardaError) as e:
+        vb.Model.load(path, precision=vb.FP32)
+    return e.value
+
+
+def test_load_rejects_missing_tensor(tmp_path):
+    err = _load_error(_small_model(tmp_path, mutate=lambda t: t.pop("proc.0.mlp1.weight")))
+    assert err.code == 2 and "missing tensor 'proc.0.mlp1.weight'" in str(err)
+
+
+def test_load_rejects_unconsumed_tensor(tmp_path):
+    err = _load_error(_small_model(tmp_path, mutate=lambda t: t.__setitem__("extra.thing", np.zeros(3, np.float32))))
+    assert err.code == 2 and "not consumed" in str(err) and "extra.thing" in str(err)
+
+
+@pytest.mark.parametrize("edit,msg", [
+    (lambda c: c["architecture"]["processor"].__setitem__("kind", "gnn"), "architecture.processor.kind"),
+    (lambda c: c["dims"].__setitem__("gelu_approximate", "erf2"), "gelu_approximate"),
+    (lambda c: c.__setitem__("format_version", 2), "format_version"),
+    (lambda c: c["bounding"].append({"type": "softplus", "index": [0]}), "bounding type"),
+    (lambda c: c["residual"].__setitem__("step", 5), "residual.step"),
+])
+def test_load_rejects_bad_config(tmp_path, edit, msg):
+    err = _load_error(_small_model(tmp_path, cfg_mutate=edit))
+    assert err.code == 2 and msg in str(err)
+
+
+def test_load_rejects_missing_file(tmp_path):
+    err = _load_error(str(tmp_path / "nope.safetensors"))
+    assert err.code == 2 and "cannot open" in str(err)
+
+
+def test_python_binding_requires_library():
+    assert os.path.exists(vb.LIB_PATH)

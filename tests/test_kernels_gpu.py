@@ -1,0 +1,221 @@
+"""Kernel parity on the B200, through the C ABI (device memory via torch as plumbing).
+
+Attention follows the reference's own unit test (tests/test_cuda_kernels.cu:98-233 of varda.cpp): a
+graph with every degree class {0,1,2,3,5,8,17,33,64} in shuffled stored order, the layouts
+(C, heads, A) it uses plus this repo's C=128/384/2048, a float64 reference with the edge term
+materialised and a two-pass softmax; tolerance 1e-5 (fp32) and 2e-3 (fp16) as there; zero in-degree
+gives x_r exactly; a destination sub-range is bitwise equal to the full launch. GEMM and LayerNorm are
+checked against float64 references of the same fp32 / autocast-fp16 arithmetic.
+"""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+import varda_b200 as vb
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+DEGREES = [0, 1, 2, 3, 5, 8, 17, 33, 64]
+
+
+def dev(a, dtype):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    return t.to(device="cuda", dtype=dtype)
+
+
+def tname(dt):
+    return torch.float32 if dt == vb.FP32 else torch.float16
+
+
+def rounded(a, dt):
+    return a.astype(np.float32) if dt == vb.FP32 else a.astype(np.float16).astype(np.float32)
+
+
+def make_graph(rng, n_src, n_dst, A):
+    s, d = [], []
+    for i in range(n_dst):
+        deg = DEGREES[i] if i < len(DEGREES) else DEGREES[int(rng.integers(len(DEGREES)))]
+        s += list(rng.integers(0, n_src, deg))
+        d += [i] * deg
+    perm = rng.permutation(len(s))
+    ei = np.stack([np.array(s, np.int64)[perm], np.array(d, np.int64)[perm]])
+    ea = rng.normal(size=(ei.shape[1], A)).astype(np.float32)
+    return ei, ea
+
+
+def attention_reference(rp, src, attr, q, k, v, xr, we, be, heads, hd):
+    """float64, e materialised and added to k and v, two-pass softmax (the reference test's maths)."""
+    C = heads * hd
+    nd = len(rp) - 1
+    out = np.zeros((nd, C))
+    for d in range(nd):
+        b0, b1 = rp[d], rp[d + 1]
+        if b1 == b0:
+            out[d] = xr[d]
+            continue
+        e = attr[b0:b1].astype(np.float64) @ we.T.astype(np.float64) + be  # [deg, C]
+        kk = k[src[b0:b1]] + e
+        vv = v[src[b0:b1]] + e
+        for h in range(heads):
+            sl = slice(h * hd, (h + 1) * hd)
+            sc = (kk[:, sl] @ q[d, sl]) / math.sqrt(hd)
+            p = np.exp(sc - sc.max())
+            p /= p.sum()
+            out[d, sl] = p @ vv[:, sl] + xr[d, sl]
+    return out
+
+
+LAYOUTS = [(1024, 16, 3), (256, 8, 3), (512, 4, 2), (256, 32, 1), (768, 12, 3), (128, 4, 3), (384, 6, 3),
+           (2048, 8, 3)]
+
+
+@pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])
+@pytest.mark.parametrize("C,heads,A", LAYOUTS)
+def test_attention(C, heads, A, dt):
+    rng = np.random.default_rng(C * 7 + heads + A + dt)
+    hd = C // heads
+    n_src, n_dst, ld = 131, 97, C + 8
+    ei, ea = make_graph(rng, n_src, n_dst, A)
+    rp, src, _, attr = vb.build_csr(ei, ea, n_src, n_dst)
+    attr = rounded(attr, dt)
+    q, k, v, xr = (rounded(rng.normal(size=(n, ld)), dt) for n in (n_dst, n_src, n_src, n_dst))
+    we = rounded(rng.normal(size=(C, A)) * 0.5, dt)
+    be = rounded(rng.normal(size=C) * 0.5, dt)
+    w4 = np.zeros((4, C), np.float32)
+    w4[:A] = we.T
+    w4[3] = be
+    edges = vb.pack_edges(src, attr, round_fp16=False)
+    T = tname(dt)
+    d_rp, d_ed, d_w = dev(rp, torch.int32), dev(edges, torch.float32), dev(w4, torch.float32)
+    d_q, d_k, d_v, d_x = dev(q, T), dev(k, T), dev(v, T), dev(xr, T)
+    out = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
+    vb.attention(dt, d_rp, d_ed, 0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld, out, C, d_w, C, heads, hd)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    ref = attention_reference(rp, src, attr, q[:, :C].astype(np.float64), k[:, :C].astype(np.float64),
+                              v[:, :C].astype(np.float64), xr[:, :C].astype(np.float64), we, be.astype(np.float64),
+                              heads, hd)
+    err = oracle.rel_absmax(got, ref)
+    tol = 1e-5 if dt == vb.FP32 else 2e-3
+    assert err <= tol, f"rel_absmax {err:.3e} > {tol}"
+    zero = np.where(rp[1:] == rp[:-1])[0]
+    assert len(zero) > 0
+    assert np.array_equal(got[zero], xr[zero, :C]), "zero in-degree must give x_r exactly"
+    if dt == vb.FP32:
+        # the oracle's restatement of cpu::graph_attention, plus x_r
+        o = oracle.graph_attention((rp, src, None, attr), 0, n_dst, q[:, :C], k[:, :C], v[:, :C],
+                                   np.ascontiguousarray(we.T), be, heads, hd) + xr[:, :C]
+        assert oracle.rel_absmax(got, o) <= 1e-5
+    # destination sub-range [13, 64): rows local, bitwise equal to the full launch
+    lo, n = 13, 51
+    out2 = torch.empty((n, C), device="cuda", dtype=T)
+    vb.attention(dt, d_rp, d_ed, lo, n, d_q[lo:], ld, d_k, d_v, ld, d_x[lo:], ld, out2, C, d_w, C, heads, hd)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, out[lo:lo + n])
+
+
+def gemm_reference(A, W, b, R, epi, gelu_tanh, fp16):
+    acc = A.astype(np.float64) @ W.astype(np.float64).T
+    rnd = (lambda x: x.astype(np.float16).astype(np.float64)) if fp16 else (lambda x: x)
+    y = acc + (b.astype(np.float64) if b is not None else 0)
+    y = rnd(y)
+    if epi == 1:
+        if gelu_tanh:
+            y = 0.5 * y * (1 + np.tanh(math.sqrt(2 / math.pi) * (y + 0.044715 * y ** 3)))
+        else:
+            from scipy.special import erf
+            y = 0.5 * y * (1 + erf(y / math.sqrt(2)))
+        y = rnd(y)
+    elif epi == 2:
+        y = rnd(y + R.astype(np.float64))
+    return y
+
+
+GEMM_SHAPES = [(1, 8, 8, 8), (77, 67, 168, 168), (300, 1024, 1024, 1024), (1000, 4096, 1024, 1024),
+               (513, 1024, 4096, 4096), (1031, 80, 1024, 1024), (4000, 2048, 184, 192), (2562, 128, 4, 8),
+               (129, 256, 64, 64)]
+
+
+@pytest.mark.parametrize("M,N,K,lda", GEMM_SHAPES)
+@pytest.mark.parametrize("epi", [0, 1, 2])
+@pytest.mark.parametrize("dt,engine", [(vb.FP32, 1), (vb.FP16, 1), (vb.FP16, 2)])
+def test_gemm(M, N, K, lda, epi, dt, engine):
+    rng = np.random.default_rng(M + N + K + epi)
+    fp16 = dt == vb.FP16
+    A = np.zeros((M, lda), np.float32)
+    A[:, :K] = rounded(rng.normal(size=(M, K)), dt)
+    ldw = lda
+    W = np.zeros((N, ldw), np.float32)
+    W[:, :K] = rounded(rng.normal(size=(N, K)) / math.sqrt(K), dt)
+    b = rounded(rng.normal(size=N) * 0.2, dt)
+    ldy = (N + 7) // 8 * 8  # 16-byte row strides, as the engine lays out its buffers
+    R = np.zeros((M, ldy), np.float32)
+    R[:, :N] = rounded(rng.normal(size=(M, N)), dt)
+    T = tname(dt)
+    dA, dW, db, dR = dev(A, T), dev(W, T), dev(b, T), dev(R, T)
+    Y = torch.full((M, ldy), float("nan"), device="cuda", dtype=T)
+    vb.gemm(dt, engine, dA, lda, dW, ldw, db, Y, ldy, dR if epi == 2 else None, ldy, M, N, K, epi,
+            gelu_tanh=(N % 2 == 1))
+    torch.cuda.synchronize()
+    vb.check_device()
+    got = Y.float().cpu().numpy()[:, :N]
+    ref = gemm_reference(A[:, :K], W[:, :K], b, R[:, :N], epi, N % 2 == 1, fp16)
+    err = oracle.rel_absmax(got, ref)
+    tol = 1e-5 if dt == vb.FP32 else 2e-3
+    assert err <= tol, f"rel_absmax {err:.3e}"
+
+
+def test_gemm_tensor_core_matches_cuda_core():
+    rng = np.random.default_rng(5)
+    M, N, K = 3000, 4096, 1024
+    A = dev(rng.normal(size=(M, K)), torch.float16)
+    W = dev(rng.normal(size=(N, K)) / 32, torch.float16)
+    b = dev(rng.normal(size=N), torch.float16)
+    Y1 = torch.empty((M, N), device="cuda", dtype=torch.float16)
+    Y2 = torch.empty_like(Y1)
+    vb.gemm(vb.FP16, 1, A, K, W, K, b, Y1, N, None, N, M, N, K, 0)
+    vb.gemm(vb.FP16, 2, A, K, W, K, b, Y2, N, None, N, M, N, K, 0)
+    torch.cuda.synchronize()
+    vb.check_device()
+    d = (Y1.float() - Y2.float()).abs().max().item() / Y1.float().abs().max().item()
+    assert d <= 2e-3
+    # repeatability: the same launch twice is bitwise equal
+    Y3 = torch.empty_like(Y1)
+    vb.gemm(vb.FP16, 2, A, K, W, K, b, Y3, N, None, N, M, N, K, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(Y2, Y3)
+
+
+@pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])
+@pytest.mark.parametrize("C", [128, 256, 384, 768, 1024, 2048])
+def test_layernorm(C, dt):
+    rng = np.random.default_rng(C)
+    rows = 333
+    x = rounded(rng.normal(size=(rows, C)) * 3 + 1, dt)
+    r = rounded(rng.normal(size=(rows, C)), dt)
+    w = rng.uniform(0.5, 1.5, C).astype(np.float32)
+    b = rng.normal(size=C).astype(np.float32)
+    T = tname(dt)
+    dx, dr, y, o1 = dev(x, T), dev(r, T), torch.empty((rows, C), device="cuda", dtype=T), \
+        torch.empty((rows, C), device="cuda", dtype=T)
+    vb.layernorm(dt, dx, C, dev(w, torch.float32), dev(b, torch.float32), y, C, rows, C, 1e-5)
+    torch.cuda.synchronize()
+
+    def ln(a):
+        a = a.astype(np.float64)
+        m = a.mean(1, keepdims=True)
+        return (a - m) / np.sqrt(((a - m) ** 2).mean(1, keepdims=True) + 1e-5) * w + b
+
+    tol = 1e-5 if dt == vb.FP32 else 2e-3
+    assert oracle.rel_absmax(y.float().cpu().numpy(), ln(x)) <= tol
+    vb.layernorm(dt, dx, C, dev(w, torch.float32), None, y, C, rows, C, 1e-5)
+    torch.cuda.synchronize()
+    assert oracle.rel_absmax(y.float().cpu().numpy(), ln(x) - b) <= tol
+    vb.add_layernorm(dt, dx, dr, o1, dev(w, torch.float32), dev(b, torch.float32), y, C, rows, C, 1e-5)
+    torch.cuda.synchronize()
+    s = rounded(x + r, dt)
+    assert np.array_equal(o1.float().cpu().numpy(), s), "residual sum must be the rounded fp32 sum"
+    assert oracle.rel_absmax(y.float().cpu().numpy(), ln(s)) <= tol

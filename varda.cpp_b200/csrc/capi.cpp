@@ -1,0 +1,307 @@
+// The C ABI (include/varda_b200.h) over the C++ engine: exceptions become status codes plus a
+// thread-local message.
+#include "../../include/varda_b200.h"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <memory>
+#include <string>
+
+#include "common.h"
+#include "engine.h"
+#include "gemm_tc.cuh"
+#include "graph.h"
+#include "kernels.cuh"
+#include "shard.h"
+
+struct vb_model {
+    std::unique_ptr<vb::Model> m;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+template <class F> int guard(F&& f) {
+    try {
+        f();
+        g_last_error.clear();
+        return VB_OK;
+    } catch (const vb::Error& e) {
+        g_last_error = e.what();
+        return e.cls;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "out of host memory";
+        return VB_ERR_INTERNAL;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return VB_ERR_INTERNAL;
+    } catch (...) {
+        g_last_error = "unknown error";
+        return VB_ERR_INTERNAL;
+    }
+}
+
+cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+vb::Options to_opts(const vb_options* o) {
+    vb::Options r;
+    if (o) {
+        if (o->precision != VB_PRECISION_FP32 && o->precision != VB_PRECISION_FP16)
+            vb::fail(vb::kInvalidArgument, "precision must be VB_PRECISION_FP32 or VB_PRECISION_FP16");
+        r.precision = o->precision;
+        r.cuda_device = o->cuda_device;
+        r.cuda_graph = o->cuda_graph != 0;
+    }
+    return r;
+}
+
+void need(const void* p, const char* what) {
+    if (!p) vb::fail(vb::kInvalidArgument, std::string(what) + " is NULL");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* vb_last_error(void) { return g_last_error.c_str(); }
+
+int vb_load(const char* path, const vb_options* opts, vb_model** out) {
+    return guard([&] {
+        need(path, "path");
+        need(out, "out");
+        *out = nullptr;
+        auto m = std::make_unique<vb_model>();
+        m->m = vb::load_model(path, to_opts(opts));
+        *out = m.release();
+    });
+}
+
+int vb_load_sharded(const char* path, const vb_options* opts, int rank, int world, const void* nccl_id,
+                    vb_model** out) {
+    return guard([&] {
+        need(path, "path");
+        need(out, "out");
+        *out = nullptr;
+        if (world < 1 || rank < 0 || rank >= world) vb::fail(vb::kInvalidArgument, "bad rank / world");
+        vb::Options o = to_opts(opts);
+        o.rank = rank, o.world = world, o.nccl_id = nccl_id;
+        if (world > 1) need(nccl_id, "nccl_id");
+        auto m = std::make_unique<vb_model>();
+        m->m = vb::load_model(path, o);
+        *out = m.release();
+    });
+}
+
+int vb_nccl_unique_id(void* out128) {
+    return guard([&] {
+        need(out128, "out");
+        vb::nccl_unique_id(out128);
+    });
+}
+
+void vb_free(vb_model* m) { delete m; }
+
+int vb_predict_step(vb_model* m, const float* x, float* y, vb_hook_fn hook, void* user) {
+    return guard([&] {
+        need(m, "model"), need(x, "x"), need(y, "y");
+        m->m->predict_step(x, y, hook, user);
+        if (vb::tc::take_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the tensor-core GEMM");
+    });
+}
+
+int vb_sizes(const vb_model* m, int64_t out8[8]) {
+    return guard([&] {
+        need(m, "model"), need(out8, "out");
+        m->m->sizes(out8);
+    });
+}
+
+int vb_data_range(const vb_model* m, int64_t* lo, int64_t* hi) {
+    return guard([&] {
+        need(m, "model"), need(lo, "lo"), need(hi, "hi");
+        m->m->data_range(lo, hi);
+    });
+}
+
+int vb_normalise(vb_model* m, const float* x, float* xn, void* stream) {
+    return guard([&] {
+        need(m, "model"), need(x, "x"), need(xn, "xn");
+        m->m->normalise(x, xn, S(stream));
+    });
+}
+int vb_forward_normalised(vb_model* m, const float* xn, float* yn, void* stream) {
+    return guard([&] {
+        need(m, "model"), need(xn, "xn"), need(yn, "yn");
+        m->m->forward_normalised(xn, yn, S(stream));
+    });
+}
+int vb_denormalise(vb_model* m, const float* yn, float* y, void* stream) {
+    return guard([&] {
+        need(m, "model"), need(yn, "yn"), need(y, "y");
+        m->m->denormalise(yn, y, S(stream));
+    });
+}
+int vb_predict_step_device(vb_model* m, const float* x, float* y, void* stream) {
+    return guard([&] {
+        need(m, "model"), need(x, "x"), need(y, "y");
+        m->m->predict_step_device(x, y, S(stream));
+    });
+}
+int vb_prepare(vb_model* m) {
+    return guard([&] {
+        need(m, "model");
+        m->m->prepare();
+    });
+}
+int vb_use_high_priority_stream(vb_model* m) {
+    return guard([&] {
+        need(m, "model");
+        m->m->use_high_priority_stream();
+    });
+}
+float* vb_device_input(vb_model* m) { return m ? m->m->device_input() : nullptr; }
+const float* vb_device_output(vb_model* m) { return m ? m->m->device_output() : nullptr; }
+void* vb_stream(vb_model* m) { return m ? static_cast<void*>(m->m->stream()) : nullptr; }
+int vb_enqueue_predict(vb_model* m) {
+    return guard([&] {
+        need(m, "model");
+        m->m->enqueue_predict();
+    });
+}
+int vb_device(const vb_model* m) { return m ? m->m->device() : -1; }
+size_t vb_weight_bytes(const vb_model* m) { return m ? m->m->weight_bytes() : 0; }
+size_t vb_activation_bytes(const vb_model* m) { return m ? m->m->activation_bytes() : 0; }
+int64_t vb_decoder_chunk_rows(const vb_model* m) { return m ? m->m->decoder_chunk_rows() : 0; }
+
+int vb_check_device(void) {
+    return guard([&] {
+        if (vb::tc::take_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the tensor-core GEMM");
+    });
+}
+
+int64_t vb_launch_count(void) { return vb::launch_counter(); }
+
+int64_t vb_profile_forward(vb_model* m, char* buf, size_t len) {
+    std::string s;
+    const int rc = guard([&] {
+        need(m, "model");
+        s = m->m->profile_forward();
+    });
+    if (rc != VB_OK) return -rc;
+    if (buf && len) {
+        const size_t n = std::min(len - 1, s.size());
+        std::memcpy(buf, s.data(), n);
+        buf[n] = 0;
+    }
+    return int64_t(s.size() + 1);
+}
+
+int vb_build_csr(const int64_t* ei, int64_t E, const float* ea, int A, int64_t n_src, int64_t n_dst, int32_t* row_ptr,
+                 int32_t* src, int32_t* edge_id, float* attr_csr) {
+    return guard([&] {
+        if (E < 0 || A < 1 || n_src < 0 || n_dst < 0) vb::fail(vb::kInvalidArgument, "bad graph sizes");
+        need(row_ptr, "row_ptr");
+        if (E > 0) need(ei, "edge_index"), need(ea, "edge_attr"), need(src, "src"), need(edge_id, "edge_id"),
+            need(attr_csr, "attr_csr");
+        vb::CsrGraph g = vb::build_csr_by_dst(ei, E, ea, A, n_src, n_dst);
+        std::memcpy(row_ptr, g.row_ptr.data(), g.row_ptr.size() * sizeof(int32_t));
+        if (E > 0) {
+            std::memcpy(src, g.src.data(), g.src.size() * sizeof(int32_t));
+            std::memcpy(edge_id, g.edge_id.data(), g.edge_id.size() * sizeof(int32_t));
+            std::memcpy(attr_csr, g.attr.data(), g.attr.size() * sizeof(float));
+        }
+    });
+}
+
+int vb_pack_edges(const int32_t* src, const float* attr, int A, int64_t E, int round_fp16, void* out16) {
+    return guard([&] {
+        vb::CsrGraph g;
+        g.n_edges = E;
+        g.attr_dim = A;
+        g.src.assign(src, src + E);
+        g.attr.assign(attr, attr + E * A);
+        auto p = vb::pack_edges(g, round_fp16 != 0);
+        std::memcpy(out16, p.data(), p.size() * sizeof(vb::EdgeRec));
+    });
+}
+
+int vb_attention(int dtype, const int32_t* row_ptr, const void* edges, int64_t dst_lo, int64_t n_rows, const void* q,
+                 int64_t ldq, const void* k, const void* v, int64_t ldkv, const void* xr, int64_t ldxr, void* out,
+                 int64_t ldo, const float* w_e, int C, int heads, int head_dim, void* stream) {
+    return guard([&] {
+        auto run = [&](auto* tag) {
+            using T = std::remove_pointer_t<decltype(tag)>;
+            vb::k::AttnArgs<T> a;
+            a.row_ptr = row_ptr, a.edges = static_cast<const vb::EdgeRec*>(edges), a.dst_lo = dst_lo;
+            a.n_rows = n_rows, a.q = static_cast<const T*>(q), a.ldq = ldq, a.k = static_cast<const T*>(k);
+            a.v = static_cast<const T*>(v), a.ldkv = ldkv, a.xr = static_cast<const T*>(xr), a.ldxr = ldxr;
+            a.out = static_cast<T*>(out), a.ldo = ldo, a.w_e = w_e, a.C = C, a.heads = heads, a.head_dim = head_dim;
+            vb::k::attention<T>(a, S(stream));
+        };
+        if (dtype == VB_PRECISION_FP32) run(static_cast<float*>(nullptr));
+        else if (dtype == VB_PRECISION_FP16) run(static_cast<__half*>(nullptr));
+        else vb::fail(vb::kInvalidArgument, "dtype");
+    });
+}
+
+int vb_gemm(int dtype, int engine, const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* Y,
+            int64_t ldy, const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int epilogue, int gelu_tanh,
+            void* stream) {
+    return guard([&] {
+        if (epilogue < 0 || epilogue > 2) vb::fail(vb::kInvalidArgument, "epilogue");
+        auto fill = [&](auto& a, auto* tag) {
+            using T = std::remove_pointer_t<decltype(tag)>;
+            a.A = static_cast<const T*>(A), a.lda = lda, a.W = static_cast<const T*>(W), a.ldw = ldw;
+            a.bias = static_cast<const T*>(bias), a.C = static_cast<T*>(Y), a.ldc = ldy;
+            a.R = static_cast<const T*>(R), a.ldr = ldr, a.M = M, a.N = N, a.K = K, a.epi = epilogue;
+            a.gelu_tanh = gelu_tanh != 0;
+        };
+        if (dtype == VB_PRECISION_FP32) {
+            if (engine == 2) vb::fail(vb::kUnsupported, "tensor-core gemm takes fp16 only");
+            vb::k::GemmArgs<float> a;
+            fill(a, static_cast<float*>(nullptr));
+            vb::k::gemm_simt<float>(a, S(stream));
+        } else if (dtype == VB_PRECISION_FP16) {
+            vb::k::GemmArgs<__half> a;
+            fill(a, static_cast<__half*>(nullptr));
+            if (engine != 1 && vb::tc::supported(a)) vb::tc::gemm(a, S(stream));
+            else if (engine == 2) vb::fail(vb::kUnsupported, "operands not aligned for the tensor-core gemm");
+            else vb::k::gemm_simt<__half>(a, S(stream));
+        } else {
+            vb::fail(vb::kInvalidArgument, "dtype");
+        }
+    });
+}
+
+int vb_layernorm(int dtype, const void* x, int64_t ldx, const float* w, const float* b, void* y, int64_t ldy,
+                 int64_t rows, int C, float eps, void* stream) {
+    return guard([&] {
+        if (dtype == VB_PRECISION_FP32)
+            vb::k::layernorm<float>(static_cast<const float*>(x), ldx, w, b, static_cast<float*>(y), ldy, rows, C, eps,
+                                    S(stream));
+        else if (dtype == VB_PRECISION_FP16)
+            vb::k::layernorm<__half>(static_cast<const __half*>(x), ldx, w, b, static_cast<__half*>(y), ldy, rows, C,
+                                     eps, S(stream));
+        else vb::fail(vb::kInvalidArgument, "dtype");
+    });
+}
+
+int vb_add_layernorm(int dtype, const void* a, const void* r, void* out1, const float* w, const float* b, void* ln,
+                     int64_t ld, int64_t rows, int C, float eps, void* stream) {
+    return guard([&] {
+        if (dtype == VB_PRECISION_FP32)
+            vb::k::add_layernorm<float>(static_cast<const float*>(a), static_cast<const float*>(r),
+                                        static_cast<float*>(out1), w, b, static_cast<float*>(ln), ld, rows, C, eps,
+                                        S(stream));
+        else if (dtype == VB_PRECISION_FP16)
+            vb::k::add_layernorm<__half>(static_cast<const __half*>(a), static_cast<const __half*>(r),
+                                         static_cast<__half*>(out1), w, b, static_cast<__half*>(ln), ld, rows, C, eps,
+                                         S(stream));
+        else vb::fail(vb::kInvalidArgument, "dtype");
+    });
+}
+
+}  // extern "C"

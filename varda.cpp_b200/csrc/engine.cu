@@ -1,0 +1,805 @@
+// Engine<T>: loading, buffers and the GraphTransformer forward pass on one B200.
+//
+// The op sequence is the reference's (CPU oracle backend_cpu.cpp:297-537; CUDA engine
+// backend_cuda.cu:523-667), restructured for this GPU:
+//   * residual adds and GELU are fused into the epilogue of the GEMM that produces them
+//     (proj + residual, mlp1 + GELU, mlp2 + residual), keeping the autocast roundings
+//     T(T(acc + b) + r) and T(gelu(T(acc + b)));
+//   * q|k|v|self (processor), q|self and k|v (mappers) are one stacked GEMM each;
+//   * the edge projection is folded into the attention kernel (no [E, C] tensor);
+//   * with 180 GB of HBM the decoder normally runs all data rows as one chunk.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <type_traits>
+#include <vector>
+
+#include "common.h"
+#include "config.h"
+#include "engine.h"
+#include "gemm_tc.cuh"
+#include "graph.h"
+#include "kernels.cuh"
+#include "safetensors.h"
+#include "shard.h"
+
+namespace vb {
+
+namespace {
+
+int64_t env_int(const char* name, int64_t dflt) {
+    const char* v = std::getenv(name);
+    return v && *v ? std::atoll(v) : dflt;
+}
+
+template <class T> struct Lin {
+    DeviceBuffer w, b;
+    int64_t N = 0, K = 0, ldw = 0;
+    const T* W() const { return w.as<T>(); }
+    const T* B() const { return b.get() ? b.as<T>() : nullptr; }
+};
+
+struct Norm {
+    DeviceBuffer w, b;  // fp32 [C]; b empty when absent
+    const float* W() const { return w.as<float>(); }
+    const float* B() const { return b.get() ? b.as<float>() : nullptr; }
+};
+
+template <class T> struct Block {
+    bool mapper = false;
+    Norm ln_src, ln_dst, ln_mlp;
+    Lin<T> qkvs, qs, kv, proj, mlp1, mlp2;
+    DeviceBuffer w_e;  // fp32 [4, C]
+};
+
+struct GraphDev {
+    std::string name;
+    DeviceBuffer row_ptr, edges;
+    int64_t n_src = 0, n_dst = 0, n_edges = 0;
+    int max_degree = 0;
+    const int32_t* rp() const { return row_ptr.as<int32_t>(); }
+    const EdgeRec* ed() const { return edges.as<EdgeRec>(); }
+};
+
+template <class T> float round_op(float x) {
+    if (std::is_same<T, float>::value) return x;
+    return __half2float(__float2half_rn(x));
+}
+
+}  // namespace
+
+// The names a model file must hold, exactly (the reference consumes every tensor with take() and
+// then requires that nothing is left, model.cpp:76; names listed in config `absent` may be missing).
+void check_tensor_set(const SafeTensorsFile& f, const Config& c) {
+    std::vector<std::string> want = {"norm.mul", "norm.add", "nodes.data.attr", "nodes.hidden.attr"};
+    for (const char* g : {"enc", "proc", "dec"})
+        want.push_back(std::string("graph.") + g + ".edge_index"), want.push_back(std::string("graph.") + g + ".edge_attr");
+    auto lin = [&](const std::string& n) {
+        want.push_back(n + ".weight");
+        if (!c.is_absent(n + ".bias")) want.push_back(n + ".bias");
+    };
+    for (const char* n : {"enc.emb_src", "enc.emb_dst", "dec.emb_dst", "dec.out_proj", "dec.out_norm"}) lin(n);
+    for (const std::string& b : c.block_names) {
+        const bool mapper = b == "enc.block" || b == "dec.block";
+        for (const char* l : {"q", "k", "v", "self", "edge", "proj", "mlp1", "mlp2", "ln_dst", "ln_mlp"}) lin(b + "." + l);
+        if (mapper) lin(b + ".ln_src");
+    }
+    for (const std::string& n : want) f.peek(n);  // throws "missing tensor"
+    std::vector<std::string> extra;
+    for (const std::string& n : f.names()) {
+        if (n == "grid.latitudes" || n == "grid.longitudes") continue;
+        if (std::find(want.begin(), want.end(), n) == want.end()) extra.push_back(n);
+    }
+    if (f.has("grid.latitudes") != f.has("grid.longitudes"))
+        fail(kFormat, f.path() + ": grid.latitudes and grid.longitudes must come together");
+    if (!extra.empty()) {
+        std::string m = std::to_string(extra.size()) + " tensor(s) not consumed by the engine:";
+        for (size_t i = 0; i < extra.size() && i < 20; ++i) m += " " + extra[i];
+        fail(kFormat, f.path() + ": " + m);
+    }
+}
+
+template <class T>
+class Engine final : public Model {
+public:
+    Engine(const std::string& path, const Options& o);
+    ~Engine() override;
+
+    void predict_step(const float* x, float* y, HookFn hook, void* user) override;
+    int64_t input_numel() const override { return int64_t(T_in_) * G_ * V_in_; }
+    int64_t output_numel() const override { return int64_t(T_out_) * G_ * V_out_; }
+    void normalise(const float* x, float* xn, cudaStream_t s) override {
+        k::normalise(x, mul_in_.as<float>(), add_in_.as<float>(), xn, input_numel(), V_in_, s);
+    }
+    void forward_normalised(const float* xn, float* yn, cudaStream_t s) override { forward(xn, yn, s, nullptr); }
+    void denormalise(const float* yn, float* y, cudaStream_t s) override {
+        k::denormalise(yn, add_out_.as<float>(), mul_out_.as<float>(), y, output_numel(), V_out_, s);
+    }
+    void predict_step_device(const float* x, float* y, cudaStream_t s) override {
+        normalise(x, xn_, s);
+        forward(xn_, yn_, s, nullptr);
+        denormalise(yn_, y, s);
+    }
+    void prepare() override;
+    void use_high_priority_stream() override;
+    float* device_input() override { return x_dev_; }
+    const float* device_output() const override { return y_dev_; }
+    cudaStream_t stream() const override { return stream_; }
+    void enqueue_predict() override;
+    int device() const override { return dev_; }
+    size_t weight_bytes() const override { return weight_bytes_; }
+    size_t activation_bytes() const override { return act_bytes_; }
+    int64_t decoder_chunk_rows() const override { return dec_rows_; }
+    void sizes(int64_t o[8]) const override {
+        o[0] = T_in_, o[1] = G_, o[2] = V_in_, o[3] = T_out_, o[4] = V_out_, o[5] = H_, o[6] = C_, o[7] = n_proc_;
+    }
+    void data_range(int64_t* lo, int64_t* hi) const override { *lo = 0, *hi = G_; }
+    std::string profile_forward() override;
+
+private:
+    struct Hook;
+    // ---- profiling (eager runs only): an event pair around every launch
+    struct ProfRec {
+        std::string name;
+        cudaEvent_t a, b;
+        double flop, bytes;
+    };
+    std::vector<ProfRec>* prof_ = nullptr;
+    struct Span {
+        Engine* e;
+        cudaStream_t s;
+        Span(Engine* en, cudaStream_t st, std::string name, double flop, double bytes) : e(en), s(st) {
+            if (!e->prof_) return;
+            ProfRec r{std::move(name), nullptr, nullptr, flop, bytes};
+            VB_CUDA(cudaEventCreate(&r.a));
+            VB_CUDA(cudaEventCreate(&r.b));
+            VB_CUDA(cudaEventRecord(r.a, s));
+            e->prof_->push_back(r);
+        }
+        ~Span() {
+            if (e->prof_) cudaEventRecord(e->prof_->back().b, s);
+        }
+    };
+    void ln(const T* x, const Norm& n, T* y, int64_t rows, cudaStream_t s) {
+        Span sp(this, s, "layernorm", 0, double(rows) * C_ * 2 * sizeof(T));
+        k::layernorm<T>(x, C_, n.W(), n.B(), y, C_, rows, C_, eps_, s);
+    }
+    Lin<T> load_linear(SafeTensorsFile& f, const std::vector<std::string>& names, int64_t N_each, int64_t K);
+    Norm load_norm(SafeTensorsFile& f, const std::string& name);
+    Block<T> load_block(SafeTensorsFile& f, const std::string& pre, bool mapper);
+    GraphDev load_graph(SafeTensorsFile& f, const std::string& g, int64_t n_src, int64_t n_dst);
+    DeviceBuffer upload(const void* h, size_t bytes);
+    T* act(size_t elems);
+    float* actf(size_t elems);
+
+    void linear(const Lin<T>& L, const T* x, int64_t ldx, T* y, int64_t ldy, int64_t M, cudaStream_t s,
+                int epi = k::kEpiBias, const T* R = nullptr, int64_t ldr = 0);
+    void attention(const GraphDev& g, const Block<T>& b, int64_t lo, int64_t n, const T* q, int64_t ldq, const T* kk,
+                   const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out, cudaStream_t s);
+    void forward(const float* xn, float* yn, cudaStream_t s, Hook* hk);
+    bool capture_graph(cudaStream_t s);
+
+    Config cfg_;
+    Options opts_;
+    int dev_ = 0;
+    cudaStream_t stream_ = nullptr;
+    bool use_tc_ = false;
+    int C_ = 0, heads_ = 0, hd_ = 0, mlp_ = 0, n_proc_ = 0, T_in_ = 0, T_out_ = 0, V_in_ = 0, V_out_ = 0, V_dec_ = 0;
+    int A_node_ = 0, F_ = 0;
+    int64_t ldF_ = 0, ldA_ = 0, ldVo_ = 0;
+    int64_t G_ = 0, H_ = 0;
+    float eps_ = 0;
+    bool gelu_tanh_ = false;
+
+    Lin<T> enc_emb_src_, enc_emb_dst_, dec_emb_dst_, dec_out_proj_;
+    Norm dec_out_norm_;
+    Block<T> enc_, dec_;
+    std::vector<Block<T>> proc_;
+    GraphDev g_enc_, g_proc_, g_dec_;
+    DeviceBuffer mul_in_, add_in_, mul_out_, add_out_, res_src_, bounds_, bidx_;
+    int n_bounds_ = 0;
+    DeviceBuffer d_attr_, h_attr_;
+    std::vector<float> h_attr_host_;
+    size_t weight_bytes_ = 0;
+
+    std::vector<DeviceBuffer> acts_;
+    size_t act_bytes_ = 0;
+    float *x_dev_ = nullptr, *xn_ = nullptr, *yn_ = nullptr, *y_dev_ = nullptr;
+    T *x_data_ = nullptr, *region_ = nullptr, *dec_out_ = nullptr;
+    T *z_enc_ = nullptr, *zA_ = nullptr, *zB_ = nullptr, *xh_ = nullptr, *qkvs_ = nullptr, *sbuf_ = nullptr;
+    T *out1_ = nullptr, *hbuf_ = nullptr;
+    int64_t dec_rows_ = 0;
+
+    DeviceBuffer hook_stage_, hook_xsrc_, hook_prebound_;
+    bool ran_eager_ = false, graph_failed_ = false;
+    cudaGraphExec_t graph_exec_ = nullptr;
+};
+
+// ====================================================================== hook
+
+template <class T>
+struct Engine<T>::Hook {
+    Engine& e;
+    HookFn fn;
+    void* user;
+    cudaStream_t s;
+
+    void host(const std::string& key, const float* d, std::vector<int64_t> shape) {
+        fn(key.c_str(), d, shape.data(), int(shape.size()), user);
+    }
+    template <class U> void fetch(const U* d, int64_t ld, int64_t rows, int64_t cols, float* dst, int64_t r0 = 0) {
+        VB_CUDA(cudaStreamSynchronize(s));
+        const int64_t stage = int64_t(1) << 24;
+        if (!e.hook_stage_.get()) e.hook_stage_.alloc(size_t(stage) * sizeof(float));
+        const int64_t blk = std::max<int64_t>(1, stage / cols);
+        for (int64_t a = 0; a < rows; a += blk) {
+            const int64_t n = std::min(blk, rows - a);
+            k::convert_2d<U, float>(d + a * ld, ld, e.hook_stage_.as<float>(), cols, n, cols, s);
+            VB_CUDA(cudaMemcpyAsync(dst + (r0 + a) * cols, e.hook_stage_.get(), size_t(n * cols) * sizeof(float),
+                                    cudaMemcpyDeviceToHost, s));
+            VB_CUDA(cudaStreamSynchronize(s));
+        }
+    }
+    template <class U> void dev(const std::string& key, const U* d, int64_t ld, int64_t rows, int64_t cols,
+                                std::vector<int64_t> shape) {
+        std::vector<float> h(size_t(rows * cols));
+        fetch(d, ld, rows, cols, h.data());
+        host(key, h.data(), shape);
+    }
+};
+
+// ====================================================================== loading
+
+template <class T>
+DeviceBuffer Engine<T>::upload(const void* h, size_t bytes) {
+    DeviceBuffer b(bytes);
+    if (bytes) VB_CUDA(cudaMemcpy(b.get(), h, bytes, cudaMemcpyHostToDevice));
+    weight_bytes_ += bytes;
+    return b;
+}
+
+// Linear layers stacked by output rows, each `<name>.weight` F32 [N_each, K] and `<name>.bias` F32
+// [N_each] unless listed absent; stored as T with the row stride padded to a multiple of 8 elements
+// (16 bytes in fp16, the tensor-memory-access alignment), zero padded.
+template <class T>
+Lin<T> Engine<T>::load_linear(SafeTensorsFile& f, const std::vector<std::string>& names, int64_t N_each, int64_t K) {
+    Lin<T> L;
+    L.K = K;
+    L.ldw = int64_t(align_up(size_t(K), 8));
+    L.N = N_each * int64_t(names.size());
+    std::vector<T> w(size_t(L.N * L.ldw), T(0.0f)), b(size_t(L.N), T(0.0f));
+    bool any_bias = false;
+    for (size_t i = 0; i < names.size(); ++i) {
+        const TensorView& tw = f.take(names[i] + ".weight", DType::F32, {N_each, K});
+        for (int64_t r = 0; r < N_each; ++r)
+            for (int64_t c = 0; c < K; ++c)
+                w[size_t((int64_t(i) * N_each + r) * L.ldw + c)] = T(tw.as<float>()[r * K + c]);
+        const std::string bn = names[i] + ".bias";
+        if (!cfg_.is_absent(bn)) {
+            const TensorView& tb = f.take(bn, DType::F32, {N_each});
+            for (int64_t r = 0; r < N_each; ++r) b[size_t(int64_t(i) * N_each + r)] = T(tb.as<float>()[r]);
+            any_bias = true;
+        }
+    }
+    L.w = upload(w.data(), w.size() * sizeof(T));
+    if (any_bias) L.b = upload(b.data(), b.size() * sizeof(T));
+    return L;
+}
+
+template <class T>
+Norm Engine<T>::load_norm(SafeTensorsFile& f, const std::string& name) {
+    Norm n;
+    const TensorView& w = f.take(name + ".weight", DType::F32, {C_});
+    n.w = upload(w.data, w.nbytes);
+    if (!cfg_.is_absent(name + ".bias")) {
+        const TensorView& b = f.take(name + ".bias", DType::F32, {C_});
+        n.b = upload(b.data, b.nbytes);
+    }
+    return n;
+}
+
+template <class T>
+Block<T> Engine<T>::load_block(SafeTensorsFile& f, const std::string& pre, bool mapper) {
+    Block<T> b;
+    b.mapper = mapper;
+    if (mapper) b.ln_src = load_norm(f, pre + ".ln_src");
+    b.ln_dst = load_norm(f, pre + ".ln_dst");
+    b.ln_mlp = load_norm(f, pre + ".ln_mlp");
+    auto P = [&](const char* n) { return pre + "." + n; };
+    if (mapper) {
+        b.qs = load_linear(f, {P("q"), P("self")}, C_, C_);
+        b.kv = load_linear(f, {P("k"), P("v")}, C_, C_);
+    } else {
+        b.qkvs = load_linear(f, {P("q"), P("k"), P("v"), P("self")}, C_, C_);
+    }
+    b.proj = load_linear(f, {P("proj")}, C_, C_);
+    b.mlp1 = load_linear(f, {P("mlp1")}, mlp_, C_);
+    b.mlp2 = load_linear(f, {P("mlp2")}, C_, mlp_);
+    const int A = cfg_.edge_attr_dim;
+    const TensorView& we = f.take(P("edge") + ".weight", DType::F32, {C_, A});
+    // [4, C], attribute-major (coalesced per-lane vector loads): W_e[:, 0..2] zero padded, then b_e.
+    // fp16 mode rounds the edge Linear's weights to fp16, as autocast does.
+    std::vector<float> w4(size_t(C_) * 4, 0.0f);
+    for (int c = 0; c < C_; ++c)
+        for (int a = 0; a < A; ++a) w4[size_t(a) * C_ + c] = round_op<T>(we.as<float>()[c * A + a]);
+    if (!cfg_.is_absent(P("edge") + ".bias")) {
+        const TensorView& bv = f.take(P("edge") + ".bias", DType::F32, {C_});
+        for (int c = 0; c < C_; ++c) w4[size_t(3) * C_ + c] = round_op<T>(bv.as<float>()[c]);
+    }
+    b.w_e = upload(w4.data(), w4.size() * sizeof(float));
+    return b;
+}
+
+template <class T>
+GraphDev Engine<T>::load_graph(SafeTensorsFile& f, const std::string& g, int64_t n_src, int64_t n_dst) {
+    const TensorView& ei = f.take("graph." + g + ".edge_index");
+    const TensorView& ea = f.take("graph." + g + ".edge_attr");
+    if (ea.shape.size() != 2 || ea.shape[1] != cfg_.edge_attr_dim)
+        fail(kFormat, ea.name + ": expected [E, " + std::to_string(cfg_.edge_attr_dim) + "], got " + ea.shape_str());
+    CsrGraph csr = build_csr_by_dst(ei, ea, n_src, n_dst);
+    std::vector<EdgeRec> packed = pack_edges(csr, !std::is_same<T, float>::value);
+    GraphDev d;
+    d.name = g;
+    d.row_ptr = upload(csr.row_ptr.data(), csr.row_ptr.size() * sizeof(int32_t));
+    d.edges = upload(packed.data(), std::max<size_t>(1, packed.size()) * sizeof(EdgeRec));
+    d.n_src = n_src;
+    d.n_dst = n_dst;
+    d.n_edges = csr.n_edges;
+    d.max_degree = csr.max_degree();
+    return d;
+}
+
+template <class T>
+T* Engine<T>::act(size_t elems) {
+    acts_.emplace_back(align_up(std::max<size_t>(1, elems) * sizeof(T), 256));
+    act_bytes_ += acts_.back().bytes();
+    return acts_.back().template as<T>();
+}
+
+template <class T>
+float* Engine<T>::actf(size_t elems) {
+    acts_.emplace_back(align_up(std::max<size_t>(1, elems) * sizeof(float), 256));
+    act_bytes_ += acts_.back().bytes();
+    return acts_.back().template as<float>();
+}
+
+template <class T>
+Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
+    dev_ = o.cuda_device;
+    SafeTensorsFile file(path);
+    if (file.metadata("varda_format") != "1")
+        fail(kFormat, path + ": unsupported varda_format " + file.metadata("varda_format"));
+    cfg_ = parse_config(file.metadata("config"));
+    check_tensor_set(file, cfg_);  // format errors surface before any device call
+    VB_CUDA(cudaSetDevice(dev_));
+    file.prefetch();
+    const Config& c = cfg_;
+    C_ = c.num_channels, heads_ = c.num_heads, hd_ = c.head_dim, mlp_ = c.mlp_hidden;
+    n_proc_ = c.num_processor_layers, T_in_ = c.n_input_steps, T_out_ = c.n_output_steps;
+    V_in_ = c.n_input_vars, V_out_ = c.n_output_vars, V_dec_ = c.dec_out_features();
+    A_node_ = c.node_attr_dim, G_ = c.n_data_nodes, H_ = c.n_hidden_nodes;
+    eps_ = c.layer_norm_eps, gelu_tanh_ = c.gelu_tanh;
+    F_ = c.src_features();
+    ldF_ = int64_t(align_up(size_t(F_), 8));
+    ldA_ = int64_t(align_up(size_t(A_node_), 8));
+    ldVo_ = int64_t(align_up(size_t(V_dec_), 8));
+    if (C_ % 128 || C_ > 2048) fail(kUnsupported, "num_channels must be a multiple of 128, <= 2048");
+    if (hd_ % 4 || hd_ > 256) fail(kUnsupported, "head_dim must be a multiple of 4, <= 256");
+    if (mlp_ % 8) fail(kUnsupported, "mlp_hidden must be a multiple of 8");
+    if (c.edge_attr_dim < 1 || c.edge_attr_dim > 3) fail(kUnsupported, "edge_attr_dim must be 1..3");
+    if (n_proc_ < 1) fail(kUnsupported, "needs at least one processor block");
+    const bool fp16 = !std::is_same<T, float>::value;
+    use_tc_ = fp16 && opts_.gemm == 0 && env_int("VB_GEMM_SIMT", 0) == 0;
+    VB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+
+    // ---- normaliser, residual, bounding
+    const TensorView& mul = file.take("norm.mul", DType::F32, {c.n_data_vars});
+    const TensorView& add = file.take("norm.add", DType::F32, {c.n_data_vars});
+    std::vector<float> mi, ai, mo, ao;
+    for (int i : c.norm_input) mi.push_back(mul.as<float>()[i]), ai.push_back(add.as<float>()[i]);
+    for (int i : c.norm_output) mo.push_back(mul.as<float>()[i]), ao.push_back(add.as<float>()[i]);
+    mul_in_ = upload(mi.data(), mi.size() * 4);
+    add_in_ = upload(ai.data(), ai.size() * 4);
+    mul_out_ = upload(mo.data(), mo.size() * 4);
+    add_out_ = upload(ao.data(), ao.size() * 4);
+    std::vector<int> rs(size_t(V_out_), -1);
+    for (size_t k2 = 0; k2 < c.residual_output.size(); ++k2) rs[size_t(c.residual_output[k2])] = c.residual_input[k2];
+    res_src_ = upload(rs.data(), rs.size() * 4);
+    std::vector<k::BoundDev> bd;
+    std::vector<int> bidx;
+    for (const Bounding& b : c.bounding) {
+        k::BoundDev d;
+        d.type = b.type == "relu" ? 0 : b.type == "hardtanh" ? 1 : 2;
+        d.n = int(b.index.size());
+        d.idx_off = int(bidx.size());
+        bidx.insert(bidx.end(), b.index.begin(), b.index.end());
+        d.tot_off = int(bidx.size());
+        d.n_tot = int(b.total_index.size());
+        bidx.insert(bidx.end(), b.total_index.begin(), b.total_index.end());
+        d.lo = b.min, d.hi = b.max;
+        for (int i : b.index)
+            for (int t : b.total_index)
+                if (i == t) fail(kUnsupported, "fraction bounding index overlaps its total_index");
+        bd.push_back(d);
+    }
+    n_bounds_ = int(bd.size());
+    if (bidx.empty()) bidx.push_back(0);
+    if (bd.empty()) bd.push_back(k::BoundDev{});
+    bounds_ = upload(bd.data(), bd.size() * sizeof(k::BoundDev));
+    bidx_ = upload(bidx.data(), bidx.size() * 4);
+
+    // ---- node attributes (and the optional grid coordinates, consumed as the reference does)
+    if (file.has("grid.latitudes") || file.has("grid.longitudes")) {
+        file.take("grid.latitudes", DType::F64, {G_});
+        file.take("grid.longitudes", DType::F64, {G_});
+    }
+    for (const auto& kv : file.metadata())
+        if (kv.first == "cutout") fail(kUnsupported, "multi-source (cutout) grids are not supported");
+    const TensorView& da = file.take("nodes.data.attr", DType::F32, {G_, A_node_});
+    const TensorView& ha = file.take("nodes.hidden.attr", DType::F32, {H_, A_node_});
+    d_attr_ = upload(da.data, da.nbytes);
+    h_attr_host_.assign(ha.as<float>(), ha.as<float>() + ha.numel());
+    {
+        std::vector<T> hp(size_t(H_ * ldA_), T(0.0f));
+        for (int64_t r = 0; r < H_; ++r)
+            for (int a = 0; a < A_node_; ++a) hp[size_t(r * ldA_ + a)] = T(ha.as<float>()[r * A_node_ + a]);
+        h_attr_ = upload(hp.data(), hp.size() * sizeof(T));
+    }
+
+    // ---- weights
+    enc_emb_src_ = load_linear(file, {"enc.emb_src"}, C_, F_);
+    enc_emb_dst_ = load_linear(file, {"enc.emb_dst"}, C_, A_node_);
+    dec_emb_dst_ = load_linear(file, {"dec.emb_dst"}, C_, F_);
+    dec_out_norm_ = load_norm(file, "dec.out_norm");
+    dec_out_proj_ = load_linear(file, {"dec.out_proj"}, V_dec_, C_);
+    enc_ = load_block(file, "enc.block", true);
+    for (int i = 0; i < n_proc_; ++i) proc_.push_back(load_block(file, "proc." + std::to_string(i), false));
+    dec_ = load_block(file, "dec.block", true);
+
+    // ---- graphs
+    g_enc_ = load_graph(file, "enc", G_, H_);
+    g_proc_ = load_graph(file, "proc", H_, H_);
+    g_dec_ = load_graph(file, "dec", H_, G_);
+    file.require_all_consumed();
+
+    // ---- activations
+    x_dev_ = actf(size_t(input_numel()));
+    xn_ = actf(size_t(input_numel()));
+    yn_ = actf(size_t(output_numel()));
+    y_dev_ = actf(size_t(output_numel()));
+    x_data_ = act(size_t(G_ * ldF_));
+    dec_out_ = act(size_t(G_ * ldVo_));
+    z_enc_ = act(size_t(H_ * C_));
+    zA_ = act(size_t(H_ * C_));
+    zB_ = act(size_t(H_ * C_));
+    xh_ = act(size_t(H_ * C_));
+    qkvs_ = act(size_t(H_ * 4 * C_));
+    sbuf_ = act(size_t(H_ * C_));
+    out1_ = act(size_t(H_ * C_));
+    hbuf_ = act(size_t(H_ * mlp_));
+    // Shared region: the encoder's source side ([G, C] embedding + [G, 2C] k|v), then the decoder's
+    // destination chunks (6C + mlp per row). All G rows in one chunk unless limited.
+    const int64_t enc_elems = G_ * 3 * C_;
+    const int64_t per_row = 6 * int64_t(C_) + mlp_;
+    int64_t rows = opts_.dec_chunk_rows > 0 ? opts_.dec_chunk_rows : env_int("VB_DEC_CHUNK_ROWS", G_);
+    rows = std::min<int64_t>(std::max<int64_t>(rows, 1), G_);
+    const int64_t nch = (G_ + rows - 1) / rows;
+    rows = std::min<int64_t>(int64_t(align_up(size_t((G_ + nch - 1) / nch), 128)), G_);
+    dec_rows_ = rows;
+    region_ = act(size_t(std::max(enc_elems, rows * per_row)));
+    VB_CUDA(cudaDeviceSynchronize());
+}
+
+template <class T>
+Engine<T>::~Engine() {
+    cudaSetDevice(dev_);
+    if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+template <class T>
+void Engine<T>::use_high_priority_stream() {
+    VB_CUDA(cudaSetDevice(dev_));
+    int least = 0, greatest = 0;
+    VB_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+    cudaStream_t s = nullptr;
+    VB_CUDA(cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, greatest));
+    VB_CUDA(cudaStreamSynchronize(stream_));
+    VB_CUDA(cudaStreamDestroy(stream_));
+    stream_ = s;
+}
+
+// ====================================================================== forward
+
+template <class T>
+void Engine<T>::linear(const Lin<T>& L, const T* x, int64_t ldx, T* y, int64_t ldy, int64_t M, cudaStream_t s,
+                       int epi, const T* R, int64_t ldr) {
+    k::GemmArgs<T> a;
+    a.A = x, a.lda = ldx, a.W = L.W(), a.ldw = L.ldw, a.bias = L.B(), a.C = y, a.ldc = ldy;
+    a.R = R, a.ldr = ldr, a.M = M, a.N = L.N, a.K = L.K, a.epi = epi, a.gelu_tanh = gelu_tanh_;
+    if constexpr (std::is_same<T, __half>::value) {
+        if (use_tc_ && tc::supported(a)) {
+            Span sp(this, s, "gemm_tc N=" + std::to_string(L.N) + " K=" + std::to_string(L.K) + " epi=" +
+                                 std::to_string(epi), 2.0 * double(M) * double(L.N) * double(L.K), 0);
+            tc::gemm(a, s);
+            return;
+        }
+    }
+    Span sp(this, s, "gemm_simt N=" + std::to_string(L.N) + " K=" + std::to_string(L.K) + " epi=" + std::to_string(epi),
+            2.0 * double(M) * double(L.N) * double(L.K), 0);
+    k::gemm_simt<T>(a, s);
+}
+
+template <class T>
+void Engine<T>::attention(const GraphDev& g, const Block<T>& b, int64_t lo, int64_t n, const T* q, int64_t ldq,
+                          const T* kk, const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out, cudaStream_t s) {
+    k::AttnArgs<T> a;
+    a.row_ptr = g.rp(), a.edges = g.ed(), a.dst_lo = lo, a.n_rows = n;
+    a.q = q, a.ldq = ldq, a.k = kk, a.v = v, a.ldkv = ldkv, a.xr = xr, a.ldxr = ldxr, a.out = out, a.ldo = C_;
+    a.w_e = b.w_e.template as<float>(), a.C = C_, a.heads = heads_, a.head_dim = hd_;
+    // compulsory bytes: q, x_r, out per destination, k and v per source, one 16-byte record per
+    // edge, row_ptr, the [4, C] edge weights
+    double edges = 0;
+    if (prof_) {
+        int32_t e0 = 0, e1 = 0;
+        VB_CUDA(cudaMemcpy(&e0, g.rp() + lo, 4, cudaMemcpyDeviceToHost));
+        VB_CUDA(cudaMemcpy(&e1, g.rp() + lo + n, 4, cudaMemcpyDeviceToHost));
+        edges = double(e1 - e0);
+    }
+    const double bytes = double(sizeof(T)) * C_ * (3.0 * n + 2.0 * double(g.n_src)) + 16.0 * edges + 4.0 * (n + 1) +
+                         16.0 * C_;
+    Span sp(this, s, "attention " + g.name, 0, bytes);
+    k::attention<T>(a, s);
+}
+
+template <class T>
+void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
+    const int64_t G = G_, H = H_, C = C_;
+    {
+        Span sp(this, s, "assemble", 0, double(G) * (T_in_ * V_in_ * 4 + A_node_ * 4 + ldF_ * sizeof(T)));
+        k::assemble<T>(xn, d_attr_.as<float>(), T_in_, G, V_in_, A_node_, x_data_, ldF_, s);
+    }
+    if (hk) {
+        if (std::is_same<T, float>::value) {
+            hk->dev("enc.x_src", x_data_, ldF_, G, F_, {G, F_});
+        } else {  // the reference's x_data is fp32; the fp16 cast happens inside the Linear
+            if (!hook_xsrc_.get()) hook_xsrc_.alloc(size_t(G * F_) * sizeof(float));
+            k::assemble<float>(xn, d_attr_.as<float>(), T_in_, G, V_in_, A_node_, hook_xsrc_.as<float>(), F_, s);
+            hk->dev("enc.x_src", hook_xsrc_.as<float>(), F_, G, F_, {G, F_});
+        }
+        hk->host("enc.x_dst", h_attr_host_.data(), {H, A_node_});
+    }
+
+    // ---- encoder, source side on all data rows: emb_src, LN_src (in place), [k | v]
+    T* emb_src = region_;
+    T* kv_enc = region_ + G * C;
+    linear(enc_emb_src_, x_data_, ldF_, emb_src, C, G, s);
+    if (hk) hk->dev("enc.emb_src", emb_src, C, G, C, {G, C});
+    ln(emb_src, enc_.ln_src, emb_src, G, s);
+    linear(enc_.kv, emb_src, C, kv_enc, 2 * C, G, s);
+
+    // ---- encoder, destination side (hidden nodes)
+    T* emb_dst = zA_;
+    linear(enc_emb_dst_, h_attr_.as<T>(), ldA_, emb_dst, C, H, s);
+    if (hk) hk->dev("enc.emb_dst", emb_dst, C, H, C, {H, C});
+    ln(emb_dst, enc_.ln_dst, xh_, H, s);
+    linear(enc_.qs, xh_, C, qkvs_, 2 * C, H, s);
+    attention(g_enc_, enc_, 0, H, qkvs_, 2 * C, kv_enc, kv_enc + C, 2 * C, qkvs_ + C, 2 * C, sbuf_, s);
+    linear(enc_.proj, sbuf_, C, out1_, C, H, s, k::kEpiResidual, emb_dst, C);
+    ln(out1_, enc_.ln_mlp, xh_, H, s);
+    linear(enc_.mlp1, xh_, C, hbuf_, mlp_, H, s, k::kEpiGelu);
+    linear(enc_.mlp2, hbuf_, mlp_, z_enc_, C, H, s, k::kEpiResidual, out1_, C);
+    if (hk) hk->dev("enc.out", z_enc_, C, H, C, {H, C});
+    ln(z_enc_, proc_[0].ln_dst, xh_, H, s);
+
+    // ---- processor; xh_ holds LN_dst of the block input
+    T* z_in = z_enc_;
+    T* latent = nullptr;
+    for (int i = 0; i < n_proc_; ++i) {
+        const Block<T>& b = proc_[size_t(i)];
+        linear(b.qkvs, xh_, C, qkvs_, 4 * C, H, s);
+        attention(g_proc_, b, 0, H, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C, 4 * C, sbuf_, s);
+        linear(b.proj, sbuf_, C, out1_, C, H, s, k::kEpiResidual, z_in, C);
+        ln(out1_, b.ln_mlp, xh_, H, s);
+        linear(b.mlp1, xh_, C, hbuf_, mlp_, H, s, k::kEpiGelu);
+        T* z_out = z_in == zA_ ? zB_ : zA_;
+        linear(b.mlp2, hbuf_, mlp_, z_out, C, H, s, k::kEpiResidual, out1_, C);
+        if (hk) hk->dev("proc." + std::to_string(i) + ".out", z_out, C, H, C, {H, C});
+        if (i + 1 < n_proc_) {
+            k::layernorm<T>(z_out, C, proc_[size_t(i + 1)].ln_dst.W(), proc_[size_t(i + 1)].ln_dst.B(), xh_, C, H,
+                            C_, eps_, s);
+        } else if (cfg_.latent_skip) {
+            latent = z_in == z_enc_ ? sbuf_ : z_in;  // a dead buffer
+            Span sp(this, s, "add_layernorm", 0, double(H) * C_ * 4 * sizeof(T));
+            k::add_layernorm<T>(z_out, z_enc_, latent, dec_.ln_src.W(), dec_.ln_src.B(), xh_, C, H, C_, eps_, s);
+        } else {
+            latent = z_out;
+            ln(z_out, dec_.ln_src, xh_, H, s);
+        }
+        z_in = z_out;
+    }
+    if (hk) hk->dev("latent", latent, C, H, C, {H, C});
+
+    // ---- decoder, source side: [k | v] of LN_src(latent)
+    T* kv_dec = qkvs_;
+    linear(dec_.kv, xh_, C, kv_dec, 2 * C, H, s);
+
+    // ---- decoder, destination chunks of data rows
+    std::vector<float> h_emb, h_bo;
+    if (hk) h_emb.resize(size_t(G * C)), h_bo.resize(size_t(G * C));
+    const int64_t R = dec_rows_;
+    T* e = region_;
+    T* t = e + R * C;
+    T* qs = t + R * C;
+    T* sb = qs + R * 2 * C;
+    T* o1 = sb + R * C;
+    T* h = o1 + R * C;
+    for (int64_t lo = 0; lo < G; lo += R) {
+        const int64_t n = std::min(R, G - lo);
+        linear(dec_emb_dst_, x_data_ + lo * ldF_, ldF_, e, C, n, s);
+        if (hk) hk->fetch(e, C, n, C, h_emb.data(), lo);
+        ln(e, dec_.ln_dst, t, n, s);
+        linear(dec_.qs, t, C, qs, 2 * C, n, s);
+        attention(g_dec_, dec_, lo, n, qs, 2 * C, kv_dec, kv_dec + C, 2 * C, qs + C, 2 * C, sb, s);
+        linear(dec_.proj, sb, C, o1, C, n, s, k::kEpiResidual, e, C);
+        ln(o1, dec_.ln_mlp, t, n, s);
+        linear(dec_.mlp1, t, C, h, mlp_, n, s, k::kEpiGelu);
+        linear(dec_.mlp2, h, mlp_, sb, C, n, s, k::kEpiResidual, o1, C);
+        if (hk) hk->fetch(sb, C, n, C, h_bo.data(), lo);
+        ln(sb, dec_out_norm_, t, n, s);
+        linear(dec_out_proj_, t, C, dec_out_ + lo * ldVo_, ldVo_, n, s);
+    }
+    if (hk) {
+        hk->host("dec.emb_dst", h_emb.data(), {G, C});
+        hk->host("dec.block_out", h_bo.data(), {G, C});
+        hk->dev("dec.out", dec_out_, ldVo_, G, V_dec_, {G, int64_t(V_dec_)});
+    }
+
+    // ---- output: per step t, fp32 cast + residual + bounding -> yn [T_out, G, V_out]
+    k::OutputArgs o;
+    o.dec = dec_out_, o.ld_dec = ldVo_;
+    o.xn_step = xn + int64_t(cfg_.residual_step) * G * V_in_;
+    o.V_in = V_in_, o.V_out = V_out_, o.T_out = T_out_, o.G = G;
+    o.res_src = res_src_.as<int>(), o.bounds = bounds_.as<k::BoundDev>(), o.n_bounds = n_bounds_;
+    o.bidx = bidx_.as<int>();
+    if (hk) {
+        if (!hook_prebound_.get()) hook_prebound_.alloc(size_t(output_numel()) * sizeof(float));
+        o.pre_bound = hook_prebound_.as<float>();
+    }
+    o.y = yn;
+    {
+        Span sp(this, s, "output_assemble", 0,
+                double(G) * (ldVo_ * sizeof(T) + V_in_ * 4) + double(T_out_) * G * V_out_ * 4);
+        k::output_assemble<T>(o, s);
+    }
+    if (hk) {
+        const std::vector<int64_t> shp = {1, T_out_, 1, G, V_out_};
+        hk->dev("out.pre_bound", hook_prebound_.as<float>(), V_out_, T_out_ * G, V_out_, shp);
+        hk->dev("out.norm", yn, V_out_, T_out_ * G, V_out_, shp);
+    }
+}
+
+template <class T>
+void Engine<T>::prepare() {
+    VB_CUDA(cudaSetDevice(dev_));
+    if (ran_eager_) return;
+    VB_CUDA(cudaMemsetAsync(x_dev_, 0, size_t(input_numel()) * sizeof(float), stream_));
+    predict_step_device(x_dev_, y_dev_, stream_);
+    VB_CUDA(cudaStreamSynchronize(stream_));
+    ran_eager_ = true;
+}
+
+// Captures predict_step_device on the internal buffers. Whatever fails inside the capture, the
+// capture is ended and the partial graph destroyed; the caller then runs eagerly.
+template <class T>
+bool Engine<T>::capture_graph(cudaStream_t s) {
+    VB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    std::string err;
+    try {
+        predict_step_device(x_dev_, y_dev_, s);
+    } catch (const std::exception& e) {
+        err = e.what();
+    }
+    cudaGraph_t g = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(s, &g);
+    if (err.empty() && ec != cudaSuccess) err = std::string("cudaStreamEndCapture: ") + cudaGetErrorString(ec);
+    if (err.empty()) {
+        const cudaError_t ei = cudaGraphInstantiate(&graph_exec_, g, 0);
+        if (ei != cudaSuccess) {
+            graph_exec_ = nullptr;
+            err = std::string("cudaGraphInstantiate: ") + cudaGetErrorString(ei);
+        }
+    }
+    if (g) cudaGraphDestroy(g);
+    if (err.empty()) return true;
+    (void)cudaGetLastError();
+    std::fprintf(stderr, "varda_b200: CUDA graph capture failed (%s); running without a graph\n", err.c_str());
+    return false;
+}
+
+template <class T>
+void Engine<T>::enqueue_predict() {
+    VB_CUDA(cudaSetDevice(dev_));
+    cudaStream_t s = stream_;
+    if (!opts_.cuda_graph || !ran_eager_) {
+        predict_step_device(x_dev_, y_dev_, s);
+        ran_eager_ = true;
+        return;
+    }
+    if (!graph_exec_ && !graph_failed_ && !capture_graph(s)) graph_failed_ = true;
+    if (graph_exec_) VB_CUDA(cudaGraphLaunch(graph_exec_, s));
+    else predict_step_device(x_dev_, y_dev_, s);
+}
+
+template <class T>
+void Engine<T>::predict_step(const float* x, float* y, HookFn hook, void* user) {
+    VB_CUDA(cudaSetDevice(dev_));
+    cudaStream_t s = stream_;
+    const int64_t in_n = input_numel(), out_n = output_numel();
+    VB_CUDA(cudaMemcpyAsync(x_dev_, x, size_t(in_n) * sizeof(float), cudaMemcpyHostToDevice, s));
+    if (hook) {
+        Hook hk{*this, hook, user, s};
+        hk.host("in.x", x, {1, T_in_, G_, V_in_});
+        normalise(x_dev_, xn_, s);
+        hk.dev("in.x_norm", xn_, in_n, 1, in_n, {1, T_in_, 1, G_, V_in_});
+        forward(xn_, yn_, s, &hk);
+        denormalise(yn_, y_dev_, s);
+        VB_CUDA(cudaMemcpyAsync(y, y_dev_, size_t(out_n) * sizeof(float), cudaMemcpyDeviceToHost, s));
+        VB_CUDA(cudaStreamSynchronize(s));
+        hk.host("out.y", y, {1, T_out_, 1, G_, V_out_});
+        ran_eager_ = true;
+        return;
+    }
+    enqueue_predict();
+    VB_CUDA(cudaMemcpyAsync(y, y_dev_, size_t(out_n) * sizeof(float), cudaMemcpyDeviceToHost, s));
+    VB_CUDA(cudaStreamSynchronize(s));
+}
+
+template <class T>
+std::string Engine<T>::profile_forward() {
+    VB_CUDA(cudaSetDevice(dev_));
+    std::vector<ProfRec> recs;
+    prof_ = &recs;
+    std::string out = "[";
+    try {
+        normalise(x_dev_, xn_, stream_);
+        forward(xn_, yn_, stream_, nullptr);
+        VB_CUDA(cudaStreamSynchronize(stream_));
+    } catch (...) {
+        prof_ = nullptr;
+        throw;
+    }
+    prof_ = nullptr;
+    for (size_t i = 0; i < recs.size(); ++i) {
+        float ms = 0;
+        VB_CUDA(cudaEventElapsedTime(&ms, recs[i].a, recs[i].b));
+        char buf[512];
+        std::snprintf(buf, sizeof buf, "%s{\"name\": \"%s\", \"ms\": %.6f, \"flop\": %.6g, \"bytes\": %.6g}", i ? ", " : "",
+                      recs[i].name.c_str(), double(ms), recs[i].flop, recs[i].bytes);
+        out += buf;
+        cudaEventDestroy(recs[i].a);
+        cudaEventDestroy(recs[i].b);
+    }
+    return out + "]";
+}
+
+template class Engine<float>;
+template class Engine<__half>;
+
+int64_t& launch_counter() {
+    static int64_t n = 0;
+    return n;
+}
+
+std::unique_ptr<Model> load_model(const std::string& path, const Options& o) {
+    if (o.world > 1) return load_sharded_model(path, o);
+    if (o.precision == 0) return std::make_unique<Engine<float>>(path, o);
+    return std::make_unique<Engine<__half>>(path, o);
+}
+
+}  // namespace vb

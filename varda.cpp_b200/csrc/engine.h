@@ -1,0 +1,61 @@
+// The B200 backend behind the C ABI: one Engine per loaded model (fp32 or fp16), holding every
+// device weight, graph and activation buffer, allocated at load. Interface mirrors the reference's
+// varda::Backend / varda::cuda::CudaBackend (src/varda/backend.h:12-17, cuda/cuda_backend.h:31-75).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <memory>
+#include <string>
+
+namespace vb {
+
+using HookFn = void (*)(const char* key, const float* data, const int64_t* shape, int ndim, void* user);
+
+struct Options {
+    int precision = 0;  // 0 fp32, 1 fp16
+    int cuda_device = 0;
+    bool cuda_graph = true;
+    int gemm = 0;                // 0 auto (tensor cores for fp16), 1 CUDA cores only
+    int64_t dec_chunk_rows = 0;  // 0: all data rows in one chunk when memory allows
+    // multi-GPU (destination partition); world == 1 for a single GPU
+    int rank = 0, world = 1;
+    const void* nccl_id = nullptr;  // 128-byte ncclUniqueId, the same on every rank
+};
+
+class Model {
+public:
+    virtual ~Model() = default;
+    // host pointers, physical units: x (1, T_in, G, V_in), y (1, T_out, 1, G, V_out)
+    virtual void predict_step(const float* x, float* y, HookFn hook, void* user) = 0;
+    virtual int64_t input_numel() const = 0;
+    virtual int64_t output_numel() const = 0;
+    virtual void normalise(const float* x, float* xn, cudaStream_t s) = 0;
+    virtual void forward_normalised(const float* xn, float* yn, cudaStream_t s) = 0;
+    virtual void denormalise(const float* yn, float* y, cudaStream_t s) = 0;
+    virtual void predict_step_device(const float* x, float* y, cudaStream_t s) = 0;
+    virtual void prepare() = 0;
+    virtual void use_high_priority_stream() = 0;
+    virtual float* device_input() = 0;
+    virtual const float* device_output() const = 0;
+    virtual cudaStream_t stream() const = 0;
+    virtual void enqueue_predict() = 0;
+    virtual int device() const = 0;
+    virtual size_t weight_bytes() const = 0;
+    virtual size_t activation_bytes() const = 0;
+    virtual int64_t decoder_chunk_rows() const = 0;
+    // sizes: T_in, G, V_in, T_out, V_out, H, C, n_proc
+    virtual void sizes(int64_t out[8]) const = 0;
+    // multi-GPU: this rank's data-node range [lo, hi)
+    virtual void data_range(int64_t* lo, int64_t* hi) const = 0;
+    // One eager forward_normalised on the internal buffers with a CUDA event pair around every
+    // launch; returns a JSON array of {"name", "ms", "flop", "bytes"} records (algorithmic FLOPs
+    // of the GEMMs, compulsory bytes of the bandwidth-bound kernels). Synchronises.
+    virtual std::string profile_forward() = 0;
+};
+
+std::unique_ptr<Model> load_model(const std::string& path, const Options& opts);
+
+}  // namespace vb

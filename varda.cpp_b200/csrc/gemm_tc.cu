@@ -1,0 +1,437 @@
+// tcgen05 GEMM (see gemm_tc.cuh).
+//
+// Persistent kernel, one 192-thread CTA per SM, warp-specialised:
+//   warp 0 (one lane)   TMA producer: A [128 x 64] and W [BN x 64] fp16 tiles, 128-byte swizzle,
+//                       into a STAGES-deep shared-memory ring (full/empty mbarriers).
+//   warp 1 (one lane)   MMA issuer: 4 x tcgen05.mma (M=128, N=BN, K=16) per 64-wide k block into
+//                       one of two TMEM accumulators; tcgen05.commit frees the smem stage, and a
+//                       commit after the last k block hands the accumulator to the epilogue.
+//   warps 2-5           epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
+//                       32 (w % 4) .. + 31 = its 32 output rows), bias / GELU / residual in fp32,
+//                       fp16 stores; then release the accumulator to the MMA warp.
+// Two accumulators (2 x BN TMEM columns) let the epilogue of tile i overlap the main loop of
+// tile i + 1. Tiles are visited m-major (n fastest) so an A row block is reused from L2 by the
+// CTAs working on its N tiles.
+//
+// Every mbarrier wait is bounded (kTimeoutNs of %globaltimer). On timeout a CTA sets the device
+// error flag, stops issuing work, waits (bounded) for its own TMA loads and MMAs in flight,
+// frees its TMEM and returns; the host reads the flag with take_error().
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "common.h"
+#include "dev.cuh"
+#include "gemm_tc.cuh"
+
+namespace vb::tc {
+
+namespace {
+
+using vb::d::from_f;
+using vb::d::gelu;
+using vb::d::rnd;
+using vb::d::to_f;
+
+constexpr int BM = 128, BK = 64;
+constexpr unsigned long long kTimeoutNs = 4000000000ull;  // 4 s
+
+__device__ int g_error = 0;
+
+struct Params {
+    const __half* bias;
+    __half* C;
+    int64_t ldc;
+    const __half* R;
+    int64_t ldr;
+    int M, N, K;
+    int epi;
+    int gelu_tanh;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase of parity `parity`. Returns false on timeout (after raising the CTA's
+// abort flag and the device error flag) or when another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_test(b, parity)) return true;
+    const uint64_t t0 = now_ns();
+    for (;;) {
+        if (mbar_test(b, parity)) return true;
+        if (*abort_flag) return false;
+        if (now_ns() - t0 > kTimeoutNs) {
+            *abort_flag = 1;
+            atomicExch(&g_error, 1);
+            return false;
+        }
+    }
+}
+// Wait that ignores the abort flag (used only to drain work in flight), still bounded.
+__device__ __forceinline__ void mbar_drain(uint64_t* b, uint32_t parity) {
+    const uint64_t t0 = now_ns();
+    while (!mbar_test(b, parity))
+        if (now_ns() - t0 > kTimeoutNs) {
+            atomicExch(&g_error, 2);
+            return;
+        }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major tile, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= uint64_t((saddr & 0x3FFFF) >> 4);  // start address
+    d |= uint64_t(1) << 16;                 // leading byte offset (unused for swizzled K-major)
+    d |= uint64_t(1024 >> 4) << 32;         // stride byte offset
+    d |= uint64_t(1) << 46;                 // descriptor version (sm_100)
+    d |= uint64_t(2) << 61;                 // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor, kind::f16: A = B = fp16, D = fp32, both K-major, M = 128, N = BN.
+template <int BN> constexpr uint32_t instr_desc() {
+    return (1u << 4)                      // D format fp32
+           | (0u << 7) | (0u << 10)       // A, B format fp16
+           | (uint32_t(BN >> 3) << 17)    // N
+           | (uint32_t(BM >> 4) << 24);   // M
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN, int STAGES> struct Layout {
+    static constexpr int kA = BM * BK * 2;  // bytes per A stage
+    static constexpr int kB = BN * BK * 2;
+    static constexpr int kTiles = STAGES * (kA + kB);
+    static constexpr int kBars = (2 * STAGES + 5) * 8;
+    static constexpr int kSmem = 1024 + kTiles + kBars + 16;  // 1024: alignment slack
+};
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_store(const Params& p, int row, int n0, float (&v)[32]) {
+    // bias, autocast rounding, GELU / residual; then 32 fp16 values = 4 x 16-byte stores
+    const bool full = n0 + 32 <= p.N;
+    __half* out = p.C + int64_t(row) * p.ldc + n0;
+    float b[32];
+    if (p.bias) {
+        if (full) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) vb::d::Vec<__half, 8>::ldg(p.bias + n0 + 8 * q, b + 8 * q);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) b[i] = n0 + i < p.N ? __half2float(p.bias[n0 + i]) : 0.f;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) b[i] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(v[i] + b[i]);
+    if (EPI == k::kEpiGelu) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(gelu(v[i], p.gelu_tanh != 0));
+    } else if (EPI == k::kEpiResidual) {
+        const __half* r = p.R + int64_t(row) * p.ldr + n0;
+        float rv[32];
+        if (full) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) vb::d::Vec<__half, 8>::load(r + 8 * q, rv + 8 * q);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) rv[i] = n0 + i < p.N ? __half2float(r[i]) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(v[i] + rv[i]);
+    }
+    if (full) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) vb::d::Vec<__half, 8>::store(out + 8 * q, v + 8 * q);
+    } else {
+        for (int i = 0; i < 32; ++i)
+            if (n0 + i < p.N) out[i] = __float2half_rn(v[i]);
+    }
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    using L = Layout<BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * L::kA;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kTiles);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* tfull = bars + 2 * STAGES;
+    uint64_t* tempty = bars + 2 * STAGES + 2;
+    uint64_t* drain = bars + 2 * STAGES + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTiles + L::kBars);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
+        for (int b = 0; b < 2; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], 4);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(2 * BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int n_m = (p.M + BM - 1) / BM, n_n = (p.N + BN - 1) / BN;
+    const int tiles = n_m * n_n, kblocks = (p.K + BK - 1) / BK;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t issued = 0, last_parity = 0;  // per-stage bit masks for the drain
+        for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+            const int mb = tile / n_n, nb = tile - mb * n_n;
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
+                mbar_expect_tx(&full[stage], uint32_t(L::kA + L::kB));
+                tma_load_2d(sA + stage * L::kA, &tmA, &full[stage], kb * BK, mb * BM);
+                tma_load_2d(sB + stage * L::kB, &tmB, &full[stage], kb * BK, nb * BN);
+                issued |= 1u << stage;
+                last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == STAGES) stage = 0, phase ^= 1;
+            }
+        }
+        if (*abort_flag)  // let every load already issued land before the CTA exits
+            for (int s = 0; s < STAGES; ++s)
+                if (issued & (1u << s)) mbar_drain(&full[s], (last_parity >> s) & 1);
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer
+        constexpr uint32_t idesc = instr_desc<BN>();
+        int stage = 0;
+        uint32_t phase = 0;
+        int it = 0;
+        bool any = false;
+        for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, ++it) {
+            const int ab = it & 1;
+            const uint32_t ap = (it >> 1) & 1;
+            if (!mbar_wait(&tempty[ab], ap ^ 1, abort_flag)) break;
+            fence_after();
+            const uint32_t d = tmem + uint32_t(ab * BN);
+            bool ok = true;
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (!mbar_wait(&full[stage], phase, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                fence_after();
+                const uint64_t a0 = smem_desc(smem_u32(sA + stage * L::kA));
+                const uint64_t b0 = smem_desc(smem_u32(sB + stage * L::kB));
+#pragma unroll
+                for (int j = 0; j < BK / 16; ++j)
+                    mma_f16(d, a0 + uint64_t(2 * j), b0 + uint64_t(2 * j), idesc, (kb | j) != 0 ? 1u : 0u);
+                mma_commit(&empty[stage]);
+                any = true;
+                if (++stage == STAGES) stage = 0, phase ^= 1;
+            }
+            if (!ok) break;
+            mma_commit(&tfull[ab]);
+        }
+        if (any) {  // every MMA issued by this thread completes before the TMEM is freed
+            mma_commit(drain);
+            mbar_drain(drain, 0);
+        }
+    } else if (warp >= 2) {
+        // ---------------- epilogue
+        const int lg = warp & 3;  // TMEM lane group this warp may access
+        int it = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+            const int ab = it & 1;
+            const uint32_t ap = (it >> 1) & 1;
+            if (!mbar_wait(&tfull[ab], ap, abort_flag)) break;
+            fence_after();
+            const int mb = tile / n_n, nb = tile - mb * n_n;
+            const int row = mb * BM + lg * 32 + lane;
+            const uint32_t taddr = tmem + (uint32_t(lg * 32) << 16) + uint32_t(ab * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                float v[32];
+                tmem_ld32(taddr + uint32_t(c * 32), v);
+                const int n0 = nb * BN + c * 32;
+                if (row < p.M && n0 < p.N) epilogue_store<EPI>(p, row, n0, v);
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[ab]);
+        }
+    }
+    fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q{};
+        void* f = nullptr;
+        VB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !f) fail(kCuda, "cuTensorMapEncodeTiled is not available");
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// 2-D fp16 tensor map over a row-major [rows, cols] matrix with leading dimension ld (elements),
+// box [box_rows, 64 columns], 128-byte swizzle, zero fill out of bounds.
+CUtensorMap make_map(const __half* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+    const cuuint32_t box[2] = {cuuint32_t(BK), cuuint32_t(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides,
+                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(kCuda, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        VB_CUDA(cudaGetDevice(&dev));
+        VB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    }
+    return n;
+}
+
+template <int BN, int STAGES, int EPI>
+void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
+    using L = Layout<BN, STAGES>;
+    static bool configured = false;  // per instantiation; the attribute is per function
+    if (!configured) {
+        VB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     L::kSmem));
+        configured = true;
+    }
+    const CUtensorMap ta = make_map(a.A, a.M, a.K, a.lda, BM);
+    const CUtensorMap tb = make_map(a.W, a.N, a.K, a.ldw, BN);
+    Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0};
+    const int64_t tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+    const int grid = int(std::min<int64_t>(tiles, sm_count()));
+    gemm_tc_kernel<BN, STAGES, EPI><<<grid, 192, L::kSmem, s>>>(ta, tb, p);
+    VB_LAUNCH();
+}
+
+template <int BN, int STAGES>
+void dispatch_epi(const k::GemmArgs<__half>& a, cudaStream_t s) {
+    switch (a.epi) {
+        case k::kEpiBias: launch<BN, STAGES, k::kEpiBias>(a, s); break;
+        case k::kEpiGelu: launch<BN, STAGES, k::kEpiGelu>(a, s); break;
+        case k::kEpiResidual: launch<BN, STAGES, k::kEpiResidual>(a, s); break;
+        default: fail(kInvalidArgument, "gemm: unknown epilogue");
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+bool supported(const k::GemmArgs<__half>& a) {
+    if (a.M <= 0 || a.N <= 0 || a.K <= 0) return false;
+    if (a.M > INT32_MAX / 2 || a.N > INT32_MAX / 2 || a.K > INT32_MAX / 2) return false;
+    if (a.lda % 8 || a.ldw % 8 || a.ldc % 8) return false;
+    if (!aligned16(a.A) || !aligned16(a.W) || !aligned16(a.C)) return false;
+    if (a.bias && !aligned16(a.bias)) return false;
+    if (a.epi == k::kEpiResidual && (!a.R || a.ldr % 8 || !aligned16(a.R))) return false;
+    return true;
+}
+
+void gemm(const k::GemmArgs<__half>& a, cudaStream_t s) {
+    if (!supported(a)) fail(kInvalidArgument, "tensor-core gemm: unsupported operand alignment");
+    if (a.N <= 128) dispatch_epi<128, 6>(a, s);
+    else dispatch_epi<256, 4>(a, s);
+}
+
+int take_error() {
+    VB_CUDA(cudaDeviceSynchronize());
+    int e = 0, zero = 0;
+    VB_CUDA(cudaMemcpyFromSymbol(&e, g_error, sizeof(int)));
+    if (e) VB_CUDA(cudaMemcpyToSymbol(g_error, &zero, sizeof(int)));
+    return e;
+}
+
+}  // namespace vb::tc

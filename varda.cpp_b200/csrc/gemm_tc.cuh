@@ -1,0 +1,22 @@
+// Tensor-core GEMM for sm_100a (tcgen05 + TMEM + TMA): y[M, N] = A[M, K] W[N, K]^T with fp16
+// operands, fp32 accumulation in tensor memory, and the fused epilogues of kernels.cuh
+// (bias, GELU, residual) applied when the accumulator is read back.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "kernels.cuh"
+
+namespace vb::tc {
+
+// True when the operands meet the tensor-memory-access rules: 16-byte aligned base pointers and
+// row strides (multiples of 8 fp16 elements).
+bool supported(const k::GemmArgs<__half>& a);
+// Enqueues the GEMM on s (no allocation, no synchronisation; capturable).
+void gemm(const k::GemmArgs<__half>& a, cudaStream_t s);
+// Reads and clears the device-side error flag set when a bounded wait inside the kernel gave up
+// (synchronises the device). Returns 0 when no wait timed out.
+int take_error();
+
+}  // namespace vb::tc

@@ -1,0 +1,82 @@
+#include "graph.h"
+
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstring>
+#include <limits>
+#include <string>
+
+#include "common.h"
+
+namespace vb {
+
+int32_t CsrGraph::max_degree() const {
+    int32_t m = 0;
+    for (int64_t d = 0; d < n_dst; ++d) m = std::max(m, row_ptr[d + 1] - row_ptr[d]);
+    return m;
+}
+
+namespace {
+template <class I>
+CsrGraph build(const I* ei, int64_t E, const float* ea, int A, int64_t n_src, int64_t n_dst, const std::string& name) {
+    constexpr int64_t kMax = std::numeric_limits<int32_t>::max();
+    if (E >= kMax || n_src >= kMax || n_dst >= kMax) fail(kFormat, name + ": graph too large for int32 indices");
+    CsrGraph g;
+    g.n_src = n_src;
+    g.n_dst = n_dst;
+    g.n_edges = E;
+    g.attr_dim = A;
+    g.row_ptr.assign(size_t(n_dst + 1), 0);
+    for (int64_t e = 0; e < E; ++e) {
+        const int64_t s = int64_t(ei[e]), d = int64_t(ei[E + e]);
+        if (s < 0 || s >= n_src || d < 0 || d >= n_dst)
+            fail(kFormat, name + ": edge " + std::to_string(e) + " out of range");
+        ++g.row_ptr[size_t(d + 1)];
+    }
+    for (int64_t d = 0; d < n_dst; ++d) g.row_ptr[size_t(d + 1)] += g.row_ptr[size_t(d)];
+    std::vector<int32_t> next(g.row_ptr.begin(), g.row_ptr.end() - 1);
+    g.src.resize(size_t(E));
+    g.edge_id.resize(size_t(E));
+    g.attr.resize(size_t(E) * size_t(A));
+    for (int64_t e = 0; e < E; ++e) {
+        const int32_t slot = next[size_t(ei[E + e])]++;
+        g.src[size_t(slot)] = int32_t(ei[e]);
+        g.edge_id[size_t(slot)] = int32_t(e);
+        std::memcpy(&g.attr[size_t(slot) * size_t(A)], ea + e * A, sizeof(float) * size_t(A));
+    }
+    return g;
+}
+}  // namespace
+
+CsrGraph build_csr_by_dst(const TensorView& ei, const TensorView& ea, int64_t n_src, int64_t n_dst) {
+    if (ei.shape.size() != 2 || ei.shape[0] != 2)
+        fail(kFormat, ei.name + ": expected shape [2, E], got " + ei.shape_str());
+    const int64_t E = ei.shape[1];
+    if (ea.dtype != DType::F32 || ea.shape.size() != 2 || ea.shape[0] != E)
+        fail(kFormat, ea.name + ": expected F32 [E, A] with E = " + std::to_string(E));
+    const int A = int(ea.shape[1]);
+    if (ei.dtype == DType::I64) return build(ei.as<int64_t>(), E, ea.as<float>(), A, n_src, n_dst, ei.name);
+    if (ei.dtype == DType::I32) return build(ei.as<int32_t>(), E, ea.as<float>(), A, n_src, n_dst, ei.name);
+    fail(kFormat, ei.name + ": edge_index must be I64 or I32");
+}
+
+CsrGraph build_csr_by_dst(const int64_t* ei, int64_t E, const float* ea, int A, int64_t n_src, int64_t n_dst) {
+    return build(ei, E, ea, A, n_src, n_dst, "edge_index");
+}
+
+std::vector<EdgeRec> pack_edges(const CsrGraph& g, bool round_fp16) {
+    if (g.attr_dim > 3) fail(kUnsupported, "edge_attr_dim must be 1..3 (16-byte edge records)");
+    std::vector<EdgeRec> out(size_t(g.n_edges));
+    for (int64_t e = 0; e < g.n_edges; ++e) {
+        float a[3] = {0.f, 0.f, 0.f};
+        for (int k = 0; k < g.attr_dim; ++k) {
+            const float v = g.attr[size_t(e) * size_t(g.attr_dim) + size_t(k)];
+            a[k] = round_fp16 ? __half2float(__float2half_rn(v)) : v;
+        }
+        out[size_t(e)] = {a[0], a[1], a[2], g.src[size_t(e)]};
+    }
+    return out;
+}
+
+}  // namespace vb

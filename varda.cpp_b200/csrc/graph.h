@@ -1,0 +1,39 @@
+// Static graphs in destination-major CSR layout, built once at load time, and their packed device
+// form. The CSR build is the reference's build_csr_by_dst (src/varda/graph.cpp:17-61, graph.h:15-25)
+// restated: a stable counting sort of the stored edges by destination, so per-destination sums
+// visit edges in stored order. Bit-exact by construction (pure integer work).
+#pragma once
+
+#include <cstdint>
+#include <vector>
+
+#include "safetensors.h"
+
+namespace vb {
+
+struct CsrGraph {
+    int64_t n_src = 0, n_dst = 0, n_edges = 0;
+    int attr_dim = 0;
+    std::vector<int32_t> row_ptr;  // [n_dst + 1]
+    std::vector<int32_t> src;      // [n_edges]
+    std::vector<int32_t> edge_id;  // [n_edges] stored index of each CSR slot
+    std::vector<float> attr;       // [n_edges, attr_dim]
+    int32_t max_degree() const;
+};
+
+// edge_index: I64 or I32 [2, E] (row 0 source, row 1 destination); edge_attr: F32 [E, A].
+CsrGraph build_csr_by_dst(const TensorView& edge_index, const TensorView& edge_attr, int64_t n_src, int64_t n_dst);
+// Same on raw host arrays (edge_index int64 [2, E]); used by the C ABI.
+CsrGraph build_csr_by_dst(const int64_t* edge_index, int64_t E, const float* edge_attr, int A, int64_t n_src,
+                          int64_t n_dst);
+
+// One 16-byte record per CSR slot: {a0, a1, a2, bitcast<float>(src)}, attributes zero-padded to
+// three and, in fp16 mode, rounded to fp16 as autocast does to the edge Linear's input.
+struct EdgeRec {
+    float a0, a1, a2;
+    int32_t src;
+};
+static_assert(sizeof(EdgeRec) == 16, "edge record must be 16 bytes");
+std::vector<EdgeRec> pack_edges(const CsrGraph& g, bool round_fp16);
+
+}  // namespace vb

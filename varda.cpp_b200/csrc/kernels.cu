@@ -1,0 +1,283 @@
+// Elementwise, LayerNorm and output kernels (see kernels.cuh).
+#include <algorithm>
+#include <string>
+
+#include "common.h"
+#include "dev.cuh"
+#include "kernels.cuh"
+
+namespace vb::k {
+
+using namespace vb::d;
+
+namespace {
+
+unsigned grid_for(int64_t n, int per_block) {
+    int64_t b = (n + per_block - 1) / per_block;
+    // grid-stride loops cover the rest; 148 SMs x 16 resident blocks x 64 waves is plenty
+    return unsigned(std::max<int64_t>(1, std::min<int64_t>(b, 148 * 16 * 64)));
+}
+
+__global__ void normalise_kernel(const float* __restrict__ x, const float* __restrict__ mul,
+                                 const float* __restrict__ add, float* __restrict__ xn, int64_t n, int V) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const int v = int(i % V);
+        xn[i] = __fadd_rn(__fmul_rn(x[i], __ldg(mul + v)), __ldg(add + v));
+    }
+}
+
+__global__ void denormalise_kernel(const float* __restrict__ yn, const float* __restrict__ add,
+                                   const float* __restrict__ mul, float* __restrict__ y, int64_t n, int V) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const int v = int(i % V);
+        y[i] = __fdiv_rn(__fsub_rn(yn[i], __ldg(add + v)), __ldg(mul + v));
+    }
+}
+
+template <class T>
+__global__ void assemble_kernel(const float* __restrict__ xn, const float* __restrict__ attr, int T_in, int64_t G,
+                                int V, int A, T* __restrict__ out, int64_t ld) {
+    const int64_t n = G * ld;
+    const int TV = T_in * V;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t g = i / ld;
+        const int f = int(i - g * ld);
+        float val = 0.0f;
+        if (f < TV) {
+            const int t = f / V, v = f - t * V;
+            val = xn[(int64_t(t) * G + g) * V + v];
+        } else if (f < TV + A) {
+            val = attr[g * A + (f - TV)];
+        }
+        out[i] = from_f<T>(val);
+    }
+}
+
+template <class Tin, class Tout>
+__global__ void convert_kernel(const Tin* __restrict__ src, int64_t lds, Tout* __restrict__ dst, int64_t ldd,
+                               int64_t rows, int64_t cols) {
+    const int64_t n = rows * cols;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = i / cols, c = i - r * cols;
+        dst[r * ldd + c] = from_f<Tout>(to_f<Tin>(src[r * lds + c]));
+    }
+}
+
+// One warp per row; lane holds vectors of 4 channels at (lane + 32 i) * 4, i < NV (C = 128 NV).
+// Two-pass fp32 statistics in registers, as torch's CUDA LayerNorm keeps fp32 statistics.
+template <int NV>
+__device__ __forceinline__ void ln_apply(float (&x)[NV][4], const float* __restrict__ w, const float* __restrict__ b,
+                                         int lane, float eps) {
+    constexpr int C = 128 * NV;
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s += x[i][j];
+    const float mean = warp_sum(s) / float(C);
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float dlt = x[i][j] - mean;
+            q += dlt * dlt;
+        }
+    const float var = warp_sum(q) / float(C);
+    const float rstd = 1.0f / sqrtf(var + eps);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c0 = (lane + 32 * i) * 4;
+        float wv[4], bv[4] = {0.f, 0.f, 0.f, 0.f};
+        Vec<float, 4>::ldg(w + c0, wv);
+        if (b) Vec<float, 4>::ldg(b + c0, bv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[i][j] = (x[i][j] - mean) * rstd * wv[j] + bv[j];
+    }
+}
+
+template <class T, int NV>
+__global__ void __launch_bounds__(256) layernorm_kernel(const T* x, int64_t ldx, const float* __restrict__ w,
+                                                        const float* __restrict__ b, T* y, int64_t ldy, int64_t rows,
+                                                        float eps) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    float v[NV][4];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) Vec<T, 4>::load(x + r * ldx + (lane + 32 * i) * 4, v[i]);
+    ln_apply<NV>(v, w, b, lane, eps);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) Vec<T, 4>::store(y + r * ldy + (lane + 32 * i) * 4, v[i]);
+}
+
+template <class T, int NV>
+__global__ void __launch_bounds__(256) add_layernorm_kernel(const T* a, const T* r1, T* out1,
+                                                            const float* __restrict__ w, const float* __restrict__ b,
+                                                            T* ln, int64_t ld, int64_t rows, float eps) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    float v[NV][4];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int64_t off = r * ld + (lane + 32 * i) * 4;
+        float p[4], q[4];
+        Vec<T, 4>::load(a + off, p);
+        Vec<T, 4>::load(r1 + off, q);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[i][j] = rnd<T>(p[j] + q[j]);
+        Vec<T, 4>::store(out1 + off, v[i]);
+    }
+    ln_apply<NV>(v, w, b, lane, eps);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) Vec<T, 4>::store(ln + r * ld + (lane + 32 * i) * 4, v[i]);
+}
+
+// One warp per output row (step t, data node g). The row is staged in shared memory; the
+// boundings then run in config order with the lanes spread over each bounding's index list.
+template <class T>
+__global__ void __launch_bounds__(256) output_kernel(OutputArgs a) {
+    extern __shared__ float sm[];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int64_t g = int64_t(blockIdx.x) * (blockDim.x >> 5) + wid;
+    if (g >= a.G) return;
+    const int t = blockIdx.y;
+    float* row = sm + wid * a.V_out;
+    const T* dec = static_cast<const T*>(a.dec) + g * a.ld_dec + int64_t(t) * a.V_out;
+    const int64_t orow = int64_t(t) * a.G + g;
+    for (int v = lane; v < a.V_out; v += 32) {
+        float val = to_f<T>(dec[v]);
+        const int rs = a.res_src[v];
+        if (rs >= 0) val = __fadd_rn(val, a.xn_step[g * a.V_in + rs]);
+        row[v] = val;
+        if (a.pre_bound) a.pre_bound[orow * a.V_out + v] = val;
+    }
+    __syncwarp();
+    for (int bi = 0; bi < a.n_bounds; ++bi) {
+        const BoundDev bd = a.bounds[bi];
+        const int* idx = a.bidx + bd.idx_off;
+        for (int j = lane; j < bd.n; j += 32) {
+            const float x = row[idx[j]];
+            if (bd.type == 0) {
+                row[idx[j]] = (x > 0.0f || x != x) ? x : 0.0f;  // relu, NaN propagates
+            } else {
+                // std::min(std::max(x, lo), hi) of the CPU reference, NaN propagating
+                const float m = (x < bd.lo) ? bd.lo : x;
+                row[idx[j]] = (bd.hi < m) ? bd.hi : m;
+            }
+        }
+        __syncwarp();
+        if (bd.type == 2) {
+            // y[idx] *= y[total] (already bounded); index and total lists are disjoint (checked at load)
+            const int* tot = a.bidx + bd.tot_off;
+            for (int j = lane; j < bd.n; j += 32) row[idx[j]] = __fmul_rn(row[idx[j]], row[tot[bd.n_tot == 1 ? 0 : j]]);
+            __syncwarp();
+        }
+    }
+    float* y = a.y + orow * a.V_out;
+    for (int v = lane; v < a.V_out; v += 32) y[v] = row[v];
+}
+
+[[noreturn]] void bad_c(int C, const char* what) {
+    fail(kUnsupported, std::string(what) + ": num_channels " + std::to_string(C) +
+                           " not supported (a multiple of 128 up to 2048)");
+}
+
+}  // namespace
+
+void normalise(const float* x, const float* mul, const float* add, float* xn, int64_t n, int V, cudaStream_t s) {
+    if (n <= 0) return;
+    normalise_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, mul, add, xn, n, V);
+    VB_LAUNCH();
+}
+
+void denormalise(const float* yn, const float* add, const float* mul, float* y, int64_t n, int V, cudaStream_t s) {
+    if (n <= 0) return;
+    denormalise_kernel<<<grid_for(n, 256), 256, 0, s>>>(yn, add, mul, y, n, V);
+    VB_LAUNCH();
+}
+
+template <class T>
+void assemble(const float* xn, const float* attr, int T_in, int64_t G, int V, int A, T* out, int64_t ld,
+              cudaStream_t s) {
+    if (G <= 0) return;
+    assemble_kernel<T><<<grid_for(G * ld, 256), 256, 0, s>>>(xn, attr, T_in, G, V, A, out, ld);
+    VB_LAUNCH();
+}
+
+template <class Tin, class Tout>
+void convert_2d(const Tin* src, int64_t lds, Tout* dst, int64_t ldd, int64_t rows, int64_t cols, cudaStream_t s) {
+    if (rows <= 0 || cols <= 0) return;
+    convert_kernel<Tin, Tout><<<grid_for(rows * cols, 256), 256, 0, s>>>(src, lds, dst, ldd, rows, cols);
+    VB_LAUNCH();
+}
+
+#define VB_NV_SWITCH(C, MACRO, what)                          \
+    switch ((C) / 128) {                                      \
+        case 1: MACRO(1); break;                              \
+        case 2: MACRO(2); break;                              \
+        case 3: MACRO(3); break;                              \
+        case 4: MACRO(4); break;                              \
+        case 5: MACRO(5); break;                              \
+        case 6: MACRO(6); break;                              \
+        case 7: MACRO(7); break;                              \
+        case 8: MACRO(8); break;                              \
+        case 10: MACRO(10); break;                            \
+        case 12: MACRO(12); break;                            \
+        case 14: MACRO(14); break;                            \
+        case 16: MACRO(16); break;                            \
+        default: bad_c(C, what);                              \
+    }
+
+template <class T>
+void layernorm(const T* x, int64_t ldx, const float* w, const float* b, T* y, int64_t ldy, int64_t rows, int C,
+               float eps, cudaStream_t s) {
+    if (rows <= 0) return;
+    if (C % 128) bad_c(C, "layernorm");
+    const unsigned grid = unsigned((rows + 7) / 8);
+#define VB_LN(NV) layernorm_kernel<T, NV><<<grid, 256, 0, s>>>(x, ldx, w, b, y, ldy, rows, eps)
+    VB_NV_SWITCH(C, VB_LN, "layernorm")
+#undef VB_LN
+    VB_LAUNCH();
+}
+
+template <class T>
+void add_layernorm(const T* a, const T* r, T* out1, const float* w, const float* b, T* ln, int64_t ld, int64_t rows,
+                   int C, float eps, cudaStream_t s) {
+    if (rows <= 0) return;
+    if (C % 128) bad_c(C, "add_layernorm");
+    const unsigned grid = unsigned((rows + 7) / 8);
+#define VB_ALN(NV) add_layernorm_kernel<T, NV><<<grid, 256, 0, s>>>(a, r, out1, w, b, ln, ld, rows, eps)
+    VB_NV_SWITCH(C, VB_ALN, "add_layernorm")
+#undef VB_ALN
+    VB_LAUNCH();
+}
+
+template <class T>
+void output_assemble(const OutputArgs& a, cudaStream_t s) {
+    if (a.G <= 0 || a.T_out <= 0) return;
+    if (a.T_out > 65535) fail(kUnsupported, "output_assemble: T_out > 65535");
+    const size_t smem = size_t(8) * a.V_out * sizeof(float);
+    if (smem > 48 * 1024) fail(kUnsupported, "output_assemble: too many output variables");
+    output_kernel<T><<<dim3(unsigned((a.G + 7) / 8), unsigned(a.T_out)), 256, smem, s>>>(a);
+    VB_LAUNCH();
+}
+
+template void assemble<float>(const float*, const float*, int, int64_t, int, int, float*, int64_t, cudaStream_t);
+template void assemble<__half>(const float*, const float*, int, int64_t, int, int, __half*, int64_t, cudaStream_t);
+template void convert_2d<float, float>(const float*, int64_t, float*, int64_t, int64_t, int64_t, cudaStream_t);
+template void convert_2d<float, __half>(const float*, int64_t, __half*, int64_t, int64_t, int64_t, cudaStream_t);
+template void convert_2d<__half, float>(const __half*, int64_t, float*, int64_t, int64_t, int64_t, cudaStream_t);
+template void layernorm<float>(const float*, int64_t, const float*, const float*, float*, int64_t, int64_t, int, float,
+                               cudaStream_t);
+template void layernorm<__half>(const __half*, int64_t, const float*, const float*, __half*, int64_t, int64_t, int,
+                                float, cudaStream_t);
+template void add_layernorm<float>(const float*, const float*, float*, const float*, const float*, float*, int64_t,
+                                   int64_t, int, float, cudaStream_t);
+template void add_layernorm<__half>(const __half*, const __half*, __half*, const float*, const float*, __half*,
+                                    int64_t, int64_t, int, float, cudaStream_t);
+template void output_assemble<float>(const OutputArgs&, cudaStream_t);
+template void output_assemble<__half>(const OutputArgs&, cudaStream_t);
+
+}  // namespace vb::k

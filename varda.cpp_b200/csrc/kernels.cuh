@@ -1,0 +1,109 @@
+// sm_100a kernels of libvarda_b200. Every launcher only enqueues on `s`: no allocation, no host
+// synchronisation, so callers may capture them in a CUDA graph. Element type T of activations is
+// float (fp32 mode) or __half (fp16 mode, the reference's autocast numerics). Row-major matrices
+// take a leading dimension in elements.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "graph.h"
+
+namespace vb::k {
+
+// ------------------------------------------------------------------ input / output
+// xn[i] = (x[i] * mul[v]) + add[v] with two separately rounded fp32 ops, v = i % V
+// (reference cuda/kernels.h:16-19, CPU backend_cpu.cpp:470-477).
+void normalise(const float* x, const float* mul, const float* add, float* xn, int64_t n, int V, cudaStream_t s);
+// y[i] = (yn[i] - add[v]) / mul[v], IEEE subtraction and division.
+void denormalise(const float* yn, const float* add, const float* mul, float* y, int64_t n, int V, cudaStream_t s);
+// out[g, t V + v] = xn[t, g, v]; out[g, T V + a] = attr[g, a]; out[g, F..ld) = 0.
+template <class T>
+void assemble(const float* xn, const float* attr, int T_in, int64_t G, int V, int A, T* out, int64_t ld,
+              cudaStream_t s);
+// dst[r, c] = Tout(src[r, c]) for c < cols.
+template <class Tin, class Tout>
+void convert_2d(const Tin* src, int64_t ld_src, Tout* dst, int64_t ld_dst, int64_t rows, int64_t cols, cudaStream_t s);
+
+struct BoundDev {
+    int type = 0;  // 0 relu, 1 hardtanh, 2 fraction
+    int n = 0, idx_off = 0, tot_off = 0, n_tot = 0;
+    float lo = 0, hi = 0;
+};
+struct OutputArgs {
+    const void* dec = nullptr;  // [G, ld_dec] T: decoder output, step t in columns [t V_out, (t+1) V_out)
+    int64_t ld_dec = 0;
+    const float* xn_step = nullptr;  // [G, V_in] normalised input of the residual step
+    int V_in = 0, V_out = 0, T_out = 1;
+    int64_t G = 0;
+    const int* res_src = nullptr;  // [V_out]: input index added to output v, or -1
+    const BoundDev* bounds = nullptr;
+    int n_bounds = 0;
+    const int* bidx = nullptr;
+    float* pre_bound = nullptr;  // optional [T_out, G, V_out]
+    float* y = nullptr;          // [T_out, G, V_out]
+};
+// Per output step: fp32 cast, prognostic residual, boundings in config order (reference
+// backend_cpu.cpp:504-522, 111-136).
+template <class T> void output_assemble(const OutputArgs& a, cudaStream_t s);
+
+// ------------------------------------------------------------------ LayerNorm (fp32 statistics)
+// y = LN(x) * w + b over C channels per row (C a multiple of 128, <= 2048); b may be null; y may
+// alias x. Output rounded to T once.
+template <class T>
+void layernorm(const T* x, int64_t ldx, const float* w, const float* b, T* y, int64_t ldy, int64_t rows, int C,
+               float eps, cudaStream_t s);
+// out1 = T(a + r) (rounded to T), then ln = LN(out1).
+template <class T>
+void add_layernorm(const T* a, const T* r, T* out1, const float* w, const float* b, T* ln, int64_t ld, int64_t rows,
+                   int C, float eps, cudaStream_t s);
+
+// ------------------------------------------------------------------ graph attention
+template <class T> struct AttnArgs {
+    const int32_t* row_ptr = nullptr;  // [n_dst + 1] of the whole graph
+    const EdgeRec* edges = nullptr;    // [n_edges] CSR order
+    int64_t dst_lo = 0, n_rows = 0;    // destinations [dst_lo, dst_lo + n_rows); q, xr, out rows are local
+    const T* q = nullptr;
+    int64_t ldq = 0;
+    const T* k = nullptr;  // rows = source ids
+    const T* v = nullptr;
+    int64_t ldkv = 0;
+    const T* xr = nullptr;
+    int64_t ldxr = 0;
+    T* out = nullptr;
+    int64_t ldo = 0;
+    const float* w_e = nullptr;  // [4, C]: edge Linear weight columns (zero padded to 3), then its bias
+    int C = 0, heads = 0, head_dim = 0;
+};
+// out[i] = T(T(att_i) + xr[i]); att_i = sum_j softmax_j(<q_i, k_j + e_ij> / sqrt(d)) (v_j + e_ij) per
+// head with e_ij = W_e a_ij + b_e folded in; fp32 online softmax; zero in-degree -> att = 0.
+// Semantics of the reference's cpu::graph_attention (cpu/kernels.cpp:98-158) plus the `+ x_r` of
+// backend_cpu.cpp:333-340 and the fp16 roundings of the autocast reference.
+template <class T> void attention(const AttnArgs<T>& a, cudaStream_t s);
+
+// ------------------------------------------------------------------ GEMM (Linear layers)
+enum Epilogue : int {
+    kEpiBias = 0,      // y = T(acc + b)
+    kEpiGelu = 1,      // y = T(gelu(T(acc + b)))
+    kEpiResidual = 2,  // y = T(T(acc + b) + r)
+};
+template <class T> struct GemmArgs {
+    const T* A = nullptr;  // [M, K] lda
+    int64_t lda = 0;
+    const T* W = nullptr;  // [N, K] ldw (nn.Linear weight)
+    int64_t ldw = 0;
+    const T* bias = nullptr;  // [N] or null
+    T* C = nullptr;           // [M, N] ldc
+    int64_t ldc = 0;
+    const T* R = nullptr;  // residual [M, N] ldr (kEpiResidual)
+    int64_t ldr = 0;
+    int64_t M = 0, N = 0, K = 0;
+    int epi = kEpiBias;
+    bool gelu_tanh = false;
+};
+// CUDA-core GEMM with fp32 accumulation (true fp32 FMA in fp32 mode).
+template <class T> void gemm_simt(const GemmArgs<T>& a, cudaStream_t s);
+
+}  // namespace vb::k

@@ -1,0 +1,264 @@
+"""Python binding of libvarda_b200 (include/varda_b200.h) through ctypes.
+
+Mirrors the reference's public C++ API (varda.cpp src/varda/varda.h:21-76): Options, Model.load,
+Model.predict_step(x, y, hook), plus the CudaBackend device entry points and the kernel-level entry
+points used by the tests. The shared library must exist (built by `make -C varda.cpp_b200`); there is
+no fallback: every call goes to the CUDA library, and a missing library raises ImportError.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libvarda_b200.so")
+
+FP32, FP16 = 0, 1
+ERRORS = {1: "invalid argument", 2: "format", 3: "cuda", 4: "unsupported", 5: "internal", 6: "timeout"}
+
+
+class VardaError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"[{ERRORS.get(code, code)}] {msg}")
+        self.code = code
+
+
+def _load_lib():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `make -C varda.cpp_b200`")
+    L = ctypes.CDLL(LIB_PATH)
+    P, I, I64, F, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+    sig = {
+        "vb_last_error": ([], ctypes.c_char_p),
+        "vb_load": ([ctypes.c_char_p, P, P], I),
+        "vb_load_sharded": ([ctypes.c_char_p, P, I, I, P, P], I),
+        "vb_nccl_unique_id": ([P], I),
+        "vb_free": ([P], None),
+        "vb_predict_step": ([P, P, P, P, P], I),
+        "vb_sizes": ([P, P], I),
+        "vb_data_range": ([P, P, P], I),
+        "vb_normalise": ([P, P, P, P], I),
+        "vb_forward_normalised": ([P, P, P, P], I),
+        "vb_denormalise": ([P, P, P, P], I),
+        "vb_predict_step_device": ([P, P, P, P], I),
+        "vb_prepare": ([P], I),
+        "vb_use_high_priority_stream": ([P], I),
+        "vb_device_input": ([P], P),
+        "vb_device_output": ([P], P),
+        "vb_stream": ([P], P),
+        "vb_enqueue_predict": ([P], I),
+        "vb_device": ([P], I),
+        "vb_weight_bytes": ([P], SZ),
+        "vb_activation_bytes": ([P], SZ),
+        "vb_decoder_chunk_rows": ([P], I64),
+        "vb_check_device": ([], I),
+        "vb_launch_count": ([], I64),
+        "vb_profile_forward": ([P, ctypes.c_char_p, SZ], I64),
+        "vb_build_csr": ([P, I64, P, I, I64, I64, P, P, P, P], I),
+        "vb_pack_edges": ([P, P, I, I64, I, P], I),
+        "vb_attention": ([I, P, P, I64, I64, P, I64, P, P, I64, P, I64, P, I64, P, I, I, I, P], I),
+        "vb_gemm": ([I, I, P, I64, P, I64, P, P, I64, P, I64, I64, I64, I64, I, I, P], I),
+        "vb_layernorm": ([I, P, I64, P, P, P, I64, I64, I, F, P], I),
+        "vb_add_layernorm": ([I, P, P, P, P, P, P, I64, I64, I, F, P], I),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    return L
+
+
+lib = _load_lib()
+
+# exported symbols, for the ABI check in the tests
+SYMBOLS = [n for n in dir(lib) if n.startswith("vb_")]
+
+
+def check(rc):
+    if rc != 0:
+        raise VardaError(rc, lib.vb_last_error().decode(errors="replace"))
+
+
+class Options(ctypes.Structure):
+    """varda::Options (varda.h:21-27)."""
+    _fields_ = [("precision", ctypes.c_int), ("cuda_device", ctypes.c_int), ("cuda_graph", ctypes.c_int),
+                ("num_threads", ctypes.c_int)]
+
+
+HOOK = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int64),
+                        ctypes.c_int, ctypes.c_void_p)
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return ctypes.c_void_p(a)
+    if hasattr(a, "data_ptr"):  # torch tensor (device memory plumbing)
+        return ctypes.c_void_p(a.data_ptr())
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+class Model:
+    """varda::Model (varda.h:37-76) on the B200 backend."""
+
+    def __init__(self, handle):
+        self._h = handle
+        s = (ctypes.c_int64 * 8)()
+        check(lib.vb_sizes(self._h, s))
+        self.T_in, self.G, self.V_in, self.T_out, self.V_out, self.H, self.C, self.n_proc = list(s)
+        lo, hi = ctypes.c_int64(), ctypes.c_int64()
+        check(lib.vb_data_range(self._h, ctypes.byref(lo), ctypes.byref(hi)))
+        self.data_lo, self.data_hi = lo.value, hi.value
+
+    @staticmethod
+    def load(path, precision=FP16, cuda_device=0, cuda_graph=True):
+        o = Options(precision, cuda_device, int(cuda_graph), 0)
+        h = ctypes.c_void_p()
+        check(lib.vb_load(os.fsencode(path), ctypes.byref(o), ctypes.byref(h)))
+        return Model(h)
+
+    @staticmethod
+    def load_sharded(path, rank, world, nccl_id, precision=FP16, cuda_device=0, cuda_graph=True):
+        o = Options(precision, cuda_device, int(cuda_graph), 0)
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+        check(lib.vb_load_sharded(os.fsencode(path), ctypes.byref(o), rank, world, buf, ctypes.byref(h)))
+        return Model(h)
+
+    def free(self):
+        if self._h:
+            lib.vb_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    @property
+    def input_shape(self):
+        return (1, self.T_in, self.G, self.V_in)
+
+    @property
+    def output_shape(self):
+        return (1, self.T_out, 1, self.G, self.V_out)
+
+    def predict_step(self, x, y=None, hook=None):
+        """Host x (1, T_in, G, V_in) fp32 -> y (1, T_out, 1, G, V_out) fp32. hook(key, array)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.size != int(np.prod(self.input_shape)):
+            raise ValueError(f"x has {x.size} elements, expected {self.input_shape}")
+        if y is None:
+            y = np.empty(self.output_shape, np.float32)
+        cb = None
+        if hook is not None:
+            def _cb(key, data, shape, ndim, user):
+                shp = tuple(shape[i] for i in range(ndim))
+                n = int(np.prod(shp)) if shp else 1
+                arr = np.ctypeslib.as_array(data, shape=(n,)).reshape(shp).copy()
+                hook(key.decode(), arr)
+            cb = HOOK(_cb)
+        check(lib.vb_predict_step(self._h, _ptr(x), _ptr(y), cb, None))
+        return y
+
+    # CudaBackend device entry points (cuda_backend.h:38-74); pointers are ints / torch tensors
+    def normalise(self, x, xn, stream=None):
+        check(lib.vb_normalise(self._h, _ptr(x), _ptr(xn), stream))
+
+    def forward_normalised(self, xn, yn, stream=None):
+        check(lib.vb_forward_normalised(self._h, _ptr(xn), _ptr(yn), stream))
+
+    def denormalise(self, yn, y, stream=None):
+        check(lib.vb_denormalise(self._h, _ptr(yn), _ptr(y), stream))
+
+    def predict_step_device(self, x, y, stream=None):
+        check(lib.vb_predict_step_device(self._h, _ptr(x), _ptr(y), stream))
+
+    def prepare(self):
+        check(lib.vb_prepare(self._h))
+
+    def enqueue_predict(self):
+        check(lib.vb_enqueue_predict(self._h))
+
+    def device_input(self):
+        return lib.vb_device_input(self._h)
+
+    def device_output(self):
+        return lib.vb_device_output(self._h)
+
+    def stream(self):
+        return lib.vb_stream(self._h)
+
+    def profile(self):
+        """One eager forward with a CUDA event pair around every launch: list of
+        {"name", "ms", "flop", "bytes"} records."""
+        import json
+        n = lib.vb_profile_forward(self._h, None, 0)
+        if n < 0:
+            check(-n)
+        buf = ctypes.create_string_buffer(int(n) + 1024)
+        n = lib.vb_profile_forward(self._h, buf, len(buf))
+        if n < 0:
+            check(-n)
+        return json.loads(buf.value.decode())
+
+    @property
+    def weight_bytes(self):
+        return lib.vb_weight_bytes(self._h)
+
+    @property
+    def activation_bytes(self):
+        return lib.vb_activation_bytes(self._h)
+
+
+# ---------------------------------------------------------------- kernel-level wrappers
+def build_csr(edge_index, edge_attr, n_src, n_dst):
+    ei = np.ascontiguousarray(edge_index, np.int64)
+    ea = np.ascontiguousarray(edge_attr, np.float32)
+    E, A = ei.shape[1], ea.shape[1]
+    rp = np.empty(n_dst + 1, np.int32)
+    src = np.empty(E, np.int32)
+    eid = np.empty(E, np.int32)
+    at = np.empty((E, A), np.float32)
+    check(lib.vb_build_csr(_ptr(ei), E, _ptr(ea), A, n_src, n_dst, _ptr(rp), _ptr(src), _ptr(eid), _ptr(at)))
+    return rp, src, eid, at
+
+
+def pack_edges(src, attr_csr, round_fp16):
+    src = np.ascontiguousarray(src, np.int32)
+    at = np.ascontiguousarray(attr_csr, np.float32)
+    out = np.empty((len(src), 4), np.float32)
+    check(lib.vb_pack_edges(_ptr(src), _ptr(at), at.shape[1], len(src), int(round_fp16), _ptr(out)))
+    return out
+
+
+def attention(dtype, row_ptr, edges, dst_lo, n_rows, q, ldq, k, v, ldkv, xr, ldxr, out, ldo, w_e, C, heads,
+              head_dim, stream=None):
+    check(lib.vb_attention(dtype, _ptr(row_ptr), _ptr(edges), dst_lo, n_rows, _ptr(q), ldq, _ptr(k), _ptr(v), ldkv,
+                           _ptr(xr), ldxr, _ptr(out), ldo, _ptr(w_e), C, heads, head_dim, stream))
+
+
+def gemm(dtype, engine, A, lda, W, ldw, bias, Y, ldy, R, ldr, M, N, K, epilogue=0, gelu_tanh=False, stream=None):
+    check(lib.vb_gemm(dtype, engine, _ptr(A), lda, _ptr(W), ldw, _ptr(bias), _ptr(Y), ldy, _ptr(R), ldr, M, N, K,
+                      epilogue, int(gelu_tanh), stream))
+
+
+def layernorm(dtype, x, ldx, w, b, y, ldy, rows, C, eps, stream=None):
+    check(lib.vb_layernorm(dtype, _ptr(x), ldx, _ptr(w), _ptr(b), _ptr(y), ldy, rows, C, eps, stream))
+
+
+def add_layernorm(dtype, a, r, out1, w, b, ln, ld, rows, C, eps, stream=None):
+    check(lib.vb_add_layernorm(dtype, _ptr(a), _ptr(r), _ptr(out1), _ptr(w), _ptr(b), _ptr(ln), ld, rows, C, eps,
+                               stream))
+
+
+def launch_count():
+    return int(lib.vb_launch_count())
+
+
+def check_device():
+    check(lib.vb_check_device())
