@@ -1,0 +1,351 @@
+"""Benchmark: ms per fp16 predict_step at the Varda shape, plus edge-attention
+HBM GB/s, on N B200s of one node.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c0]
+
+Prints one JSON line (rank 0). `value` is the device-resident time of one predict_step (the model's
+own input/output buffers, CUDA-graph replay, CUDA events on the model's stream, max over ranks);
+`e2e` is the same through the public host API vb_predict_step with pinned host buffers (H2D of x and
+D2H of y inside the timed region). `roofline` describes the dominant kernel class and
+`edge_attention` the processor-block attention, both from one eager pass with a CUDA event pair
+around every launch (vb_profile_forward). `cpu_baseline` is the reference's own CPU fp32 backend
+(oracle/_ref/ref_dump, built from the reference's sources) timed on this host on a bounded sample.
+
+--impl reference times that reference CPU backend alone (rank 0; other ranks exit 0).
+Inputs and activations (tens of GB) are far larger than the 126 MB L2, so no L2 flush is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "varda.cpp_b200"))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+CACHE = os.environ.get("VB_BENCH_CACHE", os.path.join(tempfile.gettempdir(), "varda_b200_bench"))
+REF_DUMP = os.path.join(HERE, "oracle", "_ref", "ref_dump")
+SAMPLE_FACTOR = 64  # the CPU baseline runs the C1 architecture on 1/64 of its nodes
+
+
+def peaks():
+    p = os.path.join(HERE, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ models
+def model_paths(workload):
+    from varda_b200 import synth
+    os.makedirs(CACHE, exist_ok=True)
+    mp = os.path.join(CACHE, f"{workload}.model.safetensors")
+    xp = os.path.join(CACHE, f"{workload}.input.safetensors")
+    if not (os.path.exists(mp) and os.path.exists(xp)):
+        t0 = time.time()
+        synth.generate(workload, CACHE)
+        log(f"bench: generated {workload} in {time.time() - t0:.1f} s")
+    return mp, xp
+
+
+def sample_model():
+    """C1's architecture (C=1024, 16 heads, mlp 4096, 16 blocks, T=2, V_in=90, V_out=80) on 1/64 of
+    its nodes with the same per-node edge counts (encoder kNN-4, processor kNN-14, decoder kNN-3)."""
+    from varda_b200 import synth
+    os.makedirs(CACHE, exist_ok=True)
+    mp = os.path.join(CACHE, "c1s.model.safetensors")
+    xp = os.path.join(CACHE, "c1s.input.safetensors")
+    if os.path.exists(mp) and os.path.exists(xp):
+        return mp, xp
+    G, H = 1_688_650 // SAMPLE_FACTOR, 189_809 // SAMPLE_FACTOR
+
+    def fib(n):
+        i = np.arange(n) + 0.5
+        z = 1 - 2 * i / n
+        phi = i * np.pi * (3 - 5 ** 0.5)
+        r = np.sqrt(1 - z * z)
+        return np.stack([r * np.cos(phi), r * np.sin(phi), z], 1)
+
+    data, hidden = fib(G), fib(H)
+    enc = np.stack([np.repeat(np.arange(G), 4), synth.knn(hidden, data, 4).ravel()], 1)
+    nb = synth.knn(hidden, hidden, 15)[:, 1:]
+    proc = np.stack([nb.ravel(), np.repeat(np.arange(H), 14)], 1)
+    dec = np.stack([synth.knn(hidden, data, 3).ravel(), np.repeat(np.arange(G), 3)], 1)
+    data, hidden, enc, proc, dec = synth._sort_nodes(data, hidden, enc, proc, dec)
+    names, forc = synth._c1_forcings()
+    v = synth._vars(90, 90, 80, 80)
+    cfg, t, x = synth.make_model(seed=1, C=1024, heads=16, mlp=4096, n_proc=16, T=2, data_pos=data,
+                                 hidden_pos=hidden, enc=enc, proc=proc, dec=dec, A=4, Ae=3, var_names=names,
+                                 forcings=forc, uuid="b200-c1-sample", **v)
+    synth.write_model(mp, cfg, t)
+    synth.write_input(xp, x)
+    return mp, xp
+
+
+def reference_cpu(steps, warmup, threads=0):
+    """The reference's CPU fp32 backend on the bounded sample; per-step seconds, scaled to the full
+    C1 node count (every op of the forward pass is linear in node and edge counts)."""
+    if not os.path.exists(REF_DUMP):
+        raise FileNotFoundError(f"{REF_DUMP} missing (make -C oracle with the reference sources)")
+    mp, xp = sample_model()
+    cmd = [REF_DUMP, "--model", mp, "--input", xp, "--steps", str(warmup + steps)]
+    if threads:
+        cmd += ["--threads", str(threads)]
+    r = subprocess.run(cmd, capture_output=True, text=True, check=True)
+    rec = json.loads(r.stdout.strip().splitlines()[-1])
+    times = rec["steps_s"][warmup:]
+    return times, rec["threads"], SAMPLE_FACTOR
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    def __init__(self, device):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = subprocess.Popen(
+            ["nvidia-smi", "-i", str(device), "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
+             "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+             "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+
+    def stop(self):
+        self.p.terminate()
+        try:
+            self.p.wait(5)
+        except Exception:
+            self.p.kill()
+        self.f.seek(0)
+        rows = [l.split(",") for l in self.f.read().strip().splitlines() if l.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                pass
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------ ours
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import varda_b200 as vb
+    from varda_b200 import safetensors as st
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    if rank == 0:
+        mp, xp = model_paths(args.workload)
+    if dist:
+        dist.barrier()
+    mp, xp = model_paths(args.workload)
+    t0 = time.time()
+    if world > 1:
+        uid = bytearray(128)
+        if rank == 0:
+            buf = (np.zeros(128, np.uint8))
+            import ctypes
+            b = ctypes.create_string_buffer(128)
+            vb.check(vb.lib.vb_nccl_unique_id(b))
+            uid = bytearray(b.raw)
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=0)
+        m = vb.Model.load_sharded(mp, rank, world, obj[0], precision=vb.FP16, cuda_device=local_rank)
+    else:
+        m = vb.Model.load(mp, precision=vb.FP16, cuda_device=local_rank)
+    load_s = time.time() - t0
+    x = np.array(st.read(xp)[0]["in.x"])
+    stream = torch.cuda.ExternalStream(m.stream(), device=f"cuda:{local_rank}")
+
+    # inputs into the model's own device buffer (device-resident timing)
+    xd = torch.from_numpy(x).to(f"cuda:{local_rank}")
+    import ctypes
+    rt = ctypes.CDLL("libcudart.so.12")
+    rt.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+    assert rt.cudaMemcpy(m.device_input(), xd.data_ptr(), xd.numel() * 4, 3) == 0
+    del xd
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        m.enqueue_predict()  # first call eager, then the CUDA graph
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    n_launch0 = vb.launch_count()
+    clk = Clocks(local_rank)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        m.enqueue_predict()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if dist:
+        dist.barrier()
+
+    # e2e through the host API: pinned x, y; H2D + forward + D2H every step
+    xh = torch.from_numpy(x).pin_memory().numpy()
+    yh = torch.empty(m.output_shape, dtype=torch.float32).pin_memory().numpy()
+    for _ in range(max(1, args.warmup // 2)):
+        m.predict_step(xh, yh)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        m.predict_step(xh, yh)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    lo, hi = m.data_lo, m.data_hi
+    h2d = x.nbytes if world == 1 else x.nbytes  # every rank uploads the input it needs (its own rows + halo)
+    d2h = int(np.prod(m.output_shape)) * 4 * (hi - lo) // m.G
+
+    # one profiled eager pass: per-launch device times
+    prof = m.profile()
+    vb.check_device()
+    launches_per_step = sum(1 for r in prof)  # every launch of one forward is profiled once
+    if dist:
+        t = torch.tensor([ms, e2e_ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    return dict(m=m, ms=ms, e2e_ms=e2e_ms, clocks=clocks, prof=prof, load_s=load_s, h2d=h2d, d2h=d2h,
+                launches=launches_per_step + 2, dist=dist, n_launch_timed=vb.launch_count() - n_launch0)
+
+
+def summarise(prof, pk, src):
+    by = {}
+    for r in prof:
+        cls = r["name"].split(" ")[0]
+        if r["name"].startswith("attention"):
+            cls = r["name"]
+        d = by.setdefault(cls, {"ms": 0.0, "flop": 0.0, "bytes": 0.0, "n": 0})
+        d["ms"] += r["ms"]
+        d["flop"] += r["flop"]
+        d["bytes"] += r["bytes"]
+        d["n"] += 1
+    total = sum(d["ms"] for d in by.values())
+    dom = max(by, key=lambda k: by[k]["ms"])
+    d = by[dom]
+    if d["flop"] > 0:
+        ach = d["flop"] / (d["ms"] * 1e-3) / 1e12
+        peak = pk["bf16_tflops_sustained"]
+        roof = {"kernel": dom, "bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(ach / peak, 4), "traffic": None, "launches_per_step": d["n"],
+                "share": round(d["ms"] / total, 4), "peak_source": f"{src} (sustained bf16, kernel inside a long step)"}
+    else:
+        ach = d["bytes"] / (d["ms"] * 1e-3) / 1e9
+        peak = pk["hbm_gbs"]
+        roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(ach / peak, 4), "traffic": None, "launches_per_step": d["n"],
+                "share": round(d["ms"] / total, 4), "peak_source": src}
+    att = by.get("attention proc")
+    edge = None
+    if att:
+        per = att["ms"] / att["n"]
+        gbs = att["bytes"] / (att["ms"] * 1e-3) / 1e9
+        edge = {"kernel": "attention proc", "bound": "hbm", "ms_per_launch": round(per, 4),
+                "bytes_per_launch": att["bytes"] / att["n"], "achieved": round(gbs, 1), "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None, "peak_source": src}
+    shares = {k: {"ms": round(v["ms"], 3), "share": round(v["ms"] / total, 4), "launches": v["n"]}
+              for k, v in sorted(by.items(), key=lambda kv: -kv[1]["ms"])}
+    return roof, edge, shares, total
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c1", choices=["c1", "c0", "c3"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if "WORLD_SIZE" not in os.environ and args.gpus > 1:
+        raise SystemExit("for --gpus > 1 launch with torch.distributed.run (one process per GPU)")
+    config = {"workload": "C1: full Varda-shaped forecaster predict_step (G=1,688,650 data nodes, "
+                          "H=189,809 hidden, C=1024, 16 heads, 16 processor blocks, T_in=2, V_in=90, V_out=80)",
+              "model": "GraphTransformer enc-proc-dec (varda.cpp format v3), random-init seeded weights",
+              "global_batch": 1, "seq_len": None, "parallelism": f"graph partition by destination x{world}",
+              "l2": "inputs and activations >> 126 MB L2 (no flush needed)"}
+    if args.workload == "c0":
+        config["workload"] = "C0: icosphere r5/r4 model, C=128"
+    pk, src = peaks()
+    metric = "ms/predict_step fp16 at Varda shape"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        times, threads, f = reference_cpu(args.steps, args.warmup)
+        v = statistics.median(times) * f * 1000
+        line = {"impl": "reference", "metric": metric, "value": round(v, 2), "unit": "ms", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 2), "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+                "config": config,
+                "cpu_baseline": {"value": round(v, 2), "unit": "ms", "cores": threads, "kind": "reference",
+                                 "sample": f"reference CPU fp32 backend (oracle/_ref/ref_dump, unmodified sources) on "
+                                           f"the C1 architecture with 1/{f} of its nodes (G={1688650 // f}, "
+                                           f"H={189809 // f}, same per-node edge counts); median of {len(times)} "
+                                           f"steps x {f}"},
+                "e2e": {"value": round(v, 2), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    r = run_ours(args, rank, world, local_rank)
+    roof, edge, shares, prof_total = summarise(r["prof"], pk, src)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "c1":
+        try:
+            times, threads, f = reference_cpu(2, 1)
+            v = statistics.median(times) * f * 1000
+            cpu = {"value": round(v, 1), "unit": "ms", "cores": threads, "kind": "reference",
+                   "sample": f"reference CPU fp32 backend (oracle/_ref/ref_dump) on the C1 architecture with 1/{f} of "
+                             f"its nodes, median of {len(times)} steps x {f}"}
+        except Exception as e:  # the baseline is reported, never the product
+            cpu = {"value": None, "unit": "ms", "error": str(e)[:200]}
+    if rank == 0:
+        line = {"metric": metric, "value": round(r["ms"], 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(r["ms"], 3), "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded graph, inputs "
+                "and random-init weights)", "config": config, "roofline": roof, "edge_attention": edge,
+                "cpu_baseline": cpu, "clocks": r["clocks"],
+                "e2e": {"value": round(r["e2e_ms"], 3), "unit": "ms", "h2d_bytes_per_step": int(r["h2d"]),
+                        "d2h_bytes_per_step": int(r["d2h"])},
+                "gpu_launches": int(r["launches"] * args.steps),
+                "kernel_shares": shares, "profiled_forward_ms": round(prof_total, 3), "load_s": round(r["load_s"], 1)}
+        print(json.dumps(line), flush=True)
+    if r["dist"]:
+        r["dist"].barrier()
+        r["dist"].destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
