@@ -76,6 +76,9 @@ int vb_predict_step(vb_model* m, const float* x, float* y, vb_hook_fn hook, void
  * T_out G V_out (cuda/cuda_backend.h:34-35). */
 int vb_sizes(const vb_model* m, int64_t out8[8]);
 int vb_data_range(const vb_model* m, int64_t* lo, int64_t* hi);
+/* Element counts of the device tensors of this rank: x/xn (T_in, G_local, V_in) and yn/y
+ * (T_out, own data rows, V_out); on one GPU input_numel / output_numel (cuda_backend.h:34-35). */
+int vb_io_numel(const vb_model* m, int64_t* in, int64_t* out);
 
 /* varda::cuda::CudaBackend device entry points (src/varda/cuda/cuda_backend.h:38-69). Pointers are
  * device pointers (fp32, contiguous); stream is a cudaStream_t (NULL = the legacy default stream). */
@@ -106,6 +109,13 @@ int vb_check_device(void);
  * the length it needs (call again with a larger buffer if that exceeds len). Synchronises. */
 int64_t vb_launch_count(void);
 int64_t vb_profile_forward(vb_model* m, char* buf, size_t len);
+
+/* The destination partition vb_load_sharded uses for `rank` of `world` on this model file, computed
+ * on the host only (no GPU): JSON with the hidden/data ranges of every rank, this rank's halos (global
+ * ids), its send lists per peer, and its local CSR graphs (sources in local ids). Same length
+ * convention as vb_profile_forward; a negative return is minus the error class. No reference
+ * counterpart (the reference runs on one GPU). */
+int64_t vb_shard_plan(const char* path, int world, int rank, char* buf, size_t len);
 
 /* ---------------------------------------------------------------- kernel-level entry points
  * The reference's internal kernel interface (src/varda/cuda/kernels.h, graph.h, gemm.h), exported

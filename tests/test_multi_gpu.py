@@ -1,0 +1,72 @@
+"""Multi-GPU destination partition on B200s (skipped with fewer than 2 visible GPUs): one process per
+GPU, NCCL halo exchange; every rank's output rows must be bitwise equal to the single-GPU result
+(the partition keeps every destination's edge order and every GEMM row's arithmetic)."""
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+def _worker(rank, world, mp, xp, dtype, uid_path, out_dir):
+    import time
+    import varda_b200 as vb
+    from varda_b200 import safetensors as st
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    if rank == 0:
+        with open(uid_path + ".tmp", "wb") as f:
+            f.write(vb.nccl_unique_id())
+        os.replace(uid_path + ".tmp", uid_path)
+    t0 = time.time()
+    while not os.path.exists(uid_path):
+        if time.time() - t0 > 60:
+            raise TimeoutError("no NCCL id")
+        time.sleep(0.05)
+    uid = open(uid_path, "rb").read()
+    m = vb.Model.load_sharded(mp, rank, world, uid, precision=dtype, cuda_device=rank)
+    x = np.array(st.read(xp)[0]["in.x"])
+    ys = []
+    for _ in range(3):  # eager, capture + replay, replay
+        y = np.full(m.output_shape, np.nan, np.float32)
+        m.predict_step(x, y)
+        ys.append(y[:, :, :, m.data_lo:m.data_hi].copy())
+    vb.check_device()
+    np.savez(os.path.join(out_dir, f"r{rank}.npz"), y0=ys[0], y1=ys[1], y2=ys[2], lo=m.data_lo, hi=m.data_hi)
+    m.free()
+
+
+def _single(mp, xp, dtype, out):
+    import varda_b200 as vb
+    from varda_b200 import safetensors as st
+    torch.cuda.set_device(0)
+    m = vb.Model.load(mp, precision=dtype)
+    y = m.predict_step(np.array(st.read(xp)[0]["in.x"]))
+    np.save(out, y)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("name", ["c0", "t256"])
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_sharded_equals_single_gpu(name, dtype, seeded_model, tmp_path):
+    import torch.multiprocessing as tmp
+    mp, xp = seeded_model(name)
+    world = min(torch.cuda.device_count(), 4)
+    ctx = tmp.get_context("spawn")
+    p = ctx.Process(target=_single, args=(mp, xp, dtype, str(tmp_path / "single.npy")))
+    p.start()
+    p.join(300)
+    assert p.exitcode == 0
+    y1 = np.load(tmp_path / "single.npy")
+    tmp.start_processes(_worker, args=(world, mp, xp, dtype, str(tmp_path / "uid"), str(tmp_path)), nprocs=world,
+                        join=True, start_method="spawn")
+    covered = 0
+    for r in range(world):
+        z = np.load(tmp_path / f"r{r}.npz")
+        lo, hi = int(z["lo"]), int(z["hi"])
+        covered += hi - lo
+        for k in ("y0", "y1", "y2"):
+            assert np.array_equal(z[k], y1[:, :, :, lo:hi]), f"rank {r} {k} differs from one GPU"
+    assert covered == y1.shape[3]

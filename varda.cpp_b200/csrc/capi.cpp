@@ -9,8 +9,11 @@
 #include <memory>
 #include <string>
 
+#include "comm.h"
 #include "common.h"
+#include "config.h"
 #include "engine.h"
+#include "safetensors.h"
 #include "gemm_tc.cuh"
 #include "graph.h"
 #include "kernels.cuh"
@@ -126,6 +129,13 @@ int vb_data_range(const vb_model* m, int64_t* lo, int64_t* hi) {
     });
 }
 
+int vb_io_numel(const vb_model* m, int64_t* in, int64_t* out) {
+    return guard([&] {
+        need(m, "model"), need(in, "in"), need(out, "out");
+        *in = m->m->input_numel(), *out = m->m->output_numel();
+    });
+}
+
 int vb_normalise(vb_model* m, const float* x, float* xn, void* stream) {
     return guard([&] {
         need(m, "model"), need(x, "x"), need(xn, "xn");
@@ -180,6 +190,29 @@ int vb_check_device(void) {
     return guard([&] {
         if (vb::tc::take_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the tensor-core GEMM");
     });
+}
+
+int64_t vb_shard_plan(const char* path, int world, int rank, char* buf, size_t len) {
+    std::string s;
+    const int rc = guard([&] {
+        need(path, "path");
+        vb::SafeTensorsFile f(path);
+        const vb::Config c = vb::parse_config(f.metadata("config"));
+        const int64_t G = c.n_data_nodes, H = c.n_hidden_nodes;
+        auto g = [&](const char* n, int64_t ns, int64_t nd) {
+            return vb::build_csr_by_dst(f.peek(std::string("graph.") + n + ".edge_index"),
+                                        f.peek(std::string("graph.") + n + ".edge_attr"), ns, nd);
+        };
+        const vb::CsrGraph enc = g("enc", G, H), proc = g("proc", H, H), dec = g("dec", H, G);
+        s = vb::plan_json(vb::make_plan(c, enc, proc, dec, world, rank), true);
+    });
+    if (rc != VB_OK) return -rc;
+    if (buf && len) {
+        const size_t n = std::min(len - 1, s.size());
+        std::memcpy(buf, s.data(), n);
+        buf[n] = 0;
+    }
+    return int64_t(s.size() + 1);
 }
 
 int64_t vb_launch_count(void) { return vb::launch_counter(); }

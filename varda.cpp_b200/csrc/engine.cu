@@ -19,6 +19,7 @@
 #include <type_traits>
 #include <vector>
 
+#include "comm.h"
 #include "common.h"
 #include "config.h"
 #include "engine.h"
@@ -111,8 +112,10 @@ public:
     ~Engine() override;
 
     void predict_step(const float* x, float* y, HookFn hook, void* user) override;
-    int64_t input_numel() const override { return int64_t(T_in_) * G_ * V_in_; }
-    int64_t output_numel() const override { return int64_t(T_out_) * G_ * V_out_; }
+    // device tensors hold this rank's rows: x/xn (T_in, Gx, V_in) = own data rows then the encoder's
+    // halo rows; yn/y (T_out, Gl, V_out) = own data rows (all rows on one GPU)
+    int64_t input_numel() const override { return int64_t(T_in_) * Gx_ * V_in_; }
+    int64_t output_numel() const override { return int64_t(T_out_) * Gl_ * V_out_; }
     void normalise(const float* x, float* xn, cudaStream_t s) override {
         k::normalise(x, mul_in_.as<float>(), add_in_.as<float>(), xn, input_numel(), V_in_, s);
     }
@@ -138,7 +141,7 @@ public:
     void sizes(int64_t o[8]) const override {
         o[0] = T_in_, o[1] = G_, o[2] = V_in_, o[3] = T_out_, o[4] = V_out_, o[5] = H_, o[6] = C_, o[7] = n_proc_;
     }
-    void data_range(int64_t* lo, int64_t* hi) const override { *lo = 0, *hi = G_; }
+    void data_range(int64_t* lo, int64_t* hi) const override { *lo = plan_.g_lo, *hi = plan_.g_hi; }
     std::string profile_forward() override;
 
 private:
@@ -172,7 +175,8 @@ private:
     Lin<T> load_linear(SafeTensorsFile& f, const std::vector<std::string>& names, int64_t N_each, int64_t K);
     Norm load_norm(SafeTensorsFile& f, const std::string& name);
     Block<T> load_block(SafeTensorsFile& f, const std::string& pre, bool mapper);
-    GraphDev load_graph(SafeTensorsFile& f, const std::string& g, int64_t n_src, int64_t n_dst);
+    CsrGraph read_graph(SafeTensorsFile& f, const std::string& g, int64_t n_src, int64_t n_dst);
+    GraphDev upload_graph(const CsrGraph& csr, const std::string& name);
     DeviceBuffer upload(const void* h, size_t bytes);
     T* act(size_t elems);
     float* actf(size_t elems);
@@ -218,6 +222,21 @@ private:
     DeviceBuffer hook_stage_, hook_xsrc_, hook_prebound_;
     bool ran_eager_ = false, graph_failed_ = false;
     cudaGraphExec_t graph_exec_ = nullptr;
+
+    // ---- destination partition (world == 1: the identity, no halos)
+    ShardPlan plan_;
+    int64_t Hl_ = 0, Gl_ = 0, Gx_ = 0, n_eh_ = 0, n_ph_ = 0, n_dh_ = 0;
+    std::unique_ptr<Comm> comm_;
+    struct Xchg {  // one halo exchange: pack own K|V rows per peer, send/recv, (unpack)
+        DeviceBuffer send_idx;  // local ids of the rows sent, grouped by peer
+        std::vector<int64_t> send_off, send_cnt, recv_off, recv_cnt;  // in elements
+        int64_t n_send = 0, n_recv = 0;                                // in rows
+    };
+    Xchg xp_, xd_;
+    T *xsend_ = nullptr, *xrecv_ = nullptr;
+    float* x_halo_host_ = nullptr;  // pinned staging of the encoder's halo input rows
+    void setup_exchange(Xchg& x, const HaloPlan& h);
+    void exchange(Xchg& x, const T* src, int64_t lds, T* dst, int64_t ldd, bool direct, cudaStream_t s);
 };
 
 // ====================================================================== hook
@@ -336,22 +355,72 @@ Block<T> Engine<T>::load_block(SafeTensorsFile& f, const std::string& pre, bool 
 }
 
 template <class T>
-GraphDev Engine<T>::load_graph(SafeTensorsFile& f, const std::string& g, int64_t n_src, int64_t n_dst) {
+CsrGraph Engine<T>::read_graph(SafeTensorsFile& f, const std::string& g, int64_t n_src, int64_t n_dst) {
     const TensorView& ei = f.take("graph." + g + ".edge_index");
     const TensorView& ea = f.take("graph." + g + ".edge_attr");
     if (ea.shape.size() != 2 || ea.shape[1] != cfg_.edge_attr_dim)
         fail(kFormat, ea.name + ": expected [E, " + std::to_string(cfg_.edge_attr_dim) + "], got " + ea.shape_str());
-    CsrGraph csr = build_csr_by_dst(ei, ea, n_src, n_dst);
+    return build_csr_by_dst(ei, ea, n_src, n_dst);
+}
+
+template <class T>
+GraphDev Engine<T>::upload_graph(const CsrGraph& csr, const std::string& name) {
     std::vector<EdgeRec> packed = pack_edges(csr, !std::is_same<T, float>::value);
     GraphDev d;
-    d.name = g;
+    d.name = name;
     d.row_ptr = upload(csr.row_ptr.data(), csr.row_ptr.size() * sizeof(int32_t));
     d.edges = upload(packed.data(), std::max<size_t>(1, packed.size()) * sizeof(EdgeRec));
-    d.n_src = n_src;
-    d.n_dst = n_dst;
+    d.n_src = csr.n_src;
+    d.n_dst = csr.n_dst;
     d.n_edges = csr.n_edges;
     d.max_degree = csr.max_degree();
     return d;
+}
+
+template <class T>
+void Engine<T>::setup_exchange(Xchg& x, const HaloPlan& h) {
+    const int W = plan_.world;
+    const int64_t row = 2 * int64_t(C_);
+    x.send_off.assign(size_t(W), 0), x.send_cnt.assign(size_t(W), 0);
+    x.recv_off.assign(size_t(W), 0), x.recv_cnt.assign(size_t(W), 0);
+    std::vector<int32_t> idx;
+    for (int p = 0; p < W; ++p) {
+        x.send_off[size_t(p)] = int64_t(idx.size()) * row;
+        for (int32_t g : h.send[size_t(p)]) idx.push_back(int32_t(g - plan_.h_lo));
+        x.send_cnt[size_t(p)] = int64_t(h.send[size_t(p)].size()) * row;
+    }
+    int64_t off = 0;
+    for (int p = 0; p < W; ++p) {
+        x.recv_off[size_t(p)] = off * row;
+        x.recv_cnt[size_t(p)] = h.recv_count[size_t(p)] * row;
+        off += h.recv_count[size_t(p)];
+    }
+    x.n_send = int64_t(idx.size());
+    x.n_recv = off;
+    if (idx.empty()) idx.push_back(0);
+    x.send_idx = upload(idx.data(), idx.size() * sizeof(int32_t));
+}
+
+// Halo exchange of K|V rows (2C wide): pack the own rows every peer needs from src (row stride lds)
+// into xsend_, grouped send/recv; the received rows (ascending global id = peer order) land in
+// dst rows [0, n_recv) (stride ldd) directly when `direct` (contiguous 2C rows), else via xrecv_.
+template <class T>
+void Engine<T>::exchange(Xchg& x, const T* src, int64_t lds, T* dst, int64_t ldd, bool direct, cudaStream_t s) {
+    if (plan_.world == 1) return;
+    const int64_t row = 2 * int64_t(C_);
+    {
+        Span sp(this, s, "halo_pack", 0, double(x.n_send) * row * 2 * sizeof(T));
+        k::copy_rows<T>(xsend_, row, nullptr, src, lds, x.send_idx.template as<int32_t>(), x.n_send, row, s);
+    }
+    T* recv = direct ? dst : xrecv_;
+    {
+        Span sp(this, s, "halo_exchange", 0, double(x.n_send + x.n_recv) * row * sizeof(T));
+        comm_->exchange(xsend_, x.send_off, x.send_cnt, recv, x.recv_off, x.recv_cnt, int(sizeof(T)), s);
+    }
+    if (!direct) {
+        Span sp(this, s, "halo_unpack", 0, double(x.n_recv) * row * 2 * sizeof(T));
+        k::copy_rows<T>(dst, ldd, nullptr, xrecv_, row, nullptr, x.n_recv, row, s);
+    }
 }
 
 template <class T>
@@ -433,7 +502,23 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     bounds_ = upload(bd.data(), bd.size() * sizeof(k::BoundDev));
     bidx_ = upload(bidx.data(), bidx.size() * 4);
 
-    // ---- node attributes (and the optional grid coordinates, consumed as the reference does)
+    // ---- graphs and the destination partition (the identity on one GPU)
+    {
+        CsrGraph enc = read_graph(file, "enc", G_, H_);
+        CsrGraph proc = read_graph(file, "proc", H_, H_);
+        CsrGraph dec = read_graph(file, "dec", H_, G_);
+        plan_ = make_plan(cfg_, enc, proc, dec, opts_.world, opts_.rank);
+    }
+    Hl_ = plan_.h_hi - plan_.h_lo, Gl_ = plan_.g_hi - plan_.g_lo;
+    n_eh_ = int64_t(plan_.enc_halo.size()), n_ph_ = int64_t(plan_.proc.halo.size());
+    n_dh_ = int64_t(plan_.dec.halo.size()), Gx_ = Gl_ + n_eh_;
+    g_enc_ = upload_graph(plan_.enc, "enc");
+    g_proc_ = upload_graph(plan_.proc_g, "proc");
+    g_dec_ = upload_graph(plan_.dec_g, "dec");
+    for (CsrGraph* g : {&plan_.enc, &plan_.proc_g, &plan_.dec_g}) *g = CsrGraph{};  // host copies not needed
+
+    // ---- node attributes: data rows [own | encoder halo], own hidden rows (and the optional grid
+    // coordinates, consumed as the reference does)
     if (file.has("grid.latitudes") || file.has("grid.longitudes")) {
         file.take("grid.latitudes", DType::F64, {G_});
         file.take("grid.longitudes", DType::F64, {G_});
@@ -442,12 +527,20 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         if (kv.first == "cutout") fail(kUnsupported, "multi-source (cutout) grids are not supported");
     const TensorView& da = file.take("nodes.data.attr", DType::F32, {G_, A_node_});
     const TensorView& ha = file.take("nodes.hidden.attr", DType::F32, {H_, A_node_});
-    d_attr_ = upload(da.data, da.nbytes);
-    h_attr_host_.assign(ha.as<float>(), ha.as<float>() + ha.numel());
     {
-        std::vector<T> hp(size_t(H_ * ldA_), T(0.0f));
-        for (int64_t r = 0; r < H_; ++r)
-            for (int a = 0; a < A_node_; ++a) hp[size_t(r * ldA_ + a)] = T(ha.as<float>()[r * A_node_ + a]);
+        std::vector<float> dl(size_t(Gx_ * A_node_));
+        std::memcpy(dl.data(), da.as<float>() + plan_.g_lo * A_node_, size_t(Gl_ * A_node_) * sizeof(float));
+        for (int64_t i = 0; i < n_eh_; ++i)
+            std::memcpy(&dl[size_t((Gl_ + i) * A_node_)], da.as<float>() + int64_t(plan_.enc_halo[size_t(i)]) * A_node_,
+                        size_t(A_node_) * sizeof(float));
+        d_attr_ = upload(dl.data(), dl.size() * sizeof(float));
+    }
+    if (plan_.world == 1) h_attr_host_.assign(ha.as<float>(), ha.as<float>() + ha.numel());
+    {
+        std::vector<T> hp(size_t(Hl_ * ldA_), T(0.0f));
+        for (int64_t r = 0; r < Hl_; ++r)
+            for (int a = 0; a < A_node_; ++a)
+                hp[size_t(r * ldA_ + a)] = T(ha.as<float>()[(plan_.h_lo + r) * A_node_ + a]);
         h_attr_ = upload(hp.data(), hp.size() * sizeof(T));
     }
 
@@ -460,45 +553,56 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     enc_ = load_block(file, "enc.block", true);
     for (int i = 0; i < n_proc_; ++i) proc_.push_back(load_block(file, "proc." + std::to_string(i), false));
     dec_ = load_block(file, "dec.block", true);
-
-    // ---- graphs
-    g_enc_ = load_graph(file, "enc", G_, H_);
-    g_proc_ = load_graph(file, "proc", H_, H_);
-    g_dec_ = load_graph(file, "dec", H_, G_);
     file.require_all_consumed();
 
-    // ---- activations
+    // ---- activations (this rank's rows)
     x_dev_ = actf(size_t(input_numel()));
     xn_ = actf(size_t(input_numel()));
     yn_ = actf(size_t(output_numel()));
     y_dev_ = actf(size_t(output_numel()));
-    x_data_ = act(size_t(G_ * ldF_));
-    dec_out_ = act(size_t(G_ * ldVo_));
-    z_enc_ = act(size_t(H_ * C_));
-    zA_ = act(size_t(H_ * C_));
-    zB_ = act(size_t(H_ * C_));
-    xh_ = act(size_t(H_ * C_));
-    qkvs_ = act(size_t(H_ * 4 * C_));
-    sbuf_ = act(size_t(H_ * C_));
-    out1_ = act(size_t(H_ * C_));
-    hbuf_ = act(size_t(H_ * mlp_));
-    // Shared region: the encoder's source side ([G, C] embedding + [G, 2C] k|v), then the decoder's
-    // destination chunks (6C + mlp per row). All G rows in one chunk unless limited.
-    const int64_t enc_elems = G_ * 3 * C_;
+    x_data_ = act(size_t(Gx_ * ldF_));
+    dec_out_ = act(size_t(Gl_ * ldVo_));
+    z_enc_ = act(size_t(Hl_ * C_));
+    zA_ = act(size_t(Hl_ * C_));
+    zB_ = act(size_t(Hl_ * C_));
+    xh_ = act(size_t(Hl_ * C_));
+    // q|k|v|self of own rows plus the K|V of the processor halo rows; later the decoder's k|v of
+    // own rows plus its halo
+    qkvs_ = act(size_t(std::max((Hl_ + n_ph_) * 4 * C_, (Hl_ + n_dh_) * 2 * C_)));
+    sbuf_ = act(size_t(Hl_ * C_));
+    out1_ = act(size_t(Hl_ * C_));
+    hbuf_ = act(size_t(Hl_ * mlp_));
+    // Shared region: the encoder's source side ([Gx, C] embedding + [Gx, 2C] k|v), then the decoder's
+    // destination chunks (6C + mlp per row). All own data rows in one chunk unless limited.
+    const int64_t enc_elems = Gx_ * 3 * C_;
     const int64_t per_row = 6 * int64_t(C_) + mlp_;
-    int64_t rows = opts_.dec_chunk_rows > 0 ? opts_.dec_chunk_rows : env_int("VB_DEC_CHUNK_ROWS", G_);
-    rows = std::min<int64_t>(std::max<int64_t>(rows, 1), G_);
-    const int64_t nch = (G_ + rows - 1) / rows;
-    rows = std::min<int64_t>(int64_t(align_up(size_t((G_ + nch - 1) / nch), 128)), G_);
+    int64_t rows = opts_.dec_chunk_rows > 0 ? opts_.dec_chunk_rows : env_int("VB_DEC_CHUNK_ROWS", Gl_);
+    rows = std::min<int64_t>(std::max<int64_t>(rows, 1), std::max<int64_t>(Gl_, 1));
+    const int64_t nch = (std::max<int64_t>(Gl_, 1) + rows - 1) / rows;
+    rows = std::min<int64_t>(int64_t(align_up(size_t((Gl_ + nch - 1) / nch), 128)), std::max<int64_t>(Gl_, 1));
     dec_rows_ = rows;
     region_ = act(size_t(std::max(enc_elems, rows * per_row)));
+
+    // ---- halo exchanges (multi-GPU)
+    if (plan_.world > 1) {
+        if (!opts_.nccl_id) fail(kInvalidArgument, "sharded load needs the NCCL unique id");
+        setup_exchange(xp_, plan_.proc);
+        setup_exchange(xd_, plan_.dec);
+        xsend_ = act(size_t(std::max<int64_t>(1, std::max(xp_.n_send, xd_.n_send)) * 2 * C_));
+        xrecv_ = act(size_t(std::max<int64_t>(1, xp_.n_recv) * 2 * C_));
+        if (n_eh_) VB_CUDA(cudaMallocHost(&x_halo_host_, size_t(T_in_ * n_eh_ * V_in_) * sizeof(float)));
+        comm_ = std::make_unique<Comm>(plan_.world, plan_.rank, opts_.nccl_id);
+    }
     VB_CUDA(cudaDeviceSynchronize());
 }
 
 template <class T>
 Engine<T>::~Engine() {
     cudaSetDevice(dev_);
-    if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    if (graph_exec_) cudaGraphExecDestroy(graph_exec_);  // before the communicator its nodes use
+    comm_.reset();
+    if (x_halo_host_) cudaFreeHost(x_halo_host_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -559,7 +663,9 @@ void Engine<T>::attention(const GraphDev& g, const Block<T>& b, int64_t lo, int6
 
 template <class T>
 void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
-    const int64_t G = G_, H = H_, C = C_;
+    // G: this rank's data rows (own, then the encoder's halo) for the encoder's source side;
+    // Gl: own data rows (decoder destinations); H: own hidden rows
+    const int64_t G = Gx_, Gl = Gl_, H = Hl_, C = C_;
     {
         Span sp(this, s, "assemble", 0, double(G) * (T_in_ * V_in_ * 4 + A_node_ * 4 + ldF_ * sizeof(T)));
         k::assemble<T>(xn, d_attr_.as<float>(), T_in_, G, V_in_, A_node_, x_data_, ldF_, s);
@@ -603,6 +709,7 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
     for (int i = 0; i < n_proc_; ++i) {
         const Block<T>& b = proc_[size_t(i)];
         linear(b.qkvs, xh_, C, qkvs_, 4 * C, H, s);
+        exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, s);  // K|V of remote sources
         attention(g_proc_, b, 0, H, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C, 4 * C, sbuf_, s);
         linear(b.proj, sbuf_, C, out1_, C, H, s, k::kEpiResidual, z_in, C);
         ln(out1_, b.ln_mlp, xh_, H, s);
@@ -628,10 +735,11 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
     // ---- decoder, source side: [k | v] of LN_src(latent)
     T* kv_dec = qkvs_;
     linear(dec_.kv, xh_, C, kv_dec, 2 * C, H, s);
+    exchange(xd_, kv_dec, 2 * C, kv_dec + H * 2 * C, 2 * C, true, s);
 
     // ---- decoder, destination chunks of data rows
     std::vector<float> h_emb, h_bo;
-    if (hk) h_emb.resize(size_t(G * C)), h_bo.resize(size_t(G * C));
+    if (hk) h_emb.resize(size_t(Gl * C)), h_bo.resize(size_t(Gl * C));
     const int64_t R = dec_rows_;
     T* e = region_;
     T* t = e + R * C;
@@ -639,8 +747,8 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
     T* sb = qs + R * 2 * C;
     T* o1 = sb + R * C;
     T* h = o1 + R * C;
-    for (int64_t lo = 0; lo < G; lo += R) {
-        const int64_t n = std::min(R, G - lo);
+    for (int64_t lo = 0; lo < Gl; lo += R) {
+        const int64_t n = std::min(R, Gl - lo);
         linear(dec_emb_dst_, x_data_ + lo * ldF_, ldF_, e, C, n, s);
         if (hk) hk->fetch(e, C, n, C, h_emb.data(), lo);
         ln(e, dec_.ln_dst, t, n, s);
@@ -655,16 +763,16 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
         linear(dec_out_proj_, t, C, dec_out_ + lo * ldVo_, ldVo_, n, s);
     }
     if (hk) {
-        hk->host("dec.emb_dst", h_emb.data(), {G, C});
-        hk->host("dec.block_out", h_bo.data(), {G, C});
-        hk->dev("dec.out", dec_out_, ldVo_, G, V_dec_, {G, int64_t(V_dec_)});
+        hk->host("dec.emb_dst", h_emb.data(), {Gl, C});
+        hk->host("dec.block_out", h_bo.data(), {Gl, C});
+        hk->dev("dec.out", dec_out_, ldVo_, Gl, V_dec_, {Gl, int64_t(V_dec_)});
     }
 
     // ---- output: per step t, fp32 cast + residual + bounding -> yn [T_out, G, V_out]
     k::OutputArgs o;
     o.dec = dec_out_, o.ld_dec = ldVo_;
     o.xn_step = xn + int64_t(cfg_.residual_step) * G * V_in_;
-    o.V_in = V_in_, o.V_out = V_out_, o.T_out = T_out_, o.G = G;
+    o.V_in = V_in_, o.V_out = V_out_, o.T_out = T_out_, o.G = Gl;
     o.res_src = res_src_.as<int>(), o.bounds = bounds_.as<k::BoundDev>(), o.n_bounds = n_bounds_;
     o.bidx = bidx_.as<int>();
     if (hk) {
@@ -674,13 +782,13 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
     o.y = yn;
     {
         Span sp(this, s, "output_assemble", 0,
-                double(G) * (ldVo_ * sizeof(T) + V_in_ * 4) + double(T_out_) * G * V_out_ * 4);
+                double(Gl) * (ldVo_ * sizeof(T) + V_in_ * 4) + double(T_out_) * Gl * V_out_ * 4);
         k::output_assemble<T>(o, s);
     }
     if (hk) {
-        const std::vector<int64_t> shp = {1, T_out_, 1, G, V_out_};
-        hk->dev("out.pre_bound", hook_prebound_.as<float>(), V_out_, T_out_ * G, V_out_, shp);
-        hk->dev("out.norm", yn, V_out_, T_out_ * G, V_out_, shp);
+        const std::vector<int64_t> shp = {1, T_out_, 1, Gl, V_out_};
+        hk->dev("out.pre_bound", hook_prebound_.as<float>(), V_out_, T_out_ * Gl, V_out_, shp);
+        hk->dev("out.norm", yn, V_out_, T_out_ * Gl, V_out_, shp);
     }
 }
 
@@ -741,6 +849,30 @@ void Engine<T>::predict_step(const float* x, float* y, HookFn hook, void* user) 
     VB_CUDA(cudaSetDevice(dev_));
     cudaStream_t s = stream_;
     const int64_t in_n = input_numel(), out_n = output_numel();
+    if (plan_.world > 1) {
+        // host x is the full (1, T_in, G, V_in) input: copy this rank's rows, own rows then the
+        // encoder's halo rows (gathered on the host into pinned memory); y gets this rank's rows
+        if (hook) fail(kUnsupported, "the activation hook is available on single-GPU models only");
+        for (int t = 0; t < T_in_; ++t) {
+            VB_CUDA(cudaMemcpyAsync(x_dev_ + int64_t(t) * Gx_ * V_in_, x + (int64_t(t) * G_ + plan_.g_lo) * V_in_,
+                                    size_t(Gl_ * V_in_) * sizeof(float), cudaMemcpyHostToDevice, s));
+            if (n_eh_) {
+                float* stage = x_halo_host_ + int64_t(t) * n_eh_ * V_in_;
+                VB_CUDA(cudaStreamSynchronize(s));  // the staging buffer may still feed a previous copy
+                for (int64_t i = 0; i < n_eh_; ++i)
+                    std::memcpy(stage + i * V_in_, x + (int64_t(t) * G_ + plan_.enc_halo[size_t(i)]) * V_in_,
+                                size_t(V_in_) * sizeof(float));
+                VB_CUDA(cudaMemcpyAsync(x_dev_ + (int64_t(t) * Gx_ + Gl_) * V_in_, stage,
+                                        size_t(n_eh_ * V_in_) * sizeof(float), cudaMemcpyHostToDevice, s));
+            }
+        }
+        enqueue_predict();
+        for (int t = 0; t < T_out_; ++t)
+            VB_CUDA(cudaMemcpyAsync(y + (int64_t(t) * G_ + plan_.g_lo) * V_out_, y_dev_ + int64_t(t) * Gl_ * V_out_,
+                                    size_t(Gl_ * V_out_) * sizeof(float), cudaMemcpyDeviceToHost, s));
+        VB_CUDA(cudaStreamSynchronize(s));
+        return;
+    }
     VB_CUDA(cudaMemcpyAsync(x_dev_, x, size_t(in_n) * sizeof(float), cudaMemcpyHostToDevice, s));
     if (hook) {
         Hook hk{*this, hook, user, s};
@@ -797,7 +929,6 @@ int64_t& launch_counter() {
 }
 
 std::unique_ptr<Model> load_model(const std::string& path, const Options& o) {
-    if (o.world > 1) return load_sharded_model(path, o);
     if (o.precision == 0) return std::make_unique<Engine<float>>(path, o);
     return std::make_unique<Engine<__half>>(path, o);
 }

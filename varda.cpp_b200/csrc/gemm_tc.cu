@@ -1,14 +1,15 @@
 // tcgen05 GEMM (see gemm_tc.cuh).
 //
-// Persistent kernel, one 192-thread CTA per SM, warp-specialised:
+// Persistent kernel, one 320-thread CTA per SM, warp-specialised:
 //   warp 0 (one lane)   TMA producer: A [128 x 64] and W [BN x 64] fp16 tiles, 128-byte swizzle,
 //                       into a STAGES-deep shared-memory ring (full/empty mbarriers).
 //   warp 1 (one lane)   MMA issuer: 4 x tcgen05.mma (M=128, N=BN, K=16) per 64-wide k block into
 //                       one of two TMEM accumulators; tcgen05.commit frees the smem stage, and a
 //                       commit after the last k block hands the accumulator to the epilogue.
-//   warps 2-5           epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
-//                       32 (w % 4) .. + 31 = its 32 output rows), bias / GELU / residual in fp32,
-//                       fp16 stores; then release the accumulator to the MMA warp.
+//   warps 2-9           epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
+//                       32 (w % 4) .. + 31 = its 32 output rows; warps w and w + 4 split the
+//                       columns in halves), bias / GELU / residual in fp32, fp16 stores; then
+//                       release the accumulator to the MMA warp.
 // Two accumulators (2 x BN TMEM columns) let the epilogue of tile i overlap the main loop of
 // tile i + 1. Tiles are visited m-major (n fastest) so an A row block is reused from L2 by the
 // CTAs working on its N tiles.
@@ -38,6 +39,7 @@ using vb::d::rnd;
 using vb::d::to_f;
 
 constexpr int BM = 128, BK = 64;
+constexpr int kEpiWarps = 8, kThreads = 32 * (2 + kEpiWarps);
 constexpr unsigned long long kTimeoutNs = 4000000000ull;  // 4 s
 
 __device__ int g_error = 0;
@@ -215,7 +217,7 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int row, int n0,
 }
 
 template <int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
     using L = Layout<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
@@ -234,7 +236,7 @@ __global__ void __launch_bounds__(192, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
-        for (int b = 0; b < 2; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], 4);
+        for (int b = 0; b < 2; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], kEpiWarps);
         mbar_init(drain, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -311,6 +313,7 @@ __global__ void __launch_bounds__(192, 1)
     } else if (warp >= 2) {
         // ---------------- epilogue
         const int lg = warp & 3;  // TMEM lane group this warp may access
+        const int half = (warp - 2) >> 2;  // which half of the columns
         int it = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
             const int ab = it & 1;
@@ -321,7 +324,7 @@ __global__ void __launch_bounds__(192, 1)
             const int row = mb * BM + lg * 32 + lane;
             const uint32_t taddr = tmem + (uint32_t(lg * 32) << 16) + uint32_t(ab * BN);
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
                 float v[32];
                 tmem_ld32(taddr + uint32_t(c * 32), v);
                 const int n0 = nb * BN + c * 32;
@@ -392,7 +395,7 @@ void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
     Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0};
     const int64_t tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
     const int grid = int(std::min<int64_t>(tiles, sm_count()));
-    gemm_tc_kernel<BN, STAGES, EPI><<<grid, 192, L::kSmem, s>>>(ta, tb, p);
+    gemm_tc_kernel<BN, STAGES, EPI><<<grid, kThreads, L::kSmem, s>>>(ta, tb, p);
     VB_LAUNCH();
 }
 

@@ -53,6 +53,16 @@ __global__ void assemble_kernel(const float* __restrict__ xn, const float* __res
     }
 }
 
+// One warp per row, 16-byte vectors.
+__global__ void copy_rows_kernel(uint4* dst, int64_t ldd, const int32_t* __restrict__ di, const uint4* __restrict__ src,
+                                 int64_t lds, const int32_t* __restrict__ si, int64_t rows, int64_t vecs) {
+    const int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    const int lane = threadIdx.x & 31;
+    const int64_t dr = di ? di[r] : r, sr = si ? si[r] : r;
+    for (int64_t v = lane; v < vecs; v += 32) dst[dr * ldd + v] = src[sr * lds + v];
+}
+
 template <class Tin, class Tout>
 __global__ void convert_kernel(const Tin* __restrict__ src, int64_t lds, Tout* __restrict__ dst, int64_t ldd,
                                int64_t rows, int64_t cols) {
@@ -205,6 +215,24 @@ void assemble(const float* xn, const float* attr, int T_in, int64_t G, int V, in
     assemble_kernel<T><<<grid_for(G * ld, 256), 256, 0, s>>>(xn, attr, T_in, G, V, A, out, ld);
     VB_LAUNCH();
 }
+
+template <class T>
+void copy_rows(T* dst, int64_t ldd, const int32_t* di, const T* src, int64_t lds, const int32_t* si, int64_t rows,
+               int64_t cols, cudaStream_t s) {
+    if (rows <= 0 || cols <= 0) return;
+    constexpr int64_t per = 16 / sizeof(T);
+    if (cols % per || ldd % per || lds % per || (reinterpret_cast<uintptr_t>(dst) & 15) ||
+        (reinterpret_cast<uintptr_t>(src) & 15))
+        fail(kInvalidArgument, "copy_rows: rows must be 16-byte vectors");
+    copy_rows_kernel<<<unsigned((rows + 7) / 8), 256, 0, s>>>(reinterpret_cast<uint4*>(dst), ldd / per, di,
+                                                             reinterpret_cast<const uint4*>(src), lds / per, si, rows,
+                                                             cols / per);
+    VB_LAUNCH();
+}
+template void copy_rows<float>(float*, int64_t, const int32_t*, const float*, int64_t, const int32_t*, int64_t, int64_t,
+                               cudaStream_t);
+template void copy_rows<__half>(__half*, int64_t, const int32_t*, const __half*, int64_t, const int32_t*, int64_t,
+                                int64_t, cudaStream_t);
 
 template <class Tin, class Tout>
 void convert_2d(const Tin* src, int64_t lds, Tout* dst, int64_t ldd, int64_t rows, int64_t cols, cudaStream_t s) {

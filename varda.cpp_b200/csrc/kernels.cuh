@@ -23,6 +23,11 @@ void denormalise(const float* yn, const float* add, const float* mul, float* y, 
 template <class T>
 void assemble(const float* xn, const float* attr, int T_in, int64_t G, int V, int A, T* out, int64_t ld,
               cudaStream_t s);
+// dst[di(r), 0:cols] = src[si(r), 0:cols] for r < rows, di / si the index arrays or the identity
+// when null; cols * sizeof(T) and both strides multiples of 16 bytes. Halo pack / unpack.
+template <class T>
+void copy_rows(T* dst, int64_t ldd, const int32_t* dst_idx, const T* src, int64_t lds, const int32_t* src_idx,
+               int64_t rows, int64_t cols, cudaStream_t s);
 // dst[r, c] = Tout(src[r, c]) for c < cols.
 template <class Tin, class Tout>
 void convert_2d(const Tin* src, int64_t ld_src, Tout* dst, int64_t ld_dst, int64_t rows, int64_t cols, cudaStream_t s);

@@ -39,6 +39,7 @@ def _load_lib():
         "vb_predict_step": ([P, P, P, P, P], I),
         "vb_sizes": ([P, P], I),
         "vb_data_range": ([P, P, P], I),
+        "vb_io_numel": ([P, P, P], I),
         "vb_normalise": ([P, P, P, P], I),
         "vb_forward_normalised": ([P, P, P, P], I),
         "vb_denormalise": ([P, P, P, P], I),
@@ -55,6 +56,7 @@ def _load_lib():
         "vb_decoder_chunk_rows": ([P], I64),
         "vb_check_device": ([], I),
         "vb_launch_count": ([], I64),
+        "vb_shard_plan": ([ctypes.c_char_p, I, I, ctypes.c_char_p, SZ], I64),
         "vb_profile_forward": ([P, ctypes.c_char_p, SZ], I64),
         "vb_build_csr": ([P, I64, P, I, I64, I64, P, P, P, P], I),
         "vb_pack_edges": ([P, P, I, I64, I, P], I),
@@ -112,6 +114,9 @@ class Model:
         lo, hi = ctypes.c_int64(), ctypes.c_int64()
         check(lib.vb_data_range(self._h, ctypes.byref(lo), ctypes.byref(hi)))
         self.data_lo, self.data_hi = lo.value, hi.value
+        i, o = ctypes.c_int64(), ctypes.c_int64()
+        check(lib.vb_io_numel(self._h, ctypes.byref(i), ctypes.byref(o)))
+        self.device_input_numel, self.device_output_numel = i.value, o.value
 
     @staticmethod
     def load(path, precision=FP16, cuda_device=0, cuda_graph=True):
@@ -254,6 +259,26 @@ def layernorm(dtype, x, ldx, w, b, y, ldy, rows, C, eps, stream=None):
 def add_layernorm(dtype, a, r, out1, w, b, ln, ld, rows, C, eps, stream=None):
     check(lib.vb_add_layernorm(dtype, _ptr(a), _ptr(r), _ptr(out1), _ptr(w), _ptr(b), _ptr(ln), ld, rows, C, eps,
                                stream))
+
+
+def shard_plan(path, world, rank):
+    """The destination partition of a model file for `rank` of `world` (host only, no GPU): ranges,
+    halos, send lists and the local CSR graphs (sources in local ids)."""
+    import json
+    n = lib.vb_shard_plan(os.fsencode(path), world, rank, None, 0)
+    if n < 0:
+        check(-n)
+    buf = ctypes.create_string_buffer(int(n) + 16)
+    n = lib.vb_shard_plan(os.fsencode(path), world, rank, buf, len(buf))
+    if n < 0:
+        check(-n)
+    return json.loads(buf.value.decode())
+
+
+def nccl_unique_id():
+    b = ctypes.create_string_buffer(128)
+    check(lib.vb_nccl_unique_id(b))
+    return bytes(b.raw)
 
 
 def launch_count():
