@@ -8,8 +8,10 @@
 //                       commit after the last k block hands the accumulator to the epilogue.
 //   warps 2-9           epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
 //                       32 (w % 4) .. + 31 = its 32 output rows; warps w and w + 4 split the
-//                       columns in halves), bias / GELU / residual in fp32, fp16 stores; then
-//                       release the accumulator to the MMA warp.
+//                       columns in halves), bias / GELU / residual in fp32, the 32 x 32 fp16
+//                       sub-tile staged in 64-byte-swizzled shared memory and written by one TMA
+//                       bulk tensor store (the residual sub-tile arrives the same way, one chunk
+//                       ahead); then release the accumulator to the MMA warp.
 // Two accumulators (2 x BN TMEM columns) let the epilogue of tile i overlap the main loop of
 // tile i + 1. Tiles are visited m-major (n fastest) so an A row block is reused from L2 by the
 // CTAs working on its N tiles.
@@ -163,74 +165,67 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int BN, int STAGES> struct Layout {
+// Shared memory: the A/W stage ring, then per epilogue warp two 2 KB output staging buffers (and, for
+// the residual epilogue, two 2 KB residual buffers), then the mbarriers.
+template <int BN, int STAGES, int EPI> struct Layout {
     static constexpr int kA = BM * BK * 2;  // bytes per A stage
     static constexpr int kB = BN * BK * 2;
     static constexpr int kTiles = STAGES * (kA + kB);
-    static constexpr int kBars = (2 * STAGES + 5) * 8;
-    static constexpr int kSmem = 1024 + kTiles + kBars + 16;  // 1024: alignment slack
+    static constexpr int kSub = 32 * 32 * 2;  // one 32 x 32 fp16 sub-tile
+    static constexpr int kOut = kEpiWarps * 2 * kSub;
+    static constexpr int kRes = EPI == k::kEpiResidual ? kEpiWarps * 2 * kSub : 0;
+    static constexpr int kBars = (2 * STAGES + 5 + 2 * kEpiWarps) * 8;
+    static constexpr int kSmem = 1024 + kTiles + kOut + kRes + kBars + 16;  // 1024: alignment slack
+    static_assert(kSmem <= 232448, "shared memory over the 227 KB per-CTA limit");
 };
 
-template <int EPI>
-__device__ __forceinline__ void epilogue_store(const Params& p, int row, int n0, float (&v)[32]) {
-    // bias, autocast rounding, GELU / residual; then 32 fp16 values = 4 x 16-byte stores
-    const bool full = n0 + 32 <= p.N;
-    __half* out = p.C + int64_t(row) * p.ldc + n0;
-    float b[32];
-    if (p.bias) {
-        if (full) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) vb::d::Vec<__half, 8>::ldg(p.bias + n0 + 8 * q, b + 8 * q);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) b[i] = n0 + i < p.N ? __half2float(p.bias[n0 + i]) : 0.f;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) b[i] = 0.f;
-    }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(v[i] + b[i]);
-    if (EPI == k::kEpiGelu) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(gelu(v[i], p.gelu_tanh != 0));
-    } else if (EPI == k::kEpiResidual) {
-        const __half* r = p.R + int64_t(row) * p.ldr + n0;
-        float rv[32];
-        if (full) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) vb::d::Vec<__half, 8>::load(r + 8 * q, rv + 8 * q);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) rv[i] = n0 + i < p.N ? __half2float(r[i]) : 0.f;
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(v[i] + rv[i]);
-    }
-    if (full) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) vb::d::Vec<__half, 8>::store(out + 8 * q, v + 8 * q);
-    } else {
-        for (int i = 0; i < 32; ++i)
-            if (n0 + i < p.N) out[i] = __float2half_rn(v[i]);
-    }
+// GELU for the fp16 path: x * Phi(x), Phi from the erf approximation of Abramowitz & Stegun,
+// Handbook of Mathematical Functions, formula 7.1.26 (|error of erf| <= 1.5e-7), written as
+// Phi(x) = 1 - q (x >= 0), q (x < 0) with q = P(t) exp(-z^2) / 2, z = |x| / sqrt(2), so the left tail
+// has no cancellation. Checked against the erff-based GELU by the tests.
+__device__ __forceinline__ float gelu_as(float x) {
+    const float z = fabsf(x) * 0.70710678118654752f;
+    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+    const float poly =
+        t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
+    const float q = 0.5f * poly * __expf(-z * z);
+    return x * (x >= 0.0f ? 1.0f - q : q);
 }
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk j of row r in a 32 x 64-byte sub-tile with the 64-byte swizzle of the
+// tensor map (chunk index XOR bits 1-2 of the row): conflict-free 16-byte accesses by 32 lanes.
+__device__ __forceinline__ int sw64(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
 
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
-    using L = Layout<BN, STAGES>;
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, Params p) {
+    using L = Layout<BN, STAGES, EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * L::kA;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kTiles);
+    uint8_t* sOut = smem + L::kTiles;
+    uint8_t* sRes = sOut + L::kOut;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sRes + L::kRes);
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
     uint64_t* tfull = bars + 2 * STAGES;
     uint64_t* tempty = bars + 2 * STAGES + 2;
     uint64_t* drain = bars + 2 * STAGES + 4;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTiles + L::kBars);
+    uint64_t* rbar = bars + 2 * STAGES + 5;  // [kEpiWarps][2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5 + 2 * kEpiWarps);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -238,6 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
         for (int b = 0; b < 2; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], kEpiWarps);
         mbar_init(drain, 1);
+        for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -311,29 +307,102 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_drain(drain, 0);
         }
     } else if (warp >= 2) {
-        // ---------------- epilogue
-        const int lg = warp & 3;  // TMEM lane group this warp may access
-        const int half = (warp - 2) >> 2;  // which half of the columns
+        // ---------------- epilogue: TMEM -> registers -> fused epilogue -> swizzled smem -> TMA store
+        const int ew = warp - 2;
+        const int lg = warp & 3;   // TMEM lane group this warp may access (rows 32 lg .. + 31)
+        const int half = ew >> 2;  // which half of the BN columns
+        constexpr int kChunks = BN / 64;  // 32-column chunks per half
+        uint8_t* obuf = sOut + ew * 2 * L::kSub;
+        uint8_t* rsm = sRes + ew * 2 * L::kSub;
+        uint64_t* rb = rbar + 2 * ew;
+        uint32_t n_out = 0;                 // output staging uses so far (buffer = count & 1)
+        uint32_t r_issue = 0, r_use = 0;    // residual sub-tile loads issued / consumed (buffer = i & 1)
         int it = 0;
+        auto issue_res = [&](int row0, int col0) {  // residual sub-tile into the next buffer (lane 0)
+            if (lane == 0) {
+                const uint32_t b = r_issue & 1;
+                fence_async_smem();
+                mbar_expect_tx(&rb[b], uint32_t(L::kSub));
+                tma_load_2d(rsm + b * L::kSub, &tmR, &rb[b], col0, row0);
+            }
+            ++r_issue;
+        };
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
             const int ab = it & 1;
             const uint32_t ap = (it >> 1) & 1;
+            const int mb = tile / n_n, nb = tile - mb * n_n;
+            const int row0 = mb * BM + lg * 32;
+            const int colh = nb * BN + half * (BN / 2);
+            if (EPI == k::kEpiResidual) issue_res(row0, colh);
             if (!mbar_wait(&tfull[ab], ap, abort_flag)) break;
             fence_after();
-            const int mb = tile / n_n, nb = tile - mb * n_n;
-            const int row = mb * BM + lg * 32 + lane;
-            const uint32_t taddr = tmem + (uint32_t(lg * 32) << 16) + uint32_t(ab * BN);
+            const uint32_t taddr = tmem + (uint32_t(lg * 32) << 16) + uint32_t(ab * BN + half * (BN / 2));
+            bool ok = true;
 #pragma unroll 1
-            for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+            for (int c = 0; c < kChunks; ++c) {
+                const int col0 = colh + c * 32;
                 float v[32];
                 tmem_ld32(taddr + uint32_t(c * 32), v);
-                const int n0 = nb * BN + c * 32;
-                if (row < p.M && n0 < p.N) epilogue_store<EPI>(p, row, n0, v);
+                float b[32];
+                if (p.bias && col0 + 32 <= p.N) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) vb::d::Vec<__half, 8>::ldg(p.bias + col0 + 8 * q, b + 8 * q);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) b[i] = (p.bias && col0 + i < p.N) ? __half2float(p.bias[col0 + i]) : 0.f;
+                }
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(v[i] + b[i]);
+                if (EPI == k::kEpiGelu) {
+                    if (p.gelu_tanh) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(gelu(v[i], true));
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(gelu_as(v[i]));
+                    }
+                }
+                if (EPI == k::kEpiResidual) {
+                    if (c + 1 < kChunks) issue_res(row0, col0 + 32);  // prefetch the next chunk's residual
+                    const uint32_t rbi = r_use & 1;
+                    if (!mbar_wait(&rb[rbi], (r_use >> 1) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    ++r_use;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        float r8[8];
+                        vb::d::Vec<__half, 8>::load(
+                            reinterpret_cast<const __half*>(rsm + rbi * L::kSub + sw64(lane, j)), r8);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[8 * j + i] = rnd<__half>(v[8 * j + i] + r8[i]);
+                    }
+                }
+                // stage the fp16 sub-tile (row = lane) and store it with one TMA bulk copy
+                const uint32_t obi = n_out & 1;
+                if (n_out >= 2 && lane == 0) bulk_wait_read1();  // the store that used this buffer read it
+                __syncwarp();
+                uint8_t* ob = obuf + obi * L::kSub;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) vb::d::Vec<__half, 8>::store(reinterpret_cast<__half*>(ob + sw64(lane, j)), v + 8 * j);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tmC, ob, col0, row0);
+                    bulk_commit();
+                }
+                ++n_out;
             }
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[ab]);
+            if (!ok) break;
         }
+        if (EPI == k::kEpiResidual && lane == 0)  // residual loads issued but not consumed (abort path)
+            for (uint32_t i = r_use; i < r_issue; ++i) mbar_drain(&rb[i & 1], (i >> 1) & 1);
+        if (lane == 0) bulk_wait_all();  // every TMA store has finished before the CTA exits
+        __syncwarp();
     }
     fence_before();
     __syncthreads();
@@ -357,15 +426,16 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D fp16 tensor map over a row-major [rows, cols] matrix with leading dimension ld (elements),
-// box [box_rows, 64 columns], 128-byte swizzle, zero fill out of bounds.
-CUtensorMap make_map(const __half* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// box [box_rows, box_cols], zero fill out of bounds (loads) / clipped (stores).
+CUtensorMap make_map(const __half* base, int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols = BK,
+                     CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
     CUtensorMap m;
     const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
     const cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
-    const cuuint32_t box[2] = {cuuint32_t(BK), cuuint32_t(box_rows)};
+    const cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides,
-                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) fail(kCuda, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
     return m;
@@ -383,7 +453,7 @@ int sm_count() {
 
 template <int BN, int STAGES, int EPI>
 void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
-    using L = Layout<BN, STAGES>;
+    using L = Layout<BN, STAGES, EPI>;
     static bool configured = false;  // per instantiation; the attribute is per function
     if (!configured) {
         VB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -392,19 +462,24 @@ void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
     }
     const CUtensorMap ta = make_map(a.A, a.M, a.K, a.lda, BM);
     const CUtensorMap tb = make_map(a.W, a.N, a.K, a.ldw, BN);
+    // 32 x 32 sub-tiles of the output (and residual), 64-byte swizzle: the epilogue's TMA stores / loads
+    const CUtensorMap tc = make_map(a.C, a.M, a.N, a.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    const CUtensorMap tr = EPI == k::kEpiResidual ? make_map(a.R, a.M, a.N, a.ldr, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) : tc;
     Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0};
     const int64_t tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
     const int grid = int(std::min<int64_t>(tiles, sm_count()));
-    gemm_tc_kernel<BN, STAGES, EPI><<<grid, kThreads, L::kSmem, s>>>(ta, tb, p);
+    gemm_tc_kernel<BN, STAGES, EPI><<<grid, kThreads, L::kSmem, s>>>(ta, tb, tc, tr, p);
     VB_LAUNCH();
 }
 
-template <int BN, int STAGES>
+// stage counts: as deep as the 227 KB of shared memory allows next to the epilogue staging
+template <int BN>
 void dispatch_epi(const k::GemmArgs<__half>& a, cudaStream_t s) {
+    constexpr int S = BN == 256 ? 4 : 6, SR = BN == 256 ? 3 : 5;
     switch (a.epi) {
-        case k::kEpiBias: launch<BN, STAGES, k::kEpiBias>(a, s); break;
-        case k::kEpiGelu: launch<BN, STAGES, k::kEpiGelu>(a, s); break;
-        case k::kEpiResidual: launch<BN, STAGES, k::kEpiResidual>(a, s); break;
+        case k::kEpiBias: launch<BN, S, k::kEpiBias>(a, s); break;
+        case k::kEpiGelu: launch<BN, S, k::kEpiGelu>(a, s); break;
+        case k::kEpiResidual: launch<BN, SR, k::kEpiResidual>(a, s); break;
         default: fail(kInvalidArgument, "gemm: unknown epilogue");
     }
 }
@@ -425,8 +500,8 @@ bool supported(const k::GemmArgs<__half>& a) {
 
 void gemm(const k::GemmArgs<__half>& a, cudaStream_t s) {
     if (!supported(a)) fail(kInvalidArgument, "tensor-core gemm: unsupported operand alignment");
-    if (a.N <= 128) dispatch_epi<128, 6>(a, s);
-    else dispatch_epi<256, 4>(a, s);
+    if (a.N <= 128) dispatch_epi<128>(a, s);
+    else dispatch_epi<256>(a, s);
 }
 
 int take_error() {
