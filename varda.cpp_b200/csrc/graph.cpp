@@ -79,4 +79,64 @@ std::vector<EdgeRec> pack_edges(const CsrGraph& g, bool round_fp16) {
     return out;
 }
 
+TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, bool round_fp16) {
+    TilePlan t;
+    t.edges = pack_edges(g, round_fp16);
+    std::vector<int32_t> slot(size_t(std::max<int64_t>(g.n_src, 1)), -1);  // source -> slot in the open tile
+    std::vector<int32_t> open;                                             // distinct sources of the open tile
+    int32_t row0 = -1;
+    auto close = [&](int64_t end_row) {
+        if (row0 < 0) return;
+        std::vector<int32_t> sorted = open;
+        std::sort(sorted.begin(), sorted.end());
+        for (size_t i = 0; i < sorted.size(); ++i) slot[size_t(sorted[i])] = int32_t(i);
+        for (int64_t e = g.row_ptr[size_t(row0)]; e < g.row_ptr[size_t(end_row)]; ++e)
+            t.edges[size_t(e)].src = slot[size_t(g.src[size_t(e)])];
+        t.row0.push_back(row0);
+        t.nrows.push_back(int32_t(end_row - row0));
+        t.src0.push_back(int32_t(t.srcs.size()));
+        t.nsrc.push_back(int32_t(sorted.size()));
+        t.max_nsrc = std::max(t.max_nsrc, int(sorted.size()));
+        t.srcs.insert(t.srcs.end(), sorted.begin(), sorted.end());
+        for (int32_t s : open) slot[size_t(s)] = -1;
+        open.clear();
+        row0 = -1;
+    };
+    std::vector<int32_t> fresh;
+    for (int64_t d = 0; d < g.n_dst; ++d) {
+        const int32_t b = g.row_ptr[size_t(d)], e = g.row_ptr[size_t(d + 1)];
+        // distinct sources of row d not yet in the open tile (slot -2 marks "seen in this row")
+        fresh.clear();
+        for (int32_t i = b; i < e; ++i) {
+            const int32_t s = g.src[size_t(i)];
+            if (slot[size_t(s)] == -1) slot[size_t(s)] = -2, fresh.push_back(s);
+        }
+        int own = 0;  // distinct sources of the row alone
+        {
+            std::vector<int32_t> u(g.src.begin() + b, g.src.begin() + e);
+            std::sort(u.begin(), u.end());
+            own = int(std::unique(u.begin(), u.end()) - u.begin());
+        }
+        for (int32_t s : fresh) slot[size_t(s)] = -1;
+        if (own > max_src) {  // heavy row: the gather kernel takes it
+            close(d);
+            t.heavy.push_back(int32_t(d));
+            continue;
+        }
+        const bool fits = row0 >= 0 && int(open.size() + fresh.size()) <= max_src && d - row0 < max_rows;
+        if (!fits) {
+            close(d);
+            row0 = int32_t(d);
+            fresh.clear();
+            for (int32_t i = b; i < e; ++i) {
+                const int32_t s = g.src[size_t(i)];
+                if (slot[size_t(s)] == -1) slot[size_t(s)] = -2, fresh.push_back(s);
+            }
+        }
+        for (int32_t s : fresh) slot[size_t(s)] = -3, open.push_back(s);  // -3: in the open tile
+    }
+    close(g.n_dst);
+    return t;
+}
+
 }  // namespace vb

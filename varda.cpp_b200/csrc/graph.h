@@ -36,4 +36,18 @@ struct EdgeRec {
 static_assert(sizeof(EdgeRec) == 16, "edge record must be 16 bytes");
 std::vector<EdgeRec> pack_edges(const CsrGraph& g, bool round_fp16);
 
+// Destination tiles for the shared-memory-staged attention: consecutive destination rows grouped
+// while the union of their sources stays within `max_src` and the tile within `max_rows` rows. A row
+// whose own distinct sources exceed `max_src` is "heavy" and left to the gather kernel. Per tile the
+// distinct sources are listed (ascending), and every edge of a tiled row carries, in place of its
+// source id, the slot of that source in its tile's list.
+struct TilePlan {
+    std::vector<int32_t> row0, nrows, src0, nsrc;  // per tile
+    std::vector<int32_t> srcs;                     // distinct sources of every tile, concatenated
+    std::vector<EdgeRec> edges;                    // CSR order; src = slot for tiled rows
+    std::vector<int32_t> heavy;                    // rows left to the gather kernel
+    int max_nsrc = 0;
+};
+TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, bool round_fp16);
+
 }  // namespace vb
