@@ -137,6 +137,19 @@ int vb_attention(int dtype, const int32_t* row_ptr, const void* edges, int64_t d
                  const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, const void* xr, int64_t ldxr,
                  void* out, int64_t ldo, const float* w_e, int C, int heads, int head_dim, void* stream);
 
+/* The shared-memory-staged attention the engine runs in fp16 (no reference counterpart: the
+ * reference has only the gather kernel): vb_tiles_create builds the destination tiles of a CSR graph
+ * (host arrays from vb_build_csr) and uploads them to the current device; vb_attention_tiled runs
+ * rows [dst_lo, dst_lo + n_rows) of it (tiles, then the rows too wide for a tile on the gather kernel;
+ * dst_lo must start a tile, e.g. 0); same arguments and contract as vb_attention, fp16 only. */
+typedef struct vb_tiles vb_tiles;
+int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* attr_csr, int A, int64_t n_src,
+                    int64_t n_dst, int head_dim, vb_tiles** out);
+int vb_attention_tiled(vb_tiles* t, int64_t dst_lo, int64_t n_rows, const void* q, int64_t ldq, const void* k,
+                       const void* v, int64_t ldkv, const void* xr, int64_t ldxr, void* out, int64_t ldo,
+                       const float* w_e, int C, int heads, int head_dim, void* stream);
+void vb_tiles_free(vb_tiles* t);
+
 /* Gemm::linear (src/varda/cuda/gemm.h): y[M, N] = A[M, K] W[N, K]^T (+ bias), then epilogue
  * 0 = none, 1 = GELU (gelu_tanh selects the tanh form), 2 = + residual R[M, N]. engine: 0 = auto
  * (tensor cores for fp16), 1 = CUDA cores, 2 = tensor cores (fp16 only; fails if not applicable). */

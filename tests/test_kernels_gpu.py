@@ -219,3 +219,40 @@ def test_layernorm(C, dt):
     s = rounded(x + r, dt)
     assert np.array_equal(o1.float().cpu().numpy(), s), "residual sum must be the rounded fp32 sum"
     assert oracle.rel_absmax(y.float().cpu().numpy(), ln(s)) <= tol
+
+
+@pytest.mark.parametrize("C,heads,A", [(1024, 16, 3), (256, 8, 3), (512, 4, 2), (256, 32, 1), (768, 12, 3),
+                                       (2048, 8, 3)])
+def test_attention_tiled(C, heads, A):
+    """The shared-memory-staged fp16 attention (tiles + heavy rows on the gather kernel): same graphs
+    and reference as test_attention, plus rows far wider than a tile (degree 300)."""
+    rng = np.random.default_rng(C * 11 + heads + A)
+    hd = C // heads
+    n_src, n_dst, ld = 131, 97, C + 8
+    ei, ea = make_graph(rng, n_src, n_dst, A)
+    wide = np.stack([rng.integers(0, n_src, 300), np.full(300, 50)]).astype(np.int64)  # a heavy row
+    ei = np.concatenate([ei, wide], 1)
+    ea = np.concatenate([ea, rng.normal(size=(300, A)).astype(np.float32)])
+    rp, src, _, attr = vb.build_csr(ei, ea, n_src, n_dst)
+    attr = rounded(attr, vb.FP16)
+    q, k, v, xr = (rounded(rng.normal(size=(n, ld)), vb.FP16) for n in (n_dst, n_src, n_src, n_dst))
+    we = rounded(rng.normal(size=(C, A)) * 0.5, vb.FP16)
+    be = rounded(rng.normal(size=C) * 0.5, vb.FP16)
+    w4 = np.zeros((4, C), np.float32)
+    w4[:A] = we.T
+    w4[3] = be
+    tiles = vb.Tiles(rp, src, attr, n_src, hd)
+    T = torch.float16
+    d_q, d_k, d_v, d_x = dev(q, T), dev(k, T), dev(v, T), dev(xr, T)
+    out = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
+    tiles.attention(0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld, out, C, dev(w4, torch.float32), C, heads, hd)
+    torch.cuda.synchronize()
+    vb.check_device()
+    got = out.float().cpu().numpy()
+    ref = attention_reference(rp, src, attr, q[:, :C].astype(np.float64), k[:, :C].astype(np.float64),
+                              v[:, :C].astype(np.float64), xr[:, :C].astype(np.float64), we, be.astype(np.float64),
+                              heads, hd)
+    err = oracle.rel_absmax(got, ref)
+    assert err <= 2e-3, f"rel_absmax {err:.3e}"
+    zero = np.where(rp[1:] == rp[:-1])[0]
+    assert np.array_equal(got[zero], xr[zero, :C]), "zero in-degree must give x_r exactly"

@@ -117,11 +117,12 @@ __global__ void __launch_bounds__(256, MINB) attention_kernel(AttnArgs<T> a, flo
     constexpr int P = CPL / 2;  // fp32 pairs per lane
     const int lane = threadIdx.x & 31;
     const int64_t gw = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int64_t r = gw / wpd;
-    if (r >= a.n_rows) return;  // warp-uniform
-    const int part = int(gw - r * wpd);
+    const int64_t ri = gw / wpd;
+    if (ri >= a.n_rows) return;  // warp-uniform
+    const int part = int(gw - ri * wpd);
     const int ch = part * 32 * CPL + lane * CPL;
-    const int64_t dst = a.dst_lo + r;
+    const int64_t dst = a.rows ? int64_t(__ldg(a.rows + ri)) : a.dst_lo + ri;
+    const int64_t r = dst - a.dst_lo;  // local q / x_r / out row
     const int beg = __ldg(a.row_ptr + dst), end = __ldg(a.row_ptr + dst + 1);
     const int C = a.C;
 

@@ -5,6 +5,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -189,6 +191,7 @@ int64_t vb_decoder_chunk_rows(const vb_model* m) { return m ? m->m->decoder_chun
 int vb_check_device(void) {
     return guard([&] {
         if (vb::tc::take_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the tensor-core GEMM");
+        if (vb::k::take_attention_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the attention");
     });
 }
 
@@ -279,6 +282,72 @@ int vb_attention(int dtype, const int32_t* row_ptr, const void* edges, int64_t d
         else vb::fail(vb::kInvalidArgument, "dtype");
     });
 }
+
+struct vb_tiles {
+    vb::DeviceBuffer tiles, srcs, tedges, heavy, row_ptr, edges;
+    std::vector<int32_t> row0, heavy_rows;
+};
+
+int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* attr, int A, int64_t n_src,
+                    int64_t n_dst, int head_dim, vb_tiles** out) {
+    return guard([&] {
+        need(row_ptr, "row_ptr"), need(out, "out");
+        vb::CsrGraph g;
+        g.n_src = n_src, g.n_dst = n_dst, g.attr_dim = A;
+        g.row_ptr.assign(row_ptr, row_ptr + n_dst + 1);
+        g.n_edges = g.row_ptr.back();
+        g.src.assign(src, src + g.n_edges);
+        g.attr.assign(attr, attr + g.n_edges * A);
+        vb::TilePlan tp = vb::make_tiles(g, vb::k::tiled_max_src(), 64, vb::k::tiled_max_deg(head_dim), 0, true);
+        auto t = std::make_unique<vb_tiles>();
+        auto up = [](vb::DeviceBuffer& b, const void* h, size_t n) {
+            b.alloc(std::max<size_t>(n, 16));
+            if (n) VB_CUDA(cudaMemcpy(b.get(), h, n, cudaMemcpyHostToDevice));
+        };
+        std::vector<int4> t4(tp.row0.size());
+        for (size_t i = 0; i < t4.size(); ++i) t4[i] = make_int4(tp.row0[i], tp.nrows[i], tp.src0[i], tp.nsrc[i]);
+        up(t->tiles, t4.data(), t4.size() * sizeof(int4));
+        up(t->srcs, tp.srcs.data(), tp.srcs.size() * 4);
+        up(t->tedges, tp.edges.data(), tp.edges.size() * sizeof(vb::EdgeRec));
+        up(t->heavy, tp.heavy.data(), tp.heavy.size() * 4);
+        up(t->row_ptr, g.row_ptr.data(), g.row_ptr.size() * 4);
+        auto packed = vb::pack_edges(g, true);
+        up(t->edges, packed.data(), packed.size() * sizeof(vb::EdgeRec));
+        t->row0 = tp.row0;
+        t->heavy_rows = tp.heavy;
+        *out = t.release();
+    });
+}
+
+int vb_attention_tiled(vb_tiles* t, int64_t lo, int64_t n, const void* q, int64_t ldq, const void* k, const void* v,
+                       int64_t ldkv, const void* xr, int64_t ldxr, void* out, int64_t ldo, const float* w_e, int C,
+                       int heads, int head_dim, void* stream) {
+    return guard([&] {
+        need(t, "tiles");
+        if (!vb::k::tiled_supported(C, head_dim)) vb::fail(vb::kUnsupported, "tiled attention: unsupported layout");
+        const auto t0 = std::lower_bound(t->row0.begin(), t->row0.end(), int32_t(lo));
+        const auto t1 = std::lower_bound(t->row0.begin(), t->row0.end(), int32_t(lo + n));
+        vb::k::TileArgs a;
+        a.tiles = t->tiles.as<int4>(), a.srcs = t->srcs.as<int32_t>(), a.edges = t->tedges.as<vb::EdgeRec>();
+        a.row_ptr = t->row_ptr.as<int32_t>(), a.dst_lo = lo, a.tile0 = int(t0 - t->row0.begin()), a.ntiles = int(t1 - t0);
+        a.q = static_cast<const __half*>(q), a.k = static_cast<const __half*>(k), a.v = static_cast<const __half*>(v);
+        a.xr = static_cast<const __half*>(xr), a.out = static_cast<__half*>(out);
+        a.ldq = ldq, a.ldkv = ldkv, a.ldxr = ldxr, a.ldo = ldo, a.w_e = w_e, a.C = C, a.heads = heads, a.head_dim = head_dim;
+        vb::k::attention_tiled(a, 1.4426950408889634f / std::sqrt(float(head_dim)), S(stream));
+        const auto h0 = std::lower_bound(t->heavy_rows.begin(), t->heavy_rows.end(), int32_t(lo));
+        const auto h1 = std::lower_bound(t->heavy_rows.begin(), t->heavy_rows.end(), int32_t(lo + n));
+        if (h1 > h0) {
+            vb::k::AttnArgs<__half> g;
+            g.row_ptr = t->row_ptr.as<int32_t>(), g.edges = t->edges.as<vb::EdgeRec>(), g.dst_lo = lo;
+            g.rows = t->heavy.as<int32_t>() + (h0 - t->heavy_rows.begin()), g.n_rows = int64_t(h1 - h0);
+            g.q = a.q, g.ldq = ldq, g.k = a.k, g.v = a.v, g.ldkv = ldkv, g.xr = a.xr, g.ldxr = ldxr, g.out = a.out;
+            g.ldo = ldo, g.w_e = w_e, g.C = C, g.heads = heads, g.head_dim = head_dim;
+            vb::k::attention<__half>(g, S(stream));
+        }
+    });
+}
+
+void vb_tiles_free(vb_tiles* t) { delete t; }
 
 int vb_gemm(int dtype, int engine, const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* Y,
             int64_t ldy, const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int epilogue, int gelu_tanh,

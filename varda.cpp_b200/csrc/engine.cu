@@ -11,6 +11,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -65,6 +66,10 @@ struct GraphDev {
     int max_degree = 0;
     const int32_t* rp() const { return row_ptr.as<int32_t>(); }
     const EdgeRec* ed() const { return edges.as<EdgeRec>(); }
+    // destination tiles of the shared-memory-staged attention (fp16), and the heavy rows
+    bool tiled = false;
+    DeviceBuffer tiles, srcs, tedges, heavy;
+    std::vector<int32_t> tile_row0, heavy_rows;  // host copies, to pick a chunk's tiles
 };
 
 template <class T> float round_op(float x) {
@@ -176,7 +181,7 @@ private:
     Norm load_norm(SafeTensorsFile& f, const std::string& name);
     Block<T> load_block(SafeTensorsFile& f, const std::string& pre, bool mapper);
     CsrGraph read_graph(SafeTensorsFile& f, const std::string& g, int64_t n_src, int64_t n_dst);
-    GraphDev upload_graph(const CsrGraph& csr, const std::string& name);
+    GraphDev upload_graph(const CsrGraph& csr, const std::string& name, int64_t chunk_rows);
     DeviceBuffer upload(const void* h, size_t bytes);
     T* act(size_t elems);
     float* actf(size_t elems);
@@ -364,10 +369,22 @@ CsrGraph Engine<T>::read_graph(SafeTensorsFile& f, const std::string& g, int64_t
 }
 
 template <class T>
-GraphDev Engine<T>::upload_graph(const CsrGraph& csr, const std::string& name) {
+GraphDev Engine<T>::upload_graph(const CsrGraph& csr, const std::string& name, int64_t chunk_rows) {
     std::vector<EdgeRec> packed = pack_edges(csr, !std::is_same<T, float>::value);
     GraphDev d;
     d.name = name;
+    if (std::is_same<T, __half>::value && k::tiled_supported(C_, hd_) && env_int("VB_ATT_TILED", 1) != 0) {
+        TilePlan tp = make_tiles(csr, k::tiled_max_src(), 64, k::tiled_max_deg(hd_), chunk_rows, true);
+        std::vector<int4> t4(tp.row0.size());
+        for (size_t i = 0; i < t4.size(); ++i) t4[i] = make_int4(tp.row0[i], tp.nrows[i], tp.src0[i], tp.nsrc[i]);
+        d.tiled = true;
+        d.tiles = upload(t4.data(), std::max<size_t>(1, t4.size()) * sizeof(int4));
+        d.srcs = upload(tp.srcs.data(), std::max<size_t>(1, tp.srcs.size()) * sizeof(int32_t));
+        d.tedges = upload(tp.edges.data(), std::max<size_t>(1, tp.edges.size()) * sizeof(EdgeRec));
+        d.heavy = upload(tp.heavy.data(), std::max<size_t>(1, tp.heavy.size()) * sizeof(int32_t));
+        d.tile_row0 = tp.row0;
+        d.heavy_rows = tp.heavy;
+    }
     d.row_ptr = upload(csr.row_ptr.data(), csr.row_ptr.size() * sizeof(int32_t));
     d.edges = upload(packed.data(), std::max<size_t>(1, packed.size()) * sizeof(EdgeRec));
     d.n_src = csr.n_src;
@@ -512,9 +529,16 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     Hl_ = plan_.h_hi - plan_.h_lo, Gl_ = plan_.g_hi - plan_.g_lo;
     n_eh_ = int64_t(plan_.enc_halo.size()), n_ph_ = int64_t(plan_.proc.halo.size());
     n_dh_ = int64_t(plan_.dec.halo.size()), Gx_ = Gl_ + n_eh_;
-    g_enc_ = upload_graph(plan_.enc, "enc");
-    g_proc_ = upload_graph(plan_.proc_g, "proc");
-    g_dec_ = upload_graph(plan_.dec_g, "dec");
+    {
+        // decoder destination chunk: all own data rows in one chunk unless limited
+        int64_t rows = opts_.dec_chunk_rows > 0 ? opts_.dec_chunk_rows : env_int("VB_DEC_CHUNK_ROWS", Gl_);
+        rows = std::min<int64_t>(std::max<int64_t>(rows, 1), std::max<int64_t>(Gl_, 1));
+        const int64_t nch = (std::max<int64_t>(Gl_, 1) + rows - 1) / rows;
+        dec_rows_ = std::min<int64_t>(int64_t(align_up(size_t((Gl_ + nch - 1) / nch), 128)), std::max<int64_t>(Gl_, 1));
+    }
+    g_enc_ = upload_graph(plan_.enc, "enc", 0);
+    g_proc_ = upload_graph(plan_.proc_g, "proc", 0);
+    g_dec_ = upload_graph(plan_.dec_g, "dec", dec_rows_ < Gl_ ? dec_rows_ : 0);
     for (CsrGraph* g : {&plan_.enc, &plan_.proc_g, &plan_.dec_g}) *g = CsrGraph{};  // host copies not needed
 
     // ---- node attributes: data rows [own | encoder halo], own hidden rows (and the optional grid
@@ -576,12 +600,7 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     // destination chunks (6C + mlp per row). All own data rows in one chunk unless limited.
     const int64_t enc_elems = Gx_ * 3 * C_;
     const int64_t per_row = 6 * int64_t(C_) + mlp_;
-    int64_t rows = opts_.dec_chunk_rows > 0 ? opts_.dec_chunk_rows : env_int("VB_DEC_CHUNK_ROWS", Gl_);
-    rows = std::min<int64_t>(std::max<int64_t>(rows, 1), std::max<int64_t>(Gl_, 1));
-    const int64_t nch = (std::max<int64_t>(Gl_, 1) + rows - 1) / rows;
-    rows = std::min<int64_t>(int64_t(align_up(size_t((Gl_ + nch - 1) / nch), 128)), std::max<int64_t>(Gl_, 1));
-    dec_rows_ = rows;
-    region_ = act(size_t(std::max(enc_elems, rows * per_row)));
+    region_ = act(size_t(std::max(enc_elems, dec_rows_ * per_row)));
 
     // ---- halo exchanges (multi-GPU)
     if (plan_.world > 1) {
@@ -658,6 +677,28 @@ void Engine<T>::attention(const GraphDev& g, const Block<T>& b, int64_t lo, int6
     const double bytes = double(sizeof(T)) * C_ * (3.0 * n + 2.0 * double(g.n_src)) + 16.0 * edges + 4.0 * (n + 1) +
                          16.0 * C_;
     Span sp(this, s, "attention " + g.name, 0, bytes);
+    if constexpr (std::is_same<T, __half>::value) {
+        if (g.tiled) {
+            // tiles of rows [lo, lo + n) (tiles never straddle a decoder chunk), then the heavy rows
+            const auto t0 = std::lower_bound(g.tile_row0.begin(), g.tile_row0.end(), int32_t(lo));
+            const auto t1 = std::lower_bound(g.tile_row0.begin(), g.tile_row0.end(), int32_t(lo + n));
+            k::TileArgs t;
+            t.tiles = g.tiles.template as<int4>(), t.srcs = g.srcs.template as<int32_t>();
+            t.edges = g.tedges.template as<EdgeRec>(), t.row_ptr = g.rp(), t.dst_lo = lo;
+            t.tile0 = int(t0 - g.tile_row0.begin()), t.ntiles = int(t1 - t0);
+            t.q = q, t.k = kk, t.v = v, t.xr = xr, t.out = out, t.ldq = ldq, t.ldkv = ldkv, t.ldxr = ldxr, t.ldo = C_;
+            t.w_e = a.w_e, t.C = C_, t.heads = heads_, t.head_dim = hd_;
+            k::attention_tiled(t, 1.4426950408889634f / std::sqrt(float(hd_)), s);
+            const auto h0 = std::lower_bound(g.heavy_rows.begin(), g.heavy_rows.end(), int32_t(lo));
+            const auto h1 = std::lower_bound(g.heavy_rows.begin(), g.heavy_rows.end(), int32_t(lo + n));
+            if (h1 > h0) {
+                a.rows = g.heavy.template as<int32_t>() + (h0 - g.heavy_rows.begin());
+                a.n_rows = int64_t(h1 - h0);
+                k::attention<T>(a, s);
+            }
+            return;
+        }
+    }
     k::attention<T>(a, s);
 }
 

@@ -79,7 +79,7 @@ std::vector<EdgeRec> pack_edges(const CsrGraph& g, bool round_fp16) {
     return out;
 }
 
-TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, bool round_fp16) {
+TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_deg, int64_t chunk_rows, bool round_fp16) {
     TilePlan t;
     t.edges = pack_edges(g, round_fp16);
     std::vector<int32_t> slot(size_t(std::max<int64_t>(g.n_src, 1)), -1);  // source -> slot in the open tile
@@ -105,6 +105,7 @@ TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, bool round_fp1
     std::vector<int32_t> fresh;
     for (int64_t d = 0; d < g.n_dst; ++d) {
         const int32_t b = g.row_ptr[size_t(d)], e = g.row_ptr[size_t(d + 1)];
+        if (chunk_rows > 0 && d % chunk_rows == 0) close(d);
         // distinct sources of row d not yet in the open tile (slot -2 marks "seen in this row")
         fresh.clear();
         for (int32_t i = b; i < e; ++i) {
@@ -118,7 +119,7 @@ TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, bool round_fp1
             own = int(std::unique(u.begin(), u.end()) - u.begin());
         }
         for (int32_t s : fresh) slot[size_t(s)] = -1;
-        if (own > max_src) {  // heavy row: the gather kernel takes it
+        if (own > max_src || e - b > max_deg) {  // heavy row: the gather kernel takes it
             close(d);
             t.heavy.push_back(int32_t(d));
             continue;

@@ -38,7 +38,9 @@ std::vector<EdgeRec> pack_edges(const CsrGraph& g, bool round_fp16);
 
 // Destination tiles for the shared-memory-staged attention: consecutive destination rows grouped
 // while the union of their sources stays within `max_src` and the tile within `max_rows` rows. A row
-// whose own distinct sources exceed `max_src` is "heavy" and left to the gather kernel. Per tile the
+// whose own distinct sources exceed `max_src`, or whose degree exceeds `max_deg`, is "heavy" and left to
+// the gather kernel; tiles never straddle a multiple of `chunk_rows` (the decoder's destination
+// chunks; 0: no chunking). Per tile the
 // distinct sources are listed (ascending), and every edge of a tiled row carries, in place of its
 // source id, the slot of that source in its tile's list.
 struct TilePlan {
@@ -48,6 +50,6 @@ struct TilePlan {
     std::vector<int32_t> heavy;                    // rows left to the gather kernel
     int max_nsrc = 0;
 };
-TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, bool round_fp16);
+TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_deg, int64_t chunk_rows, bool round_fp16);
 
 }  // namespace vb

@@ -81,12 +81,38 @@ template <class T> struct AttnArgs {
     int64_t ldo = 0;
     const float* w_e = nullptr;  // [4, C]: edge Linear weight columns (zero padded to 3), then its bias
     int C = 0, heads = 0, head_dim = 0;
+    // optional: the destinations as a list of graph rows (n_rows of them, each in
+    // [dst_lo, dst_lo + rows of q/out)) instead of the range [dst_lo, dst_lo + n_rows)
+    const int32_t* rows = nullptr;
 };
 // out[i] = T(T(att_i) + xr[i]); att_i = sum_j softmax_j(<q_i, k_j + e_ij> / sqrt(d)) (v_j + e_ij) per
 // head with e_ij = W_e a_ij + b_e folded in; fp32 online softmax; zero in-degree -> att = 0.
 // Semantics of the reference's cpu::graph_attention (cpu/kernels.cpp:98-158) plus the `+ x_r` of
 // backend_cpu.cpp:333-340 and the fp16 roundings of the autocast reference.
 template <class T> void attention(const AttnArgs<T>& a, cudaStream_t s);
+
+// Shared-memory-staged attention (fp16) over destination tiles (graph.h TilePlan): same contract per
+// destination row, two-pass softmax. Tiles [tile0, tile0 + ntiles) of the plan; q/x_r/out row of graph
+// row d is d - dst_lo.
+struct TileArgs {
+    const int4* tiles = nullptr;    // per tile {row0, nrows, src0, nsrc}
+    const int32_t* srcs = nullptr;  // distinct sources per tile
+    const EdgeRec* edges = nullptr;  // CSR-order records, source = slot in the tile
+    const int32_t* row_ptr = nullptr;
+    int64_t dst_lo = 0;
+    int tile0 = 0, ntiles = 0;
+    const __half *q = nullptr, *k = nullptr, *v = nullptr, *xr = nullptr;
+    __half* out = nullptr;
+    int64_t ldq = 0, ldkv = 0, ldxr = 0, ldo = 0;
+    const float* w_e = nullptr;
+    int C = 0, heads = 0, head_dim = 0;
+};
+void attention_tiled(const TileArgs& a, float scale_log2, cudaStream_t s);
+bool tiled_supported(int C, int head_dim);
+int tiled_max_src();
+int tiled_max_deg(int head_dim);
+// Synchronises; reads and clears the flag a timed-out wait of the tiled attention sets.
+int take_attention_error();
 
 // ------------------------------------------------------------------ GEMM (Linear layers)
 enum Epilogue : int {

@@ -1,7 +1,7 @@
 """Kernel microbenchmarks through the C ABI (CUDA events on the launching stream, after warm-up).
 
     python -m varda_b200.kbench gemm --M 189809 --N 4096 --K 1024 --epi 1 [--engine 2] [--iters 20]
-    python -m varda_b200.kbench attention [--config c2] [--dtype fp16] [--iters 20]
+    python -m varda_b200.kbench attention [--config c2] [--dtype fp16] [--impl tiled|gather] [--iters 20]
 
 `attention --config c2` is BASELINE config C2, the isolated processor graph-attention block: the
 hidden graph of C1 (189,809 nodes, ~2.6M directed multi-scale edges in CSR by destination), C=1024,
@@ -89,15 +89,20 @@ def attention(a):
     out = torch.empty(H, C, device="cuda", dtype=T)
     s = torch.cuda.current_stream().cuda_stream
     q, k, v, xr = (qkvs[:, i * C:] for i in range(4))
-    fn = lambda: vb.attention(dt, d_rp, d_ed, 0, H, q, 4 * C, k, v, 4 * C, xr, 4 * C, out, C, w4, C, heads,  # noqa
-                              C // heads, stream=s)
+    if a.impl == "tiled":
+        tiles = vb.Tiles(rp, src, at, H, C // heads)
+        fn = lambda: tiles.attention(0, H, q, 4 * C, k, v, 4 * C, xr, 4 * C, out, C, w4, C, heads, C // heads,  # noqa
+                                     stream=s)
+    else:
+        fn = lambda: vb.attention(dt, d_rp, d_ed, 0, H, q, 4 * C, k, v, 4 * C, xr, 4 * C, out, C, w4, C, heads,  # noqa
+                                  C // heads, stream=s)
     ms = time_launches(fn, a.iters, a.warmup)
     E = len(src)
     es = 2 if dt == vb.FP16 else 4
     byt = es * C * (3.0 * H + 2.0 * H) + 16.0 * E + 4.0 * (H + 1) + 16.0 * C
     gbs = byt / (ms * 1e-3) / 1e9
     pk = _peaks()
-    print(json.dumps({"kernel": "attention", "config": "c2", "dtype": a.dtype, "H": H, "E": E, "ms": round(ms, 4),
+    print(json.dumps({"kernel": "attention", "impl": a.impl, "config": "c2", "dtype": a.dtype, "H": H, "E": E, "ms": round(ms, 4),
                       "bytes": byt, "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4),
                       "gathered_bytes": 2.0 * E * C * es}))
 
@@ -116,6 +121,7 @@ def main():
     t = sub.add_parser("attention")
     t.add_argument("--config", default="c2")
     t.add_argument("--dtype", default="fp16")
+    t.add_argument("--impl", default="tiled", choices=["tiled", "gather"])
     t.add_argument("--iters", type=int, default=20)
     t.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
