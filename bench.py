@@ -1,7 +1,7 @@
 """Benchmark: ms per fp16 predict_step at the Varda shape, plus edge-attention
 HBM GB/s, on N B200s of one node.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c0]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c0|c3|c4]
 
 Prints one JSON line (rank 0). `value` is the device-resident time of one predict_step (the model's
 own input/output buffers, CUDA-graph replay, CUDA events on the model's stream, max over ranks);
@@ -10,6 +10,11 @@ D2H of y inside the timed region). `roofline` describes the dominant kernel clas
 `edge_attention` the processor-block attention, both from one eager pass with a CUDA event pair
 around every launch (vb_profile_forward). `cpu_baseline` is the reference's own CPU fp32 backend
 (oracle/_ref/ref_dump, built from the reference's sources) timed on this host on a bounded sample.
+
+--workload c4 is the 24-step autoregressive rollout of C1: K rollout steps through
+vb_rollout (CUDA graph per step, forcings replayed from the host, every step's output copied back to
+pinned host memory), `value` = device ms per rollout step, `e2e` = wall time of the whole rollout call
+per step.
 
 --impl reference times that reference CPU backend alone (rank 0; other ranks exit 0).
 Inputs and activations (tens of GB) are far larger than the 126 MB L2, so no L2 flush is needed.
@@ -145,10 +150,9 @@ class Clocks:
 
 
 # ------------------------------------------------------------------ ours
-def run_ours(args, rank, world, local_rank):
+def load_model(args, rank, world, local_rank):
     import torch
     import varda_b200 as vb
-    from varda_b200 import safetensors as st
 
     torch.cuda.set_device(local_rank)
     dist = None
@@ -169,6 +173,15 @@ def run_ours(args, rank, world, local_rank):
     else:
         m = vb.Model.load(mp, precision=vb.FP16, cuda_device=local_rank)
     load_s = time.time() - t0
+    return m, mp, xp, dist, load_s
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import varda_b200 as vb
+    from varda_b200 import safetensors as st
+
+    m, mp, xp, dist, load_s = load_model(args, rank, world, local_rank)
     x = np.array(st.read(xp)[0]["in.x"])
     stream = torch.cuda.ExternalStream(m.stream(), device=f"cuda:{local_rank}")
     xh = torch.from_numpy(x).pin_memory().numpy()
@@ -222,6 +235,54 @@ def run_ours(args, rank, world, local_rank):
                 launches=launches_per_step + 2, dist=dist, n_launch_timed=vb.launch_count() - n_launch0)
 
 
+def run_rollout(args, rank, world, local_rank):
+    """C4: K steps of the device rollout of C1 (vb_rollout), after a W-step warm-up rollout."""
+    import torch
+    import varda_b200 as vb
+    from varda_b200 import safetensors as st, synth
+
+    m, mp, xp, dist, load_s = load_model(args, rank, world, local_rank)
+    x = torch.from_numpy(np.array(st.read(xp)[0]["in.x"])).pin_memory().numpy()
+    cfg = json.loads(st.read(mp)[1]["config"])
+    F = len(cfg["forcings"]["dynamic_input_index"])
+    n = args.steps
+    t0 = time.time()
+    f = synth.replay_forcings(max(n, args.warmup), m.G, F, cfg["forcings"]["timestep_hours"], seed=3)
+    f = torch.from_numpy(f).pin_memory().numpy()
+    log(f"bench: forcings {f.shape} in {time.time() - t0:.1f} s")
+    sums = []
+
+    def on_step(s, rows):  # a light consumer of every step's output rows on the host
+        sums.append(float(rows[::997].sum()))
+
+    m.rollout(x, args.warmup, f[:max(args.warmup - 1, 0)], keep=False, on_step=on_step)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    n_launch0 = vb.launch_count()
+    clk = Clocks(local_rank)
+    sums.clear()
+    t0 = time.perf_counter()
+    _, step_ms = m.rollout(x, n, f[:n - 1], keep=False, on_step=on_step)
+    wall = time.perf_counter() - t0
+    clocks = clk.stop()
+    assert len(sums) == n and all(np.isfinite(sums)), "rollout outputs not finite"
+    ms = float(np.mean(step_ms))
+    e2e_ms = wall * 1000 / n
+    prof = m.profile()
+    vb.check_device()
+    if dist:
+        t = torch.tensor([ms, e2e_ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    h2d = (m.device_input_numel * 4 + (n - 1) * (m.device_input_numel // (m.T_in * m.V_in)) * F * 4) / n
+    d2h = m.device_output_numel * 4
+    return dict(m=m, ms=ms, e2e_ms=e2e_ms, clocks=clocks, prof=prof, load_s=load_s, h2d=h2d, d2h=d2h,
+                launches=len(prof) + 2 + (1 if n > 1 else 0) + (1 if world > 1 else 0), dist=dist,
+                step_ms=[round(float(v), 3) for v in step_ms], wall_s=wall,
+                n_launch_timed=vb.launch_count() - n_launch0)
+
+
 def summarise(prof, pk, src):
     by = {}
     for r in prof:
@@ -267,7 +328,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c1", choices=["c1", "c0", "c3"])
+    ap.add_argument("--workload", default="c1", choices=["c1", "c0", "c3", "c4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
@@ -284,6 +345,10 @@ def main():
         config["workload"] = "C0: icosphere r5/r4 model, C=128"
     pk, src = peaks()
     metric = "ms/predict_step fp16 at Varda shape"
+    if args.workload == "c4":
+        config["workload"] = (f"C4: {args.steps}-step autoregressive rollout of C1 in fp16 (CUDA graph per step, "
+                              "synthetic sin/cos forcings replayed from the host, outputs streamed back)")
+        metric = "ms/rollout step fp16 at Varda shape"
 
     if args.impl == "reference":
         if rank != 0:
@@ -303,10 +368,15 @@ def main():
         print(json.dumps(line), flush=True)
         return
 
-    r = run_ours(args, rank, world, local_rank)
+    if args.workload == "c4":
+        args.workload = "c1"  # the rollout runs the C1 model
+        r = run_rollout(args, rank, world, local_rank)
+        args.workload = "c4"
+    else:
+        r = run_ours(args, rank, world, local_rank)
     roof, edge, shares, prof_total = summarise(r["prof"], pk, src)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "c1":
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("c1", "c4"):
         try:
             times, threads, f = reference_cpu(2, 1)
             v = statistics.median(times) * f * 1000
@@ -325,6 +395,8 @@ def main():
                         "d2h_bytes_per_step": int(r["d2h"])},
                 "gpu_launches": int(r["launches"] * args.steps),
                 "kernel_shares": shares, "profiled_forward_ms": round(prof_total, 3), "load_s": round(r["load_s"], 1)}
+        if "step_ms" in r:
+            line["rollout"] = {"step_ms": r["step_ms"], "wall_s": round(r["wall_s"], 3)}
         print(json.dumps(line), flush=True)
     if r["dist"]:
         r["dist"].barrier()

@@ -72,6 +72,23 @@ void vb_free(vb_model* m);
  * passes the full x and writes only its own data rows of y (vb_data_range). */
 int vb_predict_step(vb_model* m, const float* x, float* y, vb_hook_fn hook, void* user);
 
+/* Autoregressive rollout with replayed forcings: varda::cuda::DeviceRollout::run
+ * (src/varda/cuda/rollout_cuda.h:40-70, rollout_cuda.cu:160-234) with RolloutRequest::replay_forcings
+ * (src/varda/rollout.h:75-85); the reference's host loop Rollout::run (rollout.cpp:116-155) has the same
+ * results. x0 (1, T_in, G, V_in) physical; forcings (n_steps - 1, G, F) in the config's
+ * `forcings.dynamic` order (forcing s is written into the window after step s; may be NULL when
+ * n_steps == 1 or F == 0); y (n_steps, G, V_out) physical receives every step's output (this rank's
+ * rows on a sharded model; may be NULL); on_step (may be NULL) gets each step's rows
+ * (rows, V_out) as soon as they are on the host, one step behind the GPU, valid during the call;
+ * step_ms (may be NULL) [n_steps] the GPU time of each step. constants_oldest: 0 = the newest slot
+ * keeps its constant inputs (ConstantSource::Newest), 1 = they come from the oldest slot
+ * (ConstantSource::Oldest, rollout.h:38-41). All ranks of a sharded model call it together with the
+ * same n_steps. Fails with VB_ERR_UNSUPPORTED when the config has no `forcings` section or more
+ * than one output step, VB_ERR_FORMAT when the index sets do not partition the inputs. */
+typedef void (*vb_step_fn)(int step, const float* y, int64_t rows, void* user);
+int vb_rollout(vb_model* m, const float* x0, int n_steps, const float* forcings, float* y, int constants_oldest,
+               vb_step_fn on_step, void* user, float* step_ms);
+
 /* sizes: [T_in, G, V_in, T_out, V_out, H, C, n_proc]; input_numel = T_in G V_in, output_numel =
  * T_out G V_out (cuda/cuda_backend.h:34-35). */
 int vb_sizes(const vb_model* m, int64_t out8[8]);
@@ -126,6 +143,14 @@ int64_t vb_shard_plan(const char* path, int world, int rank, char* buf, size_t l
  * float [E, A] -> row_ptr [n_dst + 1], src [E], edge_id [E], attr_csr [E, A]. Bit-exact. */
 int vb_build_csr(const int64_t* edge_index, int64_t E, const float* edge_attr, int A, int64_t n_src, int64_t n_dst,
                  int32_t* row_ptr, int32_t* src, int32_t* edge_id, float* attr_csr);
+
+/* The rollout's state update on the device (cuda::rollout_update, src/varda/cuda/rollout_cuda.h:34-38;
+ * StateUpdate::apply, rollout.cpp:70-92): window (T, rows, V_in) fp32 in place; kind [V_in] int8 =
+ * 0 kept, 1 prognostic <- y[src], 2 forcing <- f[src], 3 kept from the oldest slot; y rows [0, n_own)
+ * from y_own, the rest from y_halo. Device pointers. */
+int vb_rollout_update(float* window, int T, int64_t rows, int V_in, const float* y_own, const float* y_halo,
+                      int64_t n_own, int V_out, const float* f, int F, const int8_t* kind, const int* src,
+                      void* stream);
 
 /* One 16-byte record per CSR slot {a0, a1, a2, src} as the attention kernel reads it (the reference's
  * Engine::load_graph packing, backend_cuda.cu:323-348); host memory. round_fp16 rounds attributes. */

@@ -255,6 +255,81 @@ class OracleModel:
         return y
 
 
+class StateUpdate:
+    """The reference's rollout state update, restated (src/varda/rollout.cpp:28-92, rollout.h:44-64).
+
+    kind[c]: 0 constant (kept), 1 prognostic (from output src[c]), 2 dynamic forcing (column src[c]).
+    oldest=False: constants keep the newest slot's own value (ConstantSource::Newest, the default);
+    True: they take the oldest slot's old value (ConstantSource::Oldest)."""
+
+    def __init__(self, T, G, V_in, V_out, prog_in, prog_out, dyn_in, const_in, oldest=False):
+        def require(ok, what):
+            if not ok:
+                raise ValueError("rollout: " + what)
+        require(T >= 1 and G >= 0 and V_in > 0 and V_out > 0, "bad sizes")
+        require(len(prog_in) == len(prog_out), "residual_input and residual_output differ in length")
+        self.T, self.G, self.V_in, self.V_out, self.F, self.oldest = T, G, V_in, V_out, len(dyn_in), bool(oldest)
+        self.kind = np.full(V_in, -1, np.int8)
+        self.src = np.full(V_in, -1, np.int32)
+
+        def claim(c, k, s, what):
+            require(0 <= c < V_in, f"{what} index {c} out of range")
+            require(self.kind[c] < 0, f"input channel {c} is listed twice ({what})")
+            self.kind[c], self.src[c] = k, s
+        for i, o in zip(prog_in, prog_out):
+            require(0 <= o < V_out, "residual_output index out of range")
+            claim(i, 1, o, "prognostic")
+        for k, c in enumerate(dyn_in):
+            claim(c, 2, k, "dynamic forcing")
+        for c in const_in:
+            claim(c, 0, -1, "constant forcing")
+        for c in range(V_in):
+            require(self.kind[c] >= 0, f"input channel {c} is neither prognostic, dynamic forcing nor constant")
+
+    @staticmethod
+    def from_config(cfg, oldest=False):
+        """StateUpdate::from_config (rollout.cpp:62-68)."""
+        if "forcings" not in cfg:
+            raise ValueError("rollout: the model config has no `forcings` section")
+        d, ix, f = cfg["dims"], cfg["indices"], cfg["forcings"]
+        return StateUpdate(d["n_input_steps"], d["n_data_nodes"], d["n_input_vars"], d["n_output_vars"],
+                           ix["residual_input"], ix["residual_output"], f["dynamic_input_index"],
+                           f["constant_input_index"], oldest)
+
+    def apply(self, w, y, f):
+        """StateUpdate::apply (rollout.cpp:70-92) on w (T, G, V_in) in place; y (G, V_out); f (G, F).
+        Slot t <- slot t+1 in ascending order, then the newest slot's prognostic and forcing channels;
+        constants stay (newest) or take the old oldest slot's value (oldest). Pure copies."""
+        if self.F and f is None:
+            raise ValueError("rollout: forcings missing")
+        oldest = w[0].copy()
+        for t in range(self.T - 1):
+            w[t] = w[t + 1]
+        nw = w[self.T - 1]
+        p = np.nonzero(self.kind == 1)[0]
+        nw[:, p] = y[:, self.src[p]]
+        k = np.nonzero(self.kind == 2)[0]
+        if len(k):
+            nw[:, k] = f[:, self.src[k]]
+        if self.oldest:
+            c = np.nonzero(self.kind == 0)[0]
+            nw[:, c] = oldest[:, c]
+
+
+def rollout(model, x0, n_steps, forcings=None, oldest=False):
+    """Rollout::run (rollout.cpp:116-155) with replayed forcings (n_steps - 1, G, F): predict, then
+    (unless last) the update with forcing s. `model` has predict_step(x) -> (1, 1, 1, G, V_out).
+    Returns y (n_steps, G, V_out)."""
+    u = StateUpdate.from_config(model.cfg, oldest)
+    w = np.array(x0, np.float32, copy=True).reshape(u.T, u.G, u.V_in)
+    ys = np.empty((n_steps, u.G, u.V_out), np.float32)
+    for s in range(n_steps):
+        ys[s] = np.asarray(model.predict_step(w[None])).reshape(u.G, u.V_out)
+        if s + 1 < n_steps:
+            u.apply(w, ys[s], None if forcings is None else forcings[s])
+    return ys
+
+
 def rel_absmax(a, r):
     """The reference's parity metric (apps/common.h:109-127): max|a-r| / max|r| in float64;
     NaN in a -> inf."""

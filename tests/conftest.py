@@ -40,15 +40,21 @@ def seeded_model(model_dir):
     def get(name):
         if name not in _MODELS:
             mp, xp = synth.generate(name, model_dir)
-            g = os.path.join(GOLDEN, f"{name}.golden.npz")
-            if os.path.exists(g):
-                z = np.load(g)
-                assert synth.sha256_file(mp) == bytes(z["__model_sha256__"]).decode(), f"{name}: model drifted"
-                assert synth.sha256_file(xp) == bytes(z["__input_sha256__"]).decode(), f"{name}: input drifted"
+            for kind in ("golden", "rollout"):
+                g = os.path.join(GOLDEN, f"{name}.{kind}.npz")
+                if os.path.exists(g):
+                    z = np.load(g)
+                    assert synth.sha256_file(mp) == bytes(z["__model_sha256__"]).decode(), f"{name}: model drifted"
+                    assert synth.sha256_file(xp) == bytes(z["__input_sha256__"]).decode(), f"{name}: input drifted"
             _MODELS[name] = (mp, xp)
         return _MODELS[name]
 
     return get
+
+
+def rollout_golden(name):
+    z = np.load(os.path.join(GOLDEN, f"{name}.rollout.npz"))
+    return {k: z[k] for k in z.files if not k.startswith("__")}
 
 
 def golden(name):

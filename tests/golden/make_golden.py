@@ -8,6 +8,9 @@ sources and oracle/_ref built; the fixtures then travel, the reference does not)
 2. <name>.golden.npz for this repo's seeded models (varda_b200.synth: c0 and the t* parity models):
    contract activations computed by the UNMODIFIED reference CPU backend (oracle/_ref/ref_dump,
    compiled from the reference's sources), the model file's sha256, and the input's sha256.
+3. <name>.rollout.npz for the rollout variants of the parity models (t*r: a `forcings` section):
+   ROLLOUT_STEPS steps of the reference's host rollout (varda::Rollout::run on the CPU backend,
+   oracle/_ref/ref_rollout) with replayed synthetic forcings, both constant sources.
 
     python tests/golden/make_golden.py [--reference /root/reference] [--only NAME ...]
 """
@@ -35,6 +38,8 @@ MODELS = ["c0", "t128", "t256", "t512", "t768", "t1024", "t384i", "t2048"]
 # keys kept in the fixtures (the small ones; [H, C] / [G, C] keys only for small models)
 KEEP_ALWAYS = ["dec.out", "out.pre_bound", "out.norm", "out.y"]
 KEEP_SMALL = ["enc.out", "latent"]
+ROLLOUT_MODELS = ["t256r", "t128r"]
+ROLLOUT_STEPS = 4
 
 
 def pin_synthetic(ref_root, work):
@@ -77,6 +82,34 @@ def ref_golden(name, work, ref_dump):
     return {k: float(v) for k, v in worst.items()}
 
 
+def rollout_golden(name, work, ref_rollout):
+    mp, xp = synth.generate(name, work)
+    x = st.read(xp)[0]["in.x"]
+    om = oracle.OracleModel(mp)
+    F = len(om.cfg["forcings"]["dynamic_input_index"])
+    f = synth.replay_forcings(ROLLOUT_STEPS, om.G, F, om.cfg["forcings"]["timestep_hours"], seed=7)
+    rp = os.path.join(work, f"{name}.rollout_in.safetensors")
+    st.write(rp, {"in.x": x, "forcings": f}, {"producer": "tests/golden/make_golden.py"})
+    keep, worst = {}, {}
+    for oldest in (False, True):
+        out = os.path.join(work, f"{name}.{int(oldest)}.rollout.safetensors")
+        cmd = [ref_rollout, "--model", mp, "--input", rp, "--steps", str(ROLLOUT_STEPS), "--threads", "8",
+               "--out", out] + (["--oldest"] if oldest else [])
+        r = subprocess.run(cmd, capture_output=True, text=True, check=True)
+        y = np.array(st.read(out)[0]["y"], np.float32)
+        tag = "oldest" if oldest else "newest"
+        keep[f"y_{tag}"] = y
+        yo = oracle.rollout(om, x, ROLLOUT_STEPS, f, oldest)
+        worst[f"rollout.{tag}"] = max(oracle.rel_absmax(yo[s], y[s]) for s in range(ROLLOUT_STEPS))
+        print(f"{name} rollout ({tag}): reference {r.stdout.strip()} ; oracle vs reference "
+              f"worst {worst[f'rollout.{tag}']:.3e}")
+    keep["forcings"] = f
+    keep["__model_sha256__"] = np.frombuffer(synth.sha256_file(mp).encode(), np.uint8)
+    keep["__input_sha256__"] = np.frombuffer(synth.sha256_file(xp).encode(), np.uint8)
+    np.savez_compressed(os.path.join(HERE, f"{name}.rollout.npz"), **keep)
+    return worst
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -93,8 +126,11 @@ def main():
             pin = pin_synthetic(a.reference, work)
             with open(os.path.join(HERE, "synthetic_pin.json"), "w") as f:
                 json.dump(pin, f, indent=1, sort_keys=True)
-        for name in a.only or MODELS:
-            summary[name] = ref_golden(name, work, ref_dump)
+        for name in a.only or MODELS + ROLLOUT_MODELS:
+            if name in ROLLOUT_MODELS:
+                summary[name] = rollout_golden(name, work, os.path.join(REPO, "oracle", "_ref", "ref_rollout"))
+            else:
+                summary[name] = ref_golden(name, work, ref_dump)
         with open(summary_path, "w") as f:
             json.dump(summary, f, indent=1, sort_keys=True)
 

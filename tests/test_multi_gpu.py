@@ -70,3 +70,65 @@ def test_sharded_equals_single_gpu(name, dtype, seeded_model, tmp_path):
         for k in ("y0", "y1", "y2"):
             assert np.array_equal(z[k], y1[:, :, :, lo:hi]), f"rank {r} {k} differs from one GPU"
     assert covered == y1.shape[3]
+
+
+def _rollout_worker(rank, world, mp, xp, fp, dtype, uid_path, out_dir):
+    import time
+    import varda_b200 as vb
+    from varda_b200 import safetensors as st
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    if rank == 0:
+        with open(uid_path + ".tmp", "wb") as f:
+            f.write(vb.nccl_unique_id())
+        os.replace(uid_path + ".tmp", uid_path)
+    t0 = time.time()
+    while not os.path.exists(uid_path):
+        if time.time() - t0 > 60:
+            raise TimeoutError("no NCCL id")
+        time.sleep(0.05)
+    m = vb.Model.load_sharded(mp, rank, world, open(uid_path, "rb").read(), precision=dtype, cuda_device=rank)
+    x = np.array(st.read(xp)[0]["in.x"])
+    f = np.load(fp)
+    y, _ = m.rollout(x, f.shape[0] + 1, f)
+    vb.check_device()
+    np.savez(os.path.join(out_dir, f"ro{rank}.npz"), y=y[:, m.data_lo:m.data_hi], lo=m.data_lo, hi=m.data_hi)
+    m.free()
+
+
+def _rollout_single(mp, xp, fp, dtype, out):
+    import varda_b200 as vb
+    from varda_b200 import safetensors as st
+    torch.cuda.set_device(0)
+    m = vb.Model.load(mp, precision=dtype)
+    f = np.load(fp)
+    y, _ = m.rollout(np.array(st.read(xp)[0]["in.x"]), f.shape[0] + 1, f)
+    np.save(out, y)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_sharded_rollout_equals_single_gpu(dtype, seeded_model, tmp_path):
+    """The rollout's per-step exchange of the encoder-halo rows' outputs: every rank's rows of every
+    step bitwise equal to the single-GPU rollout."""
+    import torch.multiprocessing as tmp
+    from conftest import rollout_golden
+    mp, xp = seeded_model("t256r")
+    fp = str(tmp_path / "f.npy")
+    np.save(fp, rollout_golden("t256r")["forcings"])
+    world = min(torch.cuda.device_count(), 4)
+    ctx = tmp.get_context("spawn")
+    p = ctx.Process(target=_rollout_single, args=(mp, xp, fp, dtype, str(tmp_path / "single.npy")))
+    p.start()
+    p.join(300)
+    assert p.exitcode == 0
+    y1 = np.load(tmp_path / "single.npy")
+    tmp.start_processes(_rollout_worker, args=(world, mp, xp, fp, dtype, str(tmp_path / "uid"), str(tmp_path)),
+                        nprocs=world, join=True, start_method="spawn")
+    covered = 0
+    for r in range(world):
+        z = np.load(tmp_path / f"ro{r}.npz")
+        lo, hi = int(z["lo"]), int(z["hi"])
+        covered += hi - lo
+        assert np.array_equal(z["y"], y1[:, lo:hi]), f"rank {r} differs from one GPU"
+    assert covered == y1.shape[1]

@@ -117,6 +117,15 @@ int vb_predict_step(vb_model* m, const float* x, float* y, vb_hook_fn hook, void
     });
 }
 
+int vb_rollout(vb_model* m, const float* x0, int n_steps, const float* forcings, float* y, int constants_oldest,
+               vb_step_fn on_step, void* user, float* step_ms) {
+    return guard([&] {
+        need(m, "model"), need(x0, "x0");
+        m->m->rollout(x0, n_steps, forcings, y, constants_oldest != 0, on_step, user, step_ms);
+        if (vb::tc::take_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the tensor-core GEMM");
+    });
+}
+
 int vb_sizes(const vb_model* m, int64_t out8[8]) {
     return guard([&] {
         need(m, "model"), need(out8, "out");
@@ -261,6 +270,17 @@ int vb_pack_edges(const int32_t* src, const float* attr, int A, int64_t E, int r
         g.attr.assign(attr, attr + E * A);
         auto p = vb::pack_edges(g, round_fp16 != 0);
         std::memcpy(out16, p.data(), p.size() * sizeof(vb::EdgeRec));
+    });
+}
+
+int vb_rollout_update(float* window, int T, int64_t rows, int V_in, const float* y_own, const float* y_halo,
+                      int64_t n_own, int V_out, const float* f, int F, const int8_t* kind, const int* src,
+                      void* stream) {
+    return guard([&] {
+        need(window, "window"), need(kind, "kind"), need(src, "src");
+        if (T < 1 || rows < 0 || V_in < 1 || V_out < 1 || F < 0 || n_own < 0 || n_own > rows)
+            vb::fail(vb::kInvalidArgument, "rollout_update: bad sizes");
+        vb::k::rollout_update(window, T, rows, V_in, y_own, y_halo, n_own, V_out, f, F, kind, src, S(stream));
     });
 }
 

@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <string>
 #include <type_traits>
@@ -148,6 +149,8 @@ public:
     }
     void data_range(int64_t* lo, int64_t* hi) const override { *lo = plan_.g_lo, *hi = plan_.g_hi; }
     std::string profile_forward() override;
+    void rollout(const float* x0, int n_steps, const float* forcings, float* y, bool constants_oldest, StepFn cb,
+                 void* user, float* step_ms) override;
 
 private:
     struct Hook;
@@ -191,7 +194,9 @@ private:
     void attention(const GraphDev& g, const Block<T>& b, int64_t lo, int64_t n, const T* q, int64_t ldq, const T* kk,
                    const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out, cudaStream_t s);
     void forward(const float* xn, float* yn, cudaStream_t s, Hook* hk);
+    cudaGraphExec_t capture(const std::function<void(cudaStream_t)>& body, cudaStream_t s);
     bool capture_graph(cudaStream_t s);
+    void upload_input(const float* x, cudaStream_t s);
 
     Config cfg_;
     Options opts_;
@@ -240,7 +245,27 @@ private:
     Xchg xp_, xd_;
     T *xsend_ = nullptr, *xrecv_ = nullptr;
     float* x_halo_host_ = nullptr;  // pinned staging of the encoder's halo input rows
-    void setup_exchange(Xchg& x, const HaloPlan& h);
+    // send lists in local row ids (global id - lo); offsets and counts in elements of `row` per row
+    void setup_exchange(Xchg& x, const HaloPlan& h, int64_t lo, int64_t row);
+
+    // ---- rollout (set up by the first rollout call)
+    struct Roll {
+        bool ready = false;
+        int F = 0;
+        int oldest = -1;                     // constant source the kind array was built for
+        std::vector<int8_t> kind;            // [V_in] 0 kept, 1 prognostic, 2 forcing (3: kept from the oldest slot)
+        DeviceBuffer d_kind, d_src, f[2], y[2], y_halo, y_send;
+        float *hy[2] = {nullptr, nullptr}, *hf[2] = {nullptr, nullptr};
+        cudaStream_t d2h = nullptr, h2d = nullptr;
+        cudaEvent_t up[2] = {nullptr, nullptr}, down[2] = {nullptr, nullptr};
+        std::vector<cudaEvent_t> beg, end;
+        cudaGraphExec_t graph[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [parity][with update]
+        bool graph_failed = false;
+        Xchg yx;  // outputs of the encoder's halo rows, from their owners
+    } ro_;
+    void rollout_setup();
+    void rollout_body(int p, bool update, cudaStream_t s);
+    void rollout_release();
     void exchange(Xchg& x, const T* src, int64_t lds, T* dst, int64_t ldd, bool direct, cudaStream_t s);
 };
 
@@ -282,7 +307,9 @@ struct Engine<T>::Hook {
 template <class T>
 DeviceBuffer Engine<T>::upload(const void* h, size_t bytes) {
     DeviceBuffer b(bytes);
-    if (bytes) VB_CUDA(cudaMemcpy(b.get(), h, bytes, cudaMemcpyHostToDevice));
+    // an empty host vector (null data) still gets a zeroed placeholder allocation
+    if (bytes && h) VB_CUDA(cudaMemcpy(b.get(), h, bytes, cudaMemcpyHostToDevice));
+    else if (bytes) VB_CUDA(cudaMemset(b.get(), 0, bytes));
     weight_bytes_ += bytes;
     return b;
 }
@@ -395,15 +422,14 @@ GraphDev Engine<T>::upload_graph(const CsrGraph& csr, const std::string& name, i
 }
 
 template <class T>
-void Engine<T>::setup_exchange(Xchg& x, const HaloPlan& h) {
+void Engine<T>::setup_exchange(Xchg& x, const HaloPlan& h, int64_t lo, int64_t row) {
     const int W = plan_.world;
-    const int64_t row = 2 * int64_t(C_);
     x.send_off.assign(size_t(W), 0), x.send_cnt.assign(size_t(W), 0);
     x.recv_off.assign(size_t(W), 0), x.recv_cnt.assign(size_t(W), 0);
     std::vector<int32_t> idx;
     for (int p = 0; p < W; ++p) {
         x.send_off[size_t(p)] = int64_t(idx.size()) * row;
-        for (int32_t g : h.send[size_t(p)]) idx.push_back(int32_t(g - plan_.h_lo));
+        for (int32_t g : h.send[size_t(p)]) idx.push_back(int32_t(g - lo));
         x.send_cnt[size_t(p)] = int64_t(h.send[size_t(p)].size()) * row;
     }
     int64_t off = 0;
@@ -605,8 +631,8 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     // ---- halo exchanges (multi-GPU)
     if (plan_.world > 1) {
         if (!opts_.nccl_id) fail(kInvalidArgument, "sharded load needs the NCCL unique id");
-        setup_exchange(xp_, plan_.proc);
-        setup_exchange(xd_, plan_.dec);
+        setup_exchange(xp_, plan_.proc, plan_.h_lo, 2 * int64_t(C_));
+        setup_exchange(xd_, plan_.dec, plan_.h_lo, 2 * int64_t(C_));
         xsend_ = act(size_t(std::max<int64_t>(1, std::max(xp_.n_send, xd_.n_send)) * 2 * C_));
         xrecv_ = act(size_t(std::max<int64_t>(1, xp_.n_recv) * 2 * C_));
         if (n_eh_) VB_CUDA(cudaMallocHost(&x_halo_host_, size_t(T_in_ * n_eh_ * V_in_) * sizeof(float)));
@@ -620,6 +646,7 @@ Engine<T>::~Engine() {
     cudaSetDevice(dev_);
     if (stream_) cudaStreamSynchronize(stream_);
     if (graph_exec_) cudaGraphExecDestroy(graph_exec_);  // before the communicator its nodes use
+    rollout_release();
     comm_.reset();
     if (x_halo_host_) cudaFreeHost(x_halo_host_);
     if (stream_) cudaStreamDestroy(stream_);
@@ -843,32 +870,39 @@ void Engine<T>::prepare() {
     ran_eager_ = true;
 }
 
-// Captures predict_step_device on the internal buffers. Whatever fails inside the capture, the
-// capture is ended and the partial graph destroyed; the caller then runs eagerly.
+// Captures body(s) into an executable graph. Whatever fails inside the capture, the capture is ended,
+// the partial graph destroyed and nullptr returned; the caller then runs eagerly.
 template <class T>
-bool Engine<T>::capture_graph(cudaStream_t s) {
+cudaGraphExec_t Engine<T>::capture(const std::function<void(cudaStream_t)>& body, cudaStream_t s) {
     VB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     std::string err;
     try {
-        predict_step_device(x_dev_, y_dev_, s);
+        body(s);
     } catch (const std::exception& e) {
         err = e.what();
     }
     cudaGraph_t g = nullptr;
+    cudaGraphExec_t exec = nullptr;
     const cudaError_t ec = cudaStreamEndCapture(s, &g);
     if (err.empty() && ec != cudaSuccess) err = std::string("cudaStreamEndCapture: ") + cudaGetErrorString(ec);
     if (err.empty()) {
-        const cudaError_t ei = cudaGraphInstantiate(&graph_exec_, g, 0);
+        const cudaError_t ei = cudaGraphInstantiate(&exec, g, 0);
         if (ei != cudaSuccess) {
-            graph_exec_ = nullptr;
+            exec = nullptr;
             err = std::string("cudaGraphInstantiate: ") + cudaGetErrorString(ei);
         }
     }
     if (g) cudaGraphDestroy(g);
-    if (err.empty()) return true;
+    if (err.empty()) return exec;
     (void)cudaGetLastError();
     std::fprintf(stderr, "varda_b200: CUDA graph capture failed (%s); running without a graph\n", err.c_str());
-    return false;
+    return nullptr;
+}
+
+template <class T>
+bool Engine<T>::capture_graph(cudaStream_t s) {
+    graph_exec_ = capture([this](cudaStream_t st) { predict_step_device(x_dev_, y_dev_, st); }, s);
+    return graph_exec_ != nullptr;
 }
 
 template <class T>
@@ -885,28 +919,38 @@ void Engine<T>::enqueue_predict() {
     else predict_step_device(x_dev_, y_dev_, s);
 }
 
+// Host x is the full (1, T_in, G, V_in) input. One GPU: one copy. Sharded: this rank's rows, own
+// rows then the encoder's halo rows (gathered on the host into pinned memory).
+template <class T>
+void Engine<T>::upload_input(const float* x, cudaStream_t s) {
+    if (plan_.world == 1) {
+        VB_CUDA(cudaMemcpyAsync(x_dev_, x, size_t(input_numel()) * sizeof(float), cudaMemcpyHostToDevice, s));
+        return;
+    }
+    for (int t = 0; t < T_in_; ++t) {
+        VB_CUDA(cudaMemcpyAsync(x_dev_ + int64_t(t) * Gx_ * V_in_, x + (int64_t(t) * G_ + plan_.g_lo) * V_in_,
+                                size_t(Gl_ * V_in_) * sizeof(float), cudaMemcpyHostToDevice, s));
+        if (n_eh_) {
+            float* stage = x_halo_host_ + int64_t(t) * n_eh_ * V_in_;
+            VB_CUDA(cudaStreamSynchronize(s));  // the staging buffer may still feed a previous copy
+            for (int64_t i = 0; i < n_eh_; ++i)
+                std::memcpy(stage + i * V_in_, x + (int64_t(t) * G_ + plan_.enc_halo[size_t(i)]) * V_in_,
+                            size_t(V_in_) * sizeof(float));
+            VB_CUDA(cudaMemcpyAsync(x_dev_ + (int64_t(t) * Gx_ + Gl_) * V_in_, stage,
+                                    size_t(n_eh_ * V_in_) * sizeof(float), cudaMemcpyHostToDevice, s));
+        }
+    }
+}
+
 template <class T>
 void Engine<T>::predict_step(const float* x, float* y, HookFn hook, void* user) {
     VB_CUDA(cudaSetDevice(dev_));
     cudaStream_t s = stream_;
     const int64_t in_n = input_numel(), out_n = output_numel();
     if (plan_.world > 1) {
-        // host x is the full (1, T_in, G, V_in) input: copy this rank's rows, own rows then the
-        // encoder's halo rows (gathered on the host into pinned memory); y gets this rank's rows
+        // y gets this rank's rows of the full (1, T_out, 1, G, V_out) output
         if (hook) fail(kUnsupported, "the activation hook is available on single-GPU models only");
-        for (int t = 0; t < T_in_; ++t) {
-            VB_CUDA(cudaMemcpyAsync(x_dev_ + int64_t(t) * Gx_ * V_in_, x + (int64_t(t) * G_ + plan_.g_lo) * V_in_,
-                                    size_t(Gl_ * V_in_) * sizeof(float), cudaMemcpyHostToDevice, s));
-            if (n_eh_) {
-                float* stage = x_halo_host_ + int64_t(t) * n_eh_ * V_in_;
-                VB_CUDA(cudaStreamSynchronize(s));  // the staging buffer may still feed a previous copy
-                for (int64_t i = 0; i < n_eh_; ++i)
-                    std::memcpy(stage + i * V_in_, x + (int64_t(t) * G_ + plan_.enc_halo[size_t(i)]) * V_in_,
-                                size_t(V_in_) * sizeof(float));
-                VB_CUDA(cudaMemcpyAsync(x_dev_ + (int64_t(t) * Gx_ + Gl_) * V_in_, stage,
-                                        size_t(n_eh_ * V_in_) * sizeof(float), cudaMemcpyHostToDevice, s));
-            }
-        }
+        upload_input(x, s);
         enqueue_predict();
         for (int t = 0; t < T_out_; ++t)
             VB_CUDA(cudaMemcpyAsync(y + (int64_t(t) * G_ + plan_.g_lo) * V_out_, y_dev_ + int64_t(t) * Gl_ * V_out_,
@@ -931,6 +975,199 @@ void Engine<T>::predict_step(const float* x, float* y, HookFn hook, void* user) 
     enqueue_predict();
     VB_CUDA(cudaMemcpyAsync(y, y_dev_, size_t(out_n) * sizeof(float), cudaMemcpyDeviceToHost, s));
     VB_CUDA(cudaStreamSynchronize(s));
+}
+
+// ====================================================================== rollout
+
+// The state update of the reference's rollout (varda::StateUpdate::from_config / make,
+// rollout.cpp:28-68): every input channel is exactly one of prognostic (fed back from the
+// output), dynamic forcing (replayed) or constant.
+template <class T>
+void Engine<T>::rollout_setup() {
+    if (ro_.ready) return;
+    if (!cfg_.has_forcings)
+        fail(kUnsupported, "rollout: the model config has no `forcings` section (dynamic/constant forcing names "
+                           "and input indices)");
+    if (T_out_ != 1) fail(kUnsupported, "rollout: only models with one output step are supported");
+    if (cfg_.residual_input.size() != cfg_.residual_output.size())
+        fail(kFormat, "rollout: residual_input and residual_output differ in length");
+    ro_.F = int(cfg_.forcing_dynamic_index.size());
+    ro_.kind.assign(size_t(V_in_), int8_t(-1));
+    std::vector<int> src(size_t(V_in_), -1);
+    auto claim = [&](int c, int k, int from, const char* what) {
+        if (c < 0 || c >= V_in_) fail(kFormat, std::string("rollout: ") + what + " index out of range");
+        if (ro_.kind[size_t(c)] >= 0)
+            fail(kFormat, "rollout: input channel " + std::to_string(c) + " is listed twice (" + what + ")");
+        ro_.kind[size_t(c)] = int8_t(k);
+        src[size_t(c)] = from;
+    };
+    for (size_t i = 0; i < cfg_.residual_input.size(); ++i) {
+        if (cfg_.residual_output[i] < 0 || cfg_.residual_output[i] >= V_out_)
+            fail(kFormat, "rollout: residual_output index out of range");
+        claim(cfg_.residual_input[i], 1, cfg_.residual_output[i], "prognostic");
+    }
+    for (int k = 0; k < ro_.F; ++k) claim(cfg_.forcing_dynamic_index[size_t(k)], 2, k, "dynamic forcing");
+    for (int c : cfg_.forcing_constant_index) claim(c, 0, -1, "constant forcing");
+    for (int c = 0; c < V_in_; ++c)
+        if (ro_.kind[size_t(c)] < 0)
+            fail(kFormat, "rollout: input channel " + std::to_string(c) +
+                              " is neither prognostic, dynamic forcing nor constant: it cannot be rolled out");
+
+    prepare();  // one eager forward before any capture
+    const int64_t f_n = std::max<int64_t>(1, Gx_ * ro_.F), y_n = Gl_ * V_out_;
+    ro_.d_kind.alloc(size_t(V_in_));
+    ro_.d_src.alloc(size_t(V_in_) * sizeof(int));
+    VB_CUDA(cudaMemcpy(ro_.d_src.get(), src.data(), size_t(V_in_) * sizeof(int), cudaMemcpyHostToDevice));
+    for (int p = 0; p < 2; ++p) {
+        ro_.f[p].alloc(size_t(f_n) * sizeof(float));
+        VB_CUDA(cudaMemset(ro_.f[p].get(), 0, size_t(f_n) * sizeof(float)));
+        ro_.y[p].alloc(size_t(std::max<int64_t>(1, y_n)) * sizeof(float));
+        VB_CUDA(cudaMallocHost(&ro_.hy[p], size_t(std::max<int64_t>(1, y_n)) * sizeof(float)));
+        VB_CUDA(cudaMallocHost(&ro_.hf[p], size_t(f_n) * sizeof(float)));
+        VB_CUDA(cudaEventCreateWithFlags(&ro_.up[p], cudaEventDisableTiming));
+        VB_CUDA(cudaEventCreateWithFlags(&ro_.down[p], cudaEventDisableTiming));
+    }
+    ro_.y_halo.alloc(size_t(std::max<int64_t>(1, n_eh_ * V_out_)) * sizeof(float));
+    if (plan_.world > 1) {
+        setup_exchange(ro_.yx, plan_.enc_x, plan_.g_lo, V_out_);
+        ro_.y_send.alloc(size_t(std::max<int64_t>(1, ro_.yx.n_send * V_out_)) * sizeof(float));
+    }
+    VB_CUDA(cudaStreamCreateWithFlags(&ro_.d2h, cudaStreamNonBlocking));
+    VB_CUDA(cudaStreamCreateWithFlags(&ro_.h2d, cudaStreamNonBlocking));
+    ro_.ready = true;
+}
+
+template <class T>
+void Engine<T>::rollout_release() {
+    for (auto& gp : ro_.graph)
+        for (auto& g : gp)
+            if (g) cudaGraphExecDestroy(g);
+    cudaStream_t streams[2] = {ro_.d2h, ro_.h2d};
+    for (cudaStream_t st : streams) {
+        if (!st) continue;
+        cudaStreamSynchronize(st);
+        cudaStreamDestroy(st);
+    }
+    for (int p = 0; p < 2; ++p) {
+        if (ro_.hy[p]) cudaFreeHost(ro_.hy[p]);
+        if (ro_.hf[p]) cudaFreeHost(ro_.hf[p]);
+        if (ro_.up[p]) cudaEventDestroy(ro_.up[p]);
+        if (ro_.down[p]) cudaEventDestroy(ro_.down[p]);
+    }
+    for (cudaEvent_t e : ro_.beg) cudaEventDestroy(e);
+    for (cudaEvent_t e : ro_.end) cudaEventDestroy(e);
+    ro_ = Roll{};
+}
+
+// One rollout step on s: normalise the window -> forward -> denormalise into y[p]; with the update,
+// the halo rows' outputs from their owners (sharded) and the state update of the window in place.
+template <class T>
+void Engine<T>::rollout_body(int p, bool update, cudaStream_t s) {
+    float* y = ro_.y[p].template as<float>();
+    predict_step_device(x_dev_, y, s);
+    if (!update) return;
+    if (plan_.world > 1) {
+        float* send = ro_.y_send.template as<float>();
+        k::gather_rows(send, y, ro_.yx.send_idx.template as<int32_t>(), ro_.yx.n_send, V_out_, s);
+        comm_->exchange(send, ro_.yx.send_off, ro_.yx.send_cnt, ro_.y_halo.get(), ro_.yx.recv_off, ro_.yx.recv_cnt,
+                        int(sizeof(float)), s);
+    }
+    k::rollout_update(x_dev_, T_in_, Gx_, V_in_, y, ro_.y_halo.template as<float>(), Gl_, V_out_,
+                      ro_.f[p].template as<float>(), ro_.F, ro_.d_kind.template as<int8_t>(),
+                      ro_.d_src.template as<int>(), s);
+}
+
+// The device loop: step s (parity p = s % 2) replays graph[p] on the model's stream; its output y[p]
+// goes to pinned host memory on the D2H stream and is delivered (copied into y, the callback) while
+// step s + 1 runs; the forcing of step s + 1 is gathered into pinned memory and uploaded on the H2D
+// stream while step s runs. Same order of operations as the reference's host loop (Rollout::run,
+// rollout.cpp:116-155): predict, then (unless last) the update with forcing s.
+template <class T>
+void Engine<T>::rollout(const float* x0, int n, const float* forcings, float* y, bool constants_oldest, StepFn cb,
+                        void* user, float* step_ms) {
+    VB_CUDA(cudaSetDevice(dev_));
+    if (!x0 || n < 1) fail(kInvalidArgument, "rollout: need x0 and n_steps >= 1");
+    rollout_setup();
+    if (n > 1 && ro_.F > 0 && !forcings) fail(kInvalidArgument, "rollout: forcings missing");
+    cudaStream_t s = stream_;
+    if (ro_.oldest != int(constants_oldest)) {
+        std::vector<int8_t> kd = ro_.kind;
+        for (auto& k : kd)
+            if (k == 0 && constants_oldest) k = 3;
+        VB_CUDA(cudaMemcpy(ro_.d_kind.get(), kd.data(), kd.size(), cudaMemcpyHostToDevice));
+        ro_.oldest = int(constants_oldest);
+    }
+    for (int i = int(ro_.beg.size()); i < n; ++i) {
+        cudaEvent_t a, b;
+        VB_CUDA(cudaEventCreate(&a));
+        VB_CUDA(cudaEventCreate(&b));
+        ro_.beg.push_back(a), ro_.end.push_back(b);
+    }
+    const bool graphs = opts_.cuda_graph && !ro_.graph_failed;
+    if (graphs && !ro_.graph[0][0]) {
+        for (int p = 0; p < 2 && !ro_.graph_failed; ++p)
+            for (int u = 0; u < 2 && !ro_.graph_failed; ++u) {
+                ro_.graph[p][u] = capture([&](cudaStream_t st) { rollout_body(p, u == 1, st); }, s);
+                if (!ro_.graph[p][u]) ro_.graph_failed = true;
+            }
+        for (auto& gp : ro_.graph)
+            for (auto& g : gp)
+                if (g) VB_CUDA(cudaGraphUpload(g, s));
+    }
+    const int F = ro_.F;
+    const int64_t y_n = Gl_ * V_out_;
+    auto produce_forcing = [&](int st) {  // forcing written after step st, into f[st % 2]
+        const int b = st & 1;
+        const float* fs = forcings + int64_t(st) * G_ * F;
+        std::memcpy(ro_.hf[b], fs + plan_.g_lo * F, size_t(Gl_ * F) * sizeof(float));
+        for (int64_t i = 0; i < n_eh_; ++i)
+            std::memcpy(ro_.hf[b] + (Gl_ + i) * F, fs + int64_t(plan_.enc_halo[size_t(i)]) * F,
+                        size_t(F) * sizeof(float));
+        if (st >= 2) VB_CUDA(cudaStreamWaitEvent(ro_.h2d, ro_.end[size_t(st - 2)], 0));  // step st-2 read f[b]
+        VB_CUDA(cudaMemcpyAsync(ro_.f[b].get(), ro_.hf[b], size_t(Gx_ * F) * sizeof(float), cudaMemcpyHostToDevice,
+                                ro_.h2d));
+        VB_CUDA(cudaEventRecord(ro_.up[b], ro_.h2d));
+    };
+    auto deliver = [&](int st) {
+        const int b = st & 1;
+        VB_CUDA(cudaEventSynchronize(ro_.down[b]));
+        if (y) std::memcpy(y + (int64_t(st) * G_ + plan_.g_lo) * V_out_, ro_.hy[b], size_t(y_n) * sizeof(float));
+        if (cb) cb(st, ro_.hy[b], Gl_, user);
+    };
+
+    VB_CUDA(cudaStreamSynchronize(s));
+    VB_CUDA(cudaStreamSynchronize(ro_.d2h));
+    VB_CUDA(cudaStreamSynchronize(ro_.h2d));
+    upload_input(x0, s);
+    const bool feed = F > 0 && n > 1;
+    if (feed) produce_forcing(0);
+    for (int st = 0; st < n; ++st) {
+        const int p = st & 1;
+        const bool update = st + 1 < n;  // no update after the last step
+        if (update && feed) VB_CUDA(cudaStreamWaitEvent(s, ro_.up[p], 0));  // forcing st on the device
+        if (st >= 2) VB_CUDA(cudaStreamWaitEvent(s, ro_.down[p], 0));       // y[p] of step st-2 copied out
+        VB_CUDA(cudaEventRecord(ro_.beg[size_t(st)], s));
+        if (graphs && !ro_.graph_failed) VB_CUDA(cudaGraphLaunch(ro_.graph[p][update ? 1 : 0], s));
+        else rollout_body(p, update, s);
+        VB_CUDA(cudaEventRecord(ro_.end[size_t(st)], s));
+        VB_CUDA(cudaStreamWaitEvent(ro_.d2h, ro_.end[size_t(st)], 0));
+        VB_CUDA(cudaMemcpyAsync(ro_.hy[p], ro_.y[p].get(), size_t(y_n) * sizeof(float), cudaMemcpyDeviceToHost,
+                                ro_.d2h));
+        VB_CUDA(cudaEventRecord(ro_.down[p], ro_.d2h));
+        if (feed && st + 1 < n - 1) {
+            // pinned hf[1-p] last fed the upload of forcing st-1; wait for that copy
+            if (st >= 1) VB_CUDA(cudaEventSynchronize(ro_.up[1 - p]));
+            produce_forcing(st + 1);
+        }
+        if (st >= 1) deliver(st - 1);
+    }
+    deliver(n - 1);
+    VB_CUDA(cudaStreamSynchronize(s));
+    VB_CUDA(cudaStreamSynchronize(ro_.h2d));
+    if (step_ms)
+        for (int st = 0; st < n; ++st)
+            VB_CUDA(cudaEventElapsedTime(&step_ms[st], ro_.beg[size_t(st)], ro_.end[size_t(st)]));
+    ran_eager_ = true;
 }
 
 template <class T>

@@ -13,6 +13,8 @@
 namespace vb {
 
 using HookFn = void (*)(const char* key, const float* data, const int64_t* shape, int ndim, void* user);
+// Rollout output of step `step`: this rank's rows (rows, V_out) physical, host, valid during the call.
+using StepFn = void (*)(int step, const float* y, int64_t rows, void* user);
 
 struct Options {
     int precision = 0;  // 0 fp32, 1 fp16
@@ -54,6 +56,12 @@ public:
     // launch; returns a JSON array of {"name", "ms", "flop", "bytes"} records (algorithmic FLOPs
     // of the GEMMs, compulsory bytes of the bandwidth-bound kernels). Synchronises.
     virtual std::string profile_forward() = 0;
+    // Device-resident autoregressive rollout with replayed forcings (include/varda_b200.h vb_rollout):
+    // x0 (1, T_in, G, V_in) and forcings (n_steps - 1, G, F) full host arrays; y (n_steps, G, V_out)
+    // receives this rank's rows when not null; cb gets each step's rows when not null; step_ms
+    // [n_steps] the GPU time of each step when not null.
+    virtual void rollout(const float* x0, int n_steps, const float* forcings, float* y, bool constants_oldest,
+                         StepFn cb, void* user, float* step_ms) = 0;
 };
 
 std::unique_ptr<Model> load_model(const std::string& path, const Options& opts);

@@ -53,6 +53,23 @@ __global__ void assemble_kernel(const float* __restrict__ xn, const float* __res
     }
 }
 
+__global__ void rollout_update_kernel(float* __restrict__ w, int T, int64_t rows, int V, const float* __restrict__ yo,
+                                      const float* __restrict__ yh, int64_t n_own, int Vo, const float* __restrict__ f,
+                                      int F, const int8_t* __restrict__ kind, const int* __restrict__ src) {
+    const int64_t n = rows * V, slot = rows * V;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t row = i / V;
+        const int c = int(i - row * V);
+        const float oldest = w[i];
+        for (int t = 0; t + 1 < T; ++t) w[t * slot + i] = w[(t + 1) * slot + i];
+        float* newest = w + int64_t(T - 1) * slot + i;
+        const int k = kind[c];
+        if (k == 1) *newest = row < n_own ? yo[row * Vo + src[c]] : yh[(row - n_own) * Vo + src[c]];
+        else if (k == 2) *newest = f[row * F + src[c]];
+        else if (k == 3) *newest = oldest;
+    }
+}
+
 // One warp per row, 16-byte vectors.
 __global__ void copy_rows_kernel(uint4* dst, int64_t ldd, const int32_t* __restrict__ di, const uint4* __restrict__ src,
                                  int64_t lds, const int32_t* __restrict__ si, int64_t rows, int64_t vecs) {
@@ -213,6 +230,29 @@ void assemble(const float* xn, const float* attr, int T_in, int64_t G, int V, in
               cudaStream_t s) {
     if (G <= 0) return;
     assemble_kernel<T><<<grid_for(G * ld, 256), 256, 0, s>>>(xn, attr, T_in, G, V, A, out, ld);
+    VB_LAUNCH();
+}
+
+__global__ void gather_rows_kernel(float* __restrict__ dst, const float* __restrict__ src, const int32_t* __restrict__ idx,
+                                   int64_t rows, int cols) {
+    const int64_t n = rows * cols;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = i / cols;
+        dst[i] = src[int64_t(idx[r]) * cols + (i - r * cols)];
+    }
+}
+
+void gather_rows(float* dst, const float* src, const int32_t* idx, int64_t rows, int cols, cudaStream_t s) {
+    if (rows <= 0 || cols <= 0) return;
+    gather_rows_kernel<<<grid_for(rows * cols, 256), 256, 0, s>>>(dst, src, idx, rows, cols);
+    VB_LAUNCH();
+}
+
+void rollout_update(float* window, int T, int64_t rows, int V_in, const float* y_own, const float* y_halo, int64_t n_own,
+                    int V_out, const float* f, int F, const int8_t* kind, const int* src, cudaStream_t s) {
+    if (rows <= 0) return;
+    rollout_update_kernel<<<grid_for(rows * V_in, 256), 256, 0, s>>>(window, T, rows, V_in, y_own, y_halo, n_own, V_out,
+                                                                      f, F, kind, src);
     VB_LAUNCH();
 }
 

@@ -28,6 +28,8 @@ void assemble(const float* xn, const float* attr, int T_in, int64_t G, int V, in
 template <class T>
 void copy_rows(T* dst, int64_t ldd, const int32_t* dst_idx, const T* src, int64_t lds, const int32_t* src_idx,
                int64_t rows, int64_t cols, cudaStream_t s);
+// dst[r, 0:cols] = src[idx[r], 0:cols], fp32, any row width (rollout output exchange).
+void gather_rows(float* dst, const float* src, const int32_t* idx, int64_t rows, int cols, cudaStream_t s);
 // dst[r, c] = Tout(src[r, c]) for c < cols.
 template <class Tin, class Tout>
 void convert_2d(const Tin* src, int64_t ld_src, Tout* dst, int64_t ld_dst, int64_t rows, int64_t cols, cudaStream_t s);
@@ -53,6 +55,15 @@ struct OutputArgs {
 // Per output step: fp32 cast, prognostic residual, boundings in config order (reference
 // backend_cpu.cpp:504-522, 111-136).
 template <class T> void output_assemble(const OutputArgs& a, cudaStream_t s);
+
+// Rollout state update of the reference (varda::StateUpdate::apply, rollout.cpp:70-92), on the
+// window (T, rows, V_in) in place: every slot shifts down by one (slot t <- slot t+1), then the
+// newest slot's channel c takes kind[c] = 1: the output y[row][src[c]] (prognostic), 2: the forcing
+// f[row][src[c]] (dynamic forcing), 0: nothing (constant, kept in place), or 3: the oldest slot's
+// old value (constant, inherited through the roll). y rows [0, n_own) come from y_own, rows
+// [n_own, rows) from y_halo (the owners' outputs of this rank's halo rows, multi-GPU). Pure copies.
+void rollout_update(float* window, int T, int64_t rows, int V_in, const float* y_own, const float* y_halo,
+                    int64_t n_own, int V_out, const float* f, int F, const int8_t* kind, const int* src, cudaStream_t s);
 
 // ------------------------------------------------------------------ LayerNorm (fp32 statistics)
 // y = LN(x) * w + b over C channels per row (C a multiple of 128, <= 2048); b may be null; y may

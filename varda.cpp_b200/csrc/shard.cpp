@@ -138,8 +138,8 @@ ShardPlan make_plan(const Config& c, const CsrGraph& enc, const CsrGraph& proc, 
     p.proc = halos(proc, p.h_split, p.h_split, world, rank);
     p.dec = halos(dec, p.g_split, p.h_split, world, rank);
     // encoder: remote data sources of own hidden rows (uploaded from the host input, not exchanged)
-    HaloPlan eh = halos(enc, p.h_split, p.g_split, world, rank);
-    p.enc_halo = eh.halo;
+    p.enc_x = halos(enc, p.h_split, p.g_split, world, rank);
+    p.enc_halo = p.enc_x.halo;
 
     p.enc = local_graph(enc, p.h_lo, p.h_hi, p.g_lo, p.g_hi, p.enc_halo);
     p.proc_g = local_graph(proc, p.h_lo, p.h_hi, p.h_lo, p.h_hi, p.proc.halo);

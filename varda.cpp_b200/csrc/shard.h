@@ -42,6 +42,8 @@ struct ShardPlan {
     int64_t h_lo = 0, h_hi = 0, g_lo = 0, g_hi = 0;
     HaloPlan proc, dec;
     std::vector<int32_t> enc_halo;         // global data ids read by own hidden rows but owned elsewhere
+    HaloPlan enc_x;                        // the same rows as a halo plan (send lists: own data rows
+                                           // other ranks read), for the rollout's per-step output exchange
     CsrGraph enc, proc_g, dec_g;           // own destination rows, sources in local ids
 };
 

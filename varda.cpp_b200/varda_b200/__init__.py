@@ -64,6 +64,8 @@ def _load_lib():
         "vb_gemm": ([I, I, P, I64, P, I64, P, P, I64, P, I64, I64, I64, I64, I, I, P], I),
         "vb_layernorm": ([I, P, I64, P, P, P, I64, I64, I, F, P], I),
         "vb_add_layernorm": ([I, P, P, P, P, P, P, I64, I64, I, F, P], I),
+        "vb_rollout": ([P, P, I, P, P, I, P, P, P], I),
+        "vb_rollout_update": ([P, I, I64, I, P, P, I64, I, P, I, P, P, P], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -91,6 +93,7 @@ class Options(ctypes.Structure):
 
 HOOK = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int64),
                         ctypes.c_int, ctypes.c_void_p)
+STEP = ctypes.CFUNCTYPE(None, ctypes.c_int, ctypes.POINTER(ctypes.c_float), ctypes.c_int64, ctypes.c_void_p)
 
 
 def _ptr(a):
@@ -169,6 +172,26 @@ class Model:
             cb = HOOK(_cb)
         check(lib.vb_predict_step(self._h, _ptr(x), _ptr(y), cb, None))
         return y
+
+    def rollout(self, x0, n_steps, forcings=None, constants_oldest=False, keep=True, on_step=None):
+        """Device rollout with replayed forcings (vb_rollout; DeviceRollout::run, rollout_cuda.cu:160-234).
+        x0 (1, T_in, G, V_in); forcings (n_steps - 1, G, F) or None. Returns (y, step_ms) with y
+        (n_steps, G, V_out) (this rank's rows filled on a sharded model) or None when keep is False;
+        on_step(step, rows_array) gets each step's own rows (a view valid during the call)."""
+        x0 = np.ascontiguousarray(x0, dtype=np.float32)
+        if x0.size != int(np.prod(self.input_shape)):
+            raise ValueError(f"x0 has {x0.size} elements, expected {self.input_shape}")
+        f = None if forcings is None else np.ascontiguousarray(forcings, dtype=np.float32)
+        G, Vo = self.G, self.V_out
+        y = np.zeros((n_steps, G, Vo), np.float32) if keep else None
+        ms = np.zeros(n_steps, np.float32)
+        cb = None
+        if on_step is not None:
+            def _cb(step, data, rows, user):
+                on_step(step, np.ctypeslib.as_array(data, shape=(rows * Vo,)).reshape(rows, Vo))
+            cb = STEP(_cb)
+        check(lib.vb_rollout(self._h, _ptr(x0), n_steps, _ptr(f), _ptr(y), int(constants_oldest), cb, None, _ptr(ms)))
+        return y, ms
 
     # CudaBackend device entry points (cuda_backend.h:38-74); pointers are ints / torch tensors
     def normalise(self, x, xn, stream=None):
@@ -259,6 +282,11 @@ def layernorm(dtype, x, ldx, w, b, y, ldy, rows, C, eps, stream=None):
 def add_layernorm(dtype, a, r, out1, w, b, ln, ld, rows, C, eps, stream=None):
     check(lib.vb_add_layernorm(dtype, _ptr(a), _ptr(r), _ptr(out1), _ptr(w), _ptr(b), _ptr(ln), ld, rows, C, eps,
                                stream))
+
+
+def rollout_update(window, T, rows, V_in, y_own, y_halo, n_own, V_out, f, F, kind, src, stream=None):
+    check(lib.vb_rollout_update(_ptr(window), T, rows, V_in, _ptr(y_own), _ptr(y_halo), n_own, V_out, _ptr(f), F,
+                                _ptr(kind), _ptr(src), stream))
 
 
 def shard_plan(path, world, rank):

@@ -446,7 +446,9 @@ def config_test(name):
         "t384i": (16, 384, 6, 768, 2, 2, 4, 3, "none", False, 0, False, 257, 53, 6),
         "t2048": (17, 2048, 8, 512, 1, 2, 4, 3, "tanh", True, -1, True, 120, 30, 1),
     }
-    (seed, C, heads, mlp, n_proc, T, A, Ae, gelu, skip, rs, absent_kind, G, H, T_out) = specs[name]
+    rollout = name.endswith("r") and name[:-1] in specs
+    base = name[:-1] if rollout else name
+    (seed, C, heads, mlp, n_proc, T, A, Ae, gelu, skip, rs, absent_kind, G, H, T_out) = specs[base]
     rng = np.random.default_rng(1000 + seed)
     enc = random_graph(rng, G, H, [0, 1, 2, 3, 5, 8, 17, 33, 64, 9, 12])
     proc = random_graph(rng, H, H, [0, 1, 2, 3, 5, 8, 17, 33, 64, 6])
@@ -461,9 +463,35 @@ def config_test(name):
     if T_out > 1:
         kw = dict(T_out=T_out, times={"input": [0, T_out], "target": list(range(1, T_out + 1)),
                                       "frequency_hours": 1})
-    return make_model(seed=seed, C=C, heads=heads, mlp=mlp, n_proc=n_proc, T=T, G=G, H=H, enc=enc, proc=proc,
-                      dec=dec, A=A, Ae=Ae, gelu=gelu, latent_skip=skip, res_step=rs, absent=absent,
-                      edge_attr="normal", xavier=False, uuid=f"b200-{name}", **v, **kw)
+    if rollout:
+        # 6 prognostic inputs (0..5 <- outputs 0..5), dynamic forcings 6..8, constant 9
+        names = [f"v{i}" for i in range(12)]
+        kw["var_names"] = names
+        kw["forcings"] = {"dynamic": [names[i] for i in (6, 7, 8)], "dynamic_input_index": [6, 7, 8],
+                          "constant": [names[9]], "constant_input_index": [9], "timestep_hours": 6,
+                          "source": "varda_b200.synth"}
+    cfg, t, x = make_model(seed=seed, C=C, heads=heads, mlp=mlp, n_proc=n_proc, T=T, G=G, H=H, enc=enc, proc=proc,
+                           dec=dec, A=A, Ae=Ae, gelu=gelu, latent_skip=skip, res_step=rs, absent=absent,
+                           edge_attr="normal", xavier=False, uuid=f"b200-{name}", **v, **kw)
+    if rollout:
+        g = np.random.default_rng(2000 + seed)
+        t["grid.latitudes"] = g.uniform(-80.0, 80.0, G).astype(np.float64)
+        t["grid.longitudes"] = g.uniform(0.0, 360.0, G).astype(np.float64)
+    return cfg, t, x
+
+
+def replay_forcings(n_steps, G, F, timestep_hours=6, seed=0):
+    """Synthetic dynamic forcings to replay in a rollout: (n_steps - 1, G, F) fp32 sin/cos waves of the
+    valid time of each step (forcing s belongs to the output of step s) with a per-node phase."""
+    rng = np.random.default_rng(seed)
+    phase = rng.uniform(0.0, 2.0 * np.pi, (G, 1))
+    s = np.arange(1, max(n_steps, 1), dtype=np.float64)[:, None, None]
+    hours = s * timestep_hours
+    k = np.arange(F, dtype=np.float64)[None, None, :]
+    period = np.where(k % 2 == 0, 24.0, 24.0 * 365.25)
+    f = np.where(k % 3 == 2, np.cos(2 * np.pi * hours / period + phase[None]),
+                 np.sin(2 * np.pi * hours / period + phase[None] + k))
+    return np.ascontiguousarray(f.astype(np.float32))
 
 
 def sha256_file(path, chunk=1 << 24):
