@@ -111,3 +111,16 @@ def test_fp16_is_close_to_fp32(seeded_model):
     y32 = vb.Model.load(mp, precision=vb.FP32).predict_step(x)
     y16 = vb.Model.load(mp, precision=vb.FP16).predict_step(x)
     assert oracle.rel_absmax(y16, y32) <= TOL[vb.FP16]
+
+
+@pytest.mark.parametrize("name", ["t256", "t1024", "c0"])
+def test_tiled_attention_engine_path(name, seeded_model, monkeypatch):
+    """The engine with its attention on the shared-memory-staged tiled kernel (VB_ATT_TILED=1, off by
+    default): same parity bar as the default gather kernel."""
+    mp, xp = seeded_model(name)
+    x = np.array(st.read(xp)[0]["in.x"])
+    monkeypatch.setenv("VB_ATT_TILED", "1")
+    y = vb.Model.load(mp, precision=vb.FP16).predict_step(x)
+    vb.check_device()
+    ref = golden(name)["out.y"]
+    assert oracle.rel_absmax(y, ref) <= TOL[vb.FP16]

@@ -400,7 +400,7 @@ GraphDev Engine<T>::upload_graph(const CsrGraph& csr, const std::string& name, i
     std::vector<EdgeRec> packed = pack_edges(csr, !std::is_same<T, float>::value);
     GraphDev d;
     d.name = name;
-    if (std::is_same<T, __half>::value && k::tiled_supported(C_, hd_) && env_int("VB_ATT_TILED", 1) != 0) {
+    if (std::is_same<T, __half>::value && k::tiled_supported(C_, hd_) && env_int("VB_ATT_TILED", 0) != 0) {
         TilePlan tp = make_tiles(csr, k::tiled_max_src(), 64, k::tiled_max_deg(hd_), chunk_rows, true);
         std::vector<int4> t4(tp.row0.size());
         for (size_t i = 0; i < t4.size(); ++i) t4[i] = make_int4(tp.row0[i], tp.nrows[i], tp.src0[i], tp.nsrc[i]);
