@@ -162,6 +162,21 @@ int vb_attention(int dtype, const int32_t* row_ptr, const void* edges, int64_t d
                  const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, const void* xr, int64_t ldxr,
                  void* out, int64_t ldo, const float* w_e, int C, int heads, int head_dim, void* stream);
 
+/* No-allocation variant of vb_attention, no reference counterpart: same arguments and result, each
+ * destination row's edges cut into `splits` parts (1..64) whose partial softmax results go to one
+ * static device array of 16 MiB (its only device storage; nothing is allocated, nothing needs to start
+ * at zero) and are then merged. For callers that cannot allocate device memory at call time (a process
+ * whose memory pool owns the free memory, a loop that cannot take cudaMalloc's synchronisation).
+ * Limit: one row's splits x (C + 5 heads) floats must fit 16 MiB (VB_ERR_UNSUPPORTED otherwise);
+ * larger graphs run in several batches. Overlapping calls on one device race on the shared array:
+ * order them on one stream. Make the first call on each device outside stream capture (it looks up
+ * the array's device address). Destination range only; C = heads x head_dim with C a multiple of 128;
+ * leading dimensions multiples of 4 elements. */
+int vb_attention_split_noalloc(int dtype, const int32_t* row_ptr, const void* edges, int64_t dst_lo, int64_t n_rows,
+                               const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, const void* xr,
+                               int64_t ldxr, void* out, int64_t ldo, const float* w_e, int C, int heads, int head_dim,
+                               int splits, void* stream);
+
 /* The shared-memory-staged attention the engine runs in fp16 (no reference counterpart: the
  * reference has only the gather kernel): vb_tiles_create builds the destination tiles of a CSR graph
  * (host arrays from vb_build_csr) and uploads them to the current device; vb_attention_tiled runs

@@ -102,8 +102,15 @@ template <class T> struct AttnArgs {
 // backend_cpu.cpp:333-340 and the fp16 roundings of the autocast reference.
 template <class T> void attention(const AttnArgs<T>& a, cudaStream_t s);
 
+// The same contract over a destination range [dst_lo, dst_lo + n_rows) (no row list), each row's edges
+// cut into `splits` parts whose partial softmax results go to a static device scratch array and are
+// then merged; allocates nothing (attention_split.cu). Calls must not overlap on the device: they share
+// the one scratch array. Rows are processed in batches that fit it.
+template <class T> void attention_split_noalloc(const AttnArgs<T>& a, int splits, cudaStream_t s);
+size_t attention_split_scratch_bytes();
+
 // Shared-memory-staged attention (fp16) over destination tiles (graph.h TilePlan): same contract per
-// destination row, two-pass softmax. Tiles [tile0, tile0 + ntiles) of the plan; q/x_r/out row of graph
+// destination row. Tiles [tile0, tile0 + ntiles) of the plan; q/x_r/out row of graph
 // row d is d - dst_lo.
 struct TileArgs {
     const int4* tiles = nullptr;    // per tile {row0, nrows, src0, nsrc}
