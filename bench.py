@@ -330,6 +330,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c1", choices=["c1", "c0", "c3", "c4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-out", default=None, help="write the per-launch profile records (JSON) here")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", args.gpus))
@@ -375,6 +376,9 @@ def main():
     else:
         r = run_ours(args, rank, world, local_rank)
     roof, edge, shares, prof_total = summarise(r["prof"], pk, src)
+    if args.profile_out and rank == 0:
+        with open(args.profile_out, "w") as fh:
+            json.dump(r["prof"], fh, indent=0)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("c1", "c4"):
         try:

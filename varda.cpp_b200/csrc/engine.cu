@@ -401,7 +401,7 @@ GraphDev Engine<T>::upload_graph(const CsrGraph& csr, const std::string& name, i
     GraphDev d;
     d.name = name;
     if (std::is_same<T, __half>::value && k::tiled_supported(C_, hd_) && env_int("VB_ATT_TILED", 0) != 0) {
-        TilePlan tp = make_tiles(csr, k::tiled_max_src(), 64, k::tiled_max_deg(hd_), chunk_rows, true);
+        TilePlan tp = make_tiles(csr, k::tiled_max_src(), k::tiled_max_rows(), k::tiled_max_edges(), chunk_rows, true);
         std::vector<int4> t4(tp.row0.size());
         for (size_t i = 0; i < t4.size(); ++i) t4[i] = make_int4(tp.row0[i], tp.nrows[i], tp.src0[i], tp.nsrc[i]);
         d.tiled = true;
@@ -674,14 +674,15 @@ void Engine<T>::linear(const Lin<T>& L, const T* x, int64_t ldx, T* y, int64_t l
     a.R = R, a.ldr = ldr, a.M = M, a.N = L.N, a.K = L.K, a.epi = epi, a.gelu_tanh = gelu_tanh_;
     if constexpr (std::is_same<T, __half>::value) {
         if (use_tc_ && tc::supported(a)) {
-            Span sp(this, s, "gemm_tc N=" + std::to_string(L.N) + " K=" + std::to_string(L.K) + " epi=" +
-                                 std::to_string(epi), 2.0 * double(M) * double(L.N) * double(L.K), 0);
+            Span sp(this, s, "gemm_tc M=" + std::to_string(M) + " N=" + std::to_string(L.N) + " K=" +
+                                 std::to_string(L.K) + " epi=" + std::to_string(epi),
+                    2.0 * double(M) * double(L.N) * double(L.K), 0);
             tc::gemm(a, s);
             return;
         }
     }
-    Span sp(this, s, "gemm_simt N=" + std::to_string(L.N) + " K=" + std::to_string(L.K) + " epi=" + std::to_string(epi),
-            2.0 * double(M) * double(L.N) * double(L.K), 0);
+    Span sp(this, s, "gemm_simt M=" + std::to_string(M) + " N=" + std::to_string(L.N) + " K=" + std::to_string(L.K) +
+                         " epi=" + std::to_string(epi), 2.0 * double(M) * double(L.N) * double(L.K), 0);
     k::gemm_simt<T>(a, s);
 }
 

@@ -149,8 +149,10 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
+// tcgen05.ld of 32 consecutive TMEM columns of this warp's 32 lanes, without waiting; tmem_wait32
+// waits for every load of the thread and hands the registers on (they are in-out operands of the
+// wait, so no use of them can be scheduled before it).
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -160,9 +162,42 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
+// x + h (h an fp16 value, widened exactly): the sm_100 mixed-precision add, one instruction per element.
+__device__ __forceinline__ float2 add_h2(uint32_t h2, float2 x) {
+    float2 d;
+    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "add.rn.f32.f16 %0, lo, %3;\n\tadd.rn.f32.f16 %1, hi, %4;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "r"(h2), "f"(x.x), "f"(x.y));
+    return d;
+}
+// Two fp32 values rounded to fp16 and packed (low half = x.x).
+__device__ __forceinline__ uint32_t pack_h2(float2 x) {
+    const __half2 h = __floats2half2_rn(x.x, x.y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ float2 unpack_h2(uint32_t u) { return __half22float2(*reinterpret_cast<const __half2*>(&u)); }
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcpf(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 // Shared memory: the A/W stage ring, then per epilogue warp two 2 KB output staging buffers (and, for
@@ -183,13 +218,22 @@ template <int BN, int STAGES, int EPI> struct Layout {
 // Handbook of Mathematical Functions, formula 7.1.26 (|error of erf| <= 1.5e-7), written as
 // Phi(x) = 1 - q (x >= 0), q (x < 0) with q = P(t) exp(-z^2) / 2, z = |x| / sqrt(2), so the left tail
 // has no cancellation. Checked against the erff-based GELU by the tests.
-__device__ __forceinline__ float gelu_as(float x) {
-    const float z = fabsf(x) * 0.70710678118654752f;
-    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
-    const float poly =
-        t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
-    const float q = 0.5f * poly * __expf(-z * z);
-    return x * (x >= 0.0f ? 1.0f - q : q);
+// Two values at a time with packed fp32 operations; q's factor 1/2 is folded into the polynomial's
+// coefficients (exact: a power of two); exp(-z^2) = 2^(-z^2 log2 e) and 1 / (1 + p z) on the SFU.
+__device__ __forceinline__ float2 gelu_as2(float2 x) {
+    const float2 z = __fmul2_rn(make_float2(fabsf(x.x), fabsf(x.y)), make_float2(0.70710678118654752f, 0.70710678118654752f));
+    const float2 den = __ffma2_rn(make_float2(0.3275911f, 0.3275911f), z, make_float2(1.0f, 1.0f));
+    const float2 t = make_float2(rcpf(den.x), rcpf(den.y));
+    float2 p = __ffma2_rn(t, make_float2(0.5307027145f, 0.5307027145f), make_float2(-0.7265760135f, -0.7265760135f));
+    p = __ffma2_rn(t, p, make_float2(0.7107068705f, 0.7107068705f));
+    p = __ffma2_rn(t, p, make_float2(-0.142248368f, -0.142248368f));
+    p = __ffma2_rn(t, p, make_float2(0.127414796f, 0.127414796f));
+    p = __fmul2_rn(t, p);
+    // exp(-z^2) = 2^(-z^2 log2 e)
+    const float2 a = __fmul2_rn(__fmul2_rn(z, z), make_float2(-1.4426950408889634f, -1.4426950408889634f));
+    const float2 q = __fmul2_rn(p, make_float2(ex2f(a.x), ex2f(a.y)));
+    const float2 one_q = __fadd2_rn(make_float2(1.0f, 1.0f), make_float2(-q.x, -q.y));
+    return __fmul2_rn(x, make_float2(x.x >= 0.0f ? one_q.x : q.x, x.y >= 0.0f ? one_q.y : q.y));
 }
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
@@ -314,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr int kChunks = BN / 64;  // 32-column chunks per half
         uint8_t* obuf = sOut + ew * 2 * L::kSub;
         uint8_t* rsm = sRes + ew * 2 * L::kSub;
-        uint64_t* rb = rbar + 2 * ew;
+        uint64_t* rb_bar = rbar + 2 * ew;
         uint32_t n_out = 0;                 // output staging uses so far (buffer = count & 1)
         uint32_t r_issue = 0, r_use = 0;    // residual sub-tile loads issued / consumed (buffer = i & 1)
         int it = 0;
@@ -322,8 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) {
                 const uint32_t b = r_issue & 1;
                 fence_async_smem();
-                mbar_expect_tx(&rb[b], uint32_t(L::kSub));
-                tma_load_2d(rsm + b * L::kSub, &tmR, &rb[b], col0, row0);
+                mbar_expect_tx(&rb_bar[b], uint32_t(L::kSub));
+                tma_load_2d(rsm + b * L::kSub, &tmR, &rb_bar[b], col0, row0);
             }
             ++r_issue;
         };
@@ -337,46 +381,77 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(&tfull[ab], ap, abort_flag)) break;
             fence_after();
             const uint32_t taddr = tmem + (uint32_t(lg * 32) << 16) + uint32_t(ab * BN + half * (BN / 2));
-            bool ok = true;
-#pragma unroll 1
+            bool ok = true, released = false;
+            // chunk c's 32 columns are in ra (c even) / rb (c odd); chunk c + 1's load is in flight
+            // while chunk c is processed, and the accumulator goes back to the MMA warp as soon as
+            // its last chunk has been read
+            uint32_t ra[32], rb[32];
+            tmem_ld32_async(taddr, ra);
+            tmem_wait32(ra);
+#pragma unroll
             for (int c = 0; c < kChunks; ++c) {
+                uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+                uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+                if (c + 1 < kChunks) tmem_ld32_async(taddr + uint32_t((c + 1) * 32), nxt);
                 const int col0 = colh + c * 32;
-                float v[32];
-                tmem_ld32(taddr + uint32_t(c * 32), v);
-                float b[32];
+                uint32_t bh[16];  // bias, fp16 pairs (zero where absent)
                 if (p.bias && col0 + 32 <= p.N) {
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) vb::d::Vec<__half, 8>::ldg(p.bias + col0 + 8 * q, b + 8 * q);
+                    for (int q = 0; q < 4; ++q) {
+                        const uint4 u = __ldg(reinterpret_cast<const uint4*>(p.bias + col0) + q);
+                        bh[4 * q] = u.x, bh[4 * q + 1] = u.y, bh[4 * q + 2] = u.z, bh[4 * q + 3] = u.w;
+                    }
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) b[i] = (p.bias && col0 + i < p.N) ? __half2float(p.bias[col0 + i]) : 0.f;
+                    for (int i = 0; i < 16; ++i) {
+                        const int c0 = col0 + 2 * i;
+                        const uint32_t lo = (p.bias && c0 < p.N) ? __half_as_ushort(p.bias[c0]) : 0u;
+                        const uint32_t hi = (p.bias && c0 + 1 < p.N) ? __half_as_ushort(p.bias[c0 + 1]) : 0u;
+                        bh[i] = lo | (hi << 16);
+                    }
                 }
+                uint32_t o[16];  // the output sub-row, fp16 pairs
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(v[i] + b[i]);
+                for (int i = 0; i < 16; ++i) {
+                    const float2 x = add_h2(bh[i], make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])));
+                    o[i] = pack_h2(x);  // T(acc + b)
+                }
                 if (EPI == k::kEpiGelu) {
                     if (p.gelu_tanh) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(gelu(v[i], true));
+                        for (int i = 0; i < 16; ++i) {
+                            const float2 x = unpack_h2(o[i]);
+                            o[i] = pack_h2(make_float2(gelu(x.x, true), gelu(x.y, true)));
+                        }
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = rnd<__half>(gelu_as(v[i]));
+                        for (int i = 0; i < 16; ++i) o[i] = pack_h2(gelu_as2(unpack_h2(o[i])));
                     }
                 }
                 if (EPI == k::kEpiResidual) {
                     if (c + 1 < kChunks) issue_res(row0, col0 + 32);  // prefetch the next chunk's residual
                     const uint32_t rbi = r_use & 1;
-                    if (!mbar_wait(&rb[rbi], (r_use >> 1) & 1, abort_flag)) {
+                    if (!mbar_wait(&rb_bar[rbi], (r_use >> 1) & 1, abort_flag)) {
                         ok = false;
+                        if (c + 1 < kChunks) tmem_wait32(nxt);
                         break;
                     }
                     ++r_use;
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        float r8[8];
-                        vb::d::Vec<__half, 8>::load(
-                            reinterpret_cast<const __half*>(rsm + rbi * L::kSub + sw64(lane, j)), r8);
+                        const uint4 u = *reinterpret_cast<const uint4*>(rsm + rbi * L::kSub + sw64(lane, j));
+                        const uint32_t rr[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) v[8 * j + i] = rnd<__half>(v[8 * j + i] + r8[i]);
+                        for (int i = 0; i < 4; ++i) o[4 * j + i] = pack_h2(add_h2(rr[i], unpack_h2(o[4 * j + i])));
+                    }
+                }
+                if (c + 1 < kChunks) {
+                    tmem_wait32(nxt);
+                    if (c + 2 == kChunks) {  // every column of the accumulator is in registers
+                        fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[ab]);
+                        released = true;
                     }
                 }
                 // stage the fp16 sub-tile (row = lane) and store it with one TMA bulk copy
@@ -385,7 +460,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 uint8_t* ob = obuf + obi * L::kSub;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) vb::d::Vec<__half, 8>::store(reinterpret_cast<__half*>(ob + sw64(lane, j)), v + 8 * j);
+                for (int j = 0; j < 4; ++j)
+                    *reinterpret_cast<uint4*>(ob + sw64(lane, j)) = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) {
@@ -394,13 +470,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ++n_out;
             }
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[ab]);
+            if (!released) {
+                fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[ab]);
+            }
             if (!ok) break;
         }
         if (EPI == k::kEpiResidual && lane == 0)  // residual loads issued but not consumed (abort path)
-            for (uint32_t i = r_use; i < r_issue; ++i) mbar_drain(&rb[i & 1], (i >> 1) & 1);
+            for (uint32_t i = r_use; i < r_issue; ++i) mbar_drain(&rb_bar[i & 1], (i >> 1) & 1);
         if (lane == 0) bulk_wait_all();  // every TMA store has finished before the CTA exits
         __syncwarp();
     }
