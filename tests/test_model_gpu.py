@@ -113,13 +113,17 @@ def test_fp16_is_close_to_fp32(seeded_model):
     assert oracle.rel_absmax(y16, y32) <= TOL[vb.FP16]
 
 
+@pytest.mark.parametrize("tiled,chunk", [("all", ""), ("none", ""), ("dec", "64"), ("proc,enc", "")])
 @pytest.mark.parametrize("name", ["t256", "t1024", "c0"])
-def test_tiled_attention_engine_path(name, seeded_model, monkeypatch):
-    """The engine with its attention on the shared-memory-staged tiled kernel (VB_ATT_TILED=1, off by
-    default): same parity bar as the default gather kernel."""
+def test_attention_kernel_choice(name, tiled, chunk, seeded_model, monkeypatch):
+    """The engine with each graph's attention on the shared-memory-staged tiled kernel or the gather
+    kernel (VB_ATT_TILED; the default tiles the decoder only), with and without decoder chunks: the
+    same fp16 parity bar against the reference's goldens for every choice."""
     mp, xp = seeded_model(name)
     x = np.array(st.read(xp)[0]["in.x"])
-    monkeypatch.setenv("VB_ATT_TILED", "1")
+    monkeypatch.setenv("VB_ATT_TILED", tiled)
+    if chunk:
+        monkeypatch.setenv("VB_DEC_CHUNK_ROWS", chunk)
     y = vb.Model.load(mp, precision=vb.FP16).predict_step(x)
     vb.check_device()
     ref = golden(name)["out.y"]

@@ -1,19 +1,18 @@
 // Shared-memory-staged graph attention (fp16): one CTA per (destination tile, 256-channel head group).
 //
-// A tile is a run of consecutive destination rows whose distinct sources number at most kMaxSrc
-// (built at load time, graph.cpp make_tiles). The CTA first pulls, for every distinct source of its
-// tile, the head group's 256-channel slices of K and V (512 bytes each) into shared memory with TMA
-// bulk copies completing on one mbarrier, so all the tile's gathers are in flight at once and each
-// source crosses L2 once per tile; then every warp takes rows of the tile and computes them from
+// A tile is a run of consecutive destination rows with at most kMaxSrc distinct sources, kMaxRows rows
+// and kMaxTileEdges edges (built at load time, graph.cpp make_tiles). The CTA first pulls, with TMA
+// bulk copies completing on one mbarrier, the head group's 256-channel slices of K and V (512 bytes
+// each) of every distinct source and the tile's packed edge records (contiguous in CSR order), so all
+// of the tile's gathers are in flight at once and each source crosses L2 once per tile; meanwhile
+// every warp fetches the q / x_r slices of its first row. Then every warp takes rows of the tile
+// (prefetching its next row's q / x_r) and runs an fp32 online softmax over the row's edges from
 // shared memory (lane = 8 channels = one 16-byte vector, LPH = head_dim / 8 lanes per head):
-//   pass 1  s_e = (<q, k_e> + <W_e^T q, a_e> + <q, b_e>) / sqrt(d) for every edge (log2 domain),
-//           kept in a per-warp score buffer, and the row maximum m;
-//   pass 2  p_e = 2^(s_e - m), l = sum p_e, acc = sum p_e v_e, pa = sum p_e a_e;
+//   s_e = (<q, k_e> + <W_e^T q, a_e> + <q, b_e>) / sqrt(d)   (log2 domain, ex2),
+//   acc = sum p_e v_e, l = sum p_e, pa = sum p_e a_e with the running-maximum rescale;
 //   o = acc / l + W_e (pa / l) + b_e,  out = T(T(o) + x_r).
-// This is the reference's two-pass softmax (cpu/kernels.cpp:236-247) with the edge projection
-// folded; every row's arithmetic depends only on that row, so results do not depend on the tiling
-// (hence not on the GPU partition either). Rows too wide for a tile (heavy rows) go to the gather
-// kernel (attention.cu).
+// Every row's arithmetic depends only on that row, so results do not depend on the tiling (hence not
+// on the GPU partition either). Heavy rows go to the gather kernel (attention.cu).
 #include <cmath>
 #include <string>
 
@@ -27,9 +26,11 @@ using namespace vb::d;
 
 namespace {
 
-constexpr int kHG = 256;          // channels per head group (one CTA)
-constexpr int kMaxSrc = 80;       // distinct sources per tile: 80 x 1 KB of K|V slices
-constexpr int kScoreBytes = 16384;  // per-CTA score buffers (8 warps)
+constexpr int kHG = 256;             // channels per head group (one CTA)
+constexpr int kMaxSrc = 80;          // distinct sources per tile: 80 x 1 KB of K|V slices
+constexpr int kMaxRows = 64;         // rows per tile
+constexpr int kMaxTileEdges = 1024;  // edges per tile: 16 KB of packed records
+constexpr size_t kSmemBytes = size_t(kMaxSrc) * kHG * 2 * 2 + size_t(kMaxTileEdges) * sizeof(EdgeRec);
 constexpr unsigned long long kTimeoutNs = 4000000000ull;
 
 __device__ int g_att_error = 0;
@@ -79,19 +80,21 @@ __device__ __forceinline__ void w8(const float* p, float2 (&f)[4]) {
 }
 
 template <int LPH>
-__global__ void __launch_bounds__(256, 2) attention_tiled_kernel(TileArgs a, float scale_log2, int max_deg) {
+__global__ void __launch_bounds__(256, 2) attention_tiled_kernel(TileArgs a, float scale_log2) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ uint64_t bar;
-    constexpr int kHeads = kHG / (8 * LPH);  // heads per group
+    __shared__ int32_t rp[kMaxRows + 1];
     const int n_hg = a.C / kHG;
     const int t = a.tile0 + int(blockIdx.x) / n_hg, hg = int(blockIdx.x) % n_hg;
     const int4 tl = __ldg(a.tiles + t);  // row0, nrows, src0, nsrc
     const int ch0 = hg * kHG;
     __half* Ks = reinterpret_cast<__half*>(sm);
     __half* Vs = Ks + kMaxSrc * kHG;
-    float* Sbuf = reinterpret_cast<float*>(Vs + kMaxSrc * kHG);
+    const EdgeRec* Es = reinterpret_cast<const EdgeRec*>(Vs + kMaxSrc * kHG);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e0 = __ldg(a.row_ptr + tl.x), ne = __ldg(a.row_ptr + tl.x + tl.y) - e0;
 
+    for (int i = threadIdx.x; i <= tl.y; i += blockDim.x) rp[i] = __ldg(a.row_ptr + tl.x + i) - e0;
     if (threadIdx.x == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bar)));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -100,15 +103,30 @@ __global__ void __launch_bounds__(256, 2) attention_tiled_kernel(TileArgs a, flo
     if (warp == 0) {
         if (lane == 0)
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&bar)),
-                         "r"(uint32_t(tl.w) * 2u * kHG * 2u)
+                         "r"(uint32_t(tl.w) * 2u * kHG * 2u + uint32_t(ne) * uint32_t(sizeof(EdgeRec)))
                          : "memory");
         __syncwarp();
+        if (lane == 0 && ne > 0)
+            bulk_g2s(const_cast<EdgeRec*>(Es), a.edges + e0, uint32_t(ne) * uint32_t(sizeof(EdgeRec)), &bar);
         for (int i = lane; i < tl.w; i += 32) {
             const int64_t s = __ldg(a.srcs + tl.z + i);
             bulk_g2s(Ks + i * kHG, a.k + s * a.ldkv + ch0, kHG * 2, &bar);
             bulk_g2s(Vs + i * kHG, a.v + s * a.ldkv + ch0, kHG * 2, &bar);
         }
     }
+    // the first row's q / x_r slices and the edge weights of this lane's channels, while the copies fly
+    const int C = a.C;
+    const int ch = ch0 + lane * 8;
+    int r = warp;
+    uint4 qn = make_uint4(0, 0, 0, 0), xn = qn;
+    if (r < tl.y) {
+        const int64_t lr = int64_t(tl.x + r) - a.dst_lo;
+        qn = __ldg(reinterpret_cast<const uint4*>(a.q + lr * a.ldq + ch));
+        xn = __ldg(reinterpret_cast<const uint4*>(a.xr + lr * a.ldxr + ch));
+    }
+    float2 w0[4], w1[4], w2[4], wb[4];
+    w8(a.w_e + ch, w0), w8(a.w_e + C + ch, w1), w8(a.w_e + 2 * C + ch, w2), w8(a.w_e + 3 * C + ch, wb);
+
     // bounded wait for the slices; on timeout flag the error and skip the compute (the CTA's copies
     // are then the only thing left in flight, and the next wait covers them)
     bool ok = mbar_test(&bar, 0);
@@ -122,20 +140,18 @@ __global__ void __launch_bounds__(256, 2) attention_tiled_kernel(TileArgs a, flo
         return;
     }
 
-    const int C = a.C;
-    const int ch = ch0 + lane * 8;
-    const int head = lane / LPH;  // head within the group
-    float* sc = Sbuf + warp * (kScoreBytes / 8 / 4);  // this warp's [max_deg][kHeads] scores
-    for (int r = warp; r < tl.y; r += 8) {
-        const int row = tl.x + r;
-        const int64_t lr = int64_t(row) - a.dst_lo;  // local q / x_r / out row
-        const int beg = __ldg(a.row_ptr + row), end = __ldg(a.row_ptr + row + 1);
+    for (; r < tl.y; r += 8) {
+        const int64_t lr = int64_t(tl.x + r) - a.dst_lo;  // local q / x_r / out row
         float2 q[4];
-        h8(__ldg(reinterpret_cast<const uint4*>(a.q + lr * a.ldq + ch)), q);
+        h8(qn, q);
+        const uint4 xu = xn;
+        if (r + 8 < tl.y) {  // prefetch the next row's slices
+            const int64_t ln = lr + 8;
+            qn = __ldg(reinterpret_cast<const uint4*>(a.q + ln * a.ldq + ch));
+            xn = __ldg(reinterpret_cast<const uint4*>(a.xr + ln * a.ldxr + ch));
+        }
         float qe0, qe1, qe2, qb;
         {
-            float2 w0[4], w1[4], w2[4], wb[4];
-            w8(a.w_e + ch, w0), w8(a.w_e + C + ch, w1), w8(a.w_e + 2 * C + ch, w2), w8(a.w_e + 3 * C + ch, wb);
             float2 s0 = make_float2(0.f, 0.f), s1 = s0, s2 = s0, sb = s0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -145,46 +161,41 @@ __global__ void __launch_bounds__(256, 2) attention_tiled_kernel(TileArgs a, flo
             qe0 = head_sum<LPH>(s0.x + s0.y), qe1 = head_sum<LPH>(s1.x + s1.y);
             qe2 = head_sum<LPH>(s2.x + s2.y), qb = head_sum<LPH>(sb.x + sb.y);
         }
-        // pass 1: scores and the row maximum
-        float m = -INFINITY;
+        const int beg = rp[r], end = rp[r + 1];
+        float m = -INFINITY, l = 0.f, pa0 = 0.f, pa1 = 0.f, pa2 = 0.f;
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll 2
         for (int e = beg; e < end; ++e) {
-            const float4 rec = __ldg(reinterpret_cast<const float4*>(a.edges + e));
+            const float4 rec = *reinterpret_cast<const float4*>(Es + e);
             const int slot = __float_as_int(rec.w);
-            float2 kf[4];
+            float2 kf[4], vf[4];
             h8(*reinterpret_cast<const uint4*>(Ks + slot * kHG + lane * 8), kf);
+            h8(*reinterpret_cast<const uint4*>(Vs + slot * kHG + lane * 8), vf);
             float2 d2 = make_float2(0.f, 0.f);
 #pragma unroll
             for (int c = 0; c < 4; ++c) d2 = __ffma2_rn(q[c], kf[c], d2);
             const float dot = head_sum<LPH>(d2.x + d2.y);
             const float se = fmaf(qe2, rec.z, fmaf(qe1, rec.y, qe0 * rec.x));
             const float s = ((dot + se) + qb) * scale_log2;
-            if (lane % LPH == 0) sc[(e - beg) * kHeads + head] = s;
-            m = fmaxf(m, s);
-        }
-        __syncwarp();
-        // pass 2: weights and the weighted sums
-        float l = 0.f, pa0 = 0.f, pa1 = 0.f, pa2 = 0.f;
-        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-        for (int e = beg; e < end; ++e) {
-            const float4 rec = __ldg(reinterpret_cast<const float4*>(a.edges + e));
-            const int slot = __float_as_int(rec.w);
-            const float p = ex2(sc[(e - beg) * kHeads + head] - m);
-            l += p;
-            float2 vf[4];
-            h8(*reinterpret_cast<const uint4*>(Vs + slot * kHG + lane * 8), vf);
-            const float2 p2 = make_float2(p, p);
+            const float mn = fmaxf(m, s);
+            const float corr = ex2(m - mn), p = ex2(s - mn);
+            m = mn;
+            l = fmaf(l, corr, p);
+            pa0 = fmaf(pa0, corr, p * rec.x), pa1 = fmaf(pa1, corr, p * rec.y), pa2 = fmaf(pa2, corr, p * rec.z);
+            const float2 c2 = make_float2(corr, corr), p2 = make_float2(p, p);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) acc[c] = __ffma2_rn(p2, vf[c], acc[c]);
-            pa0 = fmaf(p, rec.x, pa0), pa1 = fmaf(p, rec.y, pa1), pa2 = fmaf(p, rec.z, pa2);
+            for (int c = 0; c < 4; ++c) acc[c] = __ffma2_rn(p2, vf[c], __fmul2_rn(acc[c], c2));
         }
-        __syncwarp();
         float xr[8], o[8];
-        Vec<__half, 8>::ldg(a.xr + lr * a.ldxr + ch, xr);
+        {
+            float2 xf[4];
+            h8(xu, xf);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) xr[2 * c] = xf[c].x, xr[2 * c + 1] = xf[c].y;
+        }
         if (end > beg) {
             const float inv = 1.0f / l;
             const float p0 = pa0 * inv, p1 = pa1 * inv, p2 = pa2 * inv;
-            float2 w0[4], w1[4], w2[4], wb[4];
-            w8(a.w_e + ch, w0), w8(a.w_e + C + ch, w1), w8(a.w_e + 2 * C + ch, w2), w8(a.w_e + 3 * C + ch, wb);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 o[2 * c] = fmaf(acc[c].x, inv, fmaf(w2[c].x, p2, fmaf(w1[c].x, p1, w0[c].x * p0)) + wb[c].x);
@@ -198,13 +209,13 @@ __global__ void __launch_bounds__(256, 2) attention_tiled_kernel(TileArgs a, flo
         for (int c = 0; c < 8; ++c) o[c] = rnd<__half>(rnd<__half>(o[c]) + xr[c]);
         Vec<__half, 8>::store(a.out + lr * a.ldo + ch, o);
     }
-    (void)max_deg;
 }
 
 }  // namespace
 
 int tiled_max_src() { return kMaxSrc; }
-int tiled_max_deg(int head_dim) { return kScoreBytes / 8 / 4 / (kHG / head_dim); }
+int tiled_max_rows() { return kMaxRows; }
+int tiled_max_edges() { return kMaxTileEdges; }
 bool tiled_supported(int C, int head_dim) {
     return C % kHG == 0 && head_dim % 8 == 0 && head_dim <= kHG && (head_dim / 8 & (head_dim / 8 - 1)) == 0;
 }
@@ -213,9 +224,8 @@ void attention_tiled(const TileArgs& a, float scale_log2, cudaStream_t s) {
     if (a.ntiles <= 0) return;
     if (!tiled_supported(a.C, a.head_dim)) fail(kUnsupported, "tiled attention: unsupported layout");
     const int lph = a.head_dim / 8;
-    const size_t smem = size_t(kMaxSrc) * kHG * 2 * 2 + kScoreBytes;
+    const size_t smem = kSmemBytes;
     const unsigned grid = unsigned(a.ntiles * (a.C / kHG));
-    const int md = tiled_max_deg(a.head_dim);
 #define VB_TA(L)                                                                                               \
     do {                                                                                                       \
         static bool cfg = false;                                                                               \
@@ -224,7 +234,7 @@ void attention_tiled(const TileArgs& a, float scale_log2, cudaStream_t s) {
                                          int(smem)));                                                          \
             cfg = true;                                                                                        \
         }                                                                                                      \
-        attention_tiled_kernel<L><<<grid, 256, smem, s>>>(a, scale_log2, md);                                  \
+        attention_tiled_kernel<L><<<grid, 256, smem, s>>>(a, scale_log2);                                      \
     } while (0)
     switch (lph) {
         case 1: VB_TA(1); break;

@@ -339,7 +339,7 @@ int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* att
         g.n_edges = g.row_ptr.back();
         g.src.assign(src, src + g.n_edges);
         g.attr.assign(attr, attr + g.n_edges * A);
-        vb::TilePlan tp = vb::make_tiles(g, vb::k::tiled_max_src(), 64, vb::k::tiled_max_deg(head_dim), 0, true);
+        vb::TilePlan tp = vb::make_tiles(g, vb::k::tiled_max_src(), vb::k::tiled_max_rows(), vb::k::tiled_max_edges(), 0, true);
         auto t = std::make_unique<vb_tiles>();
         auto up = [](vb::DeviceBuffer& b, const void* h, size_t n) {
             b.alloc(std::max<size_t>(n, 16));

@@ -79,7 +79,7 @@ std::vector<EdgeRec> pack_edges(const CsrGraph& g, bool round_fp16) {
     return out;
 }
 
-TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_deg, int64_t chunk_rows, bool round_fp16) {
+TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges, int64_t chunk_rows, bool round_fp16) {
     TilePlan t;
     t.edges = pack_edges(g, round_fp16);
     std::vector<int32_t> slot(size_t(std::max<int64_t>(g.n_src, 1)), -1);  // source -> slot in the open tile
@@ -119,12 +119,13 @@ TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_deg, i
             own = int(std::unique(u.begin(), u.end()) - u.begin());
         }
         for (int32_t s : fresh) slot[size_t(s)] = -1;
-        if (own > max_src || e - b > max_deg) {  // heavy row: the gather kernel takes it
+        if (own > max_src || e - b > max_edges) {  // heavy row: the gather kernel takes it
             close(d);
             t.heavy.push_back(int32_t(d));
             continue;
         }
-        const bool fits = row0 >= 0 && int(open.size() + fresh.size()) <= max_src && d - row0 < max_rows;
+        const bool fits = row0 >= 0 && int(open.size() + fresh.size()) <= max_src && d - row0 < max_rows &&
+                          e - g.row_ptr[size_t(row0)] <= max_edges;
         if (!fits) {
             close(d);
             row0 = int32_t(d);

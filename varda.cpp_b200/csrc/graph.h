@@ -50,6 +50,9 @@ struct TilePlan {
     std::vector<int32_t> heavy;                    // rows left to the gather kernel
     int max_nsrc = 0;
 };
-TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_deg, int64_t chunk_rows, bool round_fp16);
+// Tiles of consecutive destination rows with at most max_src distinct sources, max_rows rows and
+// max_edges edges; a row with more than max_src distinct sources or more than max_edges edges is heavy
+// (left to the gather kernel). Tiles never span a multiple of chunk_rows (0: no chunking).
+TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges, int64_t chunk_rows, bool round_fp16);
 
 }  // namespace vb

@@ -128,7 +128,8 @@ struct TileArgs {
 void attention_tiled(const TileArgs& a, float scale_log2, cudaStream_t s);
 bool tiled_supported(int C, int head_dim);
 int tiled_max_src();
-int tiled_max_deg(int head_dim);
+int tiled_max_rows();
+int tiled_max_edges();
 // Synchronises; reads and clears the flag a timed-out wait of the tiled attention sets.
 int take_attention_error();
 
