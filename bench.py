@@ -283,6 +283,19 @@ def run_rollout(args, rank, world, local_rank):
                 n_launch_timed=vb.launch_count() - n_launch0)
 
 
+TRAFFIC = os.path.join(HERE, "profiles", "c1_traffic.json")
+
+
+def traffic_for(kind):
+    """DRAM bytes (read + write) per launch of a kernel class of the C1 step, from the committed ncu
+    launch-list capture summarised in profiles/c1_traffic.json (None when absent)."""
+    if not os.path.exists(TRAFFIC):
+        return None, None
+    d = json.load(open(TRAFFIC))
+    rec = d.get("per_launch", {}).get(kind)
+    return (rec, d.get("source")) if rec is not None else (None, None)
+
+
 def summarise(prof, pk, src):
     by = {}
     for r in prof:
@@ -295,20 +308,22 @@ def summarise(prof, pk, src):
         d["bytes"] += r["bytes"]
         d["n"] += 1
     total = sum(d["ms"] for d in by.values())
-    dom = max(by, key=lambda k: by[k]["ms"])
+    # the dominant compute kernel class (halo_* records of a sharded run are communication and waits)
+    dom = max((k for k in by if not k.startswith("halo")), key=lambda k: by[k]["ms"])
     d = by[dom]
     if d["flop"] > 0:
         ach = d["flop"] / (d["ms"] * 1e-3) / 1e12
         peak = pk["bf16_tflops_sustained"]
         roof = {"kernel": dom, "bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(ach / peak, 4), "traffic": None, "launches_per_step": d["n"],
-                "share": round(d["ms"] / total, 4), "peak_source": f"{src} (sustained bf16, kernel inside a long step)"}
+                "frac": round(ach / peak, 4), "traffic": traffic_for(dom)[0], "launches_per_step": d["n"],
+                "share": round(d["ms"] / total, 4), "peak_source": f"{src} (sustained bf16, kernel inside a long step)",
+                "traffic_source": traffic_for(dom)[1], "flop_per_launch": d["flop"] / d["n"]}
     else:
         ach = d["bytes"] / (d["ms"] * 1e-3) / 1e9
         peak = pk["hbm_gbs"]
         roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(ach / peak, 4), "traffic": None, "launches_per_step": d["n"],
-                "share": round(d["ms"] / total, 4), "peak_source": src}
+                "frac": round(ach / peak, 4), "traffic": traffic_for(dom)[0], "launches_per_step": d["n"],
+                "share": round(d["ms"] / total, 4), "peak_source": src, "traffic_source": traffic_for(dom)[1]}
     att = by.get("attention proc")
     edge = None
     if att:
@@ -316,7 +331,8 @@ def summarise(prof, pk, src):
         gbs = att["bytes"] / (att["ms"] * 1e-3) / 1e9
         edge = {"kernel": "attention proc", "bound": "hbm", "ms_per_launch": round(per, 4),
                 "bytes_per_launch": att["bytes"] / att["n"], "achieved": round(gbs, 1), "peak": pk["hbm_gbs"],
-                "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None, "peak_source": src}
+                "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": traffic_for("attention proc")[0],
+                "peak_source": src, "traffic_source": traffic_for("attention proc")[1]}
     shares = {k: {"ms": round(v["ms"], 3), "share": round(v["ms"] / total, 4), "launches": v["n"]}
               for k, v in sorted(by.items(), key=lambda kv: -kv[1]["ms"])}
     return roof, edge, shares, total

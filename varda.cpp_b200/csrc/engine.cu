@@ -18,6 +18,7 @@
 #include <functional>
 #include <memory>
 #include <string>
+#include <thread>
 #include <type_traits>
 #include <vector>
 
@@ -58,6 +59,21 @@ bool tiled_for(const std::string& graph, const char* dflt) {
         b = e + 1;
     }
     return false;
+}
+
+// dst[i, 0:n] = src_rows[idx[i]] (row width n floats, base row stride `stride` floats) for
+// i < count, on a few host threads when the halo is large (the sharded input and forcing uploads).
+void gather_host_rows(float* dst, const float* src, int64_t stride, const int32_t* idx, int64_t count, int64_t n) {
+    auto run = [&](int64_t b, int64_t e) {
+        for (int64_t i = b; i < e; ++i)
+            std::memcpy(dst + i * n, src + int64_t(idx[i]) * stride, size_t(n) * sizeof(float));
+    };
+    const int64_t kPerThread = 32768;
+    const int nt = int(std::min<int64_t>(8, (count + kPerThread - 1) / kPerThread));
+    if (nt <= 1) return run(0, count);
+    std::vector<std::thread> ts;
+    for (int t = 0; t < nt; ++t) ts.emplace_back(run, count * t / nt, count * (t + 1) / nt);
+    for (auto& th : ts) th.join();
 }
 
 template <class T> struct Lin {
@@ -954,9 +970,7 @@ void Engine<T>::upload_input(const float* x, cudaStream_t s) {
         if (n_eh_) {
             float* stage = x_halo_host_ + int64_t(t) * n_eh_ * V_in_;
             VB_CUDA(cudaStreamSynchronize(s));  // the staging buffer may still feed a previous copy
-            for (int64_t i = 0; i < n_eh_; ++i)
-                std::memcpy(stage + i * V_in_, x + (int64_t(t) * G_ + plan_.enc_halo[size_t(i)]) * V_in_,
-                            size_t(V_in_) * sizeof(float));
+            gather_host_rows(stage, x + int64_t(t) * G_ * V_in_, V_in_, plan_.enc_halo.data(), n_eh_, V_in_);
             VB_CUDA(cudaMemcpyAsync(x_dev_ + (int64_t(t) * Gx_ + Gl_) * V_in_, stage,
                                     size_t(n_eh_ * V_in_) * sizeof(float), cudaMemcpyHostToDevice, s));
         }
@@ -1141,9 +1155,7 @@ void Engine<T>::rollout(const float* x0, int n, const float* forcings, float* y,
         const int b = st & 1;
         const float* fs = forcings + int64_t(st) * G_ * F;
         std::memcpy(ro_.hf[b], fs + plan_.g_lo * F, size_t(Gl_ * F) * sizeof(float));
-        for (int64_t i = 0; i < n_eh_; ++i)
-            std::memcpy(ro_.hf[b] + (Gl_ + i) * F, fs + int64_t(plan_.enc_halo[size_t(i)]) * F,
-                        size_t(F) * sizeof(float));
+        gather_host_rows(ro_.hf[b] + Gl_ * F, fs, F, plan_.enc_halo.data(), n_eh_, F);
         if (st >= 2) VB_CUDA(cudaStreamWaitEvent(ro_.h2d, ro_.end[size_t(st - 2)], 0));  // step st-2 read f[b]
         VB_CUDA(cudaMemcpyAsync(ro_.f[b].get(), ro_.hf[b], size_t(Gx_ * F) * sizeof(float), cudaMemcpyHostToDevice,
                                 ro_.h2d));

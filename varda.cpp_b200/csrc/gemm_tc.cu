@@ -200,17 +200,16 @@ __device__ __forceinline__ float rcpf(float x) {
     return y;
 }
 
-// Shared memory: the A/W stage ring, then per epilogue warp two 2 KB output staging buffers (and, for
-// the residual epilogue, two 2 KB residual buffers), then the mbarriers.
+// Shared memory: the A/W stage ring, then per epilogue warp two 2 KB output staging buffers, then the
+// mbarriers.
 template <int BN, int STAGES, int EPI> struct Layout {
     static constexpr int kA = BM * BK * 2;  // bytes per A stage
     static constexpr int kB = BN * BK * 2;
     static constexpr int kTiles = STAGES * (kA + kB);
     static constexpr int kSub = 32 * 32 * 2;  // one 32 x 32 fp16 sub-tile
     static constexpr int kOut = kEpiWarps * 2 * kSub;
-    static constexpr int kRes = EPI == k::kEpiResidual ? kEpiWarps * 2 * kSub : 0;
-    static constexpr int kBars = (2 * STAGES + 5 + 2 * kEpiWarps) * 8;
-    static constexpr int kSmem = 1024 + kTiles + kOut + kRes + kBars + 16;  // 1024: alignment slack
+    static constexpr int kBars = (2 * STAGES + 5) * 8;
+    static constexpr int kSmem = 1024 + kTiles + kOut + kBars + 16;  // 1024: alignment slack
     static_assert(kSmem <= 232448, "shared memory over the 227 KB per-CTA limit");
 };
 
@@ -254,22 +253,20 @@ __device__ __forceinline__ int sw64(int r, int j) { return r * 64 + ((j ^ ((r >>
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, Params p) {
+                   const __grid_constant__ CUtensorMap tmC, Params p) {
     using L = Layout<BN, STAGES, EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * L::kA;
     uint8_t* sOut = smem + L::kTiles;
-    uint8_t* sRes = sOut + L::kOut;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sRes + L::kRes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + L::kOut);
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
     uint64_t* tfull = bars + 2 * STAGES;
     uint64_t* tempty = bars + 2 * STAGES + 2;
     uint64_t* drain = bars + 2 * STAGES + 4;
-    uint64_t* rbar = bars + 2 * STAGES + 5;  // [kEpiWarps][2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5 + 2 * kEpiWarps);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -277,7 +274,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
         for (int b = 0; b < 2; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], kEpiWarps);
         mbar_init(drain, 1);
-        for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -357,19 +353,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int half = ew >> 2;  // which half of the BN columns
         constexpr int kChunks = BN / 64;  // 32-column chunks per half
         uint8_t* obuf = sOut + ew * 2 * L::kSub;
-        uint8_t* rsm = sRes + ew * 2 * L::kSub;
-        uint64_t* rb_bar = rbar + 2 * ew;
-        uint32_t n_out = 0;                 // output staging uses so far (buffer = count & 1)
-        uint32_t r_issue = 0, r_use = 0;    // residual sub-tile loads issued / consumed (buffer = i & 1)
+        uint32_t n_out = 0;  // output staging uses so far (buffer = count & 1)
         int it = 0;
-        auto issue_res = [&](int row0, int col0) {  // residual sub-tile into the next buffer (lane 0)
-            if (lane == 0) {
-                const uint32_t b = r_issue & 1;
-                fence_async_smem();
-                mbar_expect_tx(&rb_bar[b], uint32_t(L::kSub));
-                tma_load_2d(rsm + b * L::kSub, &tmR, &rb_bar[b], col0, row0);
+        // this lane's row of the residual, 32 columns from col0, as fp16 pairs (zero out of bounds)
+        auto load_res = [&](int row, int col0, uint32_t(&rr)[16]) {
+            if (row < p.M && col0 + 32 <= p.N) {
+                const uint4* src = reinterpret_cast<const uint4*>(p.R + int64_t(row) * p.ldr + col0);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 u = __ldg(src + q);
+                    rr[4 * q] = u.x, rr[4 * q + 1] = u.y, rr[4 * q + 2] = u.z, rr[4 * q + 3] = u.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c0 = col0 + 2 * i;
+                    const __half* r = p.R + int64_t(row) * p.ldr;
+                    const uint32_t lo = (row < p.M && c0 < p.N) ? __half_as_ushort(r[c0]) : 0u;
+                    const uint32_t hi = (row < p.M && c0 + 1 < p.N) ? __half_as_ushort(r[c0 + 1]) : 0u;
+                    rr[i] = lo | (hi << 16);
+                }
             }
-            ++r_issue;
         };
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
             const int ab = it & 1;
@@ -377,7 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int mb = tile / n_n, nb = tile - mb * n_n;
             const int row0 = mb * BM + lg * 32;
             const int colh = nb * BN + half * (BN / 2);
-            if (EPI == k::kEpiResidual) issue_res(row0, colh);
+            // the first chunk's residual loads fly while the accumulator is being computed
+            uint32_t resa[16], resb[16];
+            if (EPI == k::kEpiResidual) load_res(row0 + lane, colh, resa);
             if (!mbar_wait(&tfull[ab], ap, abort_flag)) break;
             fence_after();
             const uint32_t taddr = tmem + (uint32_t(lg * 32) << 16) + uint32_t(ab * BN + half * (BN / 2));
@@ -392,8 +398,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < kChunks; ++c) {
                 uint32_t(&cur)[32] = (c & 1) ? rb : ra;
                 uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+                uint32_t(&rcur)[16] = (c & 1) ? resb : resa;
+                uint32_t(&rnxt)[16] = (c & 1) ? resa : resb;
                 if (c + 1 < kChunks) tmem_ld32_async(taddr + uint32_t((c + 1) * 32), nxt);
                 const int col0 = colh + c * 32;
+                if (EPI == k::kEpiResidual && c + 1 < kChunks) load_res(row0 + lane, col0 + 32, rnxt);
                 uint32_t bh[16];  // bias, fp16 pairs (zero where absent)
                 if (p.bias && col0 + 32 <= p.N) {
 #pragma unroll
@@ -429,21 +438,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (EPI == k::kEpiResidual) {
-                    if (c + 1 < kChunks) issue_res(row0, col0 + 32);  // prefetch the next chunk's residual
-                    const uint32_t rbi = r_use & 1;
-                    if (!mbar_wait(&rb_bar[rbi], (r_use >> 1) & 1, abort_flag)) {
-                        ok = false;
-                        if (c + 1 < kChunks) tmem_wait32(nxt);
-                        break;
-                    }
-                    ++r_use;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint4 u = *reinterpret_cast<const uint4*>(rsm + rbi * L::kSub + sw64(lane, j));
-                        const uint32_t rr[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) o[4 * j + i] = pack_h2(add_h2(rr[i], unpack_h2(o[4 * j + i])));
-                    }
+                    for (int i = 0; i < 16; ++i) o[i] = pack_h2(add_h2(rcur[i], unpack_h2(o[i])));  // T(T(acc+b)+r)
                 }
                 if (c + 1 < kChunks) {
                     tmem_wait32(nxt);
@@ -477,8 +473,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok) break;
         }
-        if (EPI == k::kEpiResidual && lane == 0)  // residual loads issued but not consumed (abort path)
-            for (uint32_t i = r_use; i < r_issue; ++i) mbar_drain(&rb_bar[i & 1], (i >> 1) & 1);
         if (lane == 0) bulk_wait_all();  // every TMA store has finished before the CTA exits
         __syncwarp();
     }
@@ -540,24 +534,23 @@ void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
     }
     const CUtensorMap ta = make_map(a.A, a.M, a.K, a.lda, BM);
     const CUtensorMap tb = make_map(a.W, a.N, a.K, a.ldw, BN);
-    // 32 x 32 sub-tiles of the output (and residual), 64-byte swizzle: the epilogue's TMA stores / loads
+    // 32 x 32 sub-tiles of the output, 64-byte swizzle: the epilogue's TMA stores
     const CUtensorMap tc = make_map(a.C, a.M, a.N, a.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-    const CUtensorMap tr = EPI == k::kEpiResidual ? make_map(a.R, a.M, a.N, a.ldr, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) : tc;
     Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0};
     const int64_t tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
     const int grid = int(std::min<int64_t>(tiles, sm_count()));
-    gemm_tc_kernel<BN, STAGES, EPI><<<grid, kThreads, L::kSmem, s>>>(ta, tb, tc, tr, p);
+    gemm_tc_kernel<BN, STAGES, EPI><<<grid, kThreads, L::kSmem, s>>>(ta, tb, tc, p);
     VB_LAUNCH();
 }
 
 // stage counts: as deep as the 227 KB of shared memory allows next to the epilogue staging
 template <int BN>
 void dispatch_epi(const k::GemmArgs<__half>& a, cudaStream_t s) {
-    constexpr int S = BN == 256 ? 4 : 6, SR = BN == 256 ? 3 : 5;
+    constexpr int S = BN == 256 ? 4 : 6;
     switch (a.epi) {
         case k::kEpiBias: launch<BN, S, k::kEpiBias>(a, s); break;
         case k::kEpiGelu: launch<BN, S, k::kEpiGelu>(a, s); break;
-        case k::kEpiResidual: launch<BN, SR, k::kEpiResidual>(a, s); break;
+        case k::kEpiResidual: launch<BN, S, k::kEpiResidual>(a, s); break;
         default: fail(kInvalidArgument, "gemm: unknown epilogue");
     }
 }

@@ -2,6 +2,8 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
+#include <string>
 #include <numeric>
 
 #include "common.h"
@@ -105,32 +107,26 @@ ShardPlan make_plan(const Config& c, const CsrGraph& enc, const CsrGraph& proc, 
         p.g_split = {0, G};
     } else {
         if (H < world) fail(kUnsupported, "shard plan: fewer hidden nodes than GPUs");
-        // cost model (seconds-equivalents): GEMM FLOPs at ~1.2 PFLOP/s, edge gathers at ~5 TB/s
+        if (G < world) fail(kUnsupported, "shard plan: fewer data nodes than GPUs");
+        // Cost model (seconds-equivalents): GEMM FLOPs at ~1.2 PFLOP/s, edge gathers at ~5 TB/s. The step
+        // is a chain of phases with a halo exchange between them (encoder, 16 processor blocks,
+        // decoder), so each phase is balanced on its own: hidden rows on the encoder-destination and
+        // processor work, data rows on the encoder-source and decoder work.
         const double C = c.num_channels, M = c.mlp_hidden, F = double(align_up(size_t(c.src_features()), 8));
         const double P = c.num_processor_layers, Vd = c.dec_out_features();
         const double kF = 1.0 / 1.2e15, kB = 1.0 / 5e12, row_bytes = 2.0 * C * 2.0;
         const double flop_h = 2 * C * 2 * C + 2 * C * C + 4 * C * M + P * (2 * C * 4 * C + 2 * C * C + 4 * C * M) +
                               2 * C * 2 * C;
         const double flop_g = 2 * F * C + 2 * C * 2 * C + 2 * F * C + 2 * C * 2 * C + 2 * C * C + 4 * C * M + 2 * C * Vd;
-        std::vector<double> w(size_t(H), flop_h * kF);
-        for (int64_t h = 0; h < H; ++h) {
-            w[size_t(h)] += P * (proc.row_ptr[size_t(h + 1)] - proc.row_ptr[size_t(h)]) * row_bytes * 0.5 * kB;
-            w[size_t(h)] += (enc.row_ptr[size_t(h + 1)] - enc.row_ptr[size_t(h)]) * row_bytes * kB;
-        }
-        // a data node is charged to the hidden node of its first decoder edge (its nearest source)
-        std::vector<int32_t> pref(size_t(G), -1);
-        int32_t last = 0;
-        for (int64_t g = 0; g < G; ++g) {
-            const int32_t b = dec.row_ptr[size_t(g)], e = dec.row_ptr[size_t(g + 1)];
-            if (e > b) last = dec.src[size_t(b)];
-            pref[size_t(g)] = last;
-            w[size_t(last)] += flop_g * kF + (e - b) * row_bytes * kB;
-        }
-        p.h_split = balanced_split(w, world);
-        std::vector<int64_t> count(size_t(world), 0);
-        for (int64_t g = 0; g < G; ++g) ++count[size_t(owner_of(p.h_split, pref[size_t(g)]))];
-        p.g_split.assign(size_t(world + 1), 0);
-        for (int r = 0; r < world; ++r) p.g_split[size_t(r + 1)] = p.g_split[size_t(r)] + count[size_t(r)];
+        std::vector<double> wh(static_cast<size_t>(H)), wg(static_cast<size_t>(G));
+        for (int64_t h = 0; h < H; ++h)
+            wh[size_t(h)] = flop_h * kF +
+                            P * (proc.row_ptr[size_t(h + 1)] - proc.row_ptr[size_t(h)]) * row_bytes * 0.5 * kB +
+                            (enc.row_ptr[size_t(h + 1)] - enc.row_ptr[size_t(h)]) * row_bytes * kB;
+        for (int64_t g = 0; g < G; ++g)
+            wg[size_t(g)] = flop_g * kF + (dec.row_ptr[size_t(g + 1)] - dec.row_ptr[size_t(g)]) * row_bytes * kB;
+        p.h_split = balanced_split(wh, world);
+        p.g_split = balanced_split(wg, world);
     }
     p.h_lo = p.h_split[size_t(rank)], p.h_hi = p.h_split[size_t(rank + 1)];
     p.g_lo = p.g_split[size_t(rank)], p.g_hi = p.g_split[size_t(rank + 1)];

@@ -2,11 +2,13 @@
 // GPU. The reference runs one GPU only; this is new (no reference counterpart).
 //
 // Partition. Hidden nodes are split into `world` contiguous index ranges of equal estimated cost
-// (FLOPs of the node-wise GEMMs and bytes of the edge gathers, from the config dims and in-degrees;
-// the cost of a data node is charged to the hidden node its first decoder edge comes from). A data
-// node belongs to the rank of that hidden node; data ranges are contiguous with those counts. With
-// spatially ordered node numbering (the synthetic models use a Morton curve) the ranges are compact
-// regions and the halos small; any numbering is correct.
+// (FLOPs of the encoder-destination and processor GEMMs plus edge-gather bytes, from the config dims
+// and in-degrees), and data nodes, independently, into contiguous ranges of equal estimated cost
+// (encoder-source and decoder GEMMs plus decoder gathers). The forward pass is a chain of phases with
+// a halo exchange between each (encoder, every processor block, decoder), so every phase is balanced
+// on its own rather than each rank's total. With spatially ordered node numbering (the synthetic
+// models use a Morton curve) the ranges are compact regions and the halos small; any numbering is
+// correct.
 //
 // Halos. Rank r computes the node-wise layers of its own rows only:
 //   processor  K|V rows of remote hidden sources, exchanged once per block (NCCL send/recv);
