@@ -286,7 +286,7 @@ void attention(const AttnArgs<T>& a, cudaStream_t s) {
         case 32: VB_ATT(CPL, 32, U, MB); break;       \
     }
     if constexpr (sizeof(T) == 2) {
-        if (cpl == 16 && lph == 4 && variant) {
+        if (cpl == 16 && lph == 4 && variant >= 1 && variant <= 4) {
             switch (variant) {
                 case 1: VB_ATT(16, 4, 2, 1); break;
                 case 2: VB_ATT(16, 4, 1, 2); break;
