@@ -256,3 +256,39 @@ def test_attention_tiled(C, heads, A):
     assert err <= 2e-3, f"rel_absmax {err:.3e}"
     zero = np.where(rp[1:] == rp[:-1])[0]
     assert np.array_equal(got[zero], xr[zero, :C]), "zero in-degree must give x_r exactly"
+
+
+@pytest.mark.parametrize("variant", ["5", "6", "7", "8"])
+@pytest.mark.parametrize("C,heads", [(1024, 16), (2048, 8), (1024, 32)])
+def test_attention_variants(C, heads, variant, monkeypatch):
+    """The gather kernel's alternative launch shapes (VB_ATT_VARIANT: 8 channels per lane at 3 or 4
+    blocks per SM; one warp per 1024 channels at 1 or 2 blocks per SM) against the float64 reference,
+    with the fp16 bar of the default shape, zero in-degree giving x_r exactly."""
+    monkeypatch.setenv("VB_ATT_VARIANT", variant)
+    dt, A = vb.FP16, 3
+    rng = np.random.default_rng(C + heads + int(variant))
+    hd = C // heads
+    n_src, n_dst, ld = 131, 97, C + 8
+    ei, ea = make_graph(rng, n_src, n_dst, A)
+    rp, src, _, attr = vb.build_csr(ei, ea, n_src, n_dst)
+    attr = rounded(attr, dt)
+    q, k, v, xr = (rounded(rng.normal(size=(n, ld)), dt) for n in (n_dst, n_src, n_src, n_dst))
+    we = rounded(rng.normal(size=(C, A)) * 0.5, dt)
+    be = rounded(rng.normal(size=C) * 0.5, dt)
+    w4 = np.zeros((4, C), np.float32)
+    w4[:A] = we.T
+    w4[3] = be
+    edges = vb.pack_edges(src, attr, round_fp16=False)
+    T = tname(dt)
+    d_rp, d_ed, d_w = dev(rp, torch.int32), dev(edges, torch.float32), dev(w4, torch.float32)
+    d_q, d_k, d_v, d_x = dev(q, T), dev(k, T), dev(v, T), dev(xr, T)
+    out = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
+    vb.attention(dt, d_rp, d_ed, 0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld, out, C, d_w, C, heads, hd)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    ref = attention_reference(rp, src, attr, q[:, :C].astype(np.float64), k[:, :C].astype(np.float64),
+                              v[:, :C].astype(np.float64), xr[:, :C].astype(np.float64), we, be.astype(np.float64),
+                              heads, hd)
+    assert oracle.rel_absmax(got, ref) <= 2e-3
+    zero = np.where(rp[1:] == rp[:-1])[0]
+    assert np.array_equal(got[zero], xr[zero, :C])

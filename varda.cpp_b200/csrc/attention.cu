@@ -16,7 +16,10 @@
 //
 // Numerics (the reference's semantics, cpu/kernels.cpp:98-158 and backend_cpu.cpp:333-340):
 //   s_j  = (<q, k_j> + <W_e^T q, a_j> + <q, b_e>) / sqrt(d)    (edge projection folded, per head)
-//   fp32 online softmax over the row: m, l, acc = sum p_j v_j, pa = sum p_j a_j
+//   fp32 online softmax over the row: l = sum p_j, acc = sum p_j v_j, pa = sum p_j a_j with
+//   p_j = 2^(s_j - m) relative to a reference maximum m that is raised (and the sums rescaled) only
+//   when a score exceeds it by more than 2^8, so p_j <= 2^8 (exact in real arithmetic; only the
+//   rounding of the sums differs from rescaling at every edge)
 //   o    = acc / l + W_e (pa / l) + b_e                       (sum_j p_j / l = 1)
 //   out  = T(T(o) + x_r);  zero in-degree: o = 0, so out = x_r exactly.
 // Every destination's arithmetic depends only on its own row (not on the launch's row range), so a
@@ -112,6 +115,8 @@ __device__ __forceinline__ void load_pairs_f32(const float* p, float2 (&f)[CPL /
     }
 }
 
+constexpr float kSlack = 8.0f;  // log2 units of headroom of the softmax sums over their reference maximum
+
 template <class T, int CPL, int LPH, int U, int MINB>
 __global__ void __launch_bounds__(256, MINB) attention_kernel(AttnArgs<T> a, float scale_log2, int wpd) {
     constexpr int P = CPL / 2;  // fp32 pairs per lane
@@ -195,18 +200,27 @@ __global__ void __launch_bounds__(256, MINB) attention_kernel(AttnArgs<T> a, flo
                     const float dot = head_sum<LPH>(d2.x + d2.y);
                     const float se = fmaf(qe2, az[u], fmaf(qe1, ay[u], qe0 * ax[u]));
                     const float s = ((dot + se) + qb) * scale_log2;  // log2 domain
-                    const float mn = fmaxf(m, s);
-                    const float corr = ex2(m - mn);
-                    const float p = ex2(s - mn);
-                    m = mn;
-                    l = fmaf(l, corr, p);
-                    vr[u].get(vf);
-                    const float2 p2 = make_float2(p, p), c2 = make_float2(corr, corr);
+                    // the sums are kept relative to a reference maximum m that moves only when a score
+                    // exceeds it by more than kSlack (any lane of the warp): p <= 2^kSlack, and most
+                    // edges skip the rescale
+                    if (__any_sync(kFull, s > m + kSlack)) {
+                        const float mn = fmaxf(m, s);
+                        const float corr = ex2(m - mn);
+                        m = mn;
+                        l *= corr, pa0 *= corr, pa1 *= corr, pa2 *= corr;
+                        const float2 c2 = make_float2(corr, corr);
 #pragma unroll
-                    for (int c = 0; c < P; ++c) acc[c] = __ffma2_rn(p2, vf[c], __fmul2_rn(acc[c], c2));
-                    pa0 = fmaf(p, ax[u], pa0 * corr);
-                    pa1 = fmaf(p, ay[u], pa1 * corr);
-                    pa2 = fmaf(p, az[u], pa2 * corr);
+                        for (int c = 0; c < P; ++c) acc[c] = __fmul2_rn(acc[c], c2);
+                    }
+                    const float p = ex2(s - m);
+                    l += p;
+                    vr[u].get(vf);
+                    const float2 p2 = make_float2(p, p);
+#pragma unroll
+                    for (int c = 0; c < P; ++c) acc[c] = __ffma2_rn(p2, vf[c], acc[c]);
+                    pa0 = fmaf(p, ax[u], pa0);
+                    pa1 = fmaf(p, ay[u], pa1);
+                    pa2 = fmaf(p, az[u], pa2);
                 }
             }
         };
@@ -255,10 +269,16 @@ template <class T>
 void attention(const AttnArgs<T>& a, cudaStream_t s) {
     if (a.n_rows <= 0) return;
     if (a.C != a.heads * a.head_dim) fail(kInvalidArgument, "attention: C != heads * head_dim");
-    // widest lane vector the layout allows: 16 fp16 channels (two 16-byte loads), else 8, else 4
+    // Launch shape: channels per lane (CPL), edges per pipeline stage (U) and resident blocks per SM
+    // (MINB, the register budget). Measured on the C2 block (fp16, C = 1024, head_dim 64): 8 channels
+    // per lane at 4 blocks per SM (32 warps) 1.65 ms, 16 channels at 2 blocks 1.97 ms, 8 at 3 blocks
+    // 2.28 ms: the kernel is latency-bound and occupancy wins. VB_ATT_VARIANT picks an alternative:
+    // 1 = (16, 1, 2), 2 = (8, 2, 3), 3 = (8, 1, 5), 4 = (4, 1, 4).
+    const char* venv = std::getenv("VB_ATT_VARIANT");
+    const int variant = venv && *venv ? std::atoi(venv) : 0;
     int cpl = 4;
-    if (sizeof(T) == 2 && a.C % 512 == 0 && a.head_dim % 16 == 0) cpl = 16;
-    else if (a.C % 256 == 0 && a.head_dim % 8 == 0) cpl = 8;
+    if (sizeof(T) == 2 && variant == 1 && a.C % 512 == 0 && a.head_dim % 16 == 0) cpl = 16;
+    else if (variant != 4 && a.C % 256 == 0 && a.head_dim % 8 == 0) cpl = 8;
     if (a.C % (32 * cpl) || a.head_dim % cpl)
         fail(kUnsupported, "attention: C must be a multiple of 128 and head_dim a multiple of 4 (got C=" +
                                std::to_string(a.C) + ", head_dim=" + std::to_string(a.head_dim) + ")");
@@ -269,12 +289,6 @@ void attention(const AttnArgs<T>& a, cudaStream_t s) {
     const float scale_log2 = 1.4426950408889634f / std::sqrt(float(a.head_dim));
     const int64_t warps = a.n_rows * wpd;
     const unsigned grid = unsigned((warps + 7) / 8);
-    // launch shape: lanes' channel width, edges per pipeline stage, minimum resident blocks per SM
-    // (register budget); VB_ATT_VARIANT picks a measured alternative for the C1 layout
-    static const int variant = [] {
-        const char* v = std::getenv("VB_ATT_VARIANT");
-        return v && *v ? std::atoi(v) : 0;
-    }();
 #define VB_ATT(CPL, LPH, U, MB) attention_kernel<T, CPL, LPH, U, MB><<<grid, 256, 0, s>>>(a, scale_log2, wpd)
 #define VB_ATT_L(CPL, U, MB)                          \
     switch (lph) {                                    \
@@ -286,27 +300,16 @@ void attention(const AttnArgs<T>& a, cudaStream_t s) {
         case 32: VB_ATT(CPL, 32, U, MB); break;       \
     }
     if constexpr (sizeof(T) == 2) {
-        if (cpl == 16 && lph == 4 && variant >= 1 && variant <= 4) {
-            switch (variant) {
-                case 1: VB_ATT(16, 4, 2, 1); break;
-                case 2: VB_ATT(16, 4, 1, 2); break;
-                case 3: VB_ATT(16, 4, 1, 3); break;
-                case 4: VB_ATT(16, 4, 2, 2); break;
-                default: VB_ATT(16, 4, 1, 2);
-            }
-        } else if (cpl == 16 && variant >= 5) {
-            cpl = 8;  // variants 5-6: 8 channels per lane for the same layout
-            const int wpd8 = a.C / 256, lph8 = a.head_dim / 8;
-            const unsigned grid8 = unsigned((a.n_rows * wpd8 + 7) / 8);
-            if (lph8 == 8 && variant == 5) attention_kernel<T, 8, 8, 2, 3><<<grid8, 256, 0, s>>>(a, scale_log2, wpd8);
-            else if (lph8 == 8) attention_kernel<T, 8, 8, 1, 4><<<grid8, 256, 0, s>>>(a, scale_log2, wpd8);
-            else fail(kUnsupported, "attention variant needs head_dim 64");
-        } else if (cpl == 16) {
+        if (cpl == 16) {
             VB_ATT_L(16, 1, 2)
+        } else if (cpl == 8 && variant == 2) {
+            VB_ATT_L(8, 2, 3)
+        } else if (cpl == 8 && variant == 3) {
+            VB_ATT_L(8, 1, 5)
         } else if (cpl == 8) {
-            VB_ATT_L(8, 2, 2)
+            VB_ATT_L(8, 1, 4)
         } else {
-            VB_ATT_L(4, 2, 2)
+            VB_ATT_L(4, 1, 4)
         }
     } else {
         if (cpl == 8) {

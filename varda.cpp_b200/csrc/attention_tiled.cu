@@ -9,7 +9,8 @@
 // (prefetching its next row's q / x_r) and runs an fp32 online softmax over the row's edges from
 // shared memory (lane = 8 channels = one 16-byte vector, LPH = head_dim / 8 lanes per head):
 //   s_e = (<q, k_e> + <W_e^T q, a_e> + <q, b_e>) / sqrt(d)   (log2 domain, ex2),
-//   acc = sum p_e v_e, l = sum p_e, pa = sum p_e a_e with the running-maximum rescale;
+//   acc = sum p_e v_e, l = sum p_e, pa = sum p_e a_e, p_e = 2^(s_e - m) relative to a reference
+//   maximum m raised (and the sums rescaled) only when a score exceeds it by more than 2^8;
 //   o = acc / l + W_e (pa / l) + b_e,  out = T(T(o) + x_r).
 // Every row's arithmetic depends only on that row, so results do not depend on the tiling (hence not
 // on the GPU partition either). Heavy rows go to the gather kernel (attention.cu).
@@ -177,14 +178,22 @@ __global__ void __launch_bounds__(256, 2) attention_tiled_kernel(TileArgs a, flo
             const float dot = head_sum<LPH>(d2.x + d2.y);
             const float se = fmaf(qe2, rec.z, fmaf(qe1, rec.y, qe0 * rec.x));
             const float s = ((dot + se) + qb) * scale_log2;
-            const float mn = fmaxf(m, s);
-            const float corr = ex2(m - mn), p = ex2(s - mn);
-            m = mn;
-            l = fmaf(l, corr, p);
-            pa0 = fmaf(pa0, corr, p * rec.x), pa1 = fmaf(pa1, corr, p * rec.y), pa2 = fmaf(pa2, corr, p * rec.z);
-            const float2 c2 = make_float2(corr, corr), p2 = make_float2(p, p);
+            // sums relative to a reference maximum raised only when a score exceeds it by 2^8
+            if (__any_sync(kFull, s > m + 8.0f)) {
+                const float mn = fmaxf(m, s);
+                const float corr = ex2(m - mn);
+                m = mn;
+                l *= corr, pa0 *= corr, pa1 *= corr, pa2 *= corr;
+                const float2 c2 = make_float2(corr, corr);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) acc[c] = __ffma2_rn(p2, vf[c], __fmul2_rn(acc[c], c2));
+                for (int c = 0; c < 4; ++c) acc[c] = __fmul2_rn(acc[c], c2);
+            }
+            const float p = ex2(s - m);
+            l += p;
+            pa0 = fmaf(p, rec.x, pa0), pa1 = fmaf(p, rec.y, pa1), pa2 = fmaf(p, rec.z, pa2);
+            const float2 p2 = make_float2(p, p);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[c] = __ffma2_rn(p2, vf[c], acc[c]);
         }
         float xr[8], o[8];
         {
