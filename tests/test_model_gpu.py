@@ -128,3 +128,19 @@ def test_attention_kernel_choice(name, tiled, chunk, seeded_model, monkeypatch):
     vb.check_device()
     ref = golden(name)["out.y"]
     assert oracle.rel_absmax(y, ref) <= TOL[vb.FP16]
+
+
+@pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])
+@pytest.mark.parametrize("name", ["t256", "t512", "c0"])
+def test_wide_rows_by_parts(name, dt, seeded_model, monkeypatch):
+    """Rows of more than VB_ATT_WIDE_DEG edges cut into parts of VB_ATT_PART_EDGES edges (split
+    kernels, merged per row; the engine does this for the C1 encoder's hidden rows of more than 128
+    edges): forced down to 16 / 5 here so every test model has wide rows, same parity bar."""
+    mp, xp = seeded_model(name)
+    x = np.array(st.read(xp)[0]["in.x"])
+    monkeypatch.setenv("VB_ATT_WIDE_DEG", "16")
+    monkeypatch.setenv("VB_ATT_PART_EDGES", "5")
+    monkeypatch.setenv("VB_ATT_TILED", "none")
+    y = vb.Model.load(mp, precision=dt).predict_step(x)
+    vb.check_device()
+    assert oracle.rel_absmax(y, golden(name)["out.y"]) <= TOL[dt]

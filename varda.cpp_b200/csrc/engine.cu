@@ -107,7 +107,16 @@ struct GraphDev {
     bool tiled = false;
     DeviceBuffer tiles, srcs, tedges, heavy;
     std::vector<int32_t> tile_row0, heavy_rows;  // host copies, to pick a chunk's tiles
+    // wide rows (more than kWideDeg edges, VB_ATT_WIDE_DEG; 0 disables) cut into parts of kPartEdges
+    // edges (VB_ATT_PART_EDGES), run by the split kernels over a scratch of one partial record per
+    // part, so one row's edges no longer run serially on one warp; the other rows go to the gather
+    // kernel. A guard for extreme degrees: on the C1 encoder (rows of up to 1,456 edges) splitting at
+    // 128 measured 9.6 ms against 5.3 ms for the gather kernel alone, whose per-edge rate dominates.
+    bool wide = false;
+    DeviceBuffer light, wide_dev, part0_dev, parts, scratch;
+    std::vector<int32_t> light_rows, wide_rows, part0;  // host copies (sorted rows; part prefix)
 };
+constexpr int kWideDeg = 2048, kPartEdges = 64;
 
 template <class T> float round_op(float x) {
     if (std::is_same<T, float>::value) return x;
@@ -448,6 +457,29 @@ GraphDev Engine<T>::upload_graph(const CsrGraph& csr, const std::string& name, i
         d.tile_row0 = tp.row0;
         d.heavy_rows = tp.heavy;
     }
+    const int64_t wide_deg = env_int("VB_ATT_WIDE_DEG", kWideDeg), part_edges = env_int("VB_ATT_PART_EDGES", kPartEdges);
+    if (!d.tiled && wide_deg > 0 && part_edges > 0 && csr.max_degree() > wide_deg) {
+        std::vector<int4> pt;
+        for (int64_t r = 0; r < csr.n_dst; ++r) {
+            const int32_t b = csr.row_ptr[size_t(r)], e = csr.row_ptr[size_t(r + 1)];
+            if (e - b <= wide_deg) {
+                d.light_rows.push_back(int32_t(r));
+                continue;
+            }
+            d.wide_rows.push_back(int32_t(r));
+            d.part0.push_back(int32_t(pt.size()));
+            for (int32_t x = b; x < e; x += int32_t(part_edges))
+                pt.push_back(make_int4(int32_t(r), x, std::min(e, x + int32_t(part_edges)), 0));
+        }
+        d.part0.push_back(int32_t(pt.size()));
+        d.wide = true;
+        d.light = upload(d.light_rows.data(), std::max<size_t>(1, d.light_rows.size()) * sizeof(int32_t));
+        d.wide_dev = upload(d.wide_rows.data(), d.wide_rows.size() * sizeof(int32_t));
+        d.part0_dev = upload(d.part0.data(), d.part0.size() * sizeof(int32_t));
+        d.parts = upload(pt.data(), pt.size() * sizeof(int4));
+        d.scratch.alloc(pt.size() * size_t(k::attention_parts_record(C_, heads_)) * sizeof(float));
+        act_bytes_ += d.scratch.bytes();
+    }
     d.row_ptr = upload(csr.row_ptr.data(), csr.row_ptr.size() * sizeof(int32_t));
     d.edges = upload(packed.data(), std::max<size_t>(1, packed.size()) * sizeof(EdgeRec));
     d.n_src = csr.n_src;
@@ -762,6 +794,29 @@ void Engine<T>::attention(const GraphDev& g, const Block<T>& b, int64_t lo, int6
             }
             return;
         }
+    }
+    if (g.wide) {
+        // rows [lo, lo + n): the light ones on the gather kernel (row list), the wide ones by parts
+        const auto l0 = std::lower_bound(g.light_rows.begin(), g.light_rows.end(), int32_t(lo));
+        const auto l1 = std::lower_bound(g.light_rows.begin(), g.light_rows.end(), int32_t(lo + n));
+        if (l1 > l0) {
+            a.rows = g.light.template as<int32_t>() + (l0 - g.light_rows.begin());
+            a.n_rows = int64_t(l1 - l0);
+            k::attention<T>(a, s);
+        }
+        const auto w0 = std::lower_bound(g.wide_rows.begin(), g.wide_rows.end(), int32_t(lo));
+        const auto w1 = std::lower_bound(g.wide_rows.begin(), g.wide_rows.end(), int32_t(lo + n));
+        if (w1 > w0) {
+            k::PartsArgs p;
+            const int64_t iw0 = w0 - g.wide_rows.begin(), iw1 = w1 - g.wide_rows.begin();
+            p.parts = g.parts.template as<int4>(), p.part_lo = g.part0[size_t(iw0)];
+            p.n_parts = g.part0[size_t(iw1)] - p.part_lo;
+            p.wide_rows = g.wide_dev.template as<int32_t>(), p.part0 = g.part0_dev.template as<int32_t>();
+            p.wide_lo = iw0, p.n_wide = iw1 - iw0, p.scratch = g.scratch.template as<float>();
+            a.rows = nullptr, a.n_rows = n;
+            k::attention_parts<T>(a, p, s);
+        }
+        return;
     }
     k::attention<T>(a, s);
 }

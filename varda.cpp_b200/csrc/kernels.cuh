@@ -109,6 +109,22 @@ template <class T> void attention(const AttnArgs<T>& a, cudaStream_t s);
 template <class T> void attention_split_noalloc(const AttnArgs<T>& a, int splits, cudaStream_t s);
 size_t attention_split_scratch_bytes();
 
+// The same contract for rows whose edges are cut into explicit parts (the engine's wide rows, scratch
+// owned by the caller): part i = {graph row, first edge, end edge, -}; wide row w (graph row
+// wide_rows[w]) merges parts [part0[w], part0[w + 1]). Parts [part_lo, part_lo + n_parts) and wide rows
+// [wide_lo, wide_lo + n_wide) run; scratch holds one record of attention_parts_record(C, heads) floats
+// per part, indexed by the part's global index.
+struct PartsArgs {
+    const int4* parts = nullptr;
+    int64_t part_lo = 0, n_parts = 0;
+    const int32_t* wide_rows = nullptr;
+    const int32_t* part0 = nullptr;
+    int64_t wide_lo = 0, n_wide = 0;
+    float* scratch = nullptr;
+};
+template <class T> void attention_parts(const AttnArgs<T>& a, const PartsArgs& p, cudaStream_t s);
+int attention_parts_record(int C, int heads);
+
 // Shared-memory-staged attention (fp16) over destination tiles (graph.h TilePlan): same contract per
 // destination row. Tiles [tile0, tile0 + ntiles) of the plan; q/x_r/out row of graph
 // row d is d - dst_lo.
