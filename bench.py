@@ -220,7 +220,7 @@ def run_ours(args, rank, world, local_rank):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
-    h2d = m.device_input_numel * 4   # this rank's input rows (own + encoder halo)
+    h2d = (m.data_hi - m.data_lo) * m.T_in * m.V_in * 4  # this rank's own input rows (halo rows come over NVLink)
     d2h = m.device_output_numel * 4  # this rank's output rows
 
     # one profiled eager pass: per-launch device times
@@ -275,7 +275,8 @@ def run_rollout(args, rank, world, local_rank):
         t = torch.tensor([ms, e2e_ms], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms = t.tolist()
-    h2d = (m.device_input_numel * 4 + (n - 1) * (m.device_input_numel // (m.T_in * m.V_in)) * F * 4) / n
+    own = m.data_hi - m.data_lo  # own rows: x0 once, one forcing row per own row and step
+    h2d = (own * m.T_in * m.V_in * 4 + (n - 1) * own * F * 4) / n
     d2h = m.device_output_numel * 4
     return dict(m=m, ms=ms, e2e_ms=e2e_ms, clocks=clocks, prof=prof, load_s=load_s, h2d=h2d, d2h=d2h,
                 launches=len(prof) + 2 + (1 if n > 1 else 0) + (1 if world > 1 else 0), dist=dist,
@@ -353,13 +354,16 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if "WORLD_SIZE" not in os.environ and args.gpus > 1:
         raise SystemExit("for --gpus > 1 launch with torch.distributed.run (one process per GPU)")
-    config = {"workload": "C1: full Varda-shaped forecaster predict_step (G=1,688,650 data nodes, "
-                          "H=189,809 hidden, C=1024, 16 heads, 16 processor blocks, T_in=2, V_in=90, V_out=80)",
-              "model": "GraphTransformer enc-proc-dec (varda.cpp format v3), random-init seeded weights",
-              "global_batch": 1, "seq_len": None, "parallelism": f"graph partition by destination x{world}",
+    config = {"workload": "C1: one predict_step of the full Varda-shaped GraphTransformer forecaster (varda.cpp "
+                          "format v3, random-init seeded weights; G=1,688,650 data nodes, H=189,809 hidden, C=1024, "
+                          "16 heads, 16 processor blocks, T_in=2, V_in=90, V_out=80)",
+              "parallelism": f"graph partition by destination x{world}",
               "l2": "inputs and activations >> 126 MB L2 (no flush needed)"}
     if args.workload == "c0":
         config["workload"] = "C0: icosphere r5/r4 model, C=128"
+    if args.workload == "c3":
+        config["workload"] = ("C3: one call of the temporal-downscaler shape (C1 graph and width, fp16, two input "
+                              "states, 6 output steps of 1,688,650 x 80)")
     pk, src = peaks()
     metric = "ms/predict_step fp16 at Varda shape"
     if args.workload == "c4":

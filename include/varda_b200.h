@@ -94,7 +94,10 @@ int vb_rollout(vb_model* m, const float* x0, int n_steps, const float* forcings,
 int vb_sizes(const vb_model* m, int64_t out8[8]);
 int vb_data_range(const vb_model* m, int64_t* lo, int64_t* hi);
 /* Element counts of the device tensors of this rank: x/xn (T_in, G_local, V_in) and yn/y
- * (T_out, own data rows, V_out); on one GPU input_numel / output_numel (cuda_backend.h:34-35). */
+ * (T_out, own data rows, V_out); on one GPU input_numel / output_numel (cuda_backend.h:34-35). On a
+ * sharded model G_local = own data rows followed by the encoder's halo rows: the caller fills the own
+ * rows of x, and vb_predict_step_device / vb_enqueue_predict fill the halo rows of every input step
+ * from their owners (a collective: every rank calls them together). */
 int vb_io_numel(const vb_model* m, int64_t* in, int64_t* out);
 
 /* varda::cuda::CudaBackend device entry points (src/varda/cuda/cuda_backend.h:38-69). Pointers are

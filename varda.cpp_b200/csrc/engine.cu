@@ -18,7 +18,6 @@
 #include <functional>
 #include <memory>
 #include <string>
-#include <thread>
 #include <type_traits>
 #include <vector>
 
@@ -59,21 +58,6 @@ bool tiled_for(const std::string& graph, const char* dflt) {
         b = e + 1;
     }
     return false;
-}
-
-// dst[i, 0:n] = src_rows[idx[i]] (row width n floats, base row stride `stride` floats) for
-// i < count, on a few host threads when the halo is large (the sharded input and forcing uploads).
-void gather_host_rows(float* dst, const float* src, int64_t stride, const int32_t* idx, int64_t count, int64_t n) {
-    auto run = [&](int64_t b, int64_t e) {
-        for (int64_t i = b; i < e; ++i)
-            std::memcpy(dst + i * n, src + int64_t(idx[i]) * stride, size_t(n) * sizeof(float));
-    };
-    const int64_t kPerThread = 32768;
-    const int nt = int(std::min<int64_t>(8, (count + kPerThread - 1) / kPerThread));
-    if (nt <= 1) return run(0, count);
-    std::vector<std::thread> ts;
-    for (int t = 0; t < nt; ++t) ts.emplace_back(run, count * t / nt, count * (t + 1) / nt);
-    for (auto& th : ts) th.join();
 }
 
 template <class T> struct Lin {
@@ -174,7 +158,9 @@ public:
     void denormalise(const float* yn, float* y, cudaStream_t s) override {
         k::denormalise(yn, add_out_.as<float>(), mul_out_.as<float>(), y, output_numel(), V_out_, s);
     }
+    // sharded: x's encoder-halo rows are filled from their owners first (the caller fills own rows)
     void predict_step_device(const float* x, float* y, cudaStream_t s) override {
+        exchange_input(const_cast<float*>(x), s);
         normalise(x, xn_, s);
         forward(xn_, yn_, s, nullptr);
         denormalise(yn_, y, s);
@@ -289,7 +275,10 @@ private:
     };
     Xchg xp_, xd_;
     T *xsend_ = nullptr, *xrecv_ = nullptr;
-    float* x_halo_host_ = nullptr;  // pinned staging of the encoder's halo input rows
+    // the encoder's halo input rows (all T_in slots) from their owners, at the start of every forward
+    Xchg xx_;
+    float *xx_send_ = nullptr, *xx_recv_ = nullptr;
+    void exchange_input(float* x, cudaStream_t s);
     // send lists in local row ids (global id - lo); offsets and counts in elements of `row` per row
     void setup_exchange(Xchg& x, const HaloPlan& h, int64_t lo, int64_t row);
 
@@ -299,14 +288,13 @@ private:
         int F = 0;
         int oldest = -1;                     // constant source the kind array was built for
         std::vector<int8_t> kind;            // [V_in] 0 kept, 1 prognostic, 2 forcing (3: kept from the oldest slot)
-        DeviceBuffer d_kind, d_src, f[2], y[2], y_halo, y_send;
+        DeviceBuffer d_kind, d_src, f[2], y[2];
         float *hy[2] = {nullptr, nullptr}, *hf[2] = {nullptr, nullptr};
         cudaStream_t d2h = nullptr, h2d = nullptr;
         cudaEvent_t up[2] = {nullptr, nullptr}, down[2] = {nullptr, nullptr};
         std::vector<cudaEvent_t> beg, end;
         cudaGraphExec_t graph[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [parity][with update]
         bool graph_failed = false;
-        Xchg yx;  // outputs of the encoder's halo rows, from their owners
     } ro_;
     void rollout_setup();
     void rollout_body(int p, bool update, cudaStream_t s);
@@ -703,7 +691,9 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         setup_exchange(xd_, plan_.dec, plan_.h_lo, 2 * int64_t(C_));
         xsend_ = act(size_t(std::max<int64_t>(1, std::max(xp_.n_send, xd_.n_send)) * 2 * C_));
         xrecv_ = act(size_t(std::max<int64_t>(1, xp_.n_recv) * 2 * C_));
-        if (n_eh_) VB_CUDA(cudaMallocHost(&x_halo_host_, size_t(T_in_ * n_eh_ * V_in_) * sizeof(float)));
+        setup_exchange(xx_, plan_.enc_x, plan_.g_lo, int64_t(T_in_) * V_in_);
+        xx_send_ = actf(size_t(std::max<int64_t>(1, xx_.n_send) * T_in_ * V_in_));
+        xx_recv_ = actf(size_t(std::max<int64_t>(1, xx_.n_recv) * T_in_ * V_in_));
         comm_ = std::make_unique<Comm>(plan_.world, plan_.rank, opts_.nccl_id);
     }
     VB_CUDA(cudaDeviceSynchronize());
@@ -716,7 +706,6 @@ Engine<T>::~Engine() {
     if (graph_exec_) cudaGraphExecDestroy(graph_exec_);  // before the communicator its nodes use
     rollout_release();
     comm_.reset();
-    if (x_halo_host_) cudaFreeHost(x_halo_host_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -1011,24 +1000,38 @@ void Engine<T>::enqueue_predict() {
     else predict_step_device(x_dev_, y_dev_, s);
 }
 
-// Host x is the full (1, T_in, G, V_in) input. One GPU: one copy. Sharded: this rank's rows, own
-// rows then the encoder's halo rows (gathered on the host into pinned memory).
+// Host x is the full (1, T_in, G, V_in) input. One GPU: one copy. Sharded: this rank's own rows (one
+// contiguous range per input step); the encoder's halo rows come from their owners on the device.
 template <class T>
 void Engine<T>::upload_input(const float* x, cudaStream_t s) {
     if (plan_.world == 1) {
         VB_CUDA(cudaMemcpyAsync(x_dev_, x, size_t(input_numel()) * sizeof(float), cudaMemcpyHostToDevice, s));
         return;
     }
-    for (int t = 0; t < T_in_; ++t) {
+    for (int t = 0; t < T_in_; ++t)
         VB_CUDA(cudaMemcpyAsync(x_dev_ + int64_t(t) * Gx_ * V_in_, x + (int64_t(t) * G_ + plan_.g_lo) * V_in_,
                                 size_t(Gl_ * V_in_) * sizeof(float), cudaMemcpyHostToDevice, s));
-        if (n_eh_) {
-            float* stage = x_halo_host_ + int64_t(t) * n_eh_ * V_in_;
-            VB_CUDA(cudaStreamSynchronize(s));  // the staging buffer may still feed a previous copy
-            gather_host_rows(stage, x + int64_t(t) * G_ * V_in_, V_in_, plan_.enc_halo.data(), n_eh_, V_in_);
-            VB_CUDA(cudaMemcpyAsync(x_dev_ + (int64_t(t) * Gx_ + Gl_) * V_in_, stage,
-                                    size_t(n_eh_ * V_in_) * sizeof(float), cudaMemcpyHostToDevice, s));
-        }
+}
+
+// The encoder-halo rows of x (T_in slots of V_in values each) from their owners: pack the own rows
+// every peer reads, one grouped send/recv, unpack past the own rows of every slot. Every rank calls it
+// (a rank with nothing to send or receive still joins the group).
+template <class T>
+void Engine<T>::exchange_input(float* x, cudaStream_t s) {
+    if (plan_.world == 1) return;
+    const int64_t slot = Gx_ * V_in_;
+    {
+        Span sp(this, s, "halo_pack", 0, double(xx_.n_send) * T_in_ * V_in_ * 8.0);
+        k::gather_slots(xx_send_, x, T_in_, slot, xx_.send_idx.template as<int32_t>(), xx_.n_send, V_in_, s);
+    }
+    {
+        Span sp(this, s, "halo_exchange", 0, double(xx_.n_send + xx_.n_recv) * T_in_ * V_in_ * 4.0);
+        comm_->exchange(xx_send_, xx_.send_off, xx_.send_cnt, xx_recv_, xx_.recv_off, xx_.recv_cnt, int(sizeof(float)),
+                        s);
+    }
+    {
+        Span sp(this, s, "halo_unpack", 0, double(xx_.n_recv) * T_in_ * V_in_ * 8.0);
+        k::scatter_slots(x, T_in_, slot, Gl_, xx_recv_, xx_.n_recv, V_in_, s);
     }
 }
 
@@ -1104,7 +1107,7 @@ void Engine<T>::rollout_setup() {
                               " is neither prognostic, dynamic forcing nor constant: it cannot be rolled out");
 
     prepare();  // one eager forward before any capture
-    const int64_t f_n = std::max<int64_t>(1, Gx_ * ro_.F), y_n = Gl_ * V_out_;
+    const int64_t f_n = std::max<int64_t>(1, Gl_ * ro_.F), y_n = Gl_ * V_out_;
     ro_.d_kind.alloc(size_t(V_in_));
     ro_.d_src.alloc(size_t(V_in_) * sizeof(int));
     VB_CUDA(cudaMemcpy(ro_.d_src.get(), src.data(), size_t(V_in_) * sizeof(int), cudaMemcpyHostToDevice));
@@ -1116,11 +1119,6 @@ void Engine<T>::rollout_setup() {
         VB_CUDA(cudaMallocHost(&ro_.hf[p], size_t(f_n) * sizeof(float)));
         VB_CUDA(cudaEventCreateWithFlags(&ro_.up[p], cudaEventDisableTiming));
         VB_CUDA(cudaEventCreateWithFlags(&ro_.down[p], cudaEventDisableTiming));
-    }
-    ro_.y_halo.alloc(size_t(std::max<int64_t>(1, n_eh_ * V_out_)) * sizeof(float));
-    if (plan_.world > 1) {
-        setup_exchange(ro_.yx, plan_.enc_x, plan_.g_lo, V_out_);
-        ro_.y_send.alloc(size_t(std::max<int64_t>(1, ro_.yx.n_send * V_out_)) * sizeof(float));
     }
     VB_CUDA(cudaStreamCreateWithFlags(&ro_.d2h, cudaStreamNonBlocking));
     VB_CUDA(cudaStreamCreateWithFlags(&ro_.h2d, cudaStreamNonBlocking));
@@ -1149,22 +1147,16 @@ void Engine<T>::rollout_release() {
     ro_ = Roll{};
 }
 
-// One rollout step on s: normalise the window -> forward -> denormalise into y[p]; with the update,
-// the halo rows' outputs from their owners (sharded) and the state update of the window in place.
+// One rollout step on s: (sharded: the halo rows of every window slot from their owners) normalise
+// the window -> forward -> denormalise into y[p]; with the update, the state update of this rank's
+// own rows of the window in place.
 template <class T>
 void Engine<T>::rollout_body(int p, bool update, cudaStream_t s) {
     float* y = ro_.y[p].template as<float>();
     predict_step_device(x_dev_, y, s);
     if (!update) return;
-    if (plan_.world > 1) {
-        float* send = ro_.y_send.template as<float>();
-        k::gather_rows(send, y, ro_.yx.send_idx.template as<int32_t>(), ro_.yx.n_send, V_out_, s);
-        comm_->exchange(send, ro_.yx.send_off, ro_.yx.send_cnt, ro_.y_halo.get(), ro_.yx.recv_off, ro_.yx.recv_cnt,
-                        int(sizeof(float)), s);
-    }
-    k::rollout_update(x_dev_, T_in_, Gx_, V_in_, y, ro_.y_halo.template as<float>(), Gl_, V_out_,
-                      ro_.f[p].template as<float>(), ro_.F, ro_.d_kind.template as<int8_t>(),
-                      ro_.d_src.template as<int>(), s);
+    k::rollout_update(x_dev_, T_in_, Gl_, V_in_, y, nullptr, Gl_, V_out_, ro_.f[p].template as<float>(), ro_.F,
+                      ro_.d_kind.template as<int8_t>(), ro_.d_src.template as<int>(), s, Gx_ * int64_t(V_in_));
 }
 
 // The device loop: step s (parity p = s % 2) replays graph[p] on the model's stream; its output y[p]
@@ -1210,9 +1202,8 @@ void Engine<T>::rollout(const float* x0, int n, const float* forcings, float* y,
         const int b = st & 1;
         const float* fs = forcings + int64_t(st) * G_ * F;
         std::memcpy(ro_.hf[b], fs + plan_.g_lo * F, size_t(Gl_ * F) * sizeof(float));
-        gather_host_rows(ro_.hf[b] + Gl_ * F, fs, F, plan_.enc_halo.data(), n_eh_, F);
         if (st >= 2) VB_CUDA(cudaStreamWaitEvent(ro_.h2d, ro_.end[size_t(st - 2)], 0));  // step st-2 read f[b]
-        VB_CUDA(cudaMemcpyAsync(ro_.f[b].get(), ro_.hf[b], size_t(Gx_ * F) * sizeof(float), cudaMemcpyHostToDevice,
+        VB_CUDA(cudaMemcpyAsync(ro_.f[b].get(), ro_.hf[b], size_t(Gl_ * F) * sizeof(float), cudaMemcpyHostToDevice,
                                 ro_.h2d));
         VB_CUDA(cudaEventRecord(ro_.up[b], ro_.h2d));
     };

@@ -53,10 +53,11 @@ __global__ void assemble_kernel(const float* __restrict__ xn, const float* __res
     }
 }
 
-__global__ void rollout_update_kernel(float* __restrict__ w, int T, int64_t rows, int V, const float* __restrict__ yo,
-                                      const float* __restrict__ yh, int64_t n_own, int Vo, const float* __restrict__ f,
-                                      int F, const int8_t* __restrict__ kind, const int* __restrict__ src) {
-    const int64_t n = rows * V, slot = rows * V;
+__global__ void rollout_update_kernel(float* __restrict__ w, int T, int64_t rows, int V, int64_t slot,
+                                      const float* __restrict__ yo, const float* __restrict__ yh, int64_t n_own, int Vo,
+                                      const float* __restrict__ f, int F, const int8_t* __restrict__ kind,
+                                      const int* __restrict__ src) {
+    const int64_t n = rows * V;
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
         const int64_t row = i / V;
         const int c = int(i - row * V);
@@ -67,6 +68,28 @@ __global__ void rollout_update_kernel(float* __restrict__ w, int T, int64_t rows
         if (k == 1) *newest = row < n_own ? yo[row * Vo + src[c]] : yh[(row - n_own) * Vo + src[c]];
         else if (k == 2) *newest = f[row * F + src[c]];
         else if (k == 3) *newest = oldest;
+    }
+}
+
+__global__ void gather_slots_kernel(float* __restrict__ dst, const float* __restrict__ src, int T, int64_t slot,
+                                    const int32_t* __restrict__ idx, int64_t n, int V) {
+    const int64_t tot = n * T * V;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < tot; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = i / (int64_t(T) * V);
+        const int64_t rem = i - r * T * V;
+        const int t = int(rem / V), c = int(rem - int64_t(t) * V);
+        dst[i] = src[t * slot + int64_t(idx[r]) * V + c];
+    }
+}
+
+__global__ void scatter_slots_kernel(float* __restrict__ dst, int T, int64_t slot, int64_t row0,
+                                     const float* __restrict__ src, int64_t n, int V) {
+    const int64_t tot = n * T * V;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < tot; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = i / (int64_t(T) * V);
+        const int64_t rem = i - r * T * V;
+        const int t = int(rem / V), c = int(rem - int64_t(t) * V);
+        dst[t * slot + (row0 + r) * V + c] = src[i];
     }
 }
 
@@ -248,11 +271,26 @@ void gather_rows(float* dst, const float* src, const int32_t* idx, int64_t rows,
     VB_LAUNCH();
 }
 
-void rollout_update(float* window, int T, int64_t rows, int V_in, const float* y_own, const float* y_halo, int64_t n_own,
-                    int V_out, const float* f, int F, const int8_t* kind, const int* src, cudaStream_t s) {
+void rollout_update(float* window, int T, int64_t rows, int V_in, const float* y_own, const float* y_halo,
+                    int64_t n_own, int V_out, const float* f, int F, const int8_t* kind, const int* src, cudaStream_t s,
+                    int64_t slot_stride) {
     if (rows <= 0) return;
-    rollout_update_kernel<<<grid_for(rows * V_in, 256), 256, 0, s>>>(window, T, rows, V_in, y_own, y_halo, n_own, V_out,
-                                                                      f, F, kind, src);
+    const int64_t slot = slot_stride > 0 ? slot_stride : rows * V_in;
+    rollout_update_kernel<<<grid_for(rows * V_in, 256), 256, 0, s>>>(window, T, rows, V_in, slot, y_own, y_halo, n_own,
+                                                                     V_out, f, F, kind, src);
+    VB_LAUNCH();
+}
+
+void gather_slots(float* dst, const float* src, int T, int64_t slot, const int32_t* idx, int64_t n, int V,
+                  cudaStream_t s) {
+    if (n <= 0) return;
+    gather_slots_kernel<<<grid_for(n * T * V, 256), 256, 0, s>>>(dst, src, T, slot, idx, n, V);
+    VB_LAUNCH();
+}
+
+void scatter_slots(float* dst, int T, int64_t slot, int64_t row0, const float* src, int64_t n, int V, cudaStream_t s) {
+    if (n <= 0) return;
+    scatter_slots_kernel<<<grid_for(n * T * V, 256), 256, 0, s>>>(dst, T, slot, row0, src, n, V);
     VB_LAUNCH();
 }
 

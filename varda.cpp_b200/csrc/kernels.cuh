@@ -62,8 +62,15 @@ template <class T> void output_assemble(const OutputArgs& a, cudaStream_t s);
 // f[row][src[c]] (dynamic forcing), 0: nothing (constant, kept in place), or 3: the oldest slot's
 // old value (constant, inherited through the roll). y rows [0, n_own) come from y_own, rows
 // [n_own, rows) from y_halo (the owners' outputs of this rank's halo rows, multi-GPU). Pure copies.
+// slot_stride: elements between consecutive slots of the window (0: rows * V_in, a packed window).
 void rollout_update(float* window, int T, int64_t rows, int V_in, const float* y_own, const float* y_halo,
-                    int64_t n_own, int V_out, const float* f, int F, const int8_t* kind, const int* src, cudaStream_t s);
+                    int64_t n_own, int V_out, const float* f, int F, const int8_t* kind, const int* src, cudaStream_t s,
+                    int64_t slot_stride = 0);
+// Multi-slot rows (T slots of a (T, rows, V) window, `slot` elements apart): dst[i, t, :] =
+// src[t slot + idx[i] V, +V) (pack), and dst[t slot + (row0 + i) V, +V) = src[i, t, :] (unpack).
+void gather_slots(float* dst, const float* src, int T, int64_t slot, const int32_t* idx, int64_t n, int V,
+                  cudaStream_t s);
+void scatter_slots(float* dst, int T, int64_t slot, int64_t row0, const float* src, int64_t n, int V, cudaStream_t s);
 
 // ------------------------------------------------------------------ LayerNorm (fp32 statistics)
 // y = LN(x) * w + b over C channels per row (C a multiple of 128, <= 2048); b may be null; y may

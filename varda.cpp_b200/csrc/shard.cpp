@@ -110,8 +110,8 @@ ShardPlan make_plan(const Config& c, const CsrGraph& enc, const CsrGraph& proc, 
         if (G < world) fail(kUnsupported, "shard plan: fewer data nodes than GPUs");
         // Cost model (seconds-equivalents): GEMM FLOPs at ~1.2 PFLOP/s, edge gathers at ~5 TB/s. The step
         // is a chain of phases with a halo exchange between them (encoder, 16 processor blocks,
-        // decoder), so each phase is balanced on its own: hidden rows on the encoder-destination and
-        // processor work, data rows on the encoder-source and decoder work.
+        // decoder), so each phase is balanced on its own: hidden rows on the processor work, data rows
+        // on the encoder-source and decoder work.
         const double C = c.num_channels, M = c.mlp_hidden, F = double(align_up(size_t(c.src_features()), 8));
         const double P = c.num_processor_layers, Vd = c.dec_out_features();
         const double kF = 1.0 / 1.2e15, kB = 1.0 / 5e12, row_bytes = 2.0 * C * 2.0;
@@ -119,10 +119,11 @@ ShardPlan make_plan(const Config& c, const CsrGraph& enc, const CsrGraph& proc, 
                               2 * C * 2 * C;
         const double flop_g = 2 * F * C + 2 * C * 2 * C + 2 * F * C + 2 * C * 2 * C + 2 * C * C + 4 * C * M + 2 * C * Vd;
         std::vector<double> wh(static_cast<size_t>(H)), wg(static_cast<size_t>(G));
+        // the encoder's gathers (one phase, concentrated on the dense region's hidden rows) are left
+        // out of the hidden weights: the 16 processor phases dominate and need equal shares
         for (int64_t h = 0; h < H; ++h)
             wh[size_t(h)] = flop_h * kF +
-                            P * (proc.row_ptr[size_t(h + 1)] - proc.row_ptr[size_t(h)]) * row_bytes * 0.5 * kB +
-                            (enc.row_ptr[size_t(h + 1)] - enc.row_ptr[size_t(h)]) * row_bytes * kB;
+                            P * (proc.row_ptr[size_t(h + 1)] - proc.row_ptr[size_t(h)]) * row_bytes * 0.5 * kB;
         for (int64_t g = 0; g < G; ++g)
             wg[size_t(g)] = flop_g * kF + (dec.row_ptr[size_t(g + 1)] - dec.row_ptr[size_t(g)]) * row_bytes * kB;
         p.h_split = balanced_split(wh, world);

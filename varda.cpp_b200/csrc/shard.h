@@ -2,8 +2,8 @@
 // GPU. The reference runs one GPU only; this is new (no reference counterpart).
 //
 // Partition. Hidden nodes are split into `world` contiguous index ranges of equal estimated cost
-// (FLOPs of the encoder-destination and processor GEMMs plus edge-gather bytes, from the config dims
-// and in-degrees), and data nodes, independently, into contiguous ranges of equal estimated cost
+// (FLOPs of the node-wise GEMMs plus processor edge-gather bytes, from the config dims and
+// in-degrees), and data nodes, independently, into contiguous ranges of equal estimated cost
 // (encoder-source and decoder GEMMs plus decoder gathers). The forward pass is a chain of phases with
 // a halo exchange between each (encoder, every processor block, decoder), so every phase is balanced
 // on its own rather than each rank's total. With spatially ordered node numbering (the synthetic
