@@ -292,3 +292,33 @@ def test_attention_variants(C, heads, variant, monkeypatch):
     assert oracle.rel_absmax(got, ref) <= 2e-3
     zero = np.where(rp[1:] == rp[:-1])[0]
     assert np.array_equal(got[zero], xr[zero, :C])
+
+
+@pytest.mark.parametrize("M,N,K,lda", [(300, 1024, 1024, 1024), (1000, 4096, 1024, 1024), (513, 1024, 4096, 4096),
+                                       (4000, 2048, 184, 192), (256, 256, 64, 64), (777, 512, 320, 320)])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_gemm_cta_pair(M, N, K, lda, epi, monkeypatch):
+    """The tensor-core GEMM on CTA pairs (VB_GEMM_PAIR=1: tcgen05.mma.cta_group::2, 256-row tiles over
+    two SMs, each CTA loading its 128 rows of A and half of W): the float64 reference of the fp16
+    arithmetic within the fp16 bar, and the single-CTA kernel's result within one fp16 rounding."""
+    rng = np.random.default_rng(M + N + K + epi + 7)
+    A = np.zeros((M, lda), np.float32)
+    A[:, :K] = rounded(rng.normal(size=(M, K)), vb.FP16)
+    W = np.zeros((N, lda), np.float32)
+    W[:, :K] = rounded(rng.normal(size=(N, K)) / math.sqrt(K), vb.FP16)
+    b = rounded(rng.normal(size=N) * 0.2, vb.FP16)
+    R = rounded(rng.normal(size=(M, N)), vb.FP16)
+    T = torch.float16
+    dA, dW, db, dR = dev(A, T), dev(W, T), dev(b, T), dev(R, T)
+    outs = []
+    for pair in ("1", "0"):
+        monkeypatch.setenv("VB_GEMM_PAIR", pair)
+        Y = torch.full((M, N), float("nan"), device="cuda", dtype=T)
+        vb.gemm(vb.FP16, 2, dA, lda, dW, lda, db, Y, N, dR if epi == 2 else None, N, M, N, K, epi)
+        torch.cuda.synchronize()
+        vb.check_device()
+        outs.append(Y.float().cpu().numpy())
+    ref = gemm_reference(A[:, :K], W[:, :K], b, R, epi, False, True)
+    assert not np.isnan(outs[0]).any()
+    assert oracle.rel_absmax(outs[0], ref) <= 2e-3
+    assert oracle.rel_absmax(outs[0], outs[1]) <= 2e-3
