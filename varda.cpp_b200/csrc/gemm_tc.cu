@@ -1,20 +1,26 @@
 // tcgen05 GEMM (see gemm_tc.cuh).
 //
-// Persistent kernel, one 320-thread CTA per SM, warp-specialised:
+// Persistent kernel, one 320-thread CTA per SM (or one cluster of two CTAs per two SMs, below),
+// warp-specialised:
 //   warp 0 (one lane)   TMA producer: A [128 x 64] and W [BN x 64] fp16 tiles, 128-byte swizzle,
 //                       into a STAGES-deep shared-memory ring (full/empty mbarriers).
 //   warp 1 (one lane)   MMA issuer: 4 x tcgen05.mma (M=128, N=BN, K=16) per 64-wide k block into
 //                       one of two TMEM accumulators; tcgen05.commit frees the smem stage, and a
 //                       commit after the last k block hands the accumulator to the epilogue.
-//   warps 2-9           epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
-//                       32 (w % 4) .. + 31 = its 32 output rows; warps w and w + 4 split the
-//                       columns in halves), bias / GELU / residual in fp32, the 32 x 32 fp16
-//                       sub-tile staged in 64-byte-swizzled shared memory and written by one TMA
-//                       bulk tensor store (the residual sub-tile arrives the same way, one chunk
-//                       ahead); then release the accumulator to the MMA warp.
+//   warps 2-9           epilogue: tcgen05.ld 32 columns at a time, the next chunk in flight (warp w
+//                       reads TMEM lanes 32 (w % 4) .. + 31 = its 32 output rows; warps w and
+//                       w + 4 split the columns in halves), bias / GELU / residual in fp32 with the
+//                       fp16 operands added by mixed-precision adds (the residual row read into
+//                       registers one chunk ahead), the 32 x 32 fp16 sub-tile staged in
+//                       64-byte-swizzled shared memory and written by one TMA bulk tensor store;
+//                       the accumulator goes back to the MMA warp once its last chunk is loaded.
 // Two accumulators (2 x BN TMEM columns) let the epilogue of tile i overlap the main loop of
-// tile i + 1. Tiles are visited m-major (n fastest) so an A row block is reused from L2 by the
-// CTAs working on its N tiles.
+// tile i + 1. With N > 128 the CTAs run in clusters of two (cta_group::2): the pair computes a
+// 256-row tile with one MMA stream issued by the leader, each CTA loading its own 128 rows of A and
+// half of the W tile (TMA loads without multicast, completing on the leader's barrier) and holding
+// its 128 accumulator rows in its own TMEM; commits arrive on both CTAs' barriers, and both CTAs'
+// epilogue warps release the leader's accumulator. Tiles are visited m-major (n fastest) so an A row
+// block is reused from L2 by the CTAs working on its N tiles.
 //
 // Every mbarrier wait is bounded (kTimeoutNs of %globaltimer). On timeout a CTA sets the device
 // error flag, stops issuing work, waits (bounded) for its own TMA loads and MMAs in flight,
@@ -24,6 +30,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -127,12 +134,13 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor, kind::f16: A = B = fp16, D = fp32, both K-major, M = 128, N = BN.
-template <int BN> constexpr uint32_t instr_desc() {
+// Instruction descriptor, kind::f16: A = B = fp16, D = fp32, both K-major, M = MM (128, or 256 for a
+// CTA pair), N = BN.
+template <int BN, int MM = BM> constexpr uint32_t instr_desc() {
     return (1u << 4)                      // D format fp32
            | (0u << 7) | (0u << 10)       // A, B format fp16
            | (uint32_t(BN >> 3) << 17)    // N
-           | (uint32_t(BM >> 4) << 24);   // M
+           | (uint32_t(MM >> 4) << 24);   // M
 }
 
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
@@ -146,6 +154,56 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
+// ---- CTA pairs (cta_group::2): the MMA of a cluster of two CTAs on SMs of one TPC computes a
+// 256-row tile; each CTA holds its 128 rows of A and half of the BN rows of B in its own shared
+// memory, and its 128 rows of the accumulator in its own TMEM.
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the variable at shared::cta address `a` in the cluster's CTA `rank`
+__device__ __forceinline__ uint32_t mapa(uint32_t a, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(rank));
+    return d;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA tile load into this CTA's shared memory whose bytes complete on the barrier at `bar_cluster`
+// (the pair leader's); no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// completion of the pair's MMAs issued so far, arriving on the barrier at the same offset in both CTAs
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(uint16_t(3))
+        : "memory");
+}
+// ... and on this CTA's barrier only
+__device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -202,9 +260,9 @@ __device__ __forceinline__ float rcpf(float x) {
 
 // Shared memory: the A/W stage ring, then per epilogue warp two 2 KB output staging buffers, then the
 // mbarriers.
-template <int BN, int STAGES, int EPI> struct Layout {
-    static constexpr int kA = BM * BK * 2;  // bytes per A stage
-    static constexpr int kB = BN * BK * 2;
+template <int BN, int STAGES, int EPI, bool PAIR> struct Layout {
+    static constexpr int kA = BM * BK * 2;                   // bytes per A stage
+    static constexpr int kB = (PAIR ? BN / 2 : BN) * BK * 2;  // this CTA's rows of W per stage
     static constexpr int kTiles = STAGES * (kA + kB);
     static constexpr int kSub = 32 * 32 * 2;  // one 32 x 32 fp16 sub-tile
     static constexpr int kOut = kEpiWarps * 2 * kSub;
@@ -250,11 +308,12 @@ __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.a
 // tensor map (chunk index XOR bits 1-2 of the row): conflict-free 16-byte accesses by 32 lanes.
 __device__ __forceinline__ int sw64(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, Params p) {
-    using L = Layout<BN, STAGES, EPI>;
+    using L = Layout<BN, STAGES, EPI, PAIR>;
+    constexpr int UM = PAIR ? 2 * BM : BM;  // rows of one output tile (one CTA, or the pair)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -270,54 +329,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;  // 0: the pair leader (issues the MMAs)
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
-        for (int b = 0; b < 2; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], kEpiWarps);
+        // the leader's accumulator is released by the epilogue warps of both CTAs
+        for (int b = 0; b < 2; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);
         mbar_init(drain, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(2 * BN));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        if (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                         "r"(2 * BN));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                         "r"(2 * BN));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        }
     }
     fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
     fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    const int n_m = (p.M + BM - 1) / BM, n_n = (p.N + BN - 1) / BN;
+    const int n_m = (p.M + UM - 1) / UM, n_n = (p.N + BN - 1) / BN;
     const int tiles = n_m * n_n, kblocks = (p.K + BK - 1) / BK;
+    // tiles are handed out per CTA, or per pair (both CTAs of a pair walk the same sequence)
+    const int unit0 = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
+    const int units = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
 
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer
         int stage = 0;
         uint32_t phase = 0;
         uint32_t issued = 0, last_parity = 0;  // per-stage bit masks for the drain
-        for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+        for (int tile = unit0; tile < tiles && !*abort_flag; tile += units) {
             const int mb = tile / n_n, nb = tile - mb * n_n;
             for (int kb = 0; kb < kblocks; ++kb) {
                 if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
-                mbar_expect_tx(&full[stage], uint32_t(L::kA + L::kB));
-                tma_load_2d(sA + stage * L::kA, &tmA, &full[stage], kb * BK, mb * BM);
-                tma_load_2d(sB + stage * L::kB, &tmB, &full[stage], kb * BK, nb * BN);
+                if (PAIR) {
+                    // both CTAs' tiles complete on the leader's barrier, which expects the pair's bytes
+                    if (rank == 0) mbar_expect_tx(&full[stage], uint32_t(2 * (L::kA + L::kB)));
+                    const uint32_t fb = mapa(smem_u32(&full[stage]), 0);
+                    tma_load_2d_pair(sA + stage * L::kA, &tmA, fb, kb * BK, mb * UM + int(rank) * BM);
+                    tma_load_2d_pair(sB + stage * L::kB, &tmB, fb, kb * BK, nb * BN + int(rank) * (BN / 2));
+                } else {
+                    mbar_expect_tx(&full[stage], uint32_t(L::kA + L::kB));
+                    tma_load_2d(sA + stage * L::kA, &tmA, &full[stage], kb * BK, mb * BM);
+                    tma_load_2d(sB + stage * L::kB, &tmB, &full[stage], kb * BK, nb * BN);
+                }
                 issued |= 1u << stage;
                 last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
                 if (++stage == STAGES) stage = 0, phase ^= 1;
             }
         }
-        if (*abort_flag)  // let every load already issued land before the CTA exits
-            for (int s = 0; s < STAGES; ++s)
-                if (issued & (1u << s)) mbar_drain(&full[s], (last_parity >> s) & 1);
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer
-        constexpr uint32_t idesc = instr_desc<BN>();
+        if (*abort_flag) {  // let every load already issued land before the CTA exits
+            if (!PAIR || rank == 0) {
+                for (int s = 0; s < STAGES; ++s)
+                    if (issued & (1u << s)) mbar_drain(&full[s], (last_parity >> s) & 1);
+            } else {  // the peer's loads complete on the leader's barriers: give them time to land
+                const uint64_t t0 = now_ns();
+                while (now_ns() - t0 < 2000000ull) {
+                }
+            }
+        }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+        // ---------------- MMA issuer (the pair's leader issues for both CTAs)
+        constexpr uint32_t idesc = instr_desc<BN, UM>();
         int stage = 0;
         uint32_t phase = 0;
         int it = 0;
         bool any = false;
-        for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, ++it) {
+        for (int tile = unit0; tile < tiles && !*abort_flag; tile += units, ++it) {
             const int ab = it & 1;
             const uint32_t ap = (it >> 1) & 1;
             if (!mbar_wait(&tempty[ab], ap ^ 1, abort_flag)) break;
@@ -333,17 +419,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint64_t a0 = smem_desc(smem_u32(sA + stage * L::kA));
                 const uint64_t b0 = smem_desc(smem_u32(sB + stage * L::kB));
 #pragma unroll
-                for (int j = 0; j < BK / 16; ++j)
-                    mma_f16(d, a0 + uint64_t(2 * j), b0 + uint64_t(2 * j), idesc, (kb | j) != 0 ? 1u : 0u);
-                mma_commit(&empty[stage]);
+                for (int j = 0; j < BK / 16; ++j) {
+                    if (PAIR) mma_f16_pair(d, a0 + uint64_t(2 * j), b0 + uint64_t(2 * j), idesc, (kb | j) != 0 ? 1u : 0u);
+                    else mma_f16(d, a0 + uint64_t(2 * j), b0 + uint64_t(2 * j), idesc, (kb | j) != 0 ? 1u : 0u);
+                }
+                if (PAIR) mma_commit_pair(&empty[stage]);
+                else mma_commit(&empty[stage]);
                 any = true;
                 if (++stage == STAGES) stage = 0, phase ^= 1;
             }
             if (!ok) break;
-            mma_commit(&tfull[ab]);
+            if (PAIR) mma_commit_pair(&tfull[ab]);
+            else mma_commit(&tfull[ab]);
         }
         if (any) {  // every MMA issued by this thread completes before the TMEM is freed
-            mma_commit(drain);
+            if (PAIR) mma_commit_pair_local(drain);
+            else mma_commit(drain);
             mbar_drain(drain, 0);
         }
     } else if (warp >= 2) {
@@ -375,11 +466,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         };
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+        // the leader's tempty barriers, which both CTAs' epilogue warps release
+        const uint32_t te0 = PAIR ? mapa(smem_u32(&tempty[0]), 0) : 0u, te1 = PAIR ? mapa(smem_u32(&tempty[1]), 0) : 0u;
+        auto release = [&](int ab) {
+            fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (PAIR) mbar_arrive_cluster(ab ? te1 : te0);
+                else mbar_arrive(&tempty[ab]);
+            }
+        };
+        for (int tile = unit0; tile < tiles; tile += units, ++it) {
             const int ab = it & 1;
             const uint32_t ap = (it >> 1) & 1;
             const int mb = tile / n_n, nb = tile - mb * n_n;
-            const int row0 = mb * BM + lg * 32;
+            const int row0 = mb * UM + int(rank) * BM + lg * 32;
             const int colh = nb * BN + half * (BN / 2);
             // the first chunk's residual loads fly while the accumulator is being computed
             uint32_t resa[16], resb[16];
@@ -444,9 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (c + 1 < kChunks) {
                     tmem_wait32(nxt);
                     if (c + 2 == kChunks) {  // every column of the accumulator is in registers
-                        fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[ab]);
+                        release(ab);
                         released = true;
                     }
                 }
@@ -466,11 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ++n_out;
             }
-            if (!released) {
-                fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[ab]);
-            }
+            if (!released) release(ab);
             if (!ok) break;
         }
         if (lane == 0) bulk_wait_all();  // every TMA store has finished before the CTA exits
@@ -478,9 +573,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();  // no CTA leaves while its peer may still read its shared memory or signal it
     if (warp == 1) {
         fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+        if (PAIR) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+        else asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
     }
 }
 
@@ -523,34 +620,57 @@ int sm_count() {
     return n;
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, bool PAIR>
 void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
-    using L = Layout<BN, STAGES, EPI>;
+    using L = Layout<BN, STAGES, EPI, PAIR>;
     static bool configured = false;  // per instantiation; the attribute is per function
     if (!configured) {
-        VB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     L::kSmem));
+        VB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, EPI, PAIR>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem));
         configured = true;
     }
     const CUtensorMap ta = make_map(a.A, a.M, a.K, a.lda, BM);
-    const CUtensorMap tb = make_map(a.W, a.N, a.K, a.ldw, BN);
+    const CUtensorMap tb = make_map(a.W, a.N, a.K, a.ldw, PAIR ? BN / 2 : BN);
     // 32 x 32 sub-tiles of the output, 64-byte swizzle: the epilogue's TMA stores
     const CUtensorMap tc = make_map(a.C, a.M, a.N, a.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
     Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0};
-    const int64_t tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-    const int grid = int(std::min<int64_t>(tiles, sm_count()));
-    gemm_tc_kernel<BN, STAGES, EPI><<<grid, kThreads, L::kSmem, s>>>(ta, tb, tc, p);
-    VB_LAUNCH();
+    constexpr int UM = PAIR ? 2 * BM : BM;
+    const int64_t tiles = ((a.M + UM - 1) / UM) * ((a.N + BN - 1) / BN);
+    if (!PAIR) {
+        const int grid = int(std::min<int64_t>(tiles, sm_count()));
+        gemm_tc_kernel<BN, STAGES, EPI, PAIR><<<grid, kThreads, L::kSmem, s>>>(ta, tb, tc, p);
+        VB_LAUNCH();
+        return;
+    }
+    // clusters of two CTAs, one pair per two SMs
+    const int pairs = int(std::min<int64_t>(tiles, sm_count() / 2));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(2 * pairs));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = size_t(L::kSmem);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr, cfg.numAttrs = 1;
+    VB_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, STAGES, EPI, PAIR>, ta, tb, tc, p));
+    ++launch_counter();
 }
 
 // stage counts: as deep as the 227 KB of shared memory allows next to the epilogue staging
 template <int BN>
 void dispatch_epi(const k::GemmArgs<__half>& a, cudaStream_t s) {
     constexpr int S = BN == 256 ? 4 : 6;
+    // CTA pairs (cta_group::2) for N > 128 unless VB_GEMM_PAIR=0: on C1's shapes 3-8% faster than single
+    // CTAs (each SM loads half of W per tile: a third less L2-to-SM traffic)
+    const char* pe = std::getenv("VB_GEMM_PAIR");
+    const bool pair = BN == 256 && !(pe && *pe && std::atoi(pe) == 0) && a.M >= 2 * BM;
     switch (a.epi) {
-        case k::kEpiBias: launch<BN, S, k::kEpiBias>(a, s); break;
-        case k::kEpiGelu: launch<BN, S, k::kEpiGelu>(a, s); break;
-        case k::kEpiResidual: launch<BN, S, k::kEpiResidual>(a, s); break;
+        case k::kEpiBias: pair ? launch<BN, 6, k::kEpiBias, true>(a, s) : launch<BN, S, k::kEpiBias, false>(a, s); break;
+        case k::kEpiGelu: pair ? launch<BN, 6, k::kEpiGelu, true>(a, s) : launch<BN, S, k::kEpiGelu, false>(a, s); break;
+        case k::kEpiResidual:
+            pair ? launch<BN, 6, k::kEpiResidual, true>(a, s) : launch<BN, S, k::kEpiResidual, false>(a, s);
+            break;
         default: fail(kInvalidArgument, "gemm: unknown epilogue");
     }
 }
