@@ -165,6 +165,14 @@ int vb_attention(int dtype, const int32_t* row_ptr, const void* edges, int64_t d
                  const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, const void* xr, int64_t ldxr,
                  void* out, int64_t ldo, const float* w_e, int C, int heads, int head_dim, void* stream);
 
+/* vb_attention over an explicit list of destination rows (n_rows graph rows, ascending, each in
+ * [0, rows of q/out)): the engine's split of a sharded processor block into interior rows (computed
+ * while the halo exchange is in flight) and boundary rows. Same per-row arithmetic as vb_attention. */
+int vb_attention_rows(int dtype, const int32_t* row_ptr, const void* edges, const int32_t* rows, int64_t n_rows,
+                      const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, const void* xr,
+                      int64_t ldxr, void* out, int64_t ldo, const float* w_e, int C, int heads, int head_dim,
+                      void* stream);
+
 /* No-allocation variant of vb_attention, no reference counterpart: same arguments and result, each
  * destination row's edges cut into `splits` parts (1..64) whose partial softmax results go to one
  * static device array of 16 MiB (its only device storage; nothing is allocated, nothing needs to start

@@ -322,3 +322,32 @@ def test_gemm_cta_pair(M, N, K, lda, epi, monkeypatch):
     assert not np.isnan(outs[0]).any()
     assert oracle.rel_absmax(outs[0], ref) <= 2e-3
     assert oracle.rel_absmax(outs[0], outs[1]) <= 2e-3
+
+
+@pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])
+@pytest.mark.parametrize("C,heads", [(128, 4), (1024, 16)])
+def test_attention_row_list_bitwise(C, heads, dt):
+    """The gather attention over an explicit row list (the engine's interior / boundary split) is bitwise
+    the range launch on those rows."""
+    rng = np.random.default_rng(C + dt)
+    hd, A = C // heads, 3
+    n_src, n_dst, ld = 131, 97, C + 8
+    ei, ea = make_graph(rng, n_src, n_dst, A)
+    rp, src, _, attr = vb.build_csr(ei, ea, n_src, n_dst)
+    attr = rounded(attr, dt)
+    q, k, v, xr = (rounded(rng.normal(size=(n, ld)), dt) for n in (n_dst, n_src, n_src, n_dst))
+    w4 = np.zeros((4, C), np.float32)
+    w4[:A] = rounded(rng.normal(size=(C, A)) * 0.5, dt).T
+    edges = vb.pack_edges(src, attr, round_fp16=False)
+    T = tname(dt)
+    d_rp, d_ed, d_w = dev(rp, torch.int32), dev(edges, torch.float32), dev(w4, torch.float32)
+    d_q, d_k, d_v, d_x = dev(q, T), dev(k, T), dev(v, T), dev(xr, T)
+    ref = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
+    vb.attention(dt, d_rp, d_ed, 0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld, ref, C, d_w, C, heads, hd)
+    rows = rng.permutation(n_dst).astype(np.int32)
+    got = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
+    for part in (rows[:40], rows[40:]):
+        vb.attention_rows(dt, d_rp, d_ed, dev(np.sort(part), torch.int32), len(part), d_q, ld, d_k, d_v, ld, d_x, ld,
+                          got, C, d_w, C, heads, hd)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)

@@ -303,6 +303,27 @@ int vb_attention(int dtype, const int32_t* row_ptr, const void* edges, int64_t d
     });
 }
 
+int vb_attention_rows(int dtype, const int32_t* row_ptr, const void* edges, const int32_t* rows, int64_t n_rows,
+                      const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, const void* xr,
+                      int64_t ldxr, void* out, int64_t ldo, const float* w_e, int C, int heads, int head_dim,
+                      void* stream) {
+    return guard([&] {
+        need(row_ptr, "row_ptr"), need(rows, "rows"), need(w_e, "w_e");
+        auto run = [&](auto* tag) {
+            using T = std::remove_pointer_t<decltype(tag)>;
+            vb::k::AttnArgs<T> a;
+            a.row_ptr = row_ptr, a.edges = static_cast<const vb::EdgeRec*>(edges), a.dst_lo = 0, a.rows = rows;
+            a.n_rows = n_rows, a.q = static_cast<const T*>(q), a.ldq = ldq, a.k = static_cast<const T*>(k);
+            a.v = static_cast<const T*>(v), a.ldkv = ldkv, a.xr = static_cast<const T*>(xr), a.ldxr = ldxr;
+            a.out = static_cast<T*>(out), a.ldo = ldo, a.w_e = w_e, a.C = C, a.heads = heads, a.head_dim = head_dim;
+            vb::k::attention<T>(a, S(stream));
+        };
+        if (dtype == VB_PRECISION_FP32) run(static_cast<float*>(nullptr));
+        else if (dtype == VB_PRECISION_FP16) run(static_cast<__half*>(nullptr));
+        else vb::fail(vb::kInvalidArgument, "dtype");
+    });
+}
+
 int vb_attention_split_noalloc(int dtype, const int32_t* row_ptr, const void* edges, int64_t dst_lo, int64_t n_rows,
                                const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv, const void* xr,
                                int64_t ldxr, void* out, int64_t ldo, const float* w_e, int C, int heads, int head_dim,

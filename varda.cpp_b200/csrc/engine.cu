@@ -274,6 +274,15 @@ private:
         int64_t n_send = 0, n_recv = 0;                                // in rows
     };
     Xchg xp_, xd_;
+    // overlap (sharded, graph / eager runs without profiling): the processor's K|V halo exchange runs
+    // on cs_ while the attention of the interior rows (no remote source) runs; the boundary rows follow
+    cudaStream_t cs_ = nullptr;
+    cudaEvent_t ev_kv_ = nullptr, ev_halo_ = nullptr;
+    DeviceBuffer proc_inner_, proc_outer_;
+    int64_t n_inner_ = 0, n_outer_ = 0;
+    void attention_rows(const GraphDev& g, const Block<T>& b, const DeviceBuffer& rows, int64_t n, const T* q,
+                        int64_t ldq, const T* kk, const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out,
+                        cudaStream_t s);
     T *xsend_ = nullptr, *xrecv_ = nullptr;
     // the encoder's halo input rows (all T_in slots) from their owners, at the start of every forward
     Xchg xx_;
@@ -620,6 +629,20 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     }
     g_enc_ = upload_graph(plan_.enc, "enc", 0);
     g_proc_ = upload_graph(plan_.proc_g, "proc", 0);
+    if (plan_.world > 1) {  // processor rows with and without a remote (halo) source
+        std::vector<int32_t> inner, outer;
+        const CsrGraph& pg = plan_.proc_g;
+        for (int64_t r = 0; r < pg.n_dst; ++r) {
+            bool remote = false;
+            for (int32_t e = pg.row_ptr[size_t(r)]; e < pg.row_ptr[size_t(r + 1)] && !remote; ++e)
+                remote = pg.src[size_t(e)] >= Hl_;
+            (remote ? outer : inner).push_back(int32_t(r));
+        }
+        if (int64_t(inner.size() + outer.size()) != Hl_) fail(kInternal, "processor row split");
+        n_inner_ = int64_t(inner.size()), n_outer_ = int64_t(outer.size());
+        proc_inner_ = upload(inner.data(), std::max<size_t>(1, inner.size()) * sizeof(int32_t));
+        proc_outer_ = upload(outer.data(), std::max<size_t>(1, outer.size()) * sizeof(int32_t));
+    }
     g_dec_ = upload_graph(plan_.dec_g, "dec", dec_rows_ < Gl_ ? dec_rows_ : 0);
     for (CsrGraph* g : {&plan_.enc, &plan_.proc_g, &plan_.dec_g}) *g = CsrGraph{};  // host copies not needed
 
@@ -695,6 +718,10 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         xx_send_ = actf(size_t(std::max<int64_t>(1, xx_.n_send) * T_in_ * V_in_));
         xx_recv_ = actf(size_t(std::max<int64_t>(1, xx_.n_recv) * T_in_ * V_in_));
         comm_ = std::make_unique<Comm>(plan_.world, plan_.rank, opts_.nccl_id);
+        VB_CUDA(cudaStreamCreateWithFlags(&cs_, cudaStreamNonBlocking));
+        VB_CUDA(cudaEventCreateWithFlags(&ev_kv_, cudaEventDisableTiming));
+        VB_CUDA(cudaEventCreateWithFlags(&ev_halo_, cudaEventDisableTiming));
+
     }
     VB_CUDA(cudaDeviceSynchronize());
 }
@@ -705,6 +732,9 @@ Engine<T>::~Engine() {
     if (stream_) cudaStreamSynchronize(stream_);
     if (graph_exec_) cudaGraphExecDestroy(graph_exec_);  // before the communicator its nodes use
     rollout_release();
+    if (cs_) cudaStreamSynchronize(cs_), cudaStreamDestroy(cs_);
+    if (ev_kv_) cudaEventDestroy(ev_kv_);
+    if (ev_halo_) cudaEventDestroy(ev_halo_);
     comm_.reset();
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -810,6 +840,19 @@ void Engine<T>::attention(const GraphDev& g, const Block<T>& b, int64_t lo, int6
     k::attention<T>(a, s);
 }
 
+// The gather attention over an explicit list of rows (local ids) of graph g.
+template <class T>
+void Engine<T>::attention_rows(const GraphDev& g, const Block<T>& b, const DeviceBuffer& rows, int64_t n, const T* q,
+                               int64_t ldq, const T* kk, const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out,
+                               cudaStream_t s) {
+    if (n <= 0) return;
+    k::AttnArgs<T> a;
+    a.row_ptr = g.rp(), a.edges = g.ed(), a.dst_lo = 0, a.n_rows = n, a.rows = rows.template as<int32_t>();
+    a.q = q, a.ldq = ldq, a.k = kk, a.v = v, a.ldkv = ldkv, a.xr = xr, a.ldxr = ldxr, a.out = out, a.ldo = C_;
+    a.w_e = b.w_e.template as<float>(), a.C = C_, a.heads = heads_, a.head_dim = hd_;
+    k::attention<T>(a, s);
+}
+
 template <class T>
 void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
     // G: this rank's data rows (own, then the encoder's halo) for the encoder's source side;
@@ -853,13 +896,30 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
     ln(z_enc_, proc_[0].ln_dst, xh_, H, s);
 
     // ---- processor; xh_ holds LN_dst of the block input
+    // sharded: exchange / interior-attention overlap, except under the hook or the profiler (whose
+    // per-launch records stay serial) and when the processor runs the tiled or split kernels
+    const bool overlap = plan_.world > 1 && cs_ && !hk && !prof_ && !g_proc_.tiled && !g_proc_.wide &&
+                         env_int("VB_SHARD_OVERLAP", 1) != 0;
     T* z_in = z_enc_;
     T* latent = nullptr;
     for (int i = 0; i < n_proc_; ++i) {
         const Block<T>& b = proc_[size_t(i)];
         linear(b.qkvs, xh_, C, qkvs_, 4 * C, H, s);
-        exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, s);  // K|V of remote sources
-        attention(g_proc_, b, 0, H, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C, 4 * C, sbuf_, s);
+        if (overlap) {
+            // K|V of remote sources on the communication stream while the interior rows run
+            VB_CUDA(cudaEventRecord(ev_kv_, s));
+            VB_CUDA(cudaStreamWaitEvent(cs_, ev_kv_, 0));
+            exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, cs_);
+            VB_CUDA(cudaEventRecord(ev_halo_, cs_));
+            attention_rows(g_proc_, b, proc_inner_, n_inner_, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C,
+                           qkvs_ + 3 * C, 4 * C, sbuf_, s);
+            VB_CUDA(cudaStreamWaitEvent(s, ev_halo_, 0));
+            attention_rows(g_proc_, b, proc_outer_, n_outer_, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C,
+                           qkvs_ + 3 * C, 4 * C, sbuf_, s);
+        } else {
+            exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, s);  // K|V of remote sources
+            attention(g_proc_, b, 0, H, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C, 4 * C, sbuf_, s);
+        }
         linear(b.proj, sbuf_, C, out1_, C, H, s, k::kEpiResidual, z_in, C);
         ln(out1_, b.ln_mlp, xh_, H, s);
         linear(b.mlp1, xh_, C, hbuf_, mlp_, H, s, k::kEpiGelu);
@@ -884,7 +944,16 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
     // ---- decoder, source side: [k | v] of LN_src(latent)
     T* kv_dec = qkvs_;
     linear(dec_.kv, xh_, C, kv_dec, 2 * C, H, s);
-    exchange(xd_, kv_dec, 2 * C, kv_dec + H * 2 * C, 2 * C, true, s);
+    bool dec_halo_pending = false;
+    if (overlap) {  // the decoder's K|V halo flies while the first chunk's destination GEMMs run
+        VB_CUDA(cudaEventRecord(ev_kv_, s));
+        VB_CUDA(cudaStreamWaitEvent(cs_, ev_kv_, 0));
+        exchange(xd_, kv_dec, 2 * C, kv_dec + H * 2 * C, 2 * C, true, cs_);
+        VB_CUDA(cudaEventRecord(ev_halo_, cs_));
+        dec_halo_pending = true;
+    } else {
+        exchange(xd_, kv_dec, 2 * C, kv_dec + H * 2 * C, 2 * C, true, s);
+    }
 
     // ---- decoder, destination chunks of data rows
     std::vector<float> h_emb, h_bo;
@@ -902,6 +971,10 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
         if (hk) hk->fetch(e, C, n, C, h_emb.data(), lo);
         ln(e, dec_.ln_dst, t, n, s);
         linear(dec_.qs, t, C, qs, 2 * C, n, s);
+        if (dec_halo_pending) {
+            VB_CUDA(cudaStreamWaitEvent(s, ev_halo_, 0));
+            dec_halo_pending = false;
+        }
         attention(g_dec_, dec_, lo, n, qs, 2 * C, kv_dec, kv_dec + C, 2 * C, qs + C, 2 * C, sb, s);
         linear(dec_.proj, sb, C, o1, C, n, s, k::kEpiResidual, e, C);
         ln(o1, dec_.ln_mlp, t, n, s);

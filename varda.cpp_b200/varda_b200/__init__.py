@@ -65,6 +65,7 @@ def _load_lib():
         "vb_layernorm": ([I, P, I64, P, P, P, I64, I64, I, F, P], I),
         "vb_add_layernorm": ([I, P, P, P, P, P, P, I64, I64, I, F, P], I),
         "vb_rollout": ([P, P, I, P, P, I, P, P, P], I),
+        "vb_attention_rows": ([I, P, P, P, I64, P, I64, P, P, I64, P, I64, P, I64, P, I, I, I, P], I),
         "vb_attention_split_noalloc": ([I, P, P, I64, I64, P, I64, P, P, I64, P, I64, P, I64, P, I, I, I, I, P], I),
         "vb_rollout_update": ([P, I, I64, I, P, P, I64, I, P, I, P, P, P], I),
     }
@@ -269,6 +270,12 @@ def attention(dtype, row_ptr, edges, dst_lo, n_rows, q, ldq, k, v, ldkv, xr, ldx
               head_dim, stream=None):
     check(lib.vb_attention(dtype, _ptr(row_ptr), _ptr(edges), dst_lo, n_rows, _ptr(q), ldq, _ptr(k), _ptr(v), ldkv,
                            _ptr(xr), ldxr, _ptr(out), ldo, _ptr(w_e), C, heads, head_dim, stream))
+
+
+def attention_rows(dtype, row_ptr, edges, rows, n_rows, q, ldq, k, v, ldkv, xr, ldxr, out, ldo, w_e, C, heads,
+                   head_dim, stream=None):
+    check(lib.vb_attention_rows(dtype, _ptr(row_ptr), _ptr(edges), _ptr(rows), n_rows, _ptr(q), ldq, _ptr(k), _ptr(v),
+                                ldkv, _ptr(xr), ldxr, _ptr(out), ldo, _ptr(w_e), C, heads, head_dim, stream))
 
 
 def attention_split_noalloc(dtype, row_ptr, edges, dst_lo, n_rows, q, ldq, k, v, ldkv, xr, ldxr, out, ldo, w_e, C,
