@@ -278,6 +278,7 @@ __device__ __forceinline__ float2 gelu_as2(float2 x) {
     // to [-2.5, -1] (|x| > 6.5 rounds to x or -0 in fp16 whatever t is), a cubic first guess of 1 / d
     // (relative error 1.6e-2 on d in [1, 2.5], least-squares fit), then two Newton steps
     // t <- t + t (1 - d t): relative error 1.5e-7, the accuracy of the erf approximation itself
+#ifndef VB_GELU_SFU_RCP
     const float2 nd = __ffma2_rn(make_float2(-0.3275911f, -0.3275911f), z, make_float2(-1.0f, -1.0f));
     const float2 n = make_float2(fmaxf(nd.x, -2.5f), fmaxf(nd.y, -2.5f));
     float2 t = __ffma2_rn(n, make_float2(0.10437007f, 0.10437007f), make_float2(0.76159483f, 0.76159483f));
@@ -285,6 +286,12 @@ __device__ __forceinline__ float2 gelu_as2(float2 x) {
     t = __ffma2_rn(t, n, make_float2(2.3650432f, 2.3650432f));
     t = __ffma2_rn(t, __ffma2_rn(n, t, make_float2(1.0f, 1.0f)), t);
     t = __ffma2_rn(t, __ffma2_rn(n, t, make_float2(1.0f, 1.0f)), t);
+#else
+    const float2 den = __ffma2_rn(make_float2(0.3275911f, 0.3275911f), z, make_float2(1.0f, 1.0f));
+    float2 t;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.x) : "f"(den.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.y) : "f"(den.y));
+#endif
     float2 p = __ffma2_rn(t, make_float2(0.5307027145f, 0.5307027145f), make_float2(-0.7265760135f, -0.7265760135f));
     p = __ffma2_rn(t, p, make_float2(0.7107068705f, 0.7107068705f));
     p = __ffma2_rn(t, p, make_float2(-0.142248368f, -0.142248368f));
