@@ -108,3 +108,21 @@ def test_load_rejects_missing_file(tmp_path):
 
 def test_python_binding_requires_library():
     assert os.path.exists(vb.LIB_PATH)
+
+
+def test_build_csr_bit_exact_threaded():
+    """Above 2^20 edges the CSR build runs on several threads (per-thread counts, slots handed out in
+    range order): still the one-pass stable counting sort, bit for bit."""
+    rng = np.random.default_rng(11)
+    ns, nd, E, A = 50000, 30000, 3_000_000, 3
+    ei = random_graph(rng, ns, nd, E)
+    ea = rng.normal(size=(E, A)).astype(np.float32)
+    rp, src, eid, attr = vb.build_csr(ei, ea, ns, nd)
+    order = np.argsort(ei[1], kind="stable")
+    assert np.array_equal(eid, order)
+    assert np.array_equal(src, ei[0][order])
+    assert np.array_equal(attr, ea[order])
+    assert np.array_equal(rp, np.concatenate([[0], np.cumsum(np.bincount(ei[1], minlength=nd))]))
+    packed = vb.pack_edges(src, attr, round_fp16=True)
+    assert np.array_equal(packed[:, :3], attr.astype(np.float16).astype(np.float32))
+    assert np.array_equal(packed[:, 3].view(np.int32), src)

@@ -6,6 +6,8 @@
 #include <cstring>
 #include <limits>
 #include <string>
+#include <thread>
+#include <vector>
 
 #include "common.h"
 
@@ -18,6 +20,24 @@ int32_t CsrGraph::max_degree() const {
 }
 
 namespace {
+
+// Threads for the host-side graph passes: a few for large graphs, one below kParallelEdges edges.
+constexpr int64_t kParallelEdges = 1 << 20;
+int graph_threads(int64_t E) {
+    if (E < kParallelEdges) return 1;
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    return int(std::min<int64_t>(std::min<unsigned>(hw, 16u), E / (kParallelEdges / 2)));
+}
+template <class F> void parallel_chunks(int nt, int64_t n, F f) {  // f(t, begin, end) on nt threads
+    if (nt <= 1) return f(0, int64_t(0), n);
+    std::vector<std::thread> ts;
+    for (int t = 0; t < nt; ++t) ts.emplace_back(f, t, n * t / nt, n * (t + 1) / nt);
+    for (auto& th : ts) th.join();
+}
+
+// Stable counting sort by destination on nt threads: thread t counts the destinations of its
+// contiguous edge range, every destination's slots are handed out to the threads in range order, and
+// each thread scatters its range in order, so the result is the one-thread order exactly.
 template <class I>
 CsrGraph build(const I* ei, int64_t E, const float* ea, int A, int64_t n_src, int64_t n_dst, const std::string& name) {
     constexpr int64_t kMax = std::numeric_limits<int32_t>::max();
@@ -27,24 +47,44 @@ CsrGraph build(const I* ei, int64_t E, const float* ea, int A, int64_t n_src, in
     g.n_dst = n_dst;
     g.n_edges = E;
     g.attr_dim = A;
+    const int nt = graph_threads(E);
+    std::vector<std::vector<int32_t>> cnt(size_t(nt), std::vector<int32_t>(size_t(n_dst), 0));
+    std::vector<int64_t> bad(size_t(nt), -1);  // first out-of-range edge of each thread's range
+    parallel_chunks(nt, E, [&](int t, int64_t b, int64_t e) {
+        int32_t* c = cnt[size_t(t)].data();
+        for (int64_t i = b; i < e; ++i) {
+            const int64_t s = int64_t(ei[i]), d = int64_t(ei[E + i]);
+            if (s < 0 || s >= n_src || d < 0 || d >= n_dst) {
+                bad[size_t(t)] = i;
+                return;
+            }
+            ++c[d];
+        }
+    });
+    for (int t = 0; t < nt; ++t)
+        if (bad[size_t(t)] >= 0) fail(kFormat, name + ": edge " + std::to_string(bad[size_t(t)]) + " out of range");
     g.row_ptr.assign(size_t(n_dst + 1), 0);
-    for (int64_t e = 0; e < E; ++e) {
-        const int64_t s = int64_t(ei[e]), d = int64_t(ei[E + e]);
-        if (s < 0 || s >= n_src || d < 0 || d >= n_dst)
-            fail(kFormat, name + ": edge " + std::to_string(e) + " out of range");
-        ++g.row_ptr[size_t(d + 1)];
+    for (int64_t d = 0; d < n_dst; ++d) {  // row_ptr, and cnt[t][d] becomes thread t's first slot of d
+        int32_t off = g.row_ptr[size_t(d)];
+        for (int t = 0; t < nt; ++t) {
+            const int32_t c = cnt[size_t(t)][size_t(d)];
+            cnt[size_t(t)][size_t(d)] = off;
+            off += c;
+        }
+        g.row_ptr[size_t(d + 1)] = off;
     }
-    for (int64_t d = 0; d < n_dst; ++d) g.row_ptr[size_t(d + 1)] += g.row_ptr[size_t(d)];
-    std::vector<int32_t> next(g.row_ptr.begin(), g.row_ptr.end() - 1);
     g.src.resize(size_t(E));
     g.edge_id.resize(size_t(E));
     g.attr.resize(size_t(E) * size_t(A));
-    for (int64_t e = 0; e < E; ++e) {
-        const int32_t slot = next[size_t(ei[E + e])]++;
-        g.src[size_t(slot)] = int32_t(ei[e]);
-        g.edge_id[size_t(slot)] = int32_t(e);
-        std::memcpy(&g.attr[size_t(slot) * size_t(A)], ea + e * A, sizeof(float) * size_t(A));
-    }
+    parallel_chunks(nt, E, [&](int t, int64_t b, int64_t e) {
+        int32_t* next = cnt[size_t(t)].data();
+        for (int64_t i = b; i < e; ++i) {
+            const int32_t slot = next[ei[E + i]]++;
+            g.src[size_t(slot)] = int32_t(ei[i]);
+            g.edge_id[size_t(slot)] = int32_t(i);
+            std::memcpy(&g.attr[size_t(slot) * size_t(A)], ea + i * A, sizeof(float) * size_t(A));
+        }
+    });
     return g;
 }
 }  // namespace
@@ -68,14 +108,16 @@ CsrGraph build_csr_by_dst(const int64_t* ei, int64_t E, const float* ea, int A, 
 std::vector<EdgeRec> pack_edges(const CsrGraph& g, bool round_fp16) {
     if (g.attr_dim > 3) fail(kUnsupported, "edge_attr_dim must be 1..3 (16-byte edge records)");
     std::vector<EdgeRec> out(size_t(g.n_edges));
-    for (int64_t e = 0; e < g.n_edges; ++e) {
-        float a[3] = {0.f, 0.f, 0.f};
-        for (int k = 0; k < g.attr_dim; ++k) {
-            const float v = g.attr[size_t(e) * size_t(g.attr_dim) + size_t(k)];
-            a[k] = round_fp16 ? __half2float(__float2half_rn(v)) : v;
+    parallel_chunks(graph_threads(g.n_edges), g.n_edges, [&](int, int64_t b, int64_t end) {
+        for (int64_t e = b; e < end; ++e) {
+            float a[3] = {0.f, 0.f, 0.f};
+            for (int k = 0; k < g.attr_dim; ++k) {
+                const float v = g.attr[size_t(e) * size_t(g.attr_dim) + size_t(k)];
+                a[k] = round_fp16 ? __half2float(__float2half_rn(v)) : v;
+            }
+            out[size_t(e)] = {a[0], a[1], a[2], g.src[size_t(e)]};
         }
-        out[size_t(e)] = {a[0], a[1], a[2], g.src[size_t(e)]};
-    }
+    });
     return out;
 }
 
