@@ -11,6 +11,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -59,6 +60,18 @@ bool tiled_for(const std::string& graph, const char* dflt) {
     }
     return false;
 }
+
+// Load-stage timer: VB_LOAD_TIMING=1 prints the seconds of each stage of a model load to stderr.
+struct LoadTimer {
+    bool on = env_int("VB_LOAD_TIMING", 0) != 0;
+    std::chrono::steady_clock::time_point t = std::chrono::steady_clock::now();
+    void mark(const char* stage) {
+        if (!on) return;
+        const auto now = std::chrono::steady_clock::now();
+        std::fprintf(stderr, "varda_b200 load: %-28s %.3f s\n", stage, std::chrono::duration<double>(now - t).count());
+        t = now;
+    }
+};
 
 template <class T> struct Lin {
     DeviceBuffer w, b;
@@ -548,6 +561,7 @@ float* Engine<T>::actf(size_t elems) {
 template <class T>
 Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     dev_ = o.cuda_device;
+    LoadTimer lt;
     SafeTensorsFile file(path);
     if (file.metadata("varda_format") != "1")
         fail(kFormat, path + ": unsupported varda_format " + file.metadata("varda_format"));
@@ -612,10 +626,13 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
 
     // ---- graphs and the destination partition (the identity on one GPU)
     {
+        lt.mark("open + config");
         CsrGraph enc = read_graph(file, "enc", G_, H_);
         CsrGraph proc = read_graph(file, "proc", H_, H_);
         CsrGraph dec = read_graph(file, "dec", H_, G_);
+        lt.mark("CSR build");
         plan_ = make_plan(cfg_, enc, proc, dec, opts_.world, opts_.rank);
+        lt.mark("partition plan");
     }
     Hl_ = plan_.h_hi - plan_.h_lo, Gl_ = plan_.g_hi - plan_.g_lo;
     n_eh_ = int64_t(plan_.enc_halo.size()), n_ph_ = int64_t(plan_.proc.halo.size());
@@ -628,6 +645,7 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         dec_rows_ = std::min<int64_t>(int64_t(align_up(size_t((Gl_ + nch - 1) / nch), 128)), std::max<int64_t>(Gl_, 1));
     }
     g_enc_ = upload_graph(plan_.enc, "enc", 0);
+    lt.mark("encoder graph upload");
     g_proc_ = upload_graph(plan_.proc_g, "proc", 0);
     if (plan_.world > 1) {  // processor rows with and without a remote (halo) source
         std::vector<int32_t> inner, outer;
@@ -644,6 +662,7 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         proc_outer_ = upload(outer.data(), std::max<size_t>(1, outer.size()) * sizeof(int32_t));
     }
     g_dec_ = upload_graph(plan_.dec_g, "dec", dec_rows_ < Gl_ ? dec_rows_ : 0);
+    lt.mark("processor + decoder graphs");
     for (CsrGraph* g : {&plan_.enc, &plan_.proc_g, &plan_.dec_g}) *g = CsrGraph{};  // host copies not needed
 
     // ---- node attributes: data rows [own | encoder halo], own hidden rows (and the optional grid
@@ -673,6 +692,7 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         h_attr_ = upload(hp.data(), hp.size() * sizeof(T));
     }
 
+    lt.mark("node attributes");
     // ---- weights
     enc_emb_src_ = load_linear(file, {"enc.emb_src"}, C_, F_);
     enc_emb_dst_ = load_linear(file, {"enc.emb_dst"}, C_, A_node_);
@@ -684,6 +704,7 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     dec_ = load_block(file, "dec.block", true);
     file.require_all_consumed();
 
+    lt.mark("weights");
     // ---- activations (this rank's rows)
     x_dev_ = actf(size_t(input_numel()));
     xn_ = actf(size_t(input_numel()));
@@ -717,13 +738,16 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         setup_exchange(xx_, plan_.enc_x, plan_.g_lo, int64_t(T_in_) * V_in_);
         xx_send_ = actf(size_t(std::max<int64_t>(1, xx_.n_send) * T_in_ * V_in_));
         xx_recv_ = actf(size_t(std::max<int64_t>(1, xx_.n_recv) * T_in_ * V_in_));
+        lt.mark("activations + exchange plans");
         comm_ = std::make_unique<Comm>(plan_.world, plan_.rank, opts_.nccl_id);
+        lt.mark("NCCL communicator");
         VB_CUDA(cudaStreamCreateWithFlags(&cs_, cudaStreamNonBlocking));
         VB_CUDA(cudaEventCreateWithFlags(&ev_kv_, cudaEventDisableTiming));
         VB_CUDA(cudaEventCreateWithFlags(&ev_halo_, cudaEventDisableTiming));
 
     }
     VB_CUDA(cudaDeviceSynchronize());
+    lt.mark("done");
 }
 
 template <class T>
