@@ -324,6 +324,48 @@ def test_gemm_cta_pair(M, N, K, lda, epi, monkeypatch):
     assert oracle.rel_absmax(outs[0], outs[1]) <= 2e-3
 
 
+@pytest.mark.parametrize("M,N,K,epi", [(20000, 1024, 256, 2), (9000, 4096, 128, 1), (300, 2048, 512, 0),
+                                       (70000, 256, 64, 0), (5000, 128, 192, 2)])
+@pytest.mark.parametrize("pair", ["1", "0"])
+def test_gemm_tile_order_bitwise(M, N, K, epi, pair, monkeypatch):
+    """Dynamic tile order (each CTA or CTA pair takes its next tile from a per-stream counter) against
+    the static order (VB_GEMM_SCHED=0): the same tiles with the same k order, so bitwise equal; repeated
+    launches (the counter is zeroed by each launch's last CTA) and launches interleaved on two streams
+    (a counter each) too."""
+    rng = np.random.default_rng(M + N + K + epi)
+    T = torch.float16
+    A = dev(rounded(rng.normal(size=(M, K)), vb.FP16), T)
+    W = dev(rounded(rng.normal(size=(N, K)) / math.sqrt(K), vb.FP16), T)
+    b = dev(rounded(rng.normal(size=N) * 0.2, vb.FP16), T)
+    R = dev(rounded(rng.normal(size=(M, N)), vb.FP16), T) if epi == 2 else None
+    monkeypatch.setenv("VB_GEMM_PAIR", pair)
+
+    def run(stream=None):
+        Y = torch.full((M, N), float("nan"), device="cuda", dtype=T)
+        kw = {}
+        if stream is not None:
+            stream.wait_stream(torch.cuda.current_stream())  # the fill above is on the current stream
+            kw = {"stream": stream.cuda_stream}
+        vb.gemm(vb.FP16, 2, A, K, W, K, b, Y, N, R, N, M, N, K, epi, **kw)
+        return Y
+
+    monkeypatch.setenv("VB_GEMM_SCHED", "0")
+    ref = run()
+    torch.cuda.synchronize()
+    vb.check_device()
+    assert not torch.isnan(ref.float()).any()
+    monkeypatch.setenv("VB_GEMM_SCHED", "1")
+    outs = [run() for _ in range(3)]
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    for _ in range(2):
+        outs.append(run(s1))
+        outs.append(run(s2))
+    torch.cuda.synchronize()
+    vb.check_device()
+    for o in outs:
+        assert torch.equal(o, ref)
+
+
 @pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])
 @pytest.mark.parametrize("C,heads", [(128, 4), (1024, 16)])
 def test_attention_row_list_bitwise(C, heads, dt):

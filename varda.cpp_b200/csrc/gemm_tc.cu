@@ -31,8 +31,11 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstdlib>
+#include <map>
 #include <mutex>
 #include <string>
+#include <thread>
+#include <tuple>
 
 #include "common.h"
 #include "dev.cuh"
@@ -50,6 +53,9 @@ using vb::d::to_f;
 constexpr int BM = 128, BK = 64;
 constexpr int kEpiWarps = 8, kThreads = 32 * (2 + kEpiWarps);
 constexpr unsigned long long kTimeoutNs = 4000000000ull;  // 4 s
+// Dynamic tile order: the tile indices a CTA (pair) takes from the launch's counter pass through a
+// ring of kRing slots in shared memory, from the producer lane (the pair leader's) to every role.
+constexpr int kRing = 8;
 
 __device__ int g_error = 0;
 
@@ -62,6 +68,7 @@ struct Params {
     int M, N, K;
     int epi;
     int gelu_tanh;
+    unsigned* sched;  // dynamic tile order: [tiles handed out, fetchers done], zero between launches; or null
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
@@ -90,13 +97,27 @@ __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// ... with acquire at cluster scope (for arrivals that carry another CTA's shared-memory writes)
+__device__ __forceinline__ bool mbar_test_cl(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // Bounded wait for the phase of parity `parity`. Returns false on timeout (after raising the CTA's
 // abort flag and the device error flag) or when another role already aborted.
+template <bool CL = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
-    if (mbar_test(b, parity)) return true;
+    auto test = [&] { return CL ? mbar_test_cl(b, parity) : mbar_test(b, parity); };
+    if (test()) return true;
     const uint64_t t0 = now_ns();
     for (;;) {
-        if (mbar_test(b, parity)) return true;
+        if (test()) return true;
         if (*abort_flag) return false;
         if (now_ns() - t0 > kTimeoutNs) {
             *abort_flag = 1;
@@ -173,6 +194,9 @@ __device__ __forceinline__ void cluster_sync() {
 }
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 // TMA tile load into this CTA's shared memory whose bytes complete on the barrier at `bar_cluster`
 // (the pair leader's); no multicast.
@@ -254,15 +278,15 @@ __device__ __forceinline__ float ex2f(float x) {
 }
 
 // Shared memory: the A/W stage ring, then per epilogue warp two 2 KB output staging buffers, then the
-// mbarriers.
+// mbarriers, the TMEM address and abort flag, and the ring of tile indices (dynamic tile order).
 template <int BN, int STAGES, int EPI, bool PAIR> struct Layout {
     static constexpr int kA = BM * BK * 2;                   // bytes per A stage
     static constexpr int kB = (PAIR ? BN / 2 : BN) * BK * 2;  // this CTA's rows of W per stage
     static constexpr int kTiles = STAGES * (kA + kB);
     static constexpr int kSub = 32 * 32 * 2;  // one 32 x 32 fp16 sub-tile
     static constexpr int kOut = kEpiWarps * 2 * kSub;
-    static constexpr int kBars = (2 * STAGES + 5) * 8;
-    static constexpr int kSmem = 1024 + kTiles + kOut + kBars + 16;  // 1024: alignment slack
+    static constexpr int kBars = (2 * STAGES + 5 + 2 * kRing) * 8;
+    static constexpr int kSmem = 1024 + kTiles + kOut + kBars + 16 + 4 * kRing;  // 1024: alignment slack
     static_assert(kSmem <= 232448, "shared memory over the 227 KB per-CTA limit");
 };
 
@@ -325,8 +349,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tfull = bars + 2 * STAGES;
     uint64_t* tempty = bars + 2 * STAGES + 2;
     uint64_t* drain = bars + 2 * STAGES + 4;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    uint64_t* rfull = bars + 2 * STAGES + 5;  // tile ring: slot written
+    uint64_t* rempty = rfull + kRing;         // tile ring: slot read by every role of the CTA (pair)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + kRing);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* ring = reinterpret_cast<volatile int*>(tmem_slot + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = PAIR ? cluster_rank() : 0u;  // 0: the pair leader (issues the MMAs)
@@ -335,6 +362,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the leader's accumulator is released by the epilogue warps of both CTAs
         for (int b = 0; b < 2; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);
         mbar_init(drain, 1);
+        // ring readers: the MMA lane and the epilogue warps (+ the peer's producer lane and epilogue warps)
+        for (int r = 0; r < kRing; ++r)
+            mbar_init(&rfull[r], 1), mbar_init(&rempty[r], PAIR ? 2 + 2 * kEpiWarps : 1 + kEpiWarps);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -357,16 +387,61 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int n_m = (p.M + UM - 1) / UM, n_n = (p.N + BN - 1) / BN;
     const int tiles = n_m * n_n, kblocks = (p.K + BK - 1) / BK;
-    // tiles are handed out per CTA, or per pair (both CTAs of a pair walk the same sequence)
+    // tiles are handed out per CTA, or per pair (both CTAs of a pair walk the same sequence). Static
+    // order: tile unit0 + i * units. Dynamic order (p.sched): the first tile is unit0, each further one
+    // the next index of the launch's counter (+ units), fetched by the producer lane of the CTA (the
+    // leader's, for a pair) and passed to the other roles (and the peer CTA) through the tile ring, so
+    // the tiles in flight stay a contiguous window however the CTAs drift apart.
     const int unit0 = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
     const int units = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
+    const bool dyn = p.sched != nullptr;
+    // tile number `it` of the sequence, for the roles that read the ring (warp_wide: every lane waits
+    // and reads, lane 0 releases the slot); -1 after an abort
+    auto next_tile = [&](int it, bool warp_wide) -> int {
+        if (!dyn) return unit0 + it * units;
+        const int slot = it % kRing;
+        if (!mbar_wait<true>(&rfull[slot], uint32_t(it / kRing) & 1u, abort_flag)) return -1;
+        const int t = ring[slot];
+        if (warp_wide) __syncwarp();
+        if (!warp_wide || lane == 0) {
+            if (PAIR && rank != 0) mbar_arrive_cluster(mapa(smem_u32(&rempty[slot]), 0));
+            else mbar_arrive(&rempty[slot]);
+        }
+        return t;
+    };
+    // the fetching lane writes tile number `it` into the ring (and the peer's)
+    auto publish = [&](int it, int t) -> bool {
+        const int slot = it % kRing;
+        if (!mbar_wait<true>(&rempty[slot], (uint32_t(it / kRing) & 1u) ^ 1u, abort_flag)) return false;
+        ring[slot] = t;
+        if (PAIR) {
+            st_cluster_u32(mapa(smem_u32(const_cast<int*>(&ring[slot])), 1), uint32_t(t));
+            mbar_arrive_cluster(mapa(smem_u32(&rfull[slot]), 1));
+        }
+        mbar_arrive(&rfull[slot]);
+        return true;
+    };
 
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer
         int stage = 0;
         uint32_t phase = 0;
         uint32_t issued = 0, last_parity = 0;  // per-stage bit masks for the drain
-        for (int tile = unit0; tile < tiles && !*abort_flag; tile += units) {
+        const bool fetcher = !PAIR || rank == 0;
+        int nxt = unit0;
+        for (int it = 0; !*abort_flag; ++it) {
+            int tile;
+            if (!dyn) {
+                tile = unit0 + it * units;
+            } else if (fetcher) {
+                tile = nxt;
+                if (!publish(it, tile)) break;
+                // the following index: the atomic's latency hides behind this tile's loads
+                if (tile < tiles) nxt = units + int(atomicAdd(p.sched, 1u));
+            } else {
+                tile = next_tile(it, false);
+            }
+            if (tile < 0 || tile >= tiles) break;
             const int mb = tile / n_n, nb = tile - mb * n_n;
             for (int kb = 0; kb < kblocks; ++kb) {
                 if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
@@ -386,6 +461,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (++stage == STAGES) stage = 0, phase ^= 1;
             }
         }
+        if (dyn && fetcher) {  // the last fetcher to finish zeroes the counter for the next launch
+            __threadfence();
+            if (atomicAdd(p.sched + 1, 1u) == unsigned(units - 1)) {
+                atomicExch(p.sched, 0u);
+                atomicExch(p.sched + 1, 0u);
+            }
+        }
         if (*abort_flag) {  // let every load already issued land before the CTA exits
             if (!PAIR || rank == 0) {
                 for (int s = 0; s < STAGES; ++s)
@@ -403,7 +485,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t phase = 0;
         int it = 0;
         bool any = false;
-        for (int tile = unit0; tile < tiles && !*abort_flag; tile += units, ++it) {
+        for (;; ++it) {
+            if (*abort_flag) break;
+            const int tile = next_tile(it, false);
+            if (tile < 0 || tile >= tiles) break;
             const int ab = it & 1;
             const uint32_t ap = (it >> 1) & 1;
             if (!mbar_wait(&tempty[ab], ap ^ 1, abort_flag)) break;
@@ -476,7 +561,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 else mbar_arrive(&tempty[ab]);
             }
         };
-        for (int tile = unit0; tile < tiles; tile += units, ++it) {
+        for (;; ++it) {
+            const int tile = next_tile(it, true);
+            if (tile < 0 || tile >= tiles) break;
             const int ab = it & 1;
             const uint32_t ap = (it >> 1) & 1;
             const int mb = tile / n_n, nb = tile - mb * n_n;
@@ -610,6 +697,42 @@ CUtensorMap make_map(const __half* base, int64_t rows, int64_t cols, int64_t ld,
     return m;
 }
 
+// Per-stream tile counters for the dynamic tile order (g_sched, two words per stream: tiles handed
+// out, fetchers done; each launch leaves them zero). Launches on one stream run one after another, so a
+// counter per (device, stream) is never shared by two running launches; cudaStreamPerThread gets one
+// per thread. Static order (nullptr) when VB_GEMM_SCHED=0, when the slots are used up, or when the
+// first launch on a device comes during stream capture (the symbol lookup may load the module).
+constexpr int kSchedSlots = 1024, kMaxDevices = 64;
+__device__ unsigned g_sched[2 * kSchedSlots];
+
+unsigned* sched_counter(cudaStream_t s) {
+    const char* e = std::getenv("VB_GEMM_SCHED");
+    if (e && *e && std::atoi(e) == 0) return nullptr;
+    int dev = 0;
+    VB_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return nullptr;
+    static std::mutex mu;
+    static unsigned* base[kMaxDevices] = {};
+    static std::map<std::tuple<int, cudaStream_t, std::thread::id>, int> slot;
+    static int used[kMaxDevices] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (!base[dev]) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        VB_CUDA(cudaStreamIsCapturing(s, &cs));
+        if (cs != cudaStreamCaptureStatusNone) return nullptr;
+        void* a = nullptr;
+        VB_CUDA(cudaGetSymbolAddress(&a, g_sched));
+        base[dev] = static_cast<unsigned*>(a);
+    }
+    const auto key = std::make_tuple(dev, s, s == cudaStreamPerThread ? std::this_thread::get_id() : std::thread::id());
+    auto it = slot.find(key);
+    if (it == slot.end()) {
+        if (used[dev] == kSchedSlots) return nullptr;
+        it = slot.emplace(key, used[dev]++).first;
+    }
+    return base[dev] + 2 * it->second;
+}
+
 int sm_count() {
     static int n = 0;
     if (!n) {
@@ -633,7 +756,7 @@ void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
     const CUtensorMap tb = make_map(a.W, a.N, a.K, a.ldw, PAIR ? BN / 2 : BN);
     // 32 x 32 sub-tiles of the output, 64-byte swizzle: the epilogue's TMA stores
     const CUtensorMap tc = make_map(a.C, a.M, a.N, a.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-    Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0};
+    Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0, sched_counter(s)};
     constexpr int UM = PAIR ? 2 * BM : BM;
     const int64_t tiles = ((a.M + UM - 1) / UM) * ((a.N + BN - 1) / BN);
     if (!PAIR) {

@@ -55,11 +55,19 @@ def gemm(a):
     Y = torch.empty(a.M, a.N, device="cuda", dtype=torch.float16)
     s = torch.cuda.current_stream().cuda_stream
     fn = lambda: vb.gemm(vb.FP16, a.engine, A, a.K, W, a.K, b, Y, a.N, R, a.N, a.M, a.N, a.K, a.epi, stream=s)  # noqa
-    ms = time_launches(fn, a.iters, a.warmup)
-    tf = 2.0 * a.M * a.N * a.K / (ms * 1e-3) / 1e12
     pk = _peaks()
-    print(json.dumps({"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "engine": a.engine,
-                      "ms": round(ms, 4), "tflops": round(tf, 1), "frac_of_burst": round(tf / pk["bf16_tflops"], 3)}))
+    # --modes: comma-separated CTA-pair / tile-order settings timed one after another in this process
+    # (pair|single)_(dyn|static) -> VB_GEMM_PAIR, VB_GEMM_SCHED; default: the library's defaults
+    for mode in (a.modes.split(",") if a.modes else [""]):
+        if mode:
+            cta, order = mode.split("_")
+            os.environ["VB_GEMM_PAIR"] = "1" if cta == "pair" else "0"
+            os.environ["VB_GEMM_SCHED"] = "1" if order == "dyn" else "0"
+        ms = time_launches(fn, a.iters, a.warmup)
+        tf = 2.0 * a.M * a.N * a.K / (ms * 1e-3) / 1e12
+        print(json.dumps({"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "engine": a.engine,
+                          "mode": mode or "default", "ms": round(ms, 4), "tflops": round(tf, 1),
+                          "frac_of_burst": round(tf / pk["bf16_tflops"], 3)}))
 
 
 def c2_graph(seed=0):
@@ -118,6 +126,7 @@ def main():
     g.add_argument("--engine", type=int, default=2)
     g.add_argument("--iters", type=int, default=20)
     g.add_argument("--warmup", type=int, default=3)
+    g.add_argument("--modes", default="", help="e.g. pair_dyn,pair_static,single_dyn,single_static")
     t = sub.add_parser("attention")
     t.add_argument("--config", default="c2")
     t.add_argument("--dtype", default="fp16")
