@@ -196,6 +196,13 @@ int vb_attention_split_noalloc(int dtype, const int32_t* row_ptr, const void* ed
 typedef struct vb_tiles vb_tiles;
 int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* attr_csr, int A, int64_t n_src,
                     int64_t n_dst, int head_dim, vb_tiles** out);
+/* The same with the tile kind: VB_TILES_SMEM (the shared-memory-staged CUDA-core kernel, as
+ * vb_tiles_create) or VB_TILES_MMA (the tensor-core kernel the engine runs on the processor graph:
+ * tiles of up to 128 rows and 192 distinct sources, q.k and the value sums as tcgen05 MMAs; head_dim
+ * 64 only). vb_attention_tiled runs whichever kind the tiles were built for. */
+enum { VB_TILES_SMEM = 0, VB_TILES_MMA = 1 };
+int vb_tiles_create_kind(const int32_t* row_ptr, const int32_t* src, const float* attr_csr, int A, int64_t n_src,
+                         int64_t n_dst, int head_dim, int kind, vb_tiles** out);
 int vb_attention_tiled(vb_tiles* t, int64_t dst_lo, int64_t n_rows, const void* q, int64_t ldq, const void* k,
                        const void* v, int64_t ldkv, const void* xr, int64_t ldxr, void* out, int64_t ldo,
                        const float* w_e, int C, int heads, int head_dim, void* stream);

@@ -258,6 +258,71 @@ def test_attention_tiled(C, heads, A):
     assert np.array_equal(got[zero], xr[zero, :C]), "zero in-degree must give x_r exactly"
 
 
+def local_graph(rng, n, A, window=40):
+    """Destinations drawing their sources (with repeats) from a window around their own index, so runs
+    of consecutive rows share sources: multi-row tiles with up to the tensor-core kernel's 192 slots."""
+    s, d = [], []
+    for i in range(n):
+        deg = DEGREES[i % len(DEGREES)] if i < 3 * len(DEGREES) else int(rng.integers(0, 30))
+        s += list(np.clip(i + rng.integers(-window, window + 1, deg), 0, n - 1))
+        d += [i] * deg
+    perm = rng.permutation(len(s))
+    ei = np.stack([np.array(s, np.int64)[perm], np.array(d, np.int64)[perm]])
+    return ei, rng.normal(size=(ei.shape[1], A)).astype(np.float32)
+
+
+@pytest.mark.parametrize("graph", ["random", "local"])
+@pytest.mark.parametrize("C,heads,A", [(1024, 16, 3), (768, 12, 3), (384, 6, 3), (256, 4, 2), (128, 2, 1)])
+def test_attention_mma(C, heads, A, graph):
+    """The tensor-core attention (vb_tiles_create_kind VB_TILES_MMA: S = Q K^T and O = P V as tcgen05
+    MMAs per tile of up to 128 rows and 192 sources, P in fp16; rows with more distinct sources go to
+    the gather kernel): the float64 reference within the fp16 bar, zero in-degree rows give x_r
+    exactly, and the gather kernel's output within the same bar. Graphs: every degree class in shuffled
+    order with repeated sources plus a row of 300 edges over ~210 distinct sources (heavy), and a
+    local graph whose tiles fill 128 rows and up to 192 slots."""
+    rng = np.random.default_rng(C * 13 + heads + A + len(graph))
+    hd = C // heads
+    if graph == "random":
+        n_src, n_dst = 400, 97
+        ei, ea = make_graph(rng, n_src, n_dst, A)
+        wide = np.stack([rng.integers(0, n_src, 300), np.full(300, 50)]).astype(np.int64)
+        ei = np.concatenate([ei, wide], 1)
+        ea = np.concatenate([ea, rng.normal(size=(300, A)).astype(np.float32)])
+    else:
+        n_src = n_dst = 1500
+        ei, ea = local_graph(rng, n_dst, A)
+    ld = C + 8
+    rp, src, _, attr = vb.build_csr(ei, ea, n_src, n_dst)
+    attr = rounded(attr, vb.FP16)
+    q, k, v, xr = (rounded(rng.normal(size=(n, ld)), vb.FP16) for n in (n_dst, n_src, n_src, n_dst))
+    we = rounded(rng.normal(size=(C, A)) * 0.5, vb.FP16)
+    be = rounded(rng.normal(size=C) * 0.5, vb.FP16)
+    w4 = np.zeros((4, C), np.float32)
+    w4[:A] = we.T
+    w4[3] = be
+    tiles = vb.Tiles(rp, src, attr, n_src, hd, kind=vb.Tiles.MMA)
+    T = torch.float16
+    d_q, d_k, d_v, d_x, d_w = dev(q, T), dev(k, T), dev(v, T), dev(xr, T), dev(w4, torch.float32)
+    out = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
+    tiles.attention(0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld, out, C, d_w, C, heads, hd)
+    gat = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
+    edges = vb.pack_edges(src, attr, round_fp16=True)
+    vb.attention(vb.FP16, dev(rp, torch.int32), dev(edges, torch.float32), 0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld,
+                 gat, C, d_w, C, heads, hd)
+    torch.cuda.synchronize()
+    vb.check_device()
+    got, g = out.float().cpu().numpy(), gat.float().cpu().numpy()
+    ref = attention_reference(rp, src, attr, q[:, :C].astype(np.float64), k[:, :C].astype(np.float64),
+                              v[:, :C].astype(np.float64), xr[:, :C].astype(np.float64), we, be.astype(np.float64),
+                              heads, hd)
+    assert not np.isnan(got).any()
+    err = oracle.rel_absmax(got, ref)
+    assert err <= 2e-3, f"rel_absmax {err:.3e}"
+    assert oracle.rel_absmax(got, g) <= 2e-3
+    zero = np.where(rp[1:] == rp[:-1])[0]
+    assert np.array_equal(got[zero], xr[zero, :C]), "zero in-degree must give x_r exactly"
+
+
 @pytest.mark.parametrize("variant", ["5", "6", "7", "8"])
 @pytest.mark.parametrize("C,heads", [(1024, 16), (2048, 8), (1024, 32)])
 def test_attention_variants(C, heads, variant, monkeypatch):

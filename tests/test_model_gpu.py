@@ -130,6 +130,22 @@ def test_attention_kernel_choice(name, tiled, chunk, seeded_model, monkeypatch):
     assert oracle.rel_absmax(y, ref) <= TOL[vb.FP16]
 
 
+@pytest.mark.parametrize("mma,chunk", [("all", ""), ("proc", ""), ("dec", "32"), ("none", "")])
+@pytest.mark.parametrize("name", ["t1024", "t768", "t384i"])
+def test_attention_mma_choice(name, mma, chunk, seeded_model, monkeypatch):
+    """The engine with the tensor-core attention (VB_ATT_MMA; default: the processor graph) on each
+    graph of the head_dim-64 models, with and without decoder chunks: the fp16 parity bar against the
+    reference's goldens for every choice."""
+    mp, xp = seeded_model(name)
+    x = np.array(st.read(xp)[0]["in.x"])
+    monkeypatch.setenv("VB_ATT_MMA", mma)
+    if chunk:
+        monkeypatch.setenv("VB_DEC_CHUNK_ROWS", chunk)
+    y = vb.Model.load(mp, precision=vb.FP16).predict_step(x)
+    vb.check_device()
+    assert oracle.rel_absmax(y, golden(name)["out.y"]) <= TOL[vb.FP16]
+
+
 @pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])
 @pytest.mark.parametrize("name", ["t256", "t512", "c0"])
 def test_wide_rows_by_parts(name, dt, seeded_model, monkeypatch):

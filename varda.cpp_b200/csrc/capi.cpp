@@ -348,20 +348,32 @@ int vb_attention_split_noalloc(int dtype, const int32_t* row_ptr, const void* ed
 struct vb_tiles {
     vb::DeviceBuffer tiles, srcs, tedges, heavy, row_ptr, edges;
     std::vector<int32_t> row0, heavy_rows;
+    int kind = VB_TILES_SMEM;
 };
 
 int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* attr, int A, int64_t n_src,
                     int64_t n_dst, int head_dim, vb_tiles** out) {
+    return vb_tiles_create_kind(row_ptr, src, attr, A, n_src, n_dst, head_dim, VB_TILES_SMEM, out);
+}
+
+int vb_tiles_create_kind(const int32_t* row_ptr, const int32_t* src, const float* attr, int A, int64_t n_src,
+                         int64_t n_dst, int head_dim, int kind, vb_tiles** out) {
+    (void)head_dim;
     return guard([&] {
         need(row_ptr, "row_ptr"), need(out, "out");
+        if (kind != VB_TILES_SMEM && kind != VB_TILES_MMA) vb::fail(vb::kInvalidArgument, "tiles kind");
         vb::CsrGraph g;
         g.n_src = n_src, g.n_dst = n_dst, g.attr_dim = A;
         g.row_ptr.assign(row_ptr, row_ptr + n_dst + 1);
         g.n_edges = g.row_ptr.back();
         g.src.assign(src, src + g.n_edges);
         g.attr.assign(attr, attr + g.n_edges * A);
-        vb::TilePlan tp = vb::make_tiles(g, vb::k::tiled_max_src(), vb::k::tiled_max_rows(), vb::k::tiled_max_edges(), 0, true);
+        vb::TilePlan tp = kind == VB_TILES_MMA
+                              ? vb::make_tiles(g, vb::k::mma_max_src(), vb::k::mma_max_rows(), vb::k::mma_max_edges(), 0, true, 0, true)
+                              : vb::make_tiles(g, vb::k::tiled_max_src(), vb::k::tiled_max_rows(),
+                                               vb::k::tiled_max_edges(), 0, true);
         auto t = std::make_unique<vb_tiles>();
+        t->kind = kind;
         auto up = [](vb::DeviceBuffer& b, const void* h, size_t n) {
             b.alloc(std::max<size_t>(n, 16));
             if (n) VB_CUDA(cudaMemcpy(b.get(), h, n, cudaMemcpyHostToDevice));
@@ -386,7 +398,8 @@ int vb_attention_tiled(vb_tiles* t, int64_t lo, int64_t n, const void* q, int64_
                        int heads, int head_dim, void* stream) {
     return guard([&] {
         need(t, "tiles");
-        if (!vb::k::tiled_supported(C, head_dim)) vb::fail(vb::kUnsupported, "tiled attention: unsupported layout");
+        if (t->kind == VB_TILES_MMA ? !vb::k::mma_supported(C, head_dim) : !vb::k::tiled_supported(C, head_dim))
+            vb::fail(vb::kUnsupported, "tiled attention: unsupported layout");
         const auto t0 = std::lower_bound(t->row0.begin(), t->row0.end(), int32_t(lo));
         const auto t1 = std::lower_bound(t->row0.begin(), t->row0.end(), int32_t(lo + n));
         vb::k::TileArgs a;
@@ -395,7 +408,8 @@ int vb_attention_tiled(vb_tiles* t, int64_t lo, int64_t n, const void* q, int64_
         a.q = static_cast<const __half*>(q), a.k = static_cast<const __half*>(k), a.v = static_cast<const __half*>(v);
         a.xr = static_cast<const __half*>(xr), a.out = static_cast<__half*>(out);
         a.ldq = ldq, a.ldkv = ldkv, a.ldxr = ldxr, a.ldo = ldo, a.w_e = w_e, a.C = C, a.heads = heads, a.head_dim = head_dim;
-        vb::k::attention_tiled(a, 1.4426950408889634f / std::sqrt(float(head_dim)), S(stream));
+        if (t->kind == VB_TILES_MMA) vb::k::attention_mma(a, 1.4426950408889634f / std::sqrt(float(head_dim)), S(stream));
+        else vb::k::attention_tiled(a, 1.4426950408889634f / std::sqrt(float(head_dim)), S(stream));
         const auto h0 = std::lower_bound(t->heavy_rows.begin(), t->heavy_rows.end(), int32_t(lo));
         const auto h1 = std::lower_bound(t->heavy_rows.begin(), t->heavy_rows.end(), int32_t(lo + n));
         if (h1 > h0) {

@@ -121,7 +121,8 @@ std::vector<EdgeRec> pack_edges(const CsrGraph& g, bool round_fp16) {
     return out;
 }
 
-TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges, int64_t chunk_rows, bool round_fp16) {
+TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges, int64_t chunk_rows, bool round_fp16,
+                    int max_row_edges, bool sort_by_slot) {
     TilePlan t;
     t.edges = pack_edges(g, round_fp16);
     std::vector<int32_t> slot(size_t(std::max<int64_t>(g.n_src, 1)), -1);  // source -> slot in the open tile
@@ -134,6 +135,10 @@ TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges,
         for (size_t i = 0; i < sorted.size(); ++i) slot[size_t(sorted[i])] = int32_t(i);
         for (int64_t e = g.row_ptr[size_t(row0)]; e < g.row_ptr[size_t(end_row)]; ++e)
             t.edges[size_t(e)].src = slot[size_t(g.src[size_t(e)])];
+        if (sort_by_slot)
+            for (int64_t d = row0; d < end_row; ++d)
+                std::stable_sort(t.edges.begin() + g.row_ptr[size_t(d)], t.edges.begin() + g.row_ptr[size_t(d + 1)],
+                                 [](const EdgeRec& x, const EdgeRec& y) { return x.src < y.src; });
         t.row0.push_back(row0);
         t.nrows.push_back(int32_t(end_row - row0));
         t.src0.push_back(int32_t(t.srcs.size()));
@@ -161,7 +166,7 @@ TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges,
             own = int(std::unique(u.begin(), u.end()) - u.begin());
         }
         for (int32_t s : fresh) slot[size_t(s)] = -1;
-        if (own > max_src || e - b > max_edges) {  // heavy row: the gather kernel takes it
+        if (own > max_src || e - b > max_edges || (max_row_edges > 0 && e - b > max_row_edges)) {  // heavy row
             close(d);
             t.heavy.push_back(int32_t(d));
             continue;

@@ -51,8 +51,11 @@ struct TilePlan {
     int max_nsrc = 0;
 };
 // Tiles of consecutive destination rows with at most max_src distinct sources, max_rows rows and
-// max_edges edges; a row with more than max_src distinct sources or more than max_edges edges is heavy
-// (left to the gather kernel). Tiles never span a multiple of chunk_rows (0: no chunking).
-TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges, int64_t chunk_rows, bool round_fp16);
+// max_edges edges; a row with more than max_src distinct sources, more than max_edges edges or more
+// than max_row_edges edges (0: no limit) is heavy (left to the gather kernel). Tiles never span a
+// multiple of chunk_rows (0: no chunking). Slots number a tile's sources in increasing source order;
+// with sort_by_slot each tiled row's records are stably sorted by slot.
+TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges, int64_t chunk_rows, bool round_fp16,
+                    int max_row_edges = 0, bool sort_by_slot = false);
 
 }  // namespace vb

@@ -155,6 +155,15 @@ int tiled_max_rows();
 int tiled_max_edges();
 // Synchronises; reads and clears the flag a timed-out wait of the tiled attention sets.
 int take_attention_error();
+// Edge attention on the tensor cores (fp16, head_dim 64; attention_mma.cu) over the same tiles, built
+// with at most mma_max_src() sources, mma_max_rows() rows and mma_max_edges() edges and every row's
+// records sorted by slot; w_e is read as fp16 values.
+void attention_mma(const TileArgs& a, float scale_log2, cudaStream_t s);
+bool mma_supported(int C, int head_dim);
+int mma_max_src();
+int mma_max_rows();
+int mma_max_edges();
+int take_mma_error();  // reads and clears the tensor-core attention's timeout flag (no synchronise)
 
 // ------------------------------------------------------------------ GEMM (Linear layers)
 enum Epilogue : int {

@@ -336,13 +336,15 @@ def check_device():
 class Tiles:
     """Destination tiles of a CSR graph for the shared-memory-staged fp16 attention (vb_tiles_*)."""
 
-    def __init__(self, row_ptr, src, attr_csr, n_src, head_dim):
+    SMEM, MMA = 0, 1  # kind: CUDA-core shared-memory tiles, or the tensor-core kernel's tiles
+
+    def __init__(self, row_ptr, src, attr_csr, n_src, head_dim, kind=0):
         rp = np.ascontiguousarray(row_ptr, np.int32)
         s = np.ascontiguousarray(src, np.int32)
         at = np.ascontiguousarray(attr_csr, np.float32)
         h = ctypes.c_void_p()
-        check(lib.vb_tiles_create(_ptr(rp), _ptr(s), _ptr(at), at.shape[1], n_src, len(rp) - 1, head_dim,
-                                  ctypes.byref(h)))
+        check(lib.vb_tiles_create_kind(_ptr(rp), _ptr(s), _ptr(at), at.shape[1], n_src, len(rp) - 1, head_dim, kind,
+                                       ctypes.byref(h)))
         self._h = h
 
     def attention(self, dst_lo, n_rows, q, ldq, k, v, ldkv, xr, ldxr, out, ldo, w_e, C, heads, head_dim, stream=None):
@@ -361,6 +363,8 @@ def _bind_tiles():
     P, I, I64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
     lib.vb_tiles_create.argtypes = [P, P, P, I, I64, I64, I, P]
     lib.vb_tiles_create.restype = I
+    lib.vb_tiles_create_kind.argtypes = [P, P, P, I, I64, I64, I, I, P]
+    lib.vb_tiles_create_kind.restype = I
     lib.vb_attention_tiled.argtypes = [P, I64, I64, P, I64, P, P, I64, P, I64, P, I64, P, I, I, I, P]
     lib.vb_attention_tiled.restype = I
     lib.vb_tiles_free.argtypes = [P]

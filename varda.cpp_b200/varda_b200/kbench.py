@@ -97,8 +97,8 @@ def attention(a):
     out = torch.empty(H, C, device="cuda", dtype=T)
     s = torch.cuda.current_stream().cuda_stream
     q, k, v, xr = (qkvs[:, i * C:] for i in range(4))
-    if a.impl == "tiled":
-        tiles = vb.Tiles(rp, src, at, H, C // heads)
+    if a.impl in ("tiled", "mma"):
+        tiles = vb.Tiles(rp, src, at, H, C // heads, kind=vb.Tiles.MMA if a.impl == "mma" else vb.Tiles.SMEM)
         fn = lambda: tiles.attention(0, H, q, 4 * C, k, v, 4 * C, xr, 4 * C, out, C, w4, C, heads, C // heads,  # noqa
                                      stream=s)
     else:
@@ -130,7 +130,7 @@ def main():
     t = sub.add_parser("attention")
     t.add_argument("--config", default="c2")
     t.add_argument("--dtype", default="fp16")
-    t.add_argument("--impl", default="tiled", choices=["tiled", "gather"])
+    t.add_argument("--impl", default="tiled", choices=["tiled", "gather", "mma"])
     t.add_argument("--iters", type=int, default=20)
     t.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
