@@ -19,6 +19,7 @@
 #include <functional>
 #include <memory>
 #include <string>
+#include <thread>
 #include <type_traits>
 #include <vector>
 
@@ -66,6 +67,18 @@ bool graph_listed(const char* env, const std::string& graph, const char* dflt) {
 }
 bool tiled_for(const std::string& graph, const char* dflt) { return graph_listed("VB_ATT_TILED", graph, dflt); }
 bool mma_for(const std::string& graph) { return graph_listed("VB_ATT_MMA", graph, kMmaDefault); }
+
+// f(begin, end) over [0, n) split into contiguous ranges on up to 16 host threads (one below `grain`
+// items per thread). Used for the per-element conversions of the load path, whose results do not
+// depend on the split.
+template <class F> void parallel_ranges(int64_t n, int64_t grain, F f) {
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const int nt = int(std::max<int64_t>(1, std::min<int64_t>(std::min<unsigned>(hw, 16u), n / std::max<int64_t>(grain, 1))));
+    if (nt <= 1) return f(int64_t(0), n);
+    std::vector<std::thread> ts;
+    for (int t = 0; t < nt; ++t) ts.emplace_back(f, n * t / nt, n * (t + 1) / nt);
+    for (auto& th : ts) th.join();
+}
 
 // Load-stage timer: VB_LOAD_TIMING=1 prints the seconds of each stage of a model load to stderr.
 struct LoadTimer {
@@ -388,9 +401,12 @@ Lin<T> Engine<T>::load_linear(SafeTensorsFile& f, const std::vector<std::string>
     bool any_bias = false;
     for (size_t i = 0; i < names.size(); ++i) {
         const TensorView& tw = f.take(names[i] + ".weight", DType::F32, {N_each, K});
-        for (int64_t r = 0; r < N_each; ++r)
-            for (int64_t c = 0; c < K; ++c)
-                w[size_t((int64_t(i) * N_each + r) * L.ldw + c)] = T(tw.as<float>()[r * K + c]);
+        const float* src = tw.as<float>();
+        T* dst = w.data() + size_t(int64_t(i) * N_each * L.ldw);
+        parallel_ranges(N_each, std::max<int64_t>(1, (int64_t(1) << 20) / std::max<int64_t>(K, 1)), [&](int64_t r0, int64_t r1) {
+            for (int64_t r = r0; r < r1; ++r)
+                for (int64_t c = 0; c < K; ++c) dst[size_t(r * L.ldw + c)] = T(src[r * K + c]);
+        });
         const std::string bn = names[i] + ".bias";
         if (!cfg_.is_absent(bn)) {
             const TensorView& tb = f.take(bn, DType::F32, {N_each});
