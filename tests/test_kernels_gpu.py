@@ -323,12 +323,14 @@ def test_attention_mma(C, heads, A, graph):
     assert np.array_equal(got[zero], xr[zero, :C]), "zero in-degree must give x_r exactly"
 
 
-@pytest.mark.parametrize("variant", ["5", "6", "7", "8"])
+@pytest.mark.parametrize("variant", ["1", "2", "3", "4"])
 @pytest.mark.parametrize("C,heads", [(1024, 16), (2048, 8), (1024, 32)])
 def test_attention_variants(C, heads, variant, monkeypatch):
-    """The gather kernel's alternative launch shapes (VB_ATT_VARIANT: 8 channels per lane at 3 or 4
-    blocks per SM; one warp per 1024 channels at 1 or 2 blocks per SM) against the float64 reference,
-    with the fp16 bar of the default shape, zero in-degree giving x_r exactly."""
+    """The gather kernel's alternative launch shapes (VB_ATT_VARIANT: 1 = 16 channels per lane at 2
+    blocks per SM, 2 = 8 channels with two edges per pipeline stage at 3, 3 = 8 channels at 5, 4 = 4
+    channels at 4) against the float64 reference with the fp16 bar, zero in-degree giving x_r exactly;
+    variants that keep the default's summation order (2, 3) are bitwise equal to it. A shape whose
+    head would need more than 32 lanes (4 channels per lane, head_dim 256) is rejected."""
     monkeypatch.setenv("VB_ATT_VARIANT", variant)
     dt, A = vb.FP16, 3
     rng = np.random.default_rng(C + heads + int(variant))
@@ -348,8 +350,16 @@ def test_attention_variants(C, heads, variant, monkeypatch):
     d_rp, d_ed, d_w = dev(rp, torch.int32), dev(edges, torch.float32), dev(w4, torch.float32)
     d_q, d_k, d_v, d_x = dev(q, T), dev(k, T), dev(v, T), dev(xr, T)
     out = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
+    if variant == "4" and hd // 4 > 32:
+        with pytest.raises(vb.VardaError, match="power of two <= 32"):
+            vb.attention(dt, d_rp, d_ed, 0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld, out, C, d_w, C, heads, hd)
+        return
     vb.attention(dt, d_rp, d_ed, 0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld, out, C, d_w, C, heads, hd)
+    monkeypatch.setenv("VB_ATT_VARIANT", "0")
+    dflt = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
+    vb.attention(dt, d_rp, d_ed, 0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld, dflt, C, d_w, C, heads, hd)
     torch.cuda.synchronize()
+    vb.check_device()
     got = out.float().cpu().numpy()
     ref = attention_reference(rp, src, attr, q[:, :C].astype(np.float64), k[:, :C].astype(np.float64),
                               v[:, :C].astype(np.float64), xr[:, :C].astype(np.float64), we, be.astype(np.float64),
@@ -357,6 +367,8 @@ def test_attention_variants(C, heads, variant, monkeypatch):
     assert oracle.rel_absmax(got, ref) <= 2e-3
     zero = np.where(rp[1:] == rp[:-1])[0]
     assert np.array_equal(got[zero], xr[zero, :C])
+    if variant in ("2", "3"):
+        assert torch.equal(out, dflt), "same summation order as the default shape: bitwise equal"
 
 
 @pytest.mark.parametrize("M,N,K,lda", [(300, 1024, 1024, 1024), (1000, 4096, 1024, 1024), (513, 1024, 4096, 4096),

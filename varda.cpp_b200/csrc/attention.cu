@@ -273,7 +273,9 @@ void attention(const AttnArgs<T>& a, cudaStream_t s) {
     // (MINB, the register budget). Measured on the C2 block (fp16, C = 1024, head_dim 64): 8 channels
     // per lane at 4 blocks per SM (32 warps) 1.65 ms, 16 channels at 2 blocks 1.97 ms, 8 at 3 blocks
     // 2.28 ms: the kernel is latency-bound and occupancy wins. VB_ATT_VARIANT picks an alternative:
-    // 1 = (16, 1, 2), 2 = (8, 2, 3), 3 = (8, 1, 5), 4 = (4, 1, 4).
+    // 1 = (16, 1, 2), 2 = (8, 2, 3), 3 = (8, 1, 5), 4 = (4, 1, 4). (A variant with one broadcast record
+    // load per edge instead of the 32-record batch and shuffles, and the q.k products on the sm_100
+    // mixed-precision FMA, measured 1.70 ms against 1.57 ms.)
     const char* venv = std::getenv("VB_ATT_VARIANT");
     const int variant = venv && *venv ? std::atoi(venv) : 0;
     int cpl = 4;
