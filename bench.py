@@ -209,7 +209,9 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
 
     # e2e through the host API: pinned x, y; H2D of this rank's input rows + forward + D2H of its
-    # output rows every step
+    # output rows every step (one untimed call first: on one GPU the host path is pipelined, and its
+    # first call captures the pieces' graphs)
+    m.predict_step(xh, yh)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()

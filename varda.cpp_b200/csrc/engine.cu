@@ -257,6 +257,12 @@ private:
     void attention(const GraphDev& g, const Block<T>& b, int64_t lo, int64_t n, const T* q, int64_t ldq, const T* kk,
                    const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out, cudaStream_t s);
     void forward(const float* xn, float* yn, cudaStream_t s, Hook* hk);
+    // pieces of forward(), in its order; the pipelined host path runs them around chunked copies
+    void enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64_t n, cudaStream_t s, Hook* hk);
+    void enc_dest_pre(cudaStream_t s, Hook* hk);
+    bool middle(cudaStream_t s, Hook* hk);
+    void dec_chunk(int64_t lo, int64_t n, cudaStream_t s, Hook* hk, bool& halo_pending, float* h_emb, float* h_bo);
+    void output_rows(const float* xn, float* yn, int64_t lo, int64_t n, cudaStream_t s, float* pre_bound);
     cudaGraphExec_t capture(const std::function<void(cudaStream_t)>& body, cudaStream_t s);
     bool capture_graph(cudaStream_t s);
     void upload_input(const float* x, cudaStream_t s);
@@ -310,6 +316,21 @@ private:
     // on cs_ while the attention of the interior rows (no remote source) runs; the boundary rows follow
     cudaStream_t cs_ = nullptr;
     cudaEvent_t ev_kv_ = nullptr, ev_halo_ = nullptr;
+    // pipelined host I/O (one GPU, no hook): the host -> device copy of x in row chunks on cio_ while the
+    // encoder's source side runs on the chunks already there, and the decoder in row chunks whose
+    // outputs go back on cio_ while the next chunk runs; each compute piece is a CUDA graph
+    struct IoPipe {
+        bool on = false, ready = false;
+        int64_t in_rows = 0, dec_rows = 0;  // input chunk rows; decoder chunk rows (never straddle a tile)
+        cudaStream_t cio = nullptr;
+        cudaEvent_t start = nullptr;
+        std::vector<cudaEvent_t> in_done, out_done;
+        cudaGraphExec_t pre = nullptr, mid = nullptr;
+        std::vector<cudaGraphExec_t> src, dec;
+    } io_;
+    void io_setup();
+    void io_release();
+    void predict_pipelined(const float* x, float* y);
     DeviceBuffer proc_inner_, proc_outer_;
     int64_t n_inner_ = 0, n_outer_ = 0;
     void attention_rows(const GraphDev& g, const Block<T>& b, const DeviceBuffer& rows, int64_t n, const T* q,
@@ -685,7 +706,19 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         proc_inner_ = upload(inner.data(), std::max<size_t>(1, inner.size()) * sizeof(int32_t));
         proc_outer_ = upload(outer.data(), std::max<size_t>(1, outer.size()) * sizeof(int32_t));
     }
-    g_dec_ = upload_graph(plan_.dec_g, "dec", dec_rows_ < Gl_ ? dec_rows_ : 0);
+    // pipelined host I/O: decoder chunks of ~Gl / VB_IO_CHUNKS rows (the memory cap's chunks if set),
+    // input chunks of ~Gx / (2 VB_IO_CHUNKS) rows; the decoder tiles respect the chunk boundaries. On C1
+    // the copies (1.22 GB in at 56 GB/s, 0.54 GB out) then add ~7 ms to the 176-180 ms step instead of ~26.
+    io_.on = plan_.world == 1 && env_int("VB_IO_PIPELINE", 1) != 0;
+    if (io_.on) {
+        const int64_t nio = std::max<int64_t>(1, env_int("VB_IO_CHUNKS", 8)), gl = std::max<int64_t>(Gl_, 1);
+        io_.dec_rows = dec_rows_ < Gl_ ? dec_rows_
+                                       : std::min<int64_t>(int64_t(align_up(size_t((gl + nio - 1) / nio), 128)), gl);
+        const int64_t gx = std::max<int64_t>(Gx_, 1);
+        io_.in_rows = std::min<int64_t>(int64_t(align_up(size_t((gx + 2 * nio - 1) / (2 * nio)), 128)), gx);
+    }
+    const int64_t dec_tile_chunk = io_.on ? io_.dec_rows : dec_rows_;
+    g_dec_ = upload_graph(plan_.dec_g, "dec", dec_tile_chunk < Gl_ ? dec_tile_chunk : 0);
     lt.mark("processor + decoder graphs");
     for (CsrGraph* g : {&plan_.enc, &plan_.proc_g, &plan_.dec_g}) *g = CsrGraph{};  // host copies not needed
 
@@ -780,6 +813,7 @@ Engine<T>::~Engine() {
     if (stream_) cudaStreamSynchronize(stream_);
     if (graph_exec_) cudaGraphExecDestroy(graph_exec_);  // before the communicator its nodes use
     rollout_release();
+    io_release();
     if (cs_) cudaStreamSynchronize(cs_), cudaStreamDestroy(cs_);
     if (ev_kv_) cudaEventDestroy(ev_kv_);
     if (ev_halo_) cudaEventDestroy(ev_halo_);
@@ -902,14 +936,15 @@ void Engine<T>::attention_rows(const GraphDev& g, const Block<T>& b, const Devic
     k::attention<T>(a, s);
 }
 
+// Encoder source side on data rows [r0, r0 + n) of the Gx rows: assemble (the T_in input slots slot_rows
+// rows apart), emb_src, LN_src (in place), [k | v]. Row-wise, so any split of the rows gives the same bits.
 template <class T>
-void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
-    // G: this rank's data rows (own, then the encoder's halo) for the encoder's source side;
-    // Gl: own data rows (decoder destinations); H: own hidden rows
-    const int64_t G = Gx_, Gl = Gl_, H = Hl_, C = C_;
+void Engine<T>::enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64_t n, cudaStream_t s, Hook* hk) {
+    const int64_t G = Gx_, C = C_;
     {
-        Span sp(this, s, "assemble", 0, double(G) * (T_in_ * V_in_ * 4 + A_node_ * 4 + ldF_ * sizeof(T)));
-        k::assemble<T>(xn, d_attr_.as<float>(), T_in_, G, V_in_, A_node_, x_data_, ldF_, s);
+        Span sp(this, s, "assemble", 0, double(n) * (T_in_ * V_in_ * 4 + A_node_ * 4 + ldF_ * sizeof(T)));
+        k::assemble<T>(xn + r0 * V_in_, d_attr_.as<float>() + r0 * A_node_, T_in_, n, V_in_, A_node_,
+                       x_data_ + r0 * ldF_, ldF_, s, slot_rows);
     }
     if (hk) {
         if (std::is_same<T, float>::value) {
@@ -919,23 +954,35 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
             k::assemble<float>(xn, d_attr_.as<float>(), T_in_, G, V_in_, A_node_, hook_xsrc_.as<float>(), F_, s);
             hk->dev("enc.x_src", hook_xsrc_.as<float>(), F_, G, F_, {G, F_});
         }
-        hk->host("enc.x_dst", h_attr_host_.data(), {H, A_node_});
+        hk->host("enc.x_dst", h_attr_host_.data(), {Hl_, A_node_});
     }
+    T* emb_src = region_ + r0 * C;
+    T* kv_enc = region_ + G * C + r0 * 2 * C;
+    linear(enc_emb_src_, x_data_ + r0 * ldF_, ldF_, emb_src, C, n, s);
+    if (hk) hk->dev("enc.emb_src", emb_src, C, n, C, {n, C});
+    ln(emb_src, enc_.ln_src, emb_src, n, s);
+    linear(enc_.kv, emb_src, C, kv_enc, 2 * C, n, s);
+}
 
-    // ---- encoder, source side on all data rows: emb_src, LN_src (in place), [k | v]
-    T* emb_src = region_;
-    T* kv_enc = region_ + G * C;
-    linear(enc_emb_src_, x_data_, ldF_, emb_src, C, G, s);
-    if (hk) hk->dev("enc.emb_src", emb_src, C, G, C, {G, C});
-    ln(emb_src, enc_.ln_src, emb_src, G, s);
-    linear(enc_.kv, emb_src, C, kv_enc, 2 * C, G, s);
-
-    // ---- encoder, destination side (hidden nodes)
+// Encoder destination side before the attention (needs no input): emb_dst of the hidden attributes,
+// LN_dst, [q | self].
+template <class T>
+void Engine<T>::enc_dest_pre(cudaStream_t s, Hook* hk) {
+    const int64_t H = Hl_, C = C_;
     T* emb_dst = zA_;
     linear(enc_emb_dst_, h_attr_.as<T>(), ldA_, emb_dst, C, H, s);
     if (hk) hk->dev("enc.emb_dst", emb_dst, C, H, C, {H, C});
     ln(emb_dst, enc_.ln_dst, xh_, H, s);
     linear(enc_.qs, xh_, C, qkvs_, 2 * C, H, s);
+}
+
+// From the encoder attention to the decoder's source side ([k | v] of LN_src(latent) and its halo).
+// Returns whether the decoder halo exchange is still in flight on the communication stream.
+template <class T>
+bool Engine<T>::middle(cudaStream_t s, Hook* hk) {
+    const int64_t G = Gx_, H = Hl_, C = C_;
+    T* kv_enc = region_ + G * C;
+    T* emb_dst = zA_;
     attention(g_enc_, enc_, 0, H, qkvs_, 2 * C, kv_enc, kv_enc + C, 2 * C, qkvs_ + C, 2 * C, sbuf_, s);
     linear(enc_.proj, sbuf_, C, out1_, C, H, s, k::kEpiResidual, emb_dst, C);
     ln(out1_, enc_.ln_mlp, xh_, H, s);
@@ -993,69 +1040,86 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
     // ---- decoder, source side: [k | v] of LN_src(latent)
     T* kv_dec = qkvs_;
     linear(dec_.kv, xh_, C, kv_dec, 2 * C, H, s);
-    bool dec_halo_pending = false;
     if (overlap) {  // the decoder's K|V halo flies while the first chunk's destination GEMMs run
         VB_CUDA(cudaEventRecord(ev_kv_, s));
         VB_CUDA(cudaStreamWaitEvent(cs_, ev_kv_, 0));
         exchange(xd_, kv_dec, 2 * C, kv_dec + H * 2 * C, 2 * C, true, cs_);
         VB_CUDA(cudaEventRecord(ev_halo_, cs_));
-        dec_halo_pending = true;
-    } else {
-        exchange(xd_, kv_dec, 2 * C, kv_dec + H * 2 * C, 2 * C, true, s);
+        return true;
     }
+    exchange(xd_, kv_dec, 2 * C, kv_dec + H * 2 * C, 2 * C, true, s);
+    return false;
+}
 
-    // ---- decoder, destination chunks of data rows
-    std::vector<float> h_emb, h_bo;
-    if (hk) h_emb.resize(size_t(Gl * C)), h_bo.resize(size_t(Gl * C));
-    const int64_t R = dec_rows_;
+// Decoder destination rows [lo, lo + n) of the own data rows (at most dec_rows_ of them, and never
+// straddling a decoder tile; the chunk buffers sit in region_), through out_proj into dec_out_.
+template <class T>
+void Engine<T>::dec_chunk(int64_t lo, int64_t n, cudaStream_t s, Hook* hk, bool& halo_pending, float* h_emb,
+                          float* h_bo) {
+    const int64_t C = C_, R = dec_rows_;
+    T* kv_dec = qkvs_;
     T* e = region_;
     T* t = e + R * C;
     T* qs = t + R * C;
     T* sb = qs + R * 2 * C;
     T* o1 = sb + R * C;
     T* h = o1 + R * C;
-    for (int64_t lo = 0; lo < Gl; lo += R) {
-        const int64_t n = std::min(R, Gl - lo);
-        linear(dec_emb_dst_, x_data_ + lo * ldF_, ldF_, e, C, n, s);
-        if (hk) hk->fetch(e, C, n, C, h_emb.data(), lo);
-        ln(e, dec_.ln_dst, t, n, s);
-        linear(dec_.qs, t, C, qs, 2 * C, n, s);
-        if (dec_halo_pending) {
-            VB_CUDA(cudaStreamWaitEvent(s, ev_halo_, 0));
-            dec_halo_pending = false;
-        }
-        attention(g_dec_, dec_, lo, n, qs, 2 * C, kv_dec, kv_dec + C, 2 * C, qs + C, 2 * C, sb, s);
-        linear(dec_.proj, sb, C, o1, C, n, s, k::kEpiResidual, e, C);
-        ln(o1, dec_.ln_mlp, t, n, s);
-        linear(dec_.mlp1, t, C, h, mlp_, n, s, k::kEpiGelu);
-        linear(dec_.mlp2, h, mlp_, sb, C, n, s, k::kEpiResidual, o1, C);
-        if (hk) hk->fetch(sb, C, n, C, h_bo.data(), lo);
-        ln(sb, dec_out_norm_, t, n, s);
-        linear(dec_out_proj_, t, C, dec_out_ + lo * ldVo_, ldVo_, n, s);
+    linear(dec_emb_dst_, x_data_ + lo * ldF_, ldF_, e, C, n, s);
+    if (hk) hk->fetch(e, C, n, C, h_emb, lo);
+    ln(e, dec_.ln_dst, t, n, s);
+    linear(dec_.qs, t, C, qs, 2 * C, n, s);
+    if (halo_pending) {
+        VB_CUDA(cudaStreamWaitEvent(s, ev_halo_, 0));
+        halo_pending = false;
     }
+    attention(g_dec_, dec_, lo, n, qs, 2 * C, kv_dec, kv_dec + C, 2 * C, qs + C, 2 * C, sb, s);
+    linear(dec_.proj, sb, C, o1, C, n, s, k::kEpiResidual, e, C);
+    ln(o1, dec_.ln_mlp, t, n, s);
+    linear(dec_.mlp1, t, C, h, mlp_, n, s, k::kEpiGelu);
+    linear(dec_.mlp2, h, mlp_, sb, C, n, s, k::kEpiResidual, o1, C);
+    if (hk) hk->fetch(sb, C, n, C, h_bo, lo);
+    ln(sb, dec_out_norm_, t, n, s);
+    linear(dec_out_proj_, t, C, dec_out_ + lo * ldVo_, ldVo_, n, s);
+}
+
+// Output rows [lo, lo + n) of the own data rows: per step t, fp32 cast + residual + bounding into yn
+// ([T_out, Gl, V_out]); xn holds the normalised input ([T_in, Gx, V_in]).
+template <class T>
+void Engine<T>::output_rows(const float* xn, float* yn, int64_t lo, int64_t n, cudaStream_t s, float* pre_bound) {
+    k::OutputArgs o;
+    o.dec = dec_out_ + lo * ldVo_, o.ld_dec = ldVo_;
+    o.xn_step = xn + int64_t(cfg_.residual_step) * Gx_ * V_in_ + lo * V_in_;
+    o.V_in = V_in_, o.V_out = V_out_, o.T_out = T_out_, o.G = n, o.y_slot = Gl_;
+    o.res_src = res_src_.as<int>(), o.bounds = bounds_.as<k::BoundDev>(), o.n_bounds = n_bounds_;
+    o.bidx = bidx_.as<int>();
+    o.pre_bound = pre_bound ? pre_bound + lo * V_out_ : nullptr;
+    o.y = yn + lo * V_out_;
+    Span sp(this, s, "output_assemble", 0, double(n) * (ldVo_ * sizeof(T) + V_in_ * 4) + double(T_out_) * n * V_out_ * 4);
+    k::output_assemble<T>(o, s);
+}
+
+template <class T>
+void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
+    const int64_t Gl = Gl_, C = C_;
+    // ---- encoder: source side on all data rows (own, then the encoder's halo), destination side
+    enc_source(xn, Gx_, 0, Gx_, s, hk);
+    enc_dest_pre(s, hk);
+    bool halo_pending = middle(s, hk);
+
+    // ---- decoder, destination chunks of data rows
+    std::vector<float> h_emb, h_bo;
+    if (hk) h_emb.resize(size_t(Gl * C)), h_bo.resize(size_t(Gl * C));
+    for (int64_t lo = 0; lo < Gl; lo += dec_rows_)
+        dec_chunk(lo, std::min(dec_rows_, Gl - lo), s, hk, halo_pending, h_emb.data(), h_bo.data());
     if (hk) {
         hk->host("dec.emb_dst", h_emb.data(), {Gl, C});
         hk->host("dec.block_out", h_bo.data(), {Gl, C});
         hk->dev("dec.out", dec_out_, ldVo_, Gl, V_dec_, {Gl, int64_t(V_dec_)});
     }
 
-    // ---- output: per step t, fp32 cast + residual + bounding -> yn [T_out, G, V_out]
-    k::OutputArgs o;
-    o.dec = dec_out_, o.ld_dec = ldVo_;
-    o.xn_step = xn + int64_t(cfg_.residual_step) * G * V_in_;
-    o.V_in = V_in_, o.V_out = V_out_, o.T_out = T_out_, o.G = Gl;
-    o.res_src = res_src_.as<int>(), o.bounds = bounds_.as<k::BoundDev>(), o.n_bounds = n_bounds_;
-    o.bidx = bidx_.as<int>();
-    if (hk) {
-        if (!hook_prebound_.get()) hook_prebound_.alloc(size_t(output_numel()) * sizeof(float));
-        o.pre_bound = hook_prebound_.as<float>();
-    }
-    o.y = yn;
-    {
-        Span sp(this, s, "output_assemble", 0,
-                double(Gl) * (ldVo_ * sizeof(T) + V_in_ * 4) + double(T_out_) * Gl * V_out_ * 4);
-        k::output_assemble<T>(o, s);
-    }
+    // ---- output
+    if (hk && !hook_prebound_.get()) hook_prebound_.alloc(size_t(output_numel()) * sizeof(float));
+    output_rows(xn, yn, 0, Gl, s, hk ? hook_prebound_.as<float>() : nullptr);
     if (hk) {
         const std::vector<int64_t> shp = {1, T_out_, 1, Gl, V_out_};
         hk->dev("out.pre_bound", hook_prebound_.as<float>(), V_out_, T_out_ * Gl, V_out_, shp);
@@ -1173,6 +1237,10 @@ void Engine<T>::predict_step(const float* x, float* y, HookFn hook, void* user) 
         VB_CUDA(cudaStreamSynchronize(s));
         return;
     }
+    if (io_.on && opts_.cuda_graph && ran_eager_ && !hook) {
+        predict_pipelined(x, y);
+        return;
+    }
     VB_CUDA(cudaMemcpyAsync(x_dev_, x, size_t(in_n) * sizeof(float), cudaMemcpyHostToDevice, s));
     if (hook) {
         Hook hk{*this, hook, user, s};
@@ -1189,6 +1257,127 @@ void Engine<T>::predict_step(const float* x, float* y, HookFn hook, void* user) 
     }
     enqueue_predict();
     VB_CUDA(cudaMemcpyAsync(y, y_dev_, size_t(out_n) * sizeof(float), cudaMemcpyDeviceToHost, s));
+    VB_CUDA(cudaStreamSynchronize(s));
+}
+
+// The pieces of the pipelined predict_step as graphs (eager where a capture fails), its copy stream and
+// events. Runs after the first eager forward (so every lazy lookup has been done outside capture).
+template <class T>
+void Engine<T>::io_setup() {
+    cudaStream_t s = stream_;
+    VB_CUDA(cudaStreamCreateWithFlags(&io_.cio, cudaStreamNonBlocking));
+    VB_CUDA(cudaEventCreateWithFlags(&io_.start, cudaEventDisableTiming));
+    const int64_t n_in = (Gx_ + io_.in_rows - 1) / io_.in_rows, n_dec = (Gl_ + io_.dec_rows - 1) / io_.dec_rows;
+    io_.in_done.assign(size_t(n_in), nullptr);
+    io_.out_done.assign(size_t(n_dec), nullptr);
+    for (cudaEvent_t& e : io_.in_done) VB_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    for (cudaEvent_t& e : io_.out_done) VB_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    io_.pre = capture([&](cudaStream_t st) { enc_dest_pre(st, nullptr); }, s);
+    for (int64_t c = 0; c < n_in; ++c) {
+        const int64_t r0 = c * io_.in_rows, n = std::min(io_.in_rows, Gx_ - r0);
+        io_.src.push_back(capture(
+            [&, r0, n](cudaStream_t st) {
+                for (int t = 0; t < T_in_; ++t) {
+                    const int64_t off = (int64_t(t) * Gx_ + r0) * V_in_;
+                    k::normalise(x_dev_ + off, mul_in_.as<float>(), add_in_.as<float>(), xn_ + off, n * V_in_, V_in_, st);
+                }
+                enc_source(xn_, Gx_, r0, n, st, nullptr);
+            },
+            s));
+    }
+    io_.mid = capture([&](cudaStream_t st) { middle(st, nullptr); }, s);
+    for (int64_t d = 0; d < n_dec; ++d) {
+        const int64_t lo = d * io_.dec_rows, n = std::min(io_.dec_rows, Gl_ - lo);
+        io_.dec.push_back(capture(
+            [&, lo, n](cudaStream_t st) {
+                bool pending = false;
+                dec_chunk(lo, n, st, nullptr, pending, nullptr, nullptr);
+                output_rows(xn_, yn_, lo, n, st, nullptr);
+                for (int t = 0; t < T_out_; ++t) {
+                    const int64_t off = (int64_t(t) * Gl_ + lo) * V_out_;
+                    k::denormalise(yn_ + off, add_out_.as<float>(), mul_out_.as<float>(), y_dev_ + off, n * V_out_,
+                                   V_out_, st);
+                }
+            },
+            s));
+    }
+    io_.ready = true;
+}
+
+template <class T>
+void Engine<T>::io_release() {
+    if (io_.cio) cudaStreamSynchronize(io_.cio), cudaStreamDestroy(io_.cio);
+    if (io_.pre) cudaGraphExecDestroy(io_.pre);
+    if (io_.mid) cudaGraphExecDestroy(io_.mid);
+    for (cudaGraphExec_t g : io_.src)
+        if (g) cudaGraphExecDestroy(g);
+    for (cudaGraphExec_t g : io_.dec)
+        if (g) cudaGraphExecDestroy(g);
+    for (cudaEvent_t e : io_.in_done)
+        if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : io_.out_done)
+        if (e) cudaEventDestroy(e);
+    if (io_.start) cudaEventDestroy(io_.start);
+    io_ = IoPipe{};
+}
+
+// predict_step through host buffers with the copies overlapped: x's rows in chunks on cio_ (each
+// input step's rows of a chunk, T_in copies), the encoder's destination side (which needs no input)
+// first, then each chunk's normalise + source side as soon as it has landed, the rest of the encoder and
+// the processor, then the decoder chunk by chunk with each chunk's output rows copied back on cio_ while
+// the next one runs. The same arithmetic as the one-graph device path, row for row, so the same bits.
+template <class T>
+void Engine<T>::predict_pipelined(const float* x, float* y) {
+    cudaStream_t s = stream_;
+    if (!io_.ready) io_setup();
+    auto run = [&](cudaGraphExec_t g, const std::function<void()>& eager) {
+        if (g) VB_CUDA(cudaGraphLaunch(g, s));
+        else eager();
+    };
+    VB_CUDA(cudaEventRecord(io_.start, s));  // x_dev_ / y_dev_ are free once the work before this call is done
+    VB_CUDA(cudaStreamWaitEvent(io_.cio, io_.start, 0));
+    for (size_t c = 0; c < io_.in_done.size(); ++c) {
+        const int64_t r0 = int64_t(c) * io_.in_rows, n = std::min(io_.in_rows, Gx_ - r0);
+        for (int t = 0; t < T_in_; ++t) {
+            const int64_t off = (int64_t(t) * Gx_ + r0) * V_in_;
+            VB_CUDA(cudaMemcpyAsync(x_dev_ + off, x + off, size_t(n * V_in_) * sizeof(float), cudaMemcpyHostToDevice,
+                                    io_.cio));
+        }
+        VB_CUDA(cudaEventRecord(io_.in_done[c], io_.cio));
+    }
+    run(io_.pre, [&] { enc_dest_pre(s, nullptr); });
+    for (size_t c = 0; c < io_.in_done.size(); ++c) {
+        VB_CUDA(cudaStreamWaitEvent(s, io_.in_done[c], 0));
+        const int64_t r0 = int64_t(c) * io_.in_rows, n = std::min(io_.in_rows, Gx_ - r0);
+        run(io_.src[c], [&] {
+            for (int t = 0; t < T_in_; ++t) {
+                const int64_t off = (int64_t(t) * Gx_ + r0) * V_in_;
+                k::normalise(x_dev_ + off, mul_in_.as<float>(), add_in_.as<float>(), xn_ + off, n * V_in_, V_in_, s);
+            }
+            enc_source(xn_, Gx_, r0, n, s, nullptr);
+        });
+    }
+    run(io_.mid, [&] { middle(s, nullptr); });
+    for (size_t d = 0; d < io_.out_done.size(); ++d) {
+        const int64_t lo = int64_t(d) * io_.dec_rows, n = std::min(io_.dec_rows, Gl_ - lo);
+        run(io_.dec[d], [&] {
+            bool pending = false;
+            dec_chunk(lo, n, s, nullptr, pending, nullptr, nullptr);
+            output_rows(xn_, yn_, lo, n, s, nullptr);
+            for (int t = 0; t < T_out_; ++t) {
+                const int64_t off = (int64_t(t) * Gl_ + lo) * V_out_;
+                k::denormalise(yn_ + off, add_out_.as<float>(), mul_out_.as<float>(), y_dev_ + off, n * V_out_, V_out_, s);
+            }
+        });
+        VB_CUDA(cudaEventRecord(io_.out_done[d], s));
+        VB_CUDA(cudaStreamWaitEvent(io_.cio, io_.out_done[d], 0));
+        for (int t = 0; t < T_out_; ++t) {
+            const int64_t off = (int64_t(t) * Gl_ + lo) * V_out_;
+            VB_CUDA(cudaMemcpyAsync(y + off, y_dev_ + off, size_t(n * V_out_) * sizeof(float), cudaMemcpyDeviceToHost,
+                                    io_.cio));
+        }
+    }
+    VB_CUDA(cudaStreamSynchronize(io_.cio));
     VB_CUDA(cudaStreamSynchronize(s));
 }
 

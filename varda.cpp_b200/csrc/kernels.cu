@@ -36,7 +36,7 @@ __global__ void denormalise_kernel(const float* __restrict__ yn, const float* __
 
 template <class T>
 __global__ void assemble_kernel(const float* __restrict__ xn, const float* __restrict__ attr, int T_in, int64_t G,
-                                int V, int A, T* __restrict__ out, int64_t ld) {
+                                int V, int A, T* __restrict__ out, int64_t ld, int64_t slot_rows) {
     const int64_t n = G * ld;
     const int TV = T_in * V;
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
@@ -45,7 +45,7 @@ __global__ void assemble_kernel(const float* __restrict__ xn, const float* __res
         float val = 0.0f;
         if (f < TV) {
             const int t = f / V, v = f - t * V;
-            val = xn[(int64_t(t) * G + g) * V + v];
+            val = xn[(int64_t(t) * slot_rows + g) * V + v];
         } else if (f < TV + A) {
             val = attr[g * A + (f - TV)];
         }
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(256) output_kernel(OutputArgs a) {
     const int t = blockIdx.y;
     float* row = sm + wid * a.V_out;
     const T* dec = static_cast<const T*>(a.dec) + g * a.ld_dec + int64_t(t) * a.V_out;
-    const int64_t orow = int64_t(t) * a.G + g;
+    const int64_t orow = int64_t(t) * (a.y_slot > 0 ? a.y_slot : a.G) + g;
     for (int v = lane; v < a.V_out; v += 32) {
         float val = to_f<T>(dec[v]);
         const int rs = a.res_src[v];
@@ -250,9 +250,10 @@ void denormalise(const float* yn, const float* add, const float* mul, float* y, 
 
 template <class T>
 void assemble(const float* xn, const float* attr, int T_in, int64_t G, int V, int A, T* out, int64_t ld,
-              cudaStream_t s) {
+              cudaStream_t s, int64_t slot_rows) {
     if (G <= 0) return;
-    assemble_kernel<T><<<grid_for(G * ld, 256), 256, 0, s>>>(xn, attr, T_in, G, V, A, out, ld);
+    assemble_kernel<T><<<grid_for(G * ld, 256), 256, 0, s>>>(xn, attr, T_in, G, V, A, out, ld,
+                                                            slot_rows > 0 ? slot_rows : G);
     VB_LAUNCH();
 }
 
@@ -370,8 +371,8 @@ void output_assemble(const OutputArgs& a, cudaStream_t s) {
     VB_LAUNCH();
 }
 
-template void assemble<float>(const float*, const float*, int, int64_t, int, int, float*, int64_t, cudaStream_t);
-template void assemble<__half>(const float*, const float*, int, int64_t, int, int, __half*, int64_t, cudaStream_t);
+template void assemble<float>(const float*, const float*, int, int64_t, int, int, float*, int64_t, cudaStream_t, int64_t);
+template void assemble<__half>(const float*, const float*, int, int64_t, int, int, __half*, int64_t, cudaStream_t, int64_t);
 template void convert_2d<float, float>(const float*, int64_t, float*, int64_t, int64_t, int64_t, cudaStream_t);
 template void convert_2d<float, __half>(const float*, int64_t, __half*, int64_t, int64_t, int64_t, cudaStream_t);
 template void convert_2d<__half, float>(const __half*, int64_t, float*, int64_t, int64_t, int64_t, cudaStream_t);

@@ -19,10 +19,11 @@ namespace vb::k {
 void normalise(const float* x, const float* mul, const float* add, float* xn, int64_t n, int V, cudaStream_t s);
 // y[i] = (yn[i] - add[v]) / mul[v], IEEE subtraction and division.
 void denormalise(const float* yn, const float* add, const float* mul, float* y, int64_t n, int V, cudaStream_t s);
-// out[g, t V + v] = xn[t, g, v]; out[g, T V + a] = attr[g, a]; out[g, F..ld) = 0.
+// out[g, t V + v] = xn[t, g, v]; out[g, T V + a] = attr[g, a]; out[g, F..ld) = 0 for g < G, the input
+// slots slot_rows rows apart (0: G; a row range of a larger input passes its full row count).
 template <class T>
 void assemble(const float* xn, const float* attr, int T_in, int64_t G, int V, int A, T* out, int64_t ld,
-              cudaStream_t s);
+              cudaStream_t s, int64_t slot_rows = 0);
 // dst[di(r), 0:cols] = src[si(r), 0:cols] for r < rows, di / si the index arrays or the identity
 // when null; cols * sizeof(T) and both strides multiples of 16 bytes. Halo pack / unpack.
 template <class T>
@@ -51,6 +52,7 @@ struct OutputArgs {
     const int* bidx = nullptr;
     float* pre_bound = nullptr;  // optional [T_out, G, V_out]
     float* y = nullptr;          // [T_out, G, V_out]
+    int64_t y_slot = 0;          // rows between the output steps of y / pre_bound (0: G)
 };
 // Per output step: fp32 cast, prognostic residual, boundings in config order (reference
 // backend_cpu.cpp:504-522, 111-136).
