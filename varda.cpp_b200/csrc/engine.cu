@@ -319,15 +319,23 @@ private:
     // pipelined host I/O (one GPU, no hook): the host -> device copy of x in row chunks on cio_ while the
     // encoder's source side runs on the chunks already there, and the decoder in row chunks whose
     // outputs go back on cio_ while the next chunk runs; each compute piece is a CUDA graph
+    struct IoSeg {  // one piece of the pipelined step: a graph of `body`, or `body` run eagerly
+        std::function<void(cudaStream_t)> body;
+        cudaGraphExec_t graph = nullptr;
+    };
     struct IoPipe {
         bool on = false, ready = false;
         int64_t in_rows = 0, dec_rows = 0;  // input chunk rows; decoder chunk rows (never straddle a tile)
         cudaStream_t cio = nullptr;
         cudaEvent_t start = nullptr;
         std::vector<cudaEvent_t> in_done, out_done;
-        cudaGraphExec_t pre = nullptr, mid = nullptr;
-        std::vector<cudaGraphExec_t> src, dec;
+        IoSeg pre, halo, mid;
+        std::vector<IoSeg> src, dec;
     } io_;
+    void io_run(IoSeg& g, cudaStream_t s) {
+        if (g.graph) VB_CUDA(cudaGraphLaunch(g.graph, s));
+        else if (g.body) g.body(s);
+    }
     void io_setup();
     void io_release();
     void predict_pipelined(const float* x, float* y);
@@ -707,15 +715,14 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         proc_outer_ = upload(outer.data(), std::max<size_t>(1, outer.size()) * sizeof(int32_t));
     }
     // pipelined host I/O: decoder chunks of ~Gl / VB_IO_CHUNKS rows (the memory cap's chunks if set),
-    // input chunks of ~Gx / (2 VB_IO_CHUNKS) rows; the decoder tiles respect the chunk boundaries. On C1
+    // input chunks of ~Gl / (2 VB_IO_CHUNKS) own rows; the decoder tiles respect the chunk boundaries. On C1
     // the copies (1.22 GB in at 56 GB/s, 0.54 GB out) then add ~7 ms to the 176-180 ms step instead of ~26.
-    io_.on = plan_.world == 1 && env_int("VB_IO_PIPELINE", 1) != 0;
+    io_.on = env_int("VB_IO_PIPELINE", 1) != 0;
     if (io_.on) {
         const int64_t nio = std::max<int64_t>(1, env_int("VB_IO_CHUNKS", 8)), gl = std::max<int64_t>(Gl_, 1);
         io_.dec_rows = dec_rows_ < Gl_ ? dec_rows_
                                        : std::min<int64_t>(int64_t(align_up(size_t((gl + nio - 1) / nio), 128)), gl);
-        const int64_t gx = std::max<int64_t>(Gx_, 1);
-        io_.in_rows = std::min<int64_t>(int64_t(align_up(size_t((gx + 2 * nio - 1) / (2 * nio)), 128)), gx);
+        io_.in_rows = std::min<int64_t>(int64_t(align_up(size_t((gl + 2 * nio - 1) / (2 * nio)), 128)), gl);
     }
     const int64_t dec_tile_chunk = io_.on ? io_.dec_rows : dec_rows_;
     g_dec_ = upload_graph(plan_.dec_g, "dec", dec_tile_chunk < Gl_ ? dec_tile_chunk : 0);
@@ -940,6 +947,7 @@ void Engine<T>::attention_rows(const GraphDev& g, const Block<T>& b, const Devic
 // rows apart), emb_src, LN_src (in place), [k | v]. Row-wise, so any split of the rows gives the same bits.
 template <class T>
 void Engine<T>::enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64_t n, cudaStream_t s, Hook* hk) {
+    if (n <= 0) return;
     const int64_t G = Gx_, C = C_;
     {
         Span sp(this, s, "assemble", 0, double(n) * (T_in_ * V_in_ * 4 + A_node_ * 4 + ldF_ * sizeof(T)));
@@ -1229,6 +1237,10 @@ void Engine<T>::predict_step(const float* x, float* y, HookFn hook, void* user) 
     if (plan_.world > 1) {
         // y gets this rank's rows of the full (1, T_out, 1, G, V_out) output
         if (hook) fail(kUnsupported, "the activation hook is available on single-GPU models only");
+        if (io_.on && opts_.cuda_graph && ran_eager_) {
+            predict_pipelined(x, y);
+            return;
+        }
         upload_input(x, s);
         enqueue_predict();
         for (int t = 0; t < T_out_; ++t)
@@ -1267,52 +1279,69 @@ void Engine<T>::io_setup() {
     cudaStream_t s = stream_;
     VB_CUDA(cudaStreamCreateWithFlags(&io_.cio, cudaStreamNonBlocking));
     VB_CUDA(cudaEventCreateWithFlags(&io_.start, cudaEventDisableTiming));
-    const int64_t n_in = (Gx_ + io_.in_rows - 1) / io_.in_rows, n_dec = (Gl_ + io_.dec_rows - 1) / io_.dec_rows;
+    const int64_t n_in = (Gl_ + io_.in_rows - 1) / io_.in_rows, n_dec = (Gl_ + io_.dec_rows - 1) / io_.dec_rows;
     io_.in_done.assign(size_t(n_in), nullptr);
     io_.out_done.assign(size_t(n_dec), nullptr);
     for (cudaEvent_t& e : io_.in_done) VB_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     for (cudaEvent_t& e : io_.out_done) VB_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    io_.pre = capture([&](cudaStream_t st) { enc_dest_pre(st, nullptr); }, s);
+    // normalise + encoder source side of rows [r0, r0 + n) of the Gx rows
+    auto src_rows = [this](int64_t r0, int64_t n, cudaStream_t st) {
+        if (n <= 0) return;
+        for (int t = 0; t < T_in_; ++t) {
+            const int64_t off = (int64_t(t) * Gx_ + r0) * V_in_;
+            k::normalise(x_dev_ + off, mul_in_.as<float>(), add_in_.as<float>(), xn_ + off, n * V_in_, V_in_, st);
+        }
+        enc_source(xn_, Gx_, r0, n, st, nullptr);
+    };
+    io_.pre.body = [this](cudaStream_t st) { enc_dest_pre(st, nullptr); };
     for (int64_t c = 0; c < n_in; ++c) {
-        const int64_t r0 = c * io_.in_rows, n = std::min(io_.in_rows, Gx_ - r0);
-        io_.src.push_back(capture(
-            [&, r0, n](cudaStream_t st) {
-                for (int t = 0; t < T_in_; ++t) {
-                    const int64_t off = (int64_t(t) * Gx_ + r0) * V_in_;
-                    k::normalise(x_dev_ + off, mul_in_.as<float>(), add_in_.as<float>(), xn_ + off, n * V_in_, V_in_, st);
-                }
-                enc_source(xn_, Gx_, r0, n, st, nullptr);
-            },
-            s));
+        const int64_t r0 = c * io_.in_rows, n = std::min(io_.in_rows, Gl_ - r0);
+        io_.src.push_back(IoSeg{[src_rows, r0, n](cudaStream_t st) { src_rows(r0, n, st); }, nullptr});
     }
-    io_.mid = capture([&](cudaStream_t st) { middle(st, nullptr); }, s);
+    if (plan_.world > 1)  // the encoder's halo rows from their owners, then their source side
+        io_.halo.body = [this, src_rows](cudaStream_t st) {
+            exchange_input(x_dev_, st);
+            src_rows(Gl_, n_eh_, st);
+        };
+    io_.mid.body = [this](cudaStream_t st) {
+        if (middle(st, nullptr)) VB_CUDA(cudaStreamWaitEvent(st, ev_halo_, 0));  // the decoder halo has landed
+    };
     for (int64_t d = 0; d < n_dec; ++d) {
         const int64_t lo = d * io_.dec_rows, n = std::min(io_.dec_rows, Gl_ - lo);
-        io_.dec.push_back(capture(
-            [&, lo, n](cudaStream_t st) {
-                bool pending = false;
-                dec_chunk(lo, n, st, nullptr, pending, nullptr, nullptr);
-                output_rows(xn_, yn_, lo, n, st, nullptr);
-                for (int t = 0; t < T_out_; ++t) {
-                    const int64_t off = (int64_t(t) * Gl_ + lo) * V_out_;
-                    k::denormalise(yn_ + off, add_out_.as<float>(), mul_out_.as<float>(), y_dev_ + off, n * V_out_,
-                                   V_out_, st);
-                }
-            },
-            s));
+        io_.dec.push_back(IoSeg{[this, lo, n](cudaStream_t st) {
+                                    bool pending = false;
+                                    dec_chunk(lo, n, st, nullptr, pending, nullptr, nullptr);
+                                    output_rows(xn_, yn_, lo, n, st, nullptr);
+                                    for (int t = 0; t < T_out_; ++t) {
+                                        const int64_t off = (int64_t(t) * Gl_ + lo) * V_out_;
+                                        k::denormalise(yn_ + off, add_out_.as<float>(), mul_out_.as<float>(),
+                                                       y_dev_ + off, n * V_out_, V_out_, st);
+                                    }
+                                },
+                                nullptr});
     }
+    // every rank captures the same pieces in the same order (the halo and mid pieces hold NCCL calls)
+    auto cap = [&](IoSeg& g) {
+        if (g.body) g.graph = capture(g.body, s);
+    };
+    cap(io_.pre);
+    for (IoSeg& g : io_.src) cap(g);
+    cap(io_.halo);
+    cap(io_.mid);
+    for (IoSeg& g : io_.dec) cap(g);
     io_.ready = true;
 }
 
 template <class T>
 void Engine<T>::io_release() {
     if (io_.cio) cudaStreamSynchronize(io_.cio), cudaStreamDestroy(io_.cio);
-    if (io_.pre) cudaGraphExecDestroy(io_.pre);
-    if (io_.mid) cudaGraphExecDestroy(io_.mid);
-    for (cudaGraphExec_t g : io_.src)
-        if (g) cudaGraphExecDestroy(g);
-    for (cudaGraphExec_t g : io_.dec)
-        if (g) cudaGraphExecDestroy(g);
+    IoSeg* one[3] = {&io_.pre, &io_.halo, &io_.mid};
+    for (IoSeg* g : one)
+        if (g->graph) cudaGraphExecDestroy(g->graph);
+    for (IoSeg& g : io_.src)
+        if (g.graph) cudaGraphExecDestroy(g.graph);
+    for (IoSeg& g : io_.dec)
+        if (g.graph) cudaGraphExecDestroy(g.graph);
     for (cudaEvent_t e : io_.in_done)
         if (e) cudaEventDestroy(e);
     for (cudaEvent_t e : io_.out_done)
@@ -1330,52 +1359,31 @@ template <class T>
 void Engine<T>::predict_pipelined(const float* x, float* y) {
     cudaStream_t s = stream_;
     if (!io_.ready) io_setup();
-    auto run = [&](cudaGraphExec_t g, const std::function<void()>& eager) {
-        if (g) VB_CUDA(cudaGraphLaunch(g, s));
-        else eager();
-    };
+    // host rows of this rank: data rows [g_lo, g_hi) of every step
     VB_CUDA(cudaEventRecord(io_.start, s));  // x_dev_ / y_dev_ are free once the work before this call is done
     VB_CUDA(cudaStreamWaitEvent(io_.cio, io_.start, 0));
     for (size_t c = 0; c < io_.in_done.size(); ++c) {
-        const int64_t r0 = int64_t(c) * io_.in_rows, n = std::min(io_.in_rows, Gx_ - r0);
-        for (int t = 0; t < T_in_; ++t) {
-            const int64_t off = (int64_t(t) * Gx_ + r0) * V_in_;
-            VB_CUDA(cudaMemcpyAsync(x_dev_ + off, x + off, size_t(n * V_in_) * sizeof(float), cudaMemcpyHostToDevice,
-                                    io_.cio));
-        }
+        const int64_t r0 = int64_t(c) * io_.in_rows, n = std::min(io_.in_rows, Gl_ - r0);
+        for (int t = 0; t < T_in_; ++t)
+            VB_CUDA(cudaMemcpyAsync(x_dev_ + (int64_t(t) * Gx_ + r0) * V_in_, x + (int64_t(t) * G_ + plan_.g_lo + r0) * V_in_,
+                                    size_t(n * V_in_) * sizeof(float), cudaMemcpyHostToDevice, io_.cio));
         VB_CUDA(cudaEventRecord(io_.in_done[c], io_.cio));
     }
-    run(io_.pre, [&] { enc_dest_pre(s, nullptr); });
+    io_run(io_.pre, s);
     for (size_t c = 0; c < io_.in_done.size(); ++c) {
         VB_CUDA(cudaStreamWaitEvent(s, io_.in_done[c], 0));
-        const int64_t r0 = int64_t(c) * io_.in_rows, n = std::min(io_.in_rows, Gx_ - r0);
-        run(io_.src[c], [&] {
-            for (int t = 0; t < T_in_; ++t) {
-                const int64_t off = (int64_t(t) * Gx_ + r0) * V_in_;
-                k::normalise(x_dev_ + off, mul_in_.as<float>(), add_in_.as<float>(), xn_ + off, n * V_in_, V_in_, s);
-            }
-            enc_source(xn_, Gx_, r0, n, s, nullptr);
-        });
+        io_run(io_.src[c], s);
     }
-    run(io_.mid, [&] { middle(s, nullptr); });
+    io_run(io_.halo, s);
+    io_run(io_.mid, s);
     for (size_t d = 0; d < io_.out_done.size(); ++d) {
         const int64_t lo = int64_t(d) * io_.dec_rows, n = std::min(io_.dec_rows, Gl_ - lo);
-        run(io_.dec[d], [&] {
-            bool pending = false;
-            dec_chunk(lo, n, s, nullptr, pending, nullptr, nullptr);
-            output_rows(xn_, yn_, lo, n, s, nullptr);
-            for (int t = 0; t < T_out_; ++t) {
-                const int64_t off = (int64_t(t) * Gl_ + lo) * V_out_;
-                k::denormalise(yn_ + off, add_out_.as<float>(), mul_out_.as<float>(), y_dev_ + off, n * V_out_, V_out_, s);
-            }
-        });
+        io_run(io_.dec[d], s);
         VB_CUDA(cudaEventRecord(io_.out_done[d], s));
         VB_CUDA(cudaStreamWaitEvent(io_.cio, io_.out_done[d], 0));
-        for (int t = 0; t < T_out_; ++t) {
-            const int64_t off = (int64_t(t) * Gl_ + lo) * V_out_;
-            VB_CUDA(cudaMemcpyAsync(y + off, y_dev_ + off, size_t(n * V_out_) * sizeof(float), cudaMemcpyDeviceToHost,
-                                    io_.cio));
-        }
+        for (int t = 0; t < T_out_; ++t)
+            VB_CUDA(cudaMemcpyAsync(y + (int64_t(t) * G_ + plan_.g_lo + lo) * V_out_, y_dev_ + (int64_t(t) * Gl_ + lo) * V_out_,
+                                    size_t(n * V_out_) * sizeof(float), cudaMemcpyDeviceToHost, io_.cio));
     }
     VB_CUDA(cudaStreamSynchronize(io_.cio));
     VB_CUDA(cudaStreamSynchronize(s));
