@@ -67,6 +67,8 @@ bool graph_listed(const char* env, const std::string& graph, const char* dflt) {
 }
 bool tiled_for(const std::string& graph, const char* dflt) { return graph_listed("VB_ATT_TILED", graph, dflt); }
 bool mma_for(const std::string& graph) { return graph_listed("VB_ATT_MMA", graph, kMmaDefault); }
+// Which graphs' gather launches visit destinations in source order (VB_ATT_ORDER, same forms).
+constexpr const char* kOrderDefault = "enc";
 
 // f(begin, end) over [0, n) split into contiguous ranges on up to 16 host threads (one below `grain`
 // items per thread). Used for the per-element conversions of the load path, whose results do not
@@ -130,6 +132,9 @@ struct GraphDev {
     // 128 measured 9.6 ms against 5.3 ms for the gather kernel alone, whose per-edge rate dominates.
     bool wide = false;
     DeviceBuffer light, wide_dev, part0_dev, parts, scratch;
+    // destination visiting order for a whole-graph gather launch (VB_ATT_ORDER; empty: index order):
+    // rows sorted by their smallest source, so rows that gather the same sources run close together
+    DeviceBuffer order;
     std::vector<int32_t> light_rows, wide_rows, part0;  // host copies (sorted rows; part prefix)
 };
 constexpr int kWideDeg = 2048, kPartEdges = 64;
@@ -543,6 +548,18 @@ GraphDev Engine<T>::upload_graph(const CsrGraph& csr, const std::string& name, i
         d.scratch.alloc(pt.size() * size_t(k::attention_parts_record(C_, heads_)) * sizeof(float));
         act_bytes_ += d.scratch.bytes();
     }
+    if (!d.tiled && !d.wide && graph_listed("VB_ATT_ORDER", name, kOrderDefault) && csr.n_dst > 0) {
+        std::vector<int64_t> key(size_t(csr.n_dst));
+        for (int64_t r = 0; r < csr.n_dst; ++r) {
+            int64_t k = csr.n_src + r;  // rows without edges go last
+            for (int32_t e = csr.row_ptr[size_t(r)]; e < csr.row_ptr[size_t(r + 1)]; ++e) k = std::min<int64_t>(k, csr.src[size_t(e)]);
+            key[size_t(r)] = k;
+        }
+        std::vector<int32_t> ord(size_t(csr.n_dst));
+        for (int64_t r = 0; r < csr.n_dst; ++r) ord[size_t(r)] = int32_t(r);
+        std::stable_sort(ord.begin(), ord.end(), [&](int32_t a, int32_t b) { return key[size_t(a)] < key[size_t(b)]; });
+        d.order = upload(ord.data(), ord.size() * sizeof(int32_t));
+    }
     d.row_ptr = upload(csr.row_ptr.data(), csr.row_ptr.size() * sizeof(int32_t));
     d.edges = upload(packed.data(), std::max<size_t>(1, packed.size()) * sizeof(EdgeRec));
     d.n_src = csr.n_src;
@@ -903,6 +920,11 @@ void Engine<T>::attention(const GraphDev& g, const Block<T>& b, int64_t lo, int6
             }
             return;
         }
+    }
+    if (g.order.get() && lo == 0 && n == g.n_dst) {  // the whole graph, in source order
+        a.rows = g.order.template as<int32_t>();
+        k::attention<T>(a, s);
+        return;
     }
     if (g.wide) {
         // rows [lo, lo + n): the light ones on the gather kernel (row list), the wide ones by parts
