@@ -201,6 +201,15 @@ int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* att
  * tiles of up to 128 rows and 192 distinct sources, q.k and the value sums as tcgen05 MMAs; head_dim
  * 64 only). vb_attention_tiled runs whichever kind the tiles were built for. */
 enum { VB_TILES_SMEM = 0, VB_TILES_MMA = 1 };
+/* The tile plan of a kind on the host (no device needed), for inspection and tests: counts[0] tiles,
+ * counts[1] distinct-source entries, counts[2] heavy rows (left to the gather kernel); then, where the
+ * arrays are non-null and sized by a first call: tiles4 [tiles][4] = {row0, nrows, src0, nsrc}, srcs (each
+ * tile's distinct sources in increasing order, a tile's slot s being srcs[src0 + s]), heavy (rows),
+ * edges [E][4] (the CSR-order records {a0, a1, a2, slot or source (int bits)}, attributes rounded to
+ * fp16; for VB_TILES_MMA each tiled row's records sorted by slot). */
+int vb_tile_plan(const int32_t* row_ptr, const int32_t* src, const float* attr_csr, int A, int64_t n_src,
+                 int64_t n_dst, int kind, int64_t counts[3], int32_t* tiles4, int32_t* srcs, int32_t* heavy,
+                 float* edges);
 int vb_tiles_create_kind(const int32_t* row_ptr, const int32_t* src, const float* attr_csr, int A, int64_t n_src,
                          int64_t n_dst, int head_dim, int kind, vb_tiles** out);
 int vb_attention_tiled(vb_tiles* t, int64_t dst_lo, int64_t n_rows, const void* q, int64_t ldq, const void* k,

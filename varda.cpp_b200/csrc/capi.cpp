@@ -356,6 +356,32 @@ int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* att
     return vb_tiles_create_kind(row_ptr, src, attr, A, n_src, n_dst, head_dim, VB_TILES_SMEM, out);
 }
 
+int vb_tile_plan(const int32_t* row_ptr, const int32_t* src, const float* attr, int A, int64_t n_src, int64_t n_dst,
+                 int kind, int64_t counts[3], int32_t* tiles4, int32_t* srcs, int32_t* heavy, float* edges) {
+    return guard([&] {
+        need(row_ptr, "row_ptr"), need(counts, "counts");
+        if (kind != VB_TILES_SMEM && kind != VB_TILES_MMA) vb::fail(vb::kInvalidArgument, "tiles kind");
+        vb::CsrGraph g;
+        g.n_src = n_src, g.n_dst = n_dst, g.attr_dim = A;
+        g.row_ptr.assign(row_ptr, row_ptr + n_dst + 1);
+        g.n_edges = g.row_ptr.back();
+        g.src.assign(src, src + g.n_edges);
+        g.attr.assign(attr, attr + g.n_edges * A);
+        vb::TilePlan tp = kind == VB_TILES_MMA
+                              ? vb::make_tiles(g, vb::k::mma_max_src(), vb::k::mma_max_rows(), vb::k::mma_max_edges(), 0, true, 0, true)
+                              : vb::make_tiles(g, vb::k::tiled_max_src(), vb::k::tiled_max_rows(),
+                                               vb::k::tiled_max_edges(), 0, true);
+        counts[0] = int64_t(tp.row0.size()), counts[1] = int64_t(tp.srcs.size()), counts[2] = int64_t(tp.heavy.size());
+        if (tiles4)
+            for (size_t i = 0; i < tp.row0.size(); ++i)
+                tiles4[4 * i] = tp.row0[i], tiles4[4 * i + 1] = tp.nrows[i], tiles4[4 * i + 2] = tp.src0[i],
+                           tiles4[4 * i + 3] = tp.nsrc[i];
+        if (srcs) std::copy(tp.srcs.begin(), tp.srcs.end(), srcs);
+        if (heavy) std::copy(tp.heavy.begin(), tp.heavy.end(), heavy);
+        if (edges) std::memcpy(edges, tp.edges.data(), tp.edges.size() * sizeof(vb::EdgeRec));
+    });
+}
+
 int vb_tiles_create_kind(const int32_t* row_ptr, const int32_t* src, const float* attr, int A, int64_t n_src,
                          int64_t n_dst, int head_dim, int kind, vb_tiles** out) {
     (void)head_dim;

@@ -359,11 +359,30 @@ class Tiles:
             pass
 
 
+def tile_plan(row_ptr, src, attr_csr, n_src, kind=0):
+    """The host tile plan (vb_tile_plan): dict of tiles [n, 4] {row0, nrows, src0, nsrc}, srcs, heavy rows
+    and the packed edge records [E, 4] float32 (slot or source as int bits in column 3)."""
+    rp = np.ascontiguousarray(row_ptr, np.int32)
+    s = np.ascontiguousarray(src, np.int32)
+    at = np.ascontiguousarray(attr_csr, np.float32)
+    cnt = np.zeros(3, np.int64)
+    args = (_ptr(rp), _ptr(s), _ptr(at), at.shape[1], n_src, len(rp) - 1, kind)
+    check(lib.vb_tile_plan(*args, _ptr(cnt), None, None, None, None))
+    tiles = np.empty((int(cnt[0]), 4), np.int32)
+    srcs = np.empty(int(cnt[1]), np.int32)
+    heavy = np.empty(int(cnt[2]), np.int32)
+    edges = np.empty((len(s), 4), np.float32)
+    check(lib.vb_tile_plan(*args, _ptr(cnt), _ptr(tiles), _ptr(srcs), _ptr(heavy), _ptr(edges)))
+    return {"tiles": tiles, "srcs": srcs, "heavy": heavy, "edges": edges}
+
+
 def _bind_tiles():
     P, I, I64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
     lib.vb_tiles_create.argtypes = [P, P, P, I, I64, I64, I, P]
     lib.vb_tiles_create.restype = I
     lib.vb_tiles_create_kind.argtypes = [P, P, P, I, I64, I64, I, I, P]
+    lib.vb_tile_plan.argtypes = [P, P, P, I, I64, I64, I, P, P, P, P, P]
+    lib.vb_tile_plan.restype = I
     lib.vb_tiles_create_kind.restype = I
     lib.vb_attention_tiled.argtypes = [P, I64, I64, P, I64, P, P, I64, P, I64, P, I64, P, I, I, I, P]
     lib.vb_attention_tiled.restype = I
