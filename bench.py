@@ -6,7 +6,7 @@ HBM GB/s, on N B200s of one node.
 Prints one JSON line (rank 0). `value` is the device-resident time of one predict_step (the model's
 own input/output buffers, CUDA-graph replay, CUDA events on the model's stream, max over ranks);
 `e2e` is the same through the public host API vb_predict_step with pinned host buffers (H2D of x and
-D2H of y inside the timed region). `roofline` describes the dominant kernel class and
+D2H of y inside the timed region; the library overlaps them with the compute in row chunks). `roofline` describes the dominant kernel class and
 `edge_attention` the processor-block attention, both from one eager pass with a CUDA event pair
 around every launch (vb_profile_forward). `cpu_baseline` is the reference's own CPU fp32 backend
 (oracle/_ref/ref_dump, built from the reference's sources) timed on this host on a bounded sample.
