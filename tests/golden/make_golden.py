@@ -12,7 +12,7 @@ sources and oracle/_ref built; the fixtures then travel, the reference does not)
    ROLLOUT_STEPS steps of the reference's host rollout (varda::Rollout::run on the CPU backend,
    oracle/_ref/ref_rollout) with replayed synthetic forcings, both constant sources.
 
-    python tests/golden/make_golden.py [--reference /root/reference] [--only NAME ...]
+    python tests/golden/make_golden.py [--reference REFERENCE_TREE] [--only NAME ...]
 """
 from __future__ import annotations
 
