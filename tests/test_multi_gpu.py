@@ -1,6 +1,7 @@
 """Multi-GPU destination partition on B200s (skipped with fewer than 2 visible GPUs): one process per
 GPU, NCCL halo exchange; every rank's output rows must be bitwise equal to the single-GPU result
-(the partition keeps every destination's edge order and every GEMM row's arithmetic)."""
+(the partition keeps every destination's edge order and every GEMM row's arithmetic), with and without
+the encoder split."""
 import os
 
 import numpy as np
@@ -48,10 +49,13 @@ def _single(mp, xp, dtype, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("name", ["c0", "t256"])
+@pytest.mark.parametrize("name,enc_split", [("c0", 0), ("t256", 0), ("c0", 1), ("t1024", 1)])
 @pytest.mark.parametrize("dtype", [0, 1])
-def test_sharded_equals_single_gpu(name, dtype, seeded_model, tmp_path):
+def test_sharded_equals_single_gpu(name, enc_split, dtype, seeded_model, tmp_path, monkeypatch):
+    """enc_split: the encoder on its own hidden ranges (VB_SHARD_ENC=1), its output rows moved to their
+    processor owners; c0 and t1024 move rows between ranks at 2-4 GPUs."""
     import torch.multiprocessing as tmp
+    monkeypatch.setenv("VB_SHARD_ENC", str(enc_split))
     mp, xp = seeded_model(name)
     world = min(torch.cuda.device_count(), 4)
     ctx = tmp.get_context("spawn")

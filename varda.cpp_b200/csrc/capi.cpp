@@ -216,7 +216,7 @@ int64_t vb_shard_plan(const char* path, int world, int rank, char* buf, size_t l
                                         f.peek(std::string("graph.") + n + ".edge_attr"), ns, nd);
         };
         const vb::CsrGraph enc = g("enc", G, H), proc = g("proc", H, H), dec = g("dec", H, G);
-        s = vb::plan_json(vb::make_plan(c, enc, proc, dec, world, rank), true);
+        s = vb::plan_json(vb::make_plan(c, enc, proc, dec, world, rank, vb::enc_split_requested()), true);
     });
     if (rc != VB_OK) return -rc;
     if (buf && len) {

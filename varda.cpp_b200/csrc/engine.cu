@@ -310,7 +310,16 @@ private:
     // ---- destination partition (world == 1: the identity, no halos)
     ShardPlan plan_;
     int64_t Hl_ = 0, Gl_ = 0, Gx_ = 0, n_eh_ = 0, n_ph_ = 0, n_dh_ = 0;
+    int64_t El_ = 0;  // the encoder's destination rows (= Hl_ unless the encoder is split on its own)
     std::unique_ptr<Comm> comm_;
+    // encoder split: the encoder's output rows [e_lo, e_hi) go to their processor owners (one
+    // contiguous row range per peer each way, in elements of C; own rows by a device copy)
+    struct EncMove {
+        bool on = false;
+        std::vector<int64_t> send_off, send_cnt, recv_off, recv_cnt;
+        int64_t self_src = 0, self_dst = 0, self_rows = 0;
+    } emove_;
+    void enc_redistribute(const T* src, T* dst, cudaStream_t s);
     struct Xchg {  // one halo exchange: pack own K|V rows per peer, send/recv, (unpack)
         DeviceBuffer send_idx;  // local ids of the rows sent, grouped by peer
         std::vector<int64_t> send_off, send_cnt, recv_off, recv_cnt;  // in elements
@@ -614,6 +623,21 @@ void Engine<T>::exchange(Xchg& x, const T* src, int64_t lds, T* dst, int64_t ldd
     }
 }
 
+// Encoder split: the encoder's output rows (src, [El, C], rows [e_lo, e_hi)) to their processor owners
+// (dst, [Hl, C], rows [h_lo, h_hi)). Both sides are contiguous row ranges per peer, so the rows go
+// straight from src and into dst, without packing.
+template <class T>
+void Engine<T>::enc_redistribute(const T* src, T* dst, cudaStream_t s) {
+    double rows = double(emove_.self_rows);
+    for (int64_t n : emove_.send_cnt) rows += double(n) / double(C_);
+    for (int64_t n : emove_.recv_cnt) rows += double(n) / double(C_);
+    Span sp(this, s, "enc_redistribute", 0, rows * double(C_) * sizeof(T));
+    if (emove_.self_rows > 0)
+        VB_CUDA(cudaMemcpyAsync(dst + emove_.self_dst * C_, src + emove_.self_src * C_,
+                                size_t(emove_.self_rows * C_) * sizeof(T), cudaMemcpyDeviceToDevice, s));
+    comm_->exchange(src, emove_.send_off, emove_.send_cnt, dst, emove_.recv_off, emove_.recv_cnt, int(sizeof(T)), s);
+}
+
 template <class T>
 T* Engine<T>::act(size_t elems) {
     acts_.emplace_back(align_up(std::max<size_t>(1, elems) * sizeof(T), 256));
@@ -701,12 +725,30 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         CsrGraph proc = read_graph(file, "proc", H_, H_);
         CsrGraph dec = read_graph(file, "dec", H_, G_);
         lt.mark("CSR build");
-        plan_ = make_plan(cfg_, enc, proc, dec, opts_.world, opts_.rank);
+        plan_ = make_plan(cfg_, enc, proc, dec, opts_.world, opts_.rank, enc_split_requested());
         lt.mark("partition plan");
     }
     Hl_ = plan_.h_hi - plan_.h_lo, Gl_ = plan_.g_hi - plan_.g_lo;
     n_eh_ = int64_t(plan_.enc_halo.size()), n_ph_ = int64_t(plan_.proc.halo.size());
     n_dh_ = int64_t(plan_.dec.halo.size()), Gx_ = Gl_ + n_eh_;
+    El_ = plan_.e_hi - plan_.e_lo;
+    emove_.on = plan_.e_split != plan_.h_split;
+    if (emove_.on) {  // the plan's row ranges as element offsets into [El, C] and [Hl, C]
+        const int W = plan_.world;
+        const ShardPlan::RowMove& m = plan_.enc_move;
+        for (auto* v : {&emove_.send_off, &emove_.send_cnt, &emove_.recv_off, &emove_.recv_cnt}) v->assign(size_t(W), 0);
+        for (int p = 0; p < W; ++p) {
+            const int64_t slo = m.send_lo[size_t(p)], shi = m.send_hi[size_t(p)];
+            const int64_t rlo = m.recv_lo[size_t(p)], rhi = m.recv_hi[size_t(p)];
+            if (p == plan_.rank) {
+                emove_.self_src = slo - plan_.e_lo, emove_.self_dst = slo - plan_.h_lo;
+                emove_.self_rows = std::max<int64_t>(0, shi - slo);
+                continue;
+            }
+            if (shi > slo) emove_.send_off[size_t(p)] = (slo - plan_.e_lo) * C_, emove_.send_cnt[size_t(p)] = (shi - slo) * C_;
+            if (rhi > rlo) emove_.recv_off[size_t(p)] = (rlo - plan_.h_lo) * C_, emove_.recv_cnt[size_t(p)] = (rhi - rlo) * C_;
+        }
+    }
     {
         // decoder destination chunk: all own data rows in one chunk unless limited
         int64_t rows = opts_.dec_chunk_rows > 0 ? opts_.dec_chunk_rows : env_int("VB_DEC_CHUNK_ROWS", Gl_);
@@ -766,10 +808,10 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     }
     if (plan_.world == 1) h_attr_host_.assign(ha.as<float>(), ha.as<float>() + ha.numel());
     {
-        std::vector<T> hp(size_t(Hl_ * ldA_), T(0.0f));
-        for (int64_t r = 0; r < Hl_; ++r)
+        std::vector<T> hp(size_t(El_ * ldA_), T(0.0f));  // the encoder's destination rows
+        for (int64_t r = 0; r < El_; ++r)
             for (int a = 0; a < A_node_; ++a)
-                hp[size_t(r * ldA_ + a)] = T(ha.as<float>()[(plan_.h_lo + r) * A_node_ + a]);
+                hp[size_t(r * ldA_ + a)] = T(ha.as<float>()[(plan_.e_lo + r) * A_node_ + a]);
         h_attr_ = upload(hp.data(), hp.size() * sizeof(T));
     }
 
@@ -793,16 +835,18 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     y_dev_ = actf(size_t(output_numel()));
     x_data_ = act(size_t(Gx_ * ldF_));
     dec_out_ = act(size_t(Gl_ * ldVo_));
+    // hidden-row buffers: own processor rows, or the encoder's rows where it has more (encoder split)
+    const int64_t Hm = std::max(Hl_, El_);
     z_enc_ = act(size_t(Hl_ * C_));
-    zA_ = act(size_t(Hl_ * C_));
-    zB_ = act(size_t(Hl_ * C_));
-    xh_ = act(size_t(Hl_ * C_));
+    zA_ = act(size_t(Hm * C_));
+    zB_ = act(size_t(Hm * C_));
+    xh_ = act(size_t(Hm * C_));
     // q|k|v|self of own rows plus the K|V of the processor halo rows; later the decoder's k|v of
-    // own rows plus its halo
-    qkvs_ = act(size_t(std::max((Hl_ + n_ph_) * 4 * C_, (Hl_ + n_dh_) * 2 * C_)));
-    sbuf_ = act(size_t(Hl_ * C_));
-    out1_ = act(size_t(Hl_ * C_));
-    hbuf_ = act(size_t(Hl_ * mlp_));
+    // own rows plus its halo (first the encoder's q|self)
+    qkvs_ = act(size_t(std::max({(Hl_ + n_ph_) * 4 * C_, (Hl_ + n_dh_) * 2 * C_, El_ * 2 * C_})));
+    sbuf_ = act(size_t(Hm * C_));
+    out1_ = act(size_t(Hm * C_));
+    hbuf_ = act(size_t(Hm * mlp_));
     // Shared region: the encoder's source side ([Gx, C] embedding + [Gx, 2C] k|v), then the decoder's
     // destination chunks (6C + mlp per row). All own data rows in one chunk unless limited.
     const int64_t enc_elems = Gx_ * 3 * C_;
@@ -998,7 +1042,7 @@ void Engine<T>::enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64
 // LN_dst, [q | self].
 template <class T>
 void Engine<T>::enc_dest_pre(cudaStream_t s, Hook* hk) {
-    const int64_t H = Hl_, C = C_;
+    const int64_t H = El_, C = C_;
     T* emb_dst = zA_;
     linear(enc_emb_dst_, h_attr_.as<T>(), ldA_, emb_dst, C, H, s);
     if (hk) hk->dev("enc.emb_dst", emb_dst, C, H, C, {H, C});
@@ -1010,14 +1054,18 @@ void Engine<T>::enc_dest_pre(cudaStream_t s, Hook* hk) {
 // Returns whether the decoder halo exchange is still in flight on the communication stream.
 template <class T>
 bool Engine<T>::middle(cudaStream_t s, Hook* hk) {
-    const int64_t G = Gx_, H = Hl_, C = C_;
+    const int64_t G = Gx_, H = Hl_, C = C_, E = El_;
     T* kv_enc = region_ + G * C;
     T* emb_dst = zA_;
-    attention(g_enc_, enc_, 0, H, qkvs_, 2 * C, kv_enc, kv_enc + C, 2 * C, qkvs_ + C, 2 * C, sbuf_, s);
-    linear(enc_.proj, sbuf_, C, out1_, C, H, s, k::kEpiResidual, emb_dst, C);
-    ln(out1_, enc_.ln_mlp, xh_, H, s);
-    linear(enc_.mlp1, xh_, C, hbuf_, mlp_, H, s, k::kEpiGelu);
-    linear(enc_.mlp2, hbuf_, mlp_, z_enc_, C, H, s, k::kEpiResidual, out1_, C);
+    // encoder rows [0, E): with the encoder split the output goes to zB_ (free until the second
+    // processor block) and its rows then move to their processor owners' z_enc_
+    T* enc_out = emove_.on ? zB_ : z_enc_;
+    attention(g_enc_, enc_, 0, E, qkvs_, 2 * C, kv_enc, kv_enc + C, 2 * C, qkvs_ + C, 2 * C, sbuf_, s);
+    linear(enc_.proj, sbuf_, C, out1_, C, E, s, k::kEpiResidual, emb_dst, C);
+    ln(out1_, enc_.ln_mlp, xh_, E, s);
+    linear(enc_.mlp1, xh_, C, hbuf_, mlp_, E, s, k::kEpiGelu);
+    linear(enc_.mlp2, hbuf_, mlp_, enc_out, C, E, s, k::kEpiResidual, out1_, C);
+    if (emove_.on) enc_redistribute(enc_out, z_enc_, s);
     if (hk) hk->dev("enc.out", z_enc_, C, H, C, {H, C});
     ln(z_enc_, proc_[0].ln_dst, xh_, H, s);
 

@@ -96,8 +96,13 @@ CsrGraph local_graph(const CsrGraph& g, int64_t lo, int64_t hi, int64_t slo, int
 
 }  // namespace
 
+bool enc_split_requested() {
+    const char* e = std::getenv("VB_SHARD_ENC");
+    return e && *e && std::atoi(e) != 0;
+}
+
 ShardPlan make_plan(const Config& c, const CsrGraph& enc, const CsrGraph& proc, const CsrGraph& dec, int world,
-                    int rank) {
+                    int rank, bool enc_split) {
     if (world < 1 || rank < 0 || rank >= world) fail(kInvalidArgument, "shard plan: bad rank/world");
     ShardPlan p;
     p.world = world, p.rank = rank;
@@ -105,6 +110,7 @@ ShardPlan make_plan(const Config& c, const CsrGraph& enc, const CsrGraph& proc, 
     if (world == 1) {
         p.h_split = {0, H};
         p.g_split = {0, G};
+        p.e_split = p.h_split;
     } else {
         if (H < world) fail(kUnsupported, "shard plan: fewer hidden nodes than GPUs");
         if (G < world) fail(kUnsupported, "shard plan: fewer data nodes than GPUs");
@@ -128,17 +134,42 @@ ShardPlan make_plan(const Config& c, const CsrGraph& enc, const CsrGraph& proc, 
             wg[size_t(g)] = flop_g * kF + (dec.row_ptr[size_t(g + 1)] - dec.row_ptr[size_t(g)]) * row_bytes * kB;
         p.h_split = balanced_split(wh, world);
         p.g_split = balanced_split(wg, world);
+        p.e_split = p.h_split;
+        if (enc_split) {
+            // encoder phase alone: destination-side GEMMs per hidden row; per encoder edge its K|V read
+            // and its share of the source side (the data rows a range reads are recomputed or owned
+            // there, about E_enc / G edges per data row)
+            const double A = c.node_attr_dim;
+            const double flop_he = 2 * A * C + 2 * C * 2 * C + 2 * C * C + 4 * C * M;
+            const double flop_gs = 2 * F * C + 2 * C * 2 * C;
+            const double per_edge = row_bytes * kB + flop_gs * kF * double(G) / double(std::max<int64_t>(enc.n_edges, 1));
+            std::vector<double> we(static_cast<size_t>(H));
+            for (int64_t h = 0; h < H; ++h)
+                we[size_t(h)] = flop_he * kF + (enc.row_ptr[size_t(h + 1)] - enc.row_ptr[size_t(h)]) * per_edge;
+            std::vector<int64_t> es = balanced_split(we, world);
+            bool nonempty = true;  // an empty encoder range keeps the processor's ranges
+            for (int k = 0; k < world; ++k) nonempty = nonempty && es[size_t(k + 1)] > es[size_t(k)];
+            if (nonempty) p.e_split = es;
+        }
     }
     p.h_lo = p.h_split[size_t(rank)], p.h_hi = p.h_split[size_t(rank + 1)];
     p.g_lo = p.g_split[size_t(rank)], p.g_hi = p.g_split[size_t(rank + 1)];
+    p.e_lo = p.e_split[size_t(rank)], p.e_hi = p.e_split[size_t(rank + 1)];
+    for (int q = 0; q < world; ++q) {
+        p.enc_move.send_lo.push_back(std::max(p.e_lo, p.h_split[size_t(q)]));
+        p.enc_move.send_hi.push_back(std::min(p.e_hi, p.h_split[size_t(q + 1)]));
+        p.enc_move.recv_lo.push_back(std::max(p.h_lo, p.e_split[size_t(q)]));
+        p.enc_move.recv_hi.push_back(std::min(p.h_hi, p.e_split[size_t(q + 1)]));
+    }
 
     p.proc = halos(proc, p.h_split, p.h_split, world, rank);
     p.dec = halos(dec, p.g_split, p.h_split, world, rank);
-    // encoder: remote data sources of own hidden rows (uploaded from the host input, not exchanged)
-    p.enc_x = halos(enc, p.h_split, p.g_split, world, rank);
+    // encoder: remote data sources of own encoder rows (their inputs come from their owners, their source
+    // side is recomputed here)
+    p.enc_x = halos(enc, p.e_split, p.g_split, world, rank);
     p.enc_halo = p.enc_x.halo;
 
-    p.enc = local_graph(enc, p.h_lo, p.h_hi, p.g_lo, p.g_hi, p.enc_halo);
+    p.enc = local_graph(enc, p.e_lo, p.e_hi, p.g_lo, p.g_hi, p.enc_halo);
     p.proc_g = local_graph(proc, p.h_lo, p.h_hi, p.h_lo, p.h_hi, p.proc.halo);
     p.dec_g = local_graph(dec, p.g_lo, p.g_hi, p.h_lo, p.h_hi, p.dec.halo);
     return p;
@@ -181,6 +212,17 @@ std::string plan_json(const ShardPlan& p, bool with_graphs) {
     put_list(o, p.h_split);
     o += ",\"g_split\":";
     put_list(o, p.g_split);
+    o += ",\"e_split\":";
+    put_list(o, p.e_split);
+    o += ",\"enc_move\":{\"send_lo\":";
+    put_list(o, p.enc_move.send_lo);
+    o += ",\"send_hi\":";
+    put_list(o, p.enc_move.send_hi);
+    o += ",\"recv_lo\":";
+    put_list(o, p.enc_move.recv_lo);
+    o += ",\"recv_hi\":";
+    put_list(o, p.enc_move.recv_hi);
+    o += "}";
     o += ",\"proc\":";
     put_halo(o, p.proc);
     o += ",\"dec\":";
