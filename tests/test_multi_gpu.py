@@ -136,3 +136,20 @@ def test_sharded_rollout_equals_single_gpu(dtype, seeded_model, tmp_path):
         covered += hi - lo
         assert np.array_equal(z["y"], y1[:, lo:hi]), f"rank {r} differs from one GPU"
     assert covered == y1.shape[1]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_devices_in_one_process(seeded_model):
+    """Models on two devices of one process: kernel attributes and SM counts are set up per device, so
+    the second device's launches run as the first's do (same bits)."""
+    import varda_b200 as vb
+    from varda_b200 import safetensors as st
+    mp, xp = seeded_model("t1024")
+    x = np.array(st.read(xp)[0]["in.x"])
+    ys = []
+    for dev in (0, 1):
+        m = vb.Model.load(mp, precision=1, cuda_device=dev)
+        ys.append(m.predict_step(x))
+        m.free()
+    vb.check_device()
+    assert np.array_equal(ys[0], ys[1])

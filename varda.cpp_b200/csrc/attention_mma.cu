@@ -446,18 +446,13 @@ void attention_mma(const TileArgs& a, float scale_log2, cudaStream_t s) {
     if (a.ldq % 8 || a.ldkv % 8 || a.ldxr % 8 || a.ldo % 8 || !al16(a.q) || !al16(a.k) || !al16(a.v) || !al16(a.xr) ||
         !al16(a.out) || !al16(a.w_e) || a.C % 4)
         fail(kUnsupported, "tensor-core attention: operands must be 16-byte aligned (leading dimensions multiples of 8)");
-    static bool cfg = false;
-    static int sms = 0;
-    if (!cfg) {
+    static std::atomic<uint64_t> cfg{0};
+    once_per_device(cfg, [] {
         VB_CUDA(cudaFuncSetAttribute(attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
         VB_CUDA(cudaFuncSetAttribute(attention_mma_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      int(cudaSharedmemCarveoutMaxShared)));
-        int dev = 0;
-        VB_CUDA(cudaGetDevice(&dev));
-        VB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        cfg = true;
-    }
-    const int grid = std::min(a.ntiles, 2 * sms);  // persistent: two CTAs per SM
+    });
+    const int grid = std::min(a.ntiles, 2 * device_sm_count());  // persistent: two CTAs per SM
     attention_mma_kernel<<<unsigned(grid), kThreads, kSmem, s>>>(a, scale_log2);
     VB_LAUNCH();
 }

@@ -237,12 +237,11 @@ void attention_tiled(const TileArgs& a, float scale_log2, cudaStream_t s) {
     const unsigned grid = unsigned(a.ntiles * (a.C / kHG));
 #define VB_TA(L)                                                                                               \
     do {                                                                                                       \
-        static bool cfg = false;                                                                               \
-        if (!cfg) {                                                                                            \
+        static std::atomic<uint64_t> cfg{0};                                                                   \
+        once_per_device(cfg, [&] {                                                                             \
             VB_CUDA(cudaFuncSetAttribute(attention_tiled_kernel<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                          int(smem)));                                                          \
-            cfg = true;                                                                                        \
-        }                                                                                                      \
+        });                                                                                                    \
         attention_tiled_kernel<L><<<grid, 256, smem, s>>>(a, scale_log2);                                      \
     } while (0)
     switch (lph) {

@@ -227,7 +227,7 @@ int64_t vb_shard_plan(const char* path, int world, int rank, char* buf, size_t l
     return int64_t(s.size() + 1);
 }
 
-int64_t vb_launch_count(void) { return vb::launch_counter(); }
+int64_t vb_launch_count(void) { return vb::launch_counter().load(); }
 
 int64_t vb_profile_forward(vb_model* m, char* buf, size_t len) {
     std::string s;

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <stdexcept>
@@ -38,7 +39,7 @@ inline void cuda_check(cudaError_t e, const char* what, const char* file, int li
 
 // Number of this library's kernel launches issued by the calling process (eager launches and
 // launches recorded into a graph capture); read through vb_launch_count().
-int64_t& launch_counter();
+std::atomic<int64_t>& launch_counter();
 #define VB_LAUNCH()                                                                    \
     do {                                                                               \
         ::vb::cuda_check(cudaGetLastError(), "kernel launch", __FILE__, __LINE__);     \
@@ -46,6 +47,32 @@ int64_t& launch_counter();
     } while (0)
 
 inline size_t align_up(size_t n, size_t a) { return (n + a - 1) / a * a; }
+
+// One-time setup per CUDA device, such as a kernel's function attributes (the runtime keeps them per
+// device): runs f() on the first call made with the current device (devices 0..63; beyond that, on
+// every call), marking the device only once f() has returned. Concurrent first calls may both run
+// f(), which must be idempotent.
+template <class F> void once_per_device(std::atomic<uint64_t>& done, F&& f) {
+    int dev = 0;
+    VB_CUDA(cudaGetDevice(&dev));
+    const uint64_t bit = dev >= 0 && dev < 64 ? uint64_t(1) << dev : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return;
+    f();
+    if (bit) done.fetch_or(bit, std::memory_order_release);
+}
+
+// SM count of the current device (cached per device).
+inline int device_sm_count() {
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    VB_CUDA(cudaGetDevice(&dev));
+    int n = dev >= 0 && dev < 64 ? cache[dev].load(std::memory_order_relaxed) : 0;
+    if (!n) {
+        VB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
 
 // Owning device allocation (cudaMalloc at load time only; never inside a forward pass).
 class DeviceBuffer {

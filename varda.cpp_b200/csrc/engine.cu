@@ -1669,8 +1669,8 @@ std::string Engine<T>::profile_forward() {
 template class Engine<float>;
 template class Engine<__half>;
 
-int64_t& launch_counter() {
-    static int64_t n = 0;
+std::atomic<int64_t>& launch_counter() {
+    static std::atomic<int64_t> n{0};
     return n;
 }
 

@@ -733,25 +733,16 @@ unsigned* sched_counter(cudaStream_t s) {
     return base[dev] + 2 * it->second;
 }
 
-int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        VB_CUDA(cudaGetDevice(&dev));
-        VB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
-    }
-    return n;
-}
+int sm_count() { return device_sm_count(); }
 
 template <int BN, int STAGES, int EPI, bool PAIR>
 void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
     using L = Layout<BN, STAGES, EPI, PAIR>;
-    static bool configured = false;  // per instantiation; the attribute is per function
-    if (!configured) {
+    static std::atomic<uint64_t> configured{0};  // per instantiation and device
+    once_per_device(configured, [] {
         VB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, EPI, PAIR>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem));
-        configured = true;
-    }
+    });
     const CUtensorMap ta = make_map(a.A, a.M, a.K, a.lda, BM);
     const CUtensorMap tb = make_map(a.W, a.N, a.K, a.ldw, PAIR ? BN / 2 : BN);
     // 32 x 32 sub-tiles of the output, 64-byte swizzle: the epilogue's TMA stores
