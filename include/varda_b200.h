@@ -69,7 +69,8 @@ void vb_free(vb_model* m);
 
 /* varda::Model::predict_step (src/varda/varda.h:50, backend.h:16): host x (1, T_in, G, V_in) fp32 in
  * physical units -> host y (1, T_out, 1, G, V_out). hook may be NULL. On a sharded model every rank
- * passes the full x and writes only its own data rows of y (vb_data_range). */
+ * passes the full x and writes only its own data rows of y (vb_data_range). A bounded device-side wait
+ * that gave up in the step (GEMM or attention) makes it return VB_ERR_TIMEOUT, as vb_rollout does. */
 int vb_predict_step(vb_model* m, const float* x, float* y, vb_hook_fn hook, void* user);
 
 /* Autoregressive rollout with replayed forcings: varda::cuda::DeviceRollout::run

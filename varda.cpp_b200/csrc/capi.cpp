@@ -67,6 +67,12 @@ void need(const void* p, const char* what) {
     if (!p) vb::fail(vb::kInvalidArgument, std::string(what) + " is NULL");
 }
 
+// The kernels' device-side timeout flags (read and cleared; synchronises the device).
+void device_errors() {
+    if (vb::tc::take_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the tensor-core GEMM");
+    if (vb::k::take_attention_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the attention");
+}
+
 }  // namespace
 
 extern "C" {
@@ -113,7 +119,7 @@ int vb_predict_step(vb_model* m, const float* x, float* y, vb_hook_fn hook, void
     return guard([&] {
         need(m, "model"), need(x, "x"), need(y, "y");
         m->m->predict_step(x, y, hook, user);
-        if (vb::tc::take_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the tensor-core GEMM");
+        device_errors();
     });
 }
 
@@ -122,7 +128,7 @@ int vb_rollout(vb_model* m, const float* x0, int n_steps, const float* forcings,
     return guard([&] {
         need(m, "model"), need(x0, "x0");
         m->m->rollout(x0, n_steps, forcings, y, constants_oldest != 0, on_step, user, step_ms);
-        if (vb::tc::take_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the tensor-core GEMM");
+        device_errors();
     });
 }
 
@@ -198,10 +204,7 @@ size_t vb_activation_bytes(const vb_model* m) { return m ? m->m->activation_byte
 int64_t vb_decoder_chunk_rows(const vb_model* m) { return m ? m->m->decoder_chunk_rows() : 0; }
 
 int vb_check_device(void) {
-    return guard([&] {
-        if (vb::tc::take_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the tensor-core GEMM");
-        if (vb::k::take_attention_error()) vb::fail(vb::kTimeout, "a device-side wait timed out in the attention");
-    });
+    return guard([&] { device_errors(); });
 }
 
 int64_t vb_shard_plan(const char* path, int world, int rank, char* buf, size_t len) {
