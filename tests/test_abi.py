@@ -126,3 +126,16 @@ def test_build_csr_bit_exact_threaded():
     packed = vb.pack_edges(src, attr, round_fp16=True)
     assert np.array_equal(packed[:, :3], attr.astype(np.float16).astype(np.float32))
     assert np.array_equal(packed[:, 3].view(np.int32), src)
+
+
+def test_output_arrays_are_checked_before_the_library_writes_them():
+    """Arrays the library writes through a raw pointer (predict_step's y) must be fp32, C-contiguous,
+    writable and of the output's size; anything else is rejected in Python, before the call."""
+    ok = np.zeros((1, 2, 1, 5, 3), np.float32)
+    vb._check_out(ok, 30, "y")
+    bad = [np.zeros(30, np.float64), np.zeros((3, 20), np.float32)[:, :10], np.zeros(29, np.float32), [0.0] * 30]
+    ro = np.zeros(30, np.float32)
+    ro.flags.writeable = False
+    for a in bad + [ro]:
+        with pytest.raises(ValueError, match="y "):
+            vb._check_out(a, 30, "y")

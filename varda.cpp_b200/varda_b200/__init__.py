@@ -108,11 +108,20 @@ def _ptr(a):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
+def _check_out(a, n, what):
+    """An output array the library writes through a raw pointer: fp32, C-contiguous, writable, n elements."""
+    if not isinstance(a, np.ndarray) or a.dtype != np.float32 or not a.flags.c_contiguous or not a.flags.writeable:
+        raise ValueError(f"{what} must be a writable C-contiguous float32 numpy array")
+    if a.size != n:
+        raise ValueError(f"{what} has {a.size} elements, expected {n}")
+
+
 class Model:
     """varda::Model (varda.h:37-76) on the B200 backend."""
 
-    def __init__(self, handle):
+    def __init__(self, handle, path=None):
         self._h = handle
+        self._path = path
         s = (ctypes.c_int64 * 8)()
         check(lib.vb_sizes(self._h, s))
         self.T_in, self.G, self.V_in, self.T_out, self.V_out, self.H, self.C, self.n_proc = list(s)
@@ -128,7 +137,7 @@ class Model:
         o = Options(precision, cuda_device, int(cuda_graph), 0)
         h = ctypes.c_void_p()
         check(lib.vb_load(os.fsencode(path), ctypes.byref(o), ctypes.byref(h)))
-        return Model(h)
+        return Model(h, path)
 
     @staticmethod
     def load_sharded(path, rank, world, nccl_id, precision=FP16, cuda_device=0, cuda_graph=True):
@@ -136,7 +145,7 @@ class Model:
         h = ctypes.c_void_p()
         buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
         check(lib.vb_load_sharded(os.fsencode(path), ctypes.byref(o), rank, world, buf, ctypes.byref(h)))
-        return Model(h)
+        return Model(h, path)
 
     def free(self):
         if self._h:
@@ -164,6 +173,8 @@ class Model:
             raise ValueError(f"x has {x.size} elements, expected {self.input_shape}")
         if y is None:
             y = np.empty(self.output_shape, np.float32)
+        else:
+            _check_out(y, int(np.prod(self.output_shape)), "y")
         cb = None
         if hook is not None:
             def _cb(key, data, shape, ndim, user):
@@ -185,6 +196,9 @@ class Model:
             raise ValueError(f"x0 has {x0.size} elements, expected {self.input_shape}")
         f = None if forcings is None else np.ascontiguousarray(forcings, dtype=np.float32)
         G, Vo = self.G, self.V_out
+        F = self.n_dynamic_forcings
+        if n_steps > 1 and F and f is not None and f.size != (n_steps - 1) * G * F:
+            raise ValueError(f"forcings must be ({n_steps - 1}, {G}, {F}) for {n_steps} steps, got {f.shape}")
         y = np.zeros((n_steps, G, Vo), np.float32) if keep else None
         ms = np.zeros(n_steps, np.float32)
         cb = None
@@ -194,6 +208,17 @@ class Model:
             cb = STEP(_cb)
         check(lib.vb_rollout(self._h, _ptr(x0), n_steps, _ptr(f), _ptr(y), int(constants_oldest), cb, None, _ptr(ms)))
         return y, ms
+
+    @property
+    def n_dynamic_forcings(self):
+        """F, the number of dynamic forcings a rollout replays (the config's `forcings.dynamic`; 0
+        without a forcings section, or when the model's file is not known)."""
+        if self._path is None:
+            return 0
+        import json
+        from . import safetensors as st
+        cfg = json.loads(st.read(self._path)[1].get("config", "{}"))
+        return len(cfg.get("forcings", {}).get("dynamic_input_index", []))
 
     # CudaBackend device entry points (cuda_backend.h:38-74); pointers are ints / torch tensors
     def normalise(self, x, xn, stream=None):
