@@ -7,8 +7,9 @@ Prints one JSON line (rank 0). `value` is the device-resident time of one predic
 own input/output buffers, CUDA-graph replay, CUDA events on the model's stream, max over ranks);
 `e2e` is the same through the public host API vb_predict_step with pinned host buffers (H2D of x and
 D2H of y inside the timed region; the library overlaps them with the compute in row chunks). `roofline` describes the dominant kernel class and
-`edge_attention` the processor-block attention, both from one eager pass with a CUDA event pair
-around every launch (vb_profile_forward). `cpu_baseline` is the reference's own CPU fp32 backend
+`edge_attention` the processor-block attention (compulsory bytes; on one GPU also the K|V bytes its
+edges gather, mostly L2 hits), both from one eager pass with a CUDA event pair around every launch
+(vb_profile_forward). `cpu_baseline` is the reference's own CPU fp32 backend
 (oracle/_ref/ref_dump, built from the reference's sources) timed on this host on a bounded sample.
 
 --workload c4 is the 24-step autoregressive rollout of C1: K rollout steps through
@@ -289,6 +290,14 @@ def run_rollout(args, rank, world, local_rank):
 TRAFFIC = os.path.join(HERE, "profiles", "c1_traffic.json")
 
 
+def proc_gathered_bytes(workload, C):
+    """K|V bytes the processor attention gathers per launch, one 2C-wide fp16 row per edge (E * 2C * 2):
+    the L2-reuse figure reported beside the compulsory bytes."""
+    from varda_b200 import safetensors as st
+    mp, _ = model_paths("c1" if workload == "c4" else workload)
+    return int(st.read(mp)[0]["graph.proc.edge_index"].shape[1]) * 2 * int(C) * 2
+
+
 def traffic_for(kind):
     """DRAM bytes (read + write) per launch of a kernel class of the C1 step, from the committed ncu
     launch-list capture summarised in profiles/c1_traffic.json (None when absent)."""
@@ -398,6 +407,13 @@ def main():
     else:
         r = run_ours(args, rank, world, local_rank)
     roof, edge, shares, prof_total = summarise(r["prof"], pk, src)
+    if edge is not None and world == 1:
+        try:  # secondary figure: never in the way of the bench line
+            gb = proc_gathered_bytes(args.workload, r["m"].C)
+            edge["gathered_bytes_per_launch"] = gb
+            edge["gathered_gbs"] = round(gb / (edge["ms_per_launch"] * 1e-3) / 1e9, 1)
+        except Exception as e:
+            log(f"bench: gathered bytes unavailable ({e})")
     if args.profile_out and rank == 0:
         with open(args.profile_out, "w") as fh:
             json.dump(r["prof"], fh, indent=0)
