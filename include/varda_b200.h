@@ -132,10 +132,11 @@ int64_t vb_launch_count(void);
 int64_t vb_profile_forward(vb_model* m, char* buf, size_t len);
 
 /* The destination partition vb_load_sharded uses for `rank` of `world` on this model file, computed
- * on the host only (no GPU): JSON with the hidden/data ranges of every rank, this rank's halos (global
- * ids), its send lists per peer, and its local CSR graphs (sources in local ids). Same length
- * convention as vb_profile_forward; a negative return is minus the error class. No reference
- * counterpart (the reference runs on one GPU). */
+ * on the host only (no GPU): JSON with the hidden/data ranges of every rank (and the encoder's hidden
+ * ranges with the row moves after the encoder; they equal the hidden ranges unless VB_SHARD_ENC=1),
+ * this rank's halos (global ids), its send lists per peer, and its local CSR graphs (sources in local
+ * ids). Same length convention as vb_profile_forward; a negative return is minus the error class. No
+ * reference counterpart (the reference runs on one GPU). */
 int64_t vb_shard_plan(const char* path, int world, int rank, char* buf, size_t len);
 
 /* ---------------------------------------------------------------- kernel-level entry points
