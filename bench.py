@@ -39,7 +39,7 @@ sys.path.insert(0, os.path.join(HERE, "varda.cpp_b200"))
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 CACHE = os.environ.get("VB_BENCH_CACHE", os.path.join(tempfile.gettempdir(), "varda_b200_bench"))
 REF_DUMP = os.path.join(HERE, "oracle", "_ref", "ref_dump")
-SAMPLE_FACTOR = 64  # the CPU baseline runs the C1 architecture on 1/64 of its nodes
+SAMPLE_FACTOR = 64  # the CPU baseline runs the C1 architecture on 1/64 of its nodes (synth "c1s")
 
 
 def peaks():
@@ -68,36 +68,14 @@ def model_paths(workload):
 
 
 def sample_model():
-    """C1's architecture (C=1024, 16 heads, mlp 4096, 16 blocks, T=2, V_in=90, V_out=80) on 1/64 of
-    its nodes with the same per-node edge counts (encoder kNN-4, processor kNN-14, decoder kNN-3)."""
+    """c1s: C1's architecture on 1/SAMPLE_FACTOR of its nodes with the same per-node edge counts
+    (varda_b200.synth.config_c1_sample)."""
     from varda_b200 import synth
     os.makedirs(CACHE, exist_ok=True)
     mp = os.path.join(CACHE, "c1s.model.safetensors")
     xp = os.path.join(CACHE, "c1s.input.safetensors")
-    if os.path.exists(mp) and os.path.exists(xp):
-        return mp, xp
-    G, H = 1_688_650 // SAMPLE_FACTOR, 189_809 // SAMPLE_FACTOR
-
-    def fib(n):
-        i = np.arange(n) + 0.5
-        z = 1 - 2 * i / n
-        phi = i * np.pi * (3 - 5 ** 0.5)
-        r = np.sqrt(1 - z * z)
-        return np.stack([r * np.cos(phi), r * np.sin(phi), z], 1)
-
-    data, hidden = fib(G), fib(H)
-    enc = np.stack([np.repeat(np.arange(G), 4), synth.knn(hidden, data, 4).ravel()], 1)
-    nb = synth.knn(hidden, hidden, 15)[:, 1:]
-    proc = np.stack([nb.ravel(), np.repeat(np.arange(H), 14)], 1)
-    dec = np.stack([synth.knn(hidden, data, 3).ravel(), np.repeat(np.arange(G), 3)], 1)
-    data, hidden, enc, proc, dec = synth._sort_nodes(data, hidden, enc, proc, dec)
-    names, forc = synth._c1_forcings()
-    v = synth._vars(90, 90, 80, 80)
-    cfg, t, x = synth.make_model(seed=1, C=1024, heads=16, mlp=4096, n_proc=16, T=2, data_pos=data,
-                                 hidden_pos=hidden, enc=enc, proc=proc, dec=dec, A=4, Ae=3, var_names=names,
-                                 forcings=forc, uuid="b200-c1-sample", **v)
-    synth.write_model(mp, cfg, t)
-    synth.write_input(xp, x)
+    if not (os.path.exists(mp) and os.path.exists(xp)):
+        synth.generate("c1s", CACHE)
     return mp, xp
 
 

@@ -3,14 +3,15 @@
 // oracle/_ref/ and is never part of the product.
 //
 //   ref_dump --model M.safetensors --input X.safetensors [--key in.x] [--threads N]
-//            [--steps N] [--dump OUT.safetensors]
+//            [--steps N] [--dump OUT.safetensors] [--y-out Y.safetensors]
 //
 // Loads the model through the reference's public API (varda::Model::load, varda.h:37-50), runs
 // predict_step (model.cpp:431) `--steps` times without a hook and prints one JSON line with the
 // load time and the per-step wall times. With --dump it first runs one hooked predict_step and
 // writes every contract activation (docs/format.md section 2 of the reference) as F32 into
 // OUT.safetensors with varda::write_safetensors (format.h:82), so tests can compare against the
-// reference's own numbers.
+// reference's own numbers. With --y-out it writes the last step's output y (F32, the predict_step
+// output shape) alone, which is all a full-size model needs kept (its activations run to many GB).
 #include <omp.h>
 
 #include <chrono>
@@ -34,14 +35,15 @@ double now_s() {
 
 [[noreturn]] void usage() {
     std::fprintf(stderr,
-                 "usage: ref_dump --model M --input X [--key in.x] [--threads N] [--steps N] [--dump OUT]\n");
+                 "usage: ref_dump --model M --input X [--key in.x] [--threads N] [--steps N] [--dump OUT] "
+                 "[--y-out Y]\n");
     std::exit(2);
 }
 
 }  // namespace
 
 int main(int argc, char** argv) {
-    std::string model_path, input_path, key = "in.x", dump_path;
+    std::string model_path, input_path, key = "in.x", dump_path, y_path;
     int steps = 1;
     varda::Options opts;
     opts.device = varda::Device::CPU;
@@ -57,6 +59,7 @@ int main(int argc, char** argv) {
         else if (a == "--threads") opts.num_threads = std::atoi(next().c_str());
         else if (a == "--steps") steps = std::atoi(next().c_str());
         else if (a == "--dump") dump_path = next();
+        else if (a == "--y-out") y_path = next();
         else usage();
     }
     if (model_path.empty() || input_path.empty()) usage();
@@ -94,6 +97,11 @@ int main(int argc, char** argv) {
             model->predict_step(x.as<float>(), y.data(), nullptr);
             times.push_back(now_s() - t1);
         }
+        if (!y_path.empty())
+            varda::write_safetensors(y_path,
+                                     {{"y", varda::DType::F32,
+                                       {1, c.n_output_steps, 1, c.n_data_nodes, c.n_output_vars}, y.data()}},
+                                     {{"producer", "reference cpu fp32 (oracle/_ref/ref_dump)"}});
         double sum = 0;
         for (float v : y) sum += v;
         std::printf("{\"load_s\": %.4f, \"threads\": %d, \"steps_s\": [", t_load,

@@ -8,7 +8,9 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, os.path.join(REPO, "varda.cpp_b200"))
 sys.path.insert(0, os.path.join(REPO, "oracle"))
 GOLDEN = os.path.join(REPO, "tests", "golden")
-REFERENCE = "/root/reference"
+# The reference checkout (sources of varda.cpp) when this container has one: $VARDA_REFERENCE, else a
+# `reference` directory beside the repository. Tests that need it skip when it is absent (the GPU box).
+REFERENCE = os.environ.get("VARDA_REFERENCE") or os.path.join(os.path.dirname(REPO), "reference")
 
 
 def pytest_configure(config):
@@ -40,7 +42,7 @@ def seeded_model(model_dir):
     def get(name):
         if name not in _MODELS:
             mp, xp = synth.generate(name, model_dir)
-            for kind in ("golden", "rollout"):
+            for kind in ("golden", "rollout", "sampled"):
                 g = os.path.join(GOLDEN, f"{name}.{kind}.npz")
                 if os.path.exists(g):
                     z = np.load(g)

@@ -11,8 +11,17 @@ sources and oracle/_ref built; the fixtures then travel, the reference does not)
 3. <name>.rollout.npz for the rollout variants of the parity models (t*r: a `forcings` section):
    ROLLOUT_STEPS steps of the reference's host rollout (varda::Rollout::run on the CPU backend,
    oracle/_ref/ref_rollout) with replayed synthetic forcings, both constant sources.
+4. <name>.sampled.npz for the benchmark-width models whose activations are too large to keep whole
+   (c1s: C1's architecture, 16 blocks of C = 1024, on 1/64 of its nodes): every contract key of the
+   reference's hooked predict_step, viewed as rows of its last axis, at SAMPLE_ROWS seeded rows and
+   SAMPLE_COLS seeded columns (indices stored beside the values as <key>.rows and <key>.cols).
+5. c1.y_sample.npz: the reference's out.y on the full C1 model (one predict_step of its CPU backend,
+   `ref_dump --y-out`, about 26 GB of host memory and minutes), at C1_Y_ROWS seeded data nodes, with
+   the wall time of that step. Only with --c1-y Y MODEL INPUT: the file such a run wrote, and the
+   model and input it ran (synth "c1"; their sha256 are kept to detect drift).
 
     python tests/golden/make_golden.py [--reference REFERENCE_TREE] [--only NAME ...]
+                                       [--c1-y Y MODEL INPUT --c1-step-s S --c1-threads N --c1-rss-gb GB]
 """
 from __future__ import annotations
 
@@ -40,6 +49,53 @@ KEEP_ALWAYS = ["dec.out", "out.pre_bound", "out.norm", "out.y"]
 KEEP_SMALL = ["enc.out", "latent"]
 ROLLOUT_MODELS = ["t256r", "t128r"]
 ROLLOUT_STEPS = 4
+SAMPLED_MODELS = ["c1s"]
+SAMPLE_ROWS = 128
+SAMPLE_COLS = 128
+C1_Y_ROWS = 8192
+
+
+def sample_rows(n_rows, k, seed):
+    """k distinct row indices of n_rows (all of them when n_rows <= k), ascending; always includes the
+    first and the last row."""
+    if n_rows <= k:
+        return np.arange(n_rows, dtype=np.int64)
+    r = np.random.default_rng(seed).choice(n_rows, size=k - 2, replace=False)
+    return np.unique(np.concatenate([r, [0, n_rows - 1]])).astype(np.int64)
+
+
+def sampled_golden(name, work, ref_dump):
+    mp, xp = synth.generate(name, work)
+    dump = os.path.join(work, f"{name}.dump.safetensors")
+    r = subprocess.run([ref_dump, "--model", mp, "--input", xp, "--dump", dump, "--threads", "8"],
+                       capture_output=True, text=True, check=True)
+    acts, _ = st.read(dump)
+    keep = {}
+    for i, (k, a) in enumerate(sorted(acts.items())):
+        a2 = np.asarray(a, np.float32).reshape(-1, a.shape[-1])
+        rows = sample_rows(a2.shape[0], SAMPLE_ROWS, seed=1000 + i)
+        cols = sample_rows(a2.shape[1], SAMPLE_COLS, seed=2000 + i)
+        keep[k] = a2[rows][:, cols]
+        keep[k + ".rows"] = rows
+        keep[k + ".cols"] = cols
+        keep[k + ".shape"] = np.array(a.shape, np.int64)
+    keep["__model_sha256__"] = np.frombuffer(synth.sha256_file(mp).encode(), np.uint8)
+    keep["__input_sha256__"] = np.frombuffer(synth.sha256_file(xp).encode(), np.uint8)
+    np.savez_compressed(os.path.join(HERE, f"{name}.sampled.npz"), **keep)
+    print(f"{name}: reference ref_dump {r.stdout.strip()}; {len(acts)} keys sampled")
+    return {}
+
+
+def c1_y_sample(y_path, model_path, input_path, seconds, threads, peak_rss_gb):
+    y = np.asarray(st.read(y_path)[0]["y"], np.float32)  # (1, T_out, 1, G, V_out)
+    G = y.shape[3]
+    rows = sample_rows(G, C1_Y_ROWS, seed=2024)
+    np.savez_compressed(os.path.join(HERE, "c1.y_sample.npz"), rows=rows, y=y[0, :, 0][:, rows],
+                        shape=np.array(y.shape, np.int64), step_s=np.float64(seconds),
+                        threads=np.int64(threads), peak_rss_gb=np.float64(peak_rss_gb),
+                        __model_sha256__=np.frombuffer(synth.sha256_file(model_path).encode(), np.uint8),
+                        __input_sha256__=np.frombuffer(synth.sha256_file(input_path).encode(), np.uint8))
+    print(f"c1: {len(rows)} of {G} rows of out.y kept")
 
 
 def pin_synthetic(ref_root, work):
@@ -112,10 +168,21 @@ def rollout_golden(name, work, ref_rollout):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("VARDA_REFERENCE")
+                    or os.path.join(os.path.dirname(REPO), "reference"),
+                    help="the reference checkout ($VARDA_REFERENCE, else `reference` beside the repository)")
     ap.add_argument("--only", nargs="*")
     ap.add_argument("--skip-synthetic", action="store_true")
+    ap.add_argument("--c1-y", nargs=3, metavar=("Y", "MODEL", "INPUT"),
+                    help="out.y of a full-C1 ref_dump run (--y-out) and the model and input it ran; "
+                         "writes c1.y_sample.npz")
+    ap.add_argument("--c1-step-s", type=float, default=0.0, help="that run's step wall time (s)")
+    ap.add_argument("--c1-threads", type=int, default=0, help="that run's thread count")
+    ap.add_argument("--c1-rss-gb", type=float, default=0.0, help="that run's peak resident memory (GB)")
     a = ap.parse_args()
+    if a.c1_y:
+        c1_y_sample(*a.c1_y, a.c1_step_s, a.c1_threads, a.c1_rss_gb)
+        return
     ref_dump = os.path.join(REPO, "oracle", "_ref", "ref_dump")
     if not os.path.exists(ref_dump):
         subprocess.run(["make", "-C", os.path.join(REPO, "oracle"), f"REF={a.reference}"], check=True)
@@ -126,7 +193,10 @@ def main():
             pin = pin_synthetic(a.reference, work)
             with open(os.path.join(HERE, "synthetic_pin.json"), "w") as f:
                 json.dump(pin, f, indent=1, sort_keys=True)
-        for name in a.only or MODELS + ROLLOUT_MODELS:
+        for name in a.only or MODELS + ROLLOUT_MODELS + SAMPLED_MODELS:
+            if name in SAMPLED_MODELS:
+                sampled_golden(name, work, ref_dump)
+                continue
             if name in ROLLOUT_MODELS:
                 summary[name] = rollout_golden(name, work, os.path.join(REPO, "oracle", "_ref", "ref_rollout"))
             else:

@@ -3,7 +3,9 @@
 Mirrors the reference's public C++ API (varda.cpp src/varda/varda.h:21-76): Options, Model.load,
 Model.predict_step(x, y, hook), plus the CudaBackend device entry points and the kernel-level entry
 points used by the tests. The shared library must exist (built by `make -C varda.cpp_b200`); there is
-no fallback: every call goes to the CUDA library, and a missing library raises ImportError.
+no fallback: every call goes to the CUDA library, and a missing library raises ImportError. The library
+is loaded on the first call that needs it, so the pure-Python modules of the package (`synth`,
+`safetensors`) import without it.
 """
 from __future__ import annotations
 
@@ -73,13 +75,32 @@ def _load_lib():
         f = getattr(L, name)
         f.argtypes = args
         f.restype = res
+    _bind_tiles(L)
     return L
 
 
-lib = _load_lib()
+class _LazyLib:
+    """The ctypes handle of libvarda_b200, opened (and its signatures bound) on first attribute access."""
 
-# exported symbols, for the ABI check in the tests
-SYMBOLS = [n for n in dir(lib) if n.startswith("vb_")]
+    _handle = None
+
+    def get(self):
+        if _LazyLib._handle is None:
+            _LazyLib._handle = _load_lib()
+        return _LazyLib._handle
+
+    def __getattr__(self, name):
+        return getattr(self.get(), name)
+
+
+lib = _LazyLib()
+
+
+def __getattr__(name):
+    # exported symbols, for the ABI check in the tests (opens the library)
+    if name == "SYMBOLS":
+        return [n for n in dir(lib.get()) if n.startswith("vb_")]
+    raise AttributeError(name)
 
 
 def check(rc):
@@ -401,18 +422,15 @@ def tile_plan(row_ptr, src, attr_csr, n_src, kind=0):
     return {"tiles": tiles, "srcs": srcs, "heavy": heavy, "edges": edges}
 
 
-def _bind_tiles():
+def _bind_tiles(L):
     P, I, I64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
-    lib.vb_tiles_create.argtypes = [P, P, P, I, I64, I64, I, P]
-    lib.vb_tiles_create.restype = I
-    lib.vb_tiles_create_kind.argtypes = [P, P, P, I, I64, I64, I, I, P]
-    lib.vb_tile_plan.argtypes = [P, P, P, I, I64, I64, I, P, P, P, P, P]
-    lib.vb_tile_plan.restype = I
-    lib.vb_tiles_create_kind.restype = I
-    lib.vb_attention_tiled.argtypes = [P, I64, I64, P, I64, P, P, I64, P, I64, P, I64, P, I, I, I, P]
-    lib.vb_attention_tiled.restype = I
-    lib.vb_tiles_free.argtypes = [P]
-    lib.vb_tiles_free.restype = None
-
-
-_bind_tiles()
+    L.vb_tiles_create.argtypes = [P, P, P, I, I64, I64, I, P]
+    L.vb_tiles_create.restype = I
+    L.vb_tiles_create_kind.argtypes = [P, P, P, I, I64, I64, I, I, P]
+    L.vb_tile_plan.argtypes = [P, P, P, I, I64, I64, I, P, P, P, P, P]
+    L.vb_tile_plan.restype = I
+    L.vb_tiles_create_kind.restype = I
+    L.vb_attention_tiled.argtypes = [P, I64, I64, P, I64, P, P, I64, P, I64, P, I64, P, I, I, I, P]
+    L.vb_attention_tiled.restype = I
+    L.vb_tiles_free.argtypes = [P]
+    L.vb_tiles_free.restype = None

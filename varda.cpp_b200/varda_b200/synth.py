@@ -18,6 +18,10 @@ Configurations (the benchmark's C0-C4):
        Encoder kNN-4 data->hidden, decoder kNN-3 hidden->data, multi-scale processor edges.
        C=1024, 16 heads, mlp 4096, 16 blocks, T=2, V_in=90, V_out=80, fp32 weights.
   c3   c1 as a temporal downscaler (interpolator kind, T_out=6).
+  c1s  c1's architecture (C=1024, 16 heads, mlp 4096, 16 blocks, T=2, V_in=90, V_out=80) on 1/64 of
+       its nodes (G=26,385, H=2,965 on Fibonacci lattices) with c1's per-node edge counts: encoder
+       kNN-4, processor kNN-14, decoder kNN-3. The reference CPU backend runs it in seconds, so it is
+       the parity model at the benchmark's widths and depth and the CPU baseline's sample.
   Small random-graph models (`test_*`) cover every degree class, absent biases, the three
        boundings, tanh/erf GELU, latent skip on/off and T_out>1 for the parity tests.
 
@@ -223,17 +227,40 @@ def stretched_hidden(H, center=(46.5, 8.5), global_level=7, fine_levels=2, refin
     return v[keep], und
 
 
+def _processor_edges(hidden, und, knn_extra):
+    """The multi-scale edges `und` (undirected pairs) plus each node's knn_extra nearest hidden nodes,
+    deduplicated, in both directions: (source, destination) rows."""
+    H = len(hidden)
+    nb = knn(hidden, hidden, knn_extra + 1)[:, 1:]
+    kn = np.stack([nb.ravel(), np.repeat(np.arange(H), knn_extra)], 1)
+    kn = np.stack([np.minimum(kn[:, 0], kn[:, 1]), np.maximum(kn[:, 0], kn[:, 1])], 1)
+    und = np.unique(np.concatenate([und, kn]), axis=0)
+    return np.concatenate([und, und[:, ::-1]])
+
+
+def graph_c2(H=189_809, knn_extra=11, seed=2):
+    """C2, the isolated processor block: c1's hidden nodes and processor graph alone (same node numbering
+    as c1's hidden nodes, edges sorted by destination then source), with edge attributes uniform on
+    [0, 1) from `seed` as the benchmark's config states. Returns (positions [H, 3], edges [E, 2] as
+    (source, destination), attributes [E, 3] float32)."""
+    hidden, und = stretched_hidden(H)
+    proc = _processor_edges(hidden, und, knn_extra)
+    ph = morton_order(hidden)
+    inv_h = np.empty_like(ph)
+    inv_h[ph] = np.arange(len(ph))
+    proc = np.stack([inv_h[proc[:, 0]], inv_h[proc[:, 1]]], 1)
+    proc = proc[np.lexsort((proc[:, 0], proc[:, 1]))]
+    attr = np.random.default_rng(seed).uniform(0.0, 1.0, size=(len(proc), 3)).astype(np.float32)
+    return hidden[ph], proc, attr
+
+
 def graph_c1(G=1_688_650, H=189_809, knn_extra=11):
     """C1 graph (see module docstring). Processor edges: the multi-scale icosphere edges (one hop at
     every refinement level a node belongs to) plus each node's `knn_extra` nearest hidden nodes,
     deduplicated, in both directions."""
     data = stretched_data_nodes(G)
     hidden, und = stretched_hidden(H)
-    nb = knn(hidden, hidden, knn_extra + 1)[:, 1:]
-    kn = np.stack([nb.ravel(), np.repeat(np.arange(H), knn_extra)], 1)
-    kn = np.stack([np.minimum(kn[:, 0], kn[:, 1]), np.maximum(kn[:, 0], kn[:, 1])], 1)
-    und = np.unique(np.concatenate([und, kn]), axis=0)
-    proc = np.concatenate([und, und[:, ::-1]])
+    proc = _processor_edges(hidden, und, knn_extra)
     enc_dst = knn(hidden, data, 4)                                         # data g -> its 4 nearest hidden
     enc = np.stack([np.repeat(np.arange(G), 4), enc_dst.ravel()], 1)
     dec_src = knn(hidden, data, 3)                                         # data g <- its 3 nearest hidden
@@ -505,6 +532,33 @@ def sha256_file(path, chunk=1 << 24):
     return h.hexdigest()
 
 
+C1_SAMPLE_FACTOR = 64
+
+
+def config_c1_sample(factor=C1_SAMPLE_FACTOR):
+    """c1s: C1's architecture on 1/factor of its nodes, with the same per-node edge counts."""
+    G, H = 1_688_650 // factor, 189_809 // factor
+
+    def fib(n):
+        i = np.arange(n) + 0.5
+        z = 1 - 2 * i / n
+        phi = i * np.pi * (3 - 5 ** 0.5)
+        r = np.sqrt(1 - z * z)
+        return np.stack([r * np.cos(phi), r * np.sin(phi), z], 1)
+
+    data, hidden = fib(G), fib(H)
+    enc = np.stack([np.repeat(np.arange(G), 4), knn(hidden, data, 4).ravel()], 1)
+    nb = knn(hidden, hidden, 15)[:, 1:]
+    proc = np.stack([nb.ravel(), np.repeat(np.arange(H), 14)], 1)
+    dec = np.stack([knn(hidden, data, 3).ravel(), np.repeat(np.arange(G), 3)], 1)
+    data, hidden, enc, proc, dec = _sort_nodes(data, hidden, enc, proc, dec)
+    names, forc = _c1_forcings()
+    v = _vars(90, 90, 80, 80)
+    return make_model(seed=1, C=1024, heads=16, mlp=4096, n_proc=16, T=2, data_pos=data, hidden_pos=hidden,
+                      enc=enc, proc=proc, dec=dec, A=4, Ae=3, var_names=names, forcings=forc,
+                      uuid="b200-c1-sample", **v)
+
+
 def generate(name, out_dir, **kw):
     """Writes <out_dir>/<name>.model.safetensors and <name>.input.safetensors; returns the paths."""
     os.makedirs(out_dir, exist_ok=True)
@@ -516,6 +570,8 @@ def generate(name, out_dir, **kw):
         cfg, t, x = config_c1(**kw)
     elif name == "c3":
         cfg, t, x = config_c1(T_out=6, **kw)
+    elif name == "c1s":
+        cfg, t, x = config_c1_sample(**kw)
     else:
         cfg, t, x = config_test(name)
     write_model(mp, cfg, t)
