@@ -120,8 +120,8 @@ def test_c2_attention_parity(c2_graph):
     vf = np.ascontiguousarray(qkvs[:, 2 * C:3 * C].astype(np.float32))
     xf = qkvs[:, 3 * C:].astype(np.float32)
     for s0 in starts:
-        ref = oracle.graph_attention((rp, src, None, at), int(s0), 256, qf[s0:s0 + 256], kf, vf, we, be, heads,
-                                     hd) + xf[s0:s0 + 256]
+        ref = oracle.graph_attention((rp, src, None, at), int(s0), 256, qf[s0:s0 + 256], kf, vf,
+                                     np.ascontiguousarray(we.T), be, heads, hd) + xf[s0:s0 + 256]
         for path, o in outs.items():
             got = o[s0:s0 + 256].float().cpu().numpy()
             e = oracle.rel_absmax(got, ref)
