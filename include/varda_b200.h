@@ -190,25 +190,30 @@ int vb_attention_split_noalloc(int dtype, const int32_t* row_ptr, const void* ed
                                int64_t ldxr, void* out, int64_t ldo, const float* w_e, int C, int heads, int head_dim,
                                int splits, void* stream);
 
-/* The shared-memory-staged attention the engine runs in fp16 (no reference counterpart: the
- * reference has only the gather kernel): vb_tiles_create builds the destination tiles of a CSR graph
- * (host arrays from vb_build_csr) and uploads them to the current device; vb_attention_tiled runs
- * rows [dst_lo, dst_lo + n_rows) of it (tiles, then the rows too wide for a tile on the gather kernel;
- * dst_lo must start a tile, e.g. 0); same arguments and contract as vb_attention, fp16 only. */
+/* The tiled fp16 attention kernels the engine runs (no reference counterpart: the reference has only
+ * the gather kernel, attention_kernel in src/varda/cuda/kernels.cu:290-419): vb_tiles_create builds the
+ * destination tiles of a CSR graph (host arrays from vb_build_csr) and uploads them to the current
+ * device; vb_attention_tiled runs rows [dst_lo, dst_lo + n_rows) of it (the tiles, then the rows no
+ * tile covers on the gather kernel; dst_lo must start a tile, e.g. 0); same arguments and contract as
+ * vb_attention, fp16 only. */
 typedef struct vb_tiles vb_tiles;
 int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* attr_csr, int A, int64_t n_src,
                     int64_t n_dst, int head_dim, vb_tiles** out);
-/* The same with the tile kind: VB_TILES_SMEM (the shared-memory-staged CUDA-core kernel, as
- * vb_tiles_create) or VB_TILES_MMA (the tensor-core kernel the engine runs on the processor graph:
- * tiles of up to 128 rows and 192 distinct sources, q.k and the value sums as tcgen05 MMAs; head_dim
- * 64 only). vb_attention_tiled runs whichever kind the tiles were built for. */
-enum { VB_TILES_SMEM = 0, VB_TILES_MMA = 1 };
+/* The same with the tile kind: VB_TILES_SMEM (the shared-memory-staged CUDA-core kernel the engine runs
+ * on the decoder graph, as vb_tiles_create) or VB_TILES_TC (the tile-sparse tensor-core kernel the
+ * engine runs on the processor graph: tiles of up to 64 consecutive rows reaching at most 128 distinct
+ * sources, restarting every 256 rows; per 16-row block and head q.k and the value sums as tensor-core
+ * products over the 8-column blocks that hold edges; head_dim 64 and at most 32 heads; rows with a
+ * repeated source or more than 128 sources run on the gather kernel). vb_attention_tiled runs whichever
+ * kind the tiles were built for. */
+enum { VB_TILES_SMEM = 0, VB_TILES_TC = 1 };
 /* The tile plan of a kind on the host (no device needed), for inspection and tests: counts[0] tiles,
- * counts[1] distinct-source entries, counts[2] heavy rows (left to the gather kernel); then, where the
- * arrays are non-null and sized by a first call: tiles4 [tiles][4] = {row0, nrows, src0, nsrc}, srcs (each
- * tile's distinct sources in increasing order, a tile's slot s being srcs[src0 + s]), heavy (rows),
- * edges [E][4] (the CSR-order records {a0, a1, a2, slot or source (int bits)}, attributes rounded to
- * fp16; for VB_TILES_MMA each tiled row's records sorted by slot). */
+ * counts[1] source entries, counts[2] heavy rows (left to the gather kernel); then, where the arrays
+ * are non-null and sized by a first call: tiles4 [tiles][4] = {row0, nrows, src0, nsrc}, srcs (a tile's
+ * slot s being srcs[src0 + s]: for VB_TILES_SMEM each tile's distinct sources in increasing order, for
+ * VB_TILES_TC in order of first appearance along the tile's edges, padded with the last one to a
+ * multiple of 4), heavy (rows), edges [E][4] (the CSR-order records {a0, a1, a2, slot or, for heavy
+ * rows, source (int bits)}, attributes rounded to fp16). */
 int vb_tile_plan(const int32_t* row_ptr, const int32_t* src, const float* attr_csr, int A, int64_t n_src,
                  int64_t n_dst, int kind, int64_t counts[3], int32_t* tiles4, int32_t* srcs, int32_t* heavy,
                  float* edges);

@@ -258,28 +258,34 @@ def test_attention_tiled(C, heads, A):
     assert np.array_equal(got[zero], xr[zero, :C]), "zero in-degree must give x_r exactly"
 
 
-def local_graph(rng, n, A, window=40):
-    """Destinations drawing their sources (with repeats) from a window around their own index, so runs
-    of consecutive rows share sources: multi-row tiles with up to the tensor-core kernel's 192 slots."""
+def local_graph(rng, n, A, window=40, unique=False):
+    """Destinations drawing their sources from a window around their own index, so runs of
+    consecutive rows share sources (multi-row tiles); with unique=False sources may repeat within a
+    row, with unique=True they do not (rows the tensor-core kernel tiles)."""
     s, d = [], []
     for i in range(n):
         deg = DEGREES[i % len(DEGREES)] if i < 3 * len(DEGREES) else int(rng.integers(0, 30))
-        s += list(np.clip(i + rng.integers(-window, window + 1, deg), 0, n - 1))
-        d += [i] * deg
+        if unique:
+            off = rng.choice(np.arange(-window, window + 1), min(deg, 2 * window + 1), replace=False)
+            s += list(np.unique(np.clip(i + off, 0, n - 1)))
+        else:
+            s += list(np.clip(i + rng.integers(-window, window + 1, deg), 0, n - 1))
+        d += [i] * (len(s) - len(d))
     perm = rng.permutation(len(s))
     ei = np.stack([np.array(s, np.int64)[perm], np.array(d, np.int64)[perm]])
     return ei, rng.normal(size=(ei.shape[1], A)).astype(np.float32)
 
 
-@pytest.mark.parametrize("graph", ["random", "local"])
-@pytest.mark.parametrize("C,heads,A", [(1024, 16, 3), (768, 12, 3), (384, 6, 3), (256, 4, 2), (128, 2, 1)])
-def test_attention_mma(C, heads, A, graph):
-    """The tensor-core attention (vb_tiles_create_kind VB_TILES_MMA: S = Q K^T and O = P V as tcgen05
-    MMAs per tile of up to 128 rows and 192 sources, P in fp16; rows with more distinct sources go to
-    the gather kernel): the float64 reference within the fp16 bar, zero in-degree rows give x_r
-    exactly, and the gather kernel's output within the same bar. Graphs: every degree class in shuffled
-    order with repeated sources plus a row of 300 edges over ~210 distinct sources (heavy), and a
-    local graph whose tiles fill 128 rows and up to 192 slots."""
+@pytest.mark.parametrize("graph", ["random", "local", "unique"])
+@pytest.mark.parametrize("C,heads,A", [(1024, 16, 3), (512, 8, 2), (256, 4, 3), (128, 2, 1), (2048, 32, 3)])
+def test_attention_tc(C, heads, A, graph):
+    """The tile-sparse tensor-core attention (vb_tiles_create_kind VB_TILES_TC: per 16-row block and
+    head, q.k and the value sums as mma.sync products over the column blocks that hold edges; heavy rows
+    on the gather kernel): the float64 reference within the reference unit test's fp16 bar (2e-3), the
+    gather kernel within the same bar, zero in-degree rows give x_r exactly, a row range starting at a
+    tile gives the same bits as the full launch, and a second launch gives the same bits. Graphs: every
+    degree class with repeated sources (mostly heavy rows) plus a row of 300 edges, a local graph with
+    repeats, and a local graph of distinct sources whose tiles fill 64 rows."""
     rng = np.random.default_rng(C * 13 + heads + A + len(graph))
     hd = C // heads
     if graph == "random":
@@ -290,7 +296,7 @@ def test_attention_mma(C, heads, A, graph):
         ea = np.concatenate([ea, rng.normal(size=(300, A)).astype(np.float32)])
     else:
         n_src = n_dst = 1500
-        ei, ea = local_graph(rng, n_dst, A)
+        ei, ea = local_graph(rng, n_dst, A, unique=graph == "unique")
     ld = C + 8
     rp, src, _, attr = vb.build_csr(ei, ea, n_src, n_dst)
     attr = rounded(attr, vb.FP16)
@@ -300,11 +306,16 @@ def test_attention_mma(C, heads, A, graph):
     w4 = np.zeros((4, C), np.float32)
     w4[:A] = we.T
     w4[3] = be
-    tiles = vb.Tiles(rp, src, attr, n_src, hd, kind=vb.Tiles.MMA)
+    tiles = vb.Tiles(rp, src, attr, n_src, hd, kind=vb.Tiles.TC)
+    plan = vb.tile_plan(rp, src, attr, n_src, vb.Tiles.TC)
+    if graph == "unique":
+        assert len(plan["heavy"]) == 0 and plan["tiles"][:, 1].mean() > 30
     T = torch.float16
     d_q, d_k, d_v, d_x, d_w = dev(q, T), dev(k, T), dev(v, T), dev(xr, T), dev(w4, torch.float32)
     out = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
     tiles.attention(0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld, out, C, d_w, C, heads, hd)
+    again = torch.full_like(out, float("nan"))
+    tiles.attention(0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld, again, C, d_w, C, heads, hd)
     gat = torch.full((n_dst, C), float("nan"), device="cuda", dtype=T)
     edges = vb.pack_edges(src, attr, round_fp16=True)
     vb.attention(vb.FP16, dev(rp, torch.int32), dev(edges, torch.float32), 0, n_dst, d_q, ld, d_k, d_v, ld, d_x, ld,
@@ -319,8 +330,18 @@ def test_attention_mma(C, heads, A, graph):
     err = oracle.rel_absmax(got, ref)
     assert err <= 2e-3, f"rel_absmax {err:.3e}"
     assert oracle.rel_absmax(got, g) <= 2e-3
+    assert torch.equal(out, again), "a second launch gives the same bits"
     zero = np.where(rp[1:] == rp[:-1])[0]
+    assert len(zero) > 0
     assert np.array_equal(got[zero], xr[zero, :C]), "zero in-degree must give x_r exactly"
+    # rows from the start of a middle tile to the end: the same bits as the full launch
+    t = plan["tiles"]
+    lo = int(t[len(t) // 2, 0]) if len(t) > 1 else 0
+    n = n_dst - lo
+    part = torch.full((n, C), float("nan"), device="cuda", dtype=T)
+    tiles.attention(lo, n, d_q[lo:], ld, d_k, d_v, ld, d_x[lo:], ld, part, C, d_w, C, heads, hd)
+    torch.cuda.synchronize()
+    assert torch.equal(part, out[lo:]), "a row range gives the full launch's bits"
 
 
 @pytest.mark.parametrize("variant", ["1", "2", "3", "4"])

@@ -153,6 +153,7 @@ def test_attention_kernel_choice(name, tiled, chunk, seeded_model, monkeypatch):
     mp, xp = seeded_model(name)
     x = np.array(st.read(xp)[0]["in.x"])
     monkeypatch.setenv("VB_ATT_TILED", tiled)
+    monkeypatch.setenv("VB_ATT_TC", "none")
     if chunk:
         monkeypatch.setenv("VB_DEC_CHUNK_ROWS", chunk)
     y = vb.Model.load(mp, precision=vb.FP16).predict_step(x)
@@ -161,15 +162,16 @@ def test_attention_kernel_choice(name, tiled, chunk, seeded_model, monkeypatch):
     assert oracle.rel_absmax(y, ref) <= TOL[vb.FP16]
 
 
-@pytest.mark.parametrize("mma,chunk", [("all", ""), ("proc", ""), ("dec", "32"), ("none", "")])
+@pytest.mark.parametrize("tc,chunk", [("all", ""), ("proc", ""), ("dec", "256"), ("dec", "32"), ("none", "")])
 @pytest.mark.parametrize("name", ["t1024", "t768", "t384i"])
-def test_attention_mma_choice(name, mma, chunk, seeded_model, monkeypatch):
-    """The engine with the tensor-core attention (VB_ATT_MMA; default: the processor graph) on each
-    graph of the head_dim-64 models, with and without decoder chunks: the fp16 parity bar against the
-    reference's goldens for every choice."""
+def test_attention_tc_choice(name, tc, chunk, seeded_model, monkeypatch):
+    """The engine with the tile-sparse tensor-core attention (VB_ATT_TC; default: the processor graph)
+    on each graph of the head_dim-64 models, with decoder chunks on the tiles' 256-row grid and off it
+    (then the decoder keeps the shared-memory kernel): the fp16 parity bar against the reference's
+    goldens for every choice."""
     mp, xp = seeded_model(name)
     x = np.array(st.read(xp)[0]["in.x"])
-    monkeypatch.setenv("VB_ATT_MMA", mma)
+    monkeypatch.setenv("VB_ATT_TC", tc)
     if chunk:
         monkeypatch.setenv("VB_DEC_CHUNK_ROWS", chunk)
     y = vb.Model.load(mp, precision=vb.FP16).predict_step(x)
@@ -188,6 +190,7 @@ def test_wide_rows_by_parts(name, dt, seeded_model, monkeypatch):
     monkeypatch.setenv("VB_ATT_WIDE_DEG", "16")
     monkeypatch.setenv("VB_ATT_PART_EDGES", "5")
     monkeypatch.setenv("VB_ATT_TILED", "none")
+    monkeypatch.setenv("VB_ATT_TC", "none")
     y = vb.Model.load(mp, precision=dt).predict_step(x)
     vb.check_device()
     assert oracle.rel_absmax(y, golden(name)["out.y"]) <= TOL[dt]

@@ -1,7 +1,9 @@
 """Multi-GPU destination partition on B200s (skipped with fewer than 2 visible GPUs): one process per
 GPU, NCCL halo exchange; every rank's output rows must be bitwise equal to the single-GPU result
-(the partition keeps every destination's edge order and every GEMM row's arithmetic), with and without
-the encoder split."""
+(the partition keeps every destination's edge order and every GEMM row's arithmetic, and, on graphs of
+at least 128 hidden rows per GPU, the tensor-core attention's tiles), with and without the encoder
+split. On smaller graphs the hidden ranges are not on the tiles' 64-row grid, so those models run the
+processor on the gather kernel here (VB_ATT_TC=none)."""
 import os
 
 import numpy as np
@@ -49,15 +51,23 @@ def _single(mp, xp, dtype, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("name,enc_split", [("c0", 0), ("t256", 0), ("c0", 1), ("t1024", 1)])
+@pytest.mark.parametrize("name,enc_split", [("c0", 0), ("t256", 0), ("c0", 1), ("t1024", 1), ("c1s", 0), ("c1s", 1)])
 @pytest.mark.parametrize("dtype", [0, 1])
 def test_sharded_equals_single_gpu(name, enc_split, dtype, seeded_model, tmp_path, monkeypatch):
     """enc_split: the encoder on its own hidden ranges (VB_SHARD_ENC=1), its output rows moved to their
-    processor owners; c0 and t1024 move rows between ranks at 2-4 GPUs."""
+    processor owners; c0 and t1024 move rows between ranks at 2-4 GPUs. c1s (C1's widths, 2,965 hidden
+    rows) runs its processor on the tensor-core attention (fp16)."""
     import torch.multiprocessing as tmp
+    if name == "c1s" and dtype == 0:
+        pytest.skip("c1s: the fp16 tensor-core path is what it covers")
     monkeypatch.setenv("VB_SHARD_ENC", str(enc_split))
     mp, xp = seeded_model(name)
     world = min(torch.cuda.device_count(), 4)
+    from varda_b200 import safetensors as st
+    import json
+    H = json.loads(st.read(mp)[1]["config"])["dims"]["n_hidden_nodes"]
+    if H < 128 * world:
+        monkeypatch.setenv("VB_ATT_TC", "none")
     ctx = tmp.get_context("spawn")
     p = ctx.Process(target=_single, args=(mp, xp, dtype, str(tmp_path / "single.npy")))
     p.start()

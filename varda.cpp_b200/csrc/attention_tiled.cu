@@ -262,7 +262,7 @@ int take_attention_error() {
     int e = 0, zero = 0;
     VB_CUDA(cudaMemcpyFromSymbol(&e, g_att_error, sizeof(int)));
     if (e) VB_CUDA(cudaMemcpyToSymbol(g_att_error, &zero, sizeof(int)));
-    return e | take_mma_error();
+    return e | take_tc_error();
 }
 
 }  // namespace vb::k

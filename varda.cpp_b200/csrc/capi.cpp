@@ -349,9 +349,10 @@ int vb_attention_split_noalloc(int dtype, const int32_t* row_ptr, const void* ed
 }
 
 struct vb_tiles {
-    vb::DeviceBuffer tiles, srcs, tedges, heavy, row_ptr, edges;
-    std::vector<int32_t> row0, heavy_rows;
+    vb::DeviceBuffer tiles, srcs, tedges, heavy, row_ptr, edges, blob;
+    std::vector<int32_t> row0, row_end, heavy_rows;  // host copies: tile row ranges, heavy rows
     int kind = VB_TILES_SMEM;
+    int64_t n_src = 0;
 };
 
 int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* attr, int A, int64_t n_src,
@@ -359,21 +360,58 @@ int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* att
     return vb_tiles_create_kind(row_ptr, src, attr, A, n_src, n_dst, head_dim, VB_TILES_SMEM, out);
 }
 
+namespace {
+
+vb::CsrGraph host_csr(const int32_t* row_ptr, const int32_t* src, const float* attr, int A, int64_t n_src,
+                      int64_t n_dst) {
+    vb::CsrGraph g;
+    g.n_src = n_src, g.n_dst = n_dst, g.attr_dim = A;
+    g.row_ptr.assign(row_ptr, row_ptr + n_dst + 1);
+    g.n_edges = g.row_ptr.back();
+    g.src.assign(src, src + g.n_edges);
+    g.attr.assign(attr, attr + g.n_edges * A);
+    return g;
+}
+
+// The tensor-core tiles' CSR-order records in the vb_tile_plan form {a0, a1, a2, slot (int bits)}
+// (heavy rows: their source), and each tile's {row0, nrows, src_off, nsrc}.
+void tc_plan_export(const vb::CsrGraph& g, const vb::TcPlan& tp, int32_t* tiles4, float* edges) {
+    if (tiles4)
+        for (size_t i = 0; i < tp.tiles.size(); ++i)
+            tiles4[4 * i] = tp.tiles[i].row0, tiles4[4 * i + 1] = tp.tiles[i].nrows,
+                       tiles4[4 * i + 2] = tp.tiles[i].src_off, tiles4[4 * i + 3] = tp.tiles[i].nsrc;
+    if (!edges) return;
+    const auto packed = vb::pack_edges(g, true);
+    std::memcpy(edges, packed.data(), packed.size() * sizeof(vb::EdgeRec));
+    for (const vb::TcTile& t : tp.tiles) {
+        const uint16_t* rec = reinterpret_cast<const uint16_t*>(tp.blob.data() + t.blob_off + vb::kTcEdgeOff);
+        const int64_t e0 = g.row_ptr[size_t(t.row0)];
+        for (int i = 0; i < t.n_edges; ++i) {
+            const int32_t sl = rec[4 * i];
+            std::memcpy(edges + 4 * (e0 + i) + 3, &sl, 4);
+        }
+    }
+}
+
+}  // namespace
+
 int vb_tile_plan(const int32_t* row_ptr, const int32_t* src, const float* attr, int A, int64_t n_src, int64_t n_dst,
                  int kind, int64_t counts[3], int32_t* tiles4, int32_t* srcs, int32_t* heavy, float* edges) {
     return guard([&] {
         need(row_ptr, "row_ptr"), need(counts, "counts");
-        if (kind != VB_TILES_SMEM && kind != VB_TILES_MMA) vb::fail(vb::kInvalidArgument, "tiles kind");
-        vb::CsrGraph g;
-        g.n_src = n_src, g.n_dst = n_dst, g.attr_dim = A;
-        g.row_ptr.assign(row_ptr, row_ptr + n_dst + 1);
-        g.n_edges = g.row_ptr.back();
-        g.src.assign(src, src + g.n_edges);
-        g.attr.assign(attr, attr + g.n_edges * A);
-        vb::TilePlan tp = kind == VB_TILES_MMA
-                              ? vb::make_tiles(g, vb::k::mma_max_src(), vb::k::mma_max_rows(), vb::k::mma_max_edges(), 0, true, 0, true)
-                              : vb::make_tiles(g, vb::k::tiled_max_src(), vb::k::tiled_max_rows(),
-                                               vb::k::tiled_max_edges(), 0, true);
+        if (kind != VB_TILES_SMEM && kind != VB_TILES_TC) vb::fail(vb::kInvalidArgument, "tiles kind");
+        const vb::CsrGraph g = host_csr(row_ptr, src, attr, A, n_src, n_dst);
+        if (kind == VB_TILES_TC) {
+            const vb::TcPlan tp = vb::make_tc_tiles(g, vb::kTcAlignRows);
+            counts[0] = int64_t(tp.tiles.size()), counts[1] = int64_t(tp.srcs.size());
+            counts[2] = int64_t(tp.heavy.size());
+            tc_plan_export(g, tp, tiles4, edges);
+            if (srcs) std::copy(tp.srcs.begin(), tp.srcs.end(), srcs);
+            if (heavy) std::copy(tp.heavy.begin(), tp.heavy.end(), heavy);
+            return;
+        }
+        vb::TilePlan tp = vb::make_tiles(g, vb::k::tiled_max_src(), vb::k::tiled_max_rows(), vb::k::tiled_max_edges(),
+                                         0, true);
         counts[0] = int64_t(tp.row0.size()), counts[1] = int64_t(tp.srcs.size()), counts[2] = int64_t(tp.heavy.size());
         if (tiles4)
             for (size_t i = 0; i < tp.row0.size(); ++i)
@@ -390,34 +428,37 @@ int vb_tiles_create_kind(const int32_t* row_ptr, const int32_t* src, const float
     (void)head_dim;
     return guard([&] {
         need(row_ptr, "row_ptr"), need(out, "out");
-        if (kind != VB_TILES_SMEM && kind != VB_TILES_MMA) vb::fail(vb::kInvalidArgument, "tiles kind");
-        vb::CsrGraph g;
-        g.n_src = n_src, g.n_dst = n_dst, g.attr_dim = A;
-        g.row_ptr.assign(row_ptr, row_ptr + n_dst + 1);
-        g.n_edges = g.row_ptr.back();
-        g.src.assign(src, src + g.n_edges);
-        g.attr.assign(attr, attr + g.n_edges * A);
-        vb::TilePlan tp = kind == VB_TILES_MMA
-                              ? vb::make_tiles(g, vb::k::mma_max_src(), vb::k::mma_max_rows(), vb::k::mma_max_edges(), 0, true, 0, true)
-                              : vb::make_tiles(g, vb::k::tiled_max_src(), vb::k::tiled_max_rows(),
-                                               vb::k::tiled_max_edges(), 0, true);
+        if (kind != VB_TILES_SMEM && kind != VB_TILES_TC) vb::fail(vb::kInvalidArgument, "tiles kind");
+        const vb::CsrGraph g = host_csr(row_ptr, src, attr, A, n_src, n_dst);
         auto t = std::make_unique<vb_tiles>();
-        t->kind = kind;
+        t->kind = kind, t->n_src = n_src;
         auto up = [](vb::DeviceBuffer& b, const void* h, size_t n) {
             b.alloc(std::max<size_t>(n, 16));
             if (n) VB_CUDA(cudaMemcpy(b.get(), h, n, cudaMemcpyHostToDevice));
         };
-        std::vector<int4> t4(tp.row0.size());
-        for (size_t i = 0; i < t4.size(); ++i) t4[i] = make_int4(tp.row0[i], tp.nrows[i], tp.src0[i], tp.nsrc[i]);
-        up(t->tiles, t4.data(), t4.size() * sizeof(int4));
-        up(t->srcs, tp.srcs.data(), tp.srcs.size() * 4);
-        up(t->tedges, tp.edges.data(), tp.edges.size() * sizeof(vb::EdgeRec));
-        up(t->heavy, tp.heavy.data(), tp.heavy.size() * 4);
+        if (kind == VB_TILES_TC) {
+            const vb::TcPlan tp = vb::make_tc_tiles(g, vb::kTcAlignRows);
+            up(t->tiles, tp.tiles.data(), tp.tiles.size() * sizeof(vb::TcTile));
+            up(t->srcs, tp.srcs.data(), tp.srcs.size() * 4);
+            up(t->blob, tp.blob.data(), tp.blob.size());
+            for (const vb::TcTile& x : tp.tiles) t->row0.push_back(x.row0), t->row_end.push_back(x.row0 + x.nrows);
+            t->heavy_rows = tp.heavy;
+        } else {
+            vb::TilePlan tp = vb::make_tiles(g, vb::k::tiled_max_src(), vb::k::tiled_max_rows(),
+                                             vb::k::tiled_max_edges(), 0, true);
+            std::vector<int4> t4(tp.row0.size());
+            for (size_t i = 0; i < t4.size(); ++i) t4[i] = make_int4(tp.row0[i], tp.nrows[i], tp.src0[i], tp.nsrc[i]);
+            up(t->tiles, t4.data(), t4.size() * sizeof(int4));
+            up(t->srcs, tp.srcs.data(), tp.srcs.size() * 4);
+            up(t->tedges, tp.edges.data(), tp.edges.size() * sizeof(vb::EdgeRec));
+            t->row0 = tp.row0;
+            for (size_t i = 0; i < tp.row0.size(); ++i) t->row_end.push_back(tp.row0[i] + tp.nrows[i]);
+            t->heavy_rows = tp.heavy;
+        }
+        up(t->heavy, t->heavy_rows.data(), t->heavy_rows.size() * 4);
         up(t->row_ptr, g.row_ptr.data(), g.row_ptr.size() * 4);
         auto packed = vb::pack_edges(g, true);
         up(t->edges, packed.data(), packed.size() * sizeof(vb::EdgeRec));
-        t->row0 = tp.row0;
-        t->heavy_rows = tp.heavy;
         *out = t.release();
     });
 }
@@ -426,27 +467,49 @@ int vb_attention_tiled(vb_tiles* t, int64_t lo, int64_t n, const void* q, int64_
                        int64_t ldkv, const void* xr, int64_t ldxr, void* out, int64_t ldo, const float* w_e, int C,
                        int heads, int head_dim, void* stream) {
     return guard([&] {
-        need(t, "tiles");
-        if (t->kind == VB_TILES_MMA ? !vb::k::mma_supported(C, head_dim) : !vb::k::tiled_supported(C, head_dim))
+        need(t, "tiles"), need(q, "q"), need(k, "k"), need(v, "v"), need(xr, "xr"), need(out, "out"), need(w_e, "w_e");
+        if (t->kind == VB_TILES_TC ? !vb::k::tc_attention_supported(C, heads, head_dim)
+                                   : !vb::k::tiled_supported(C, head_dim))
             vb::fail(vb::kUnsupported, "tiled attention: unsupported layout");
+        if (lo < 0 || n < 0 || lo + n > int64_t(t->row_ptr.bytes() / 4) - 1)
+            vb::fail(vb::kInvalidArgument, "tiled attention: rows out of range");
         const auto t0 = std::lower_bound(t->row0.begin(), t->row0.end(), int32_t(lo));
         const auto t1 = std::lower_bound(t->row0.begin(), t->row0.end(), int32_t(lo + n));
-        vb::k::TileArgs a;
-        a.tiles = t->tiles.as<int4>(), a.srcs = t->srcs.as<int32_t>(), a.edges = t->tedges.as<vb::EdgeRec>();
-        a.row_ptr = t->row_ptr.as<int32_t>(), a.dst_lo = lo, a.tile0 = int(t0 - t->row0.begin()), a.ntiles = int(t1 - t0);
-        a.q = static_cast<const __half*>(q), a.k = static_cast<const __half*>(k), a.v = static_cast<const __half*>(v);
-        a.xr = static_cast<const __half*>(xr), a.out = static_cast<__half*>(out);
-        a.ldq = ldq, a.ldkv = ldkv, a.ldxr = ldxr, a.ldo = ldo, a.w_e = w_e, a.C = C, a.heads = heads, a.head_dim = head_dim;
-        if (t->kind == VB_TILES_MMA) vb::k::attention_mma(a, 1.4426950408889634f / std::sqrt(float(head_dim)), S(stream));
-        else vb::k::attention_tiled(a, 1.4426950408889634f / std::sqrt(float(head_dim)), S(stream));
+        // the rows must not cut a tile: a tile writes all of its rows
+        if (t1 > t0 && t->row_end[size_t(t1 - t->row0.begin()) - 1] > lo + n)
+            vb::fail(vb::kInvalidArgument, "tiled attention: rows [dst_lo, dst_lo + n_rows) must end at a tile end");
+        if (t0 != t->row0.end() && t0 != t->row0.begin() && t->row_end[size_t(t0 - t->row0.begin()) - 1] > lo)
+            vb::fail(vb::kInvalidArgument, "tiled attention: dst_lo must start a tile");
+        if (t->kind == VB_TILES_TC) {
+            vb::k::TcArgs a;
+            a.tiles = t->tiles.as<vb::TcTile>(), a.srcs = t->srcs.as<int32_t>(), a.blob = t->blob.as<uint8_t>();
+            a.tile0 = int(t0 - t->row0.begin()), a.ntiles = int(t1 - t0), a.dst_lo = lo;
+            a.q = static_cast<const __half*>(q), a.k = static_cast<const __half*>(k), a.v = static_cast<const __half*>(v);
+            a.xr = static_cast<const __half*>(xr), a.out = static_cast<__half*>(out);
+            a.ldq = ldq, a.ldkv = ldkv, a.ldxr = ldxr, a.ldo = ldo, a.n_q_rows = n;
+            a.w_e = w_e, a.C = C, a.heads = heads, a.head_dim = head_dim;
+            a.n_src = t->n_src;
+            vb::k::attention_tc(a, S(stream));
+        } else {
+            vb::k::TileArgs a;
+            a.tiles = t->tiles.as<int4>(), a.srcs = t->srcs.as<int32_t>(), a.edges = t->tedges.as<vb::EdgeRec>();
+            a.row_ptr = t->row_ptr.as<int32_t>(), a.dst_lo = lo, a.tile0 = int(t0 - t->row0.begin());
+            a.ntiles = int(t1 - t0);
+            a.q = static_cast<const __half*>(q), a.k = static_cast<const __half*>(k), a.v = static_cast<const __half*>(v);
+            a.xr = static_cast<const __half*>(xr), a.out = static_cast<__half*>(out);
+            a.ldq = ldq, a.ldkv = ldkv, a.ldxr = ldxr, a.ldo = ldo, a.w_e = w_e, a.C = C, a.heads = heads;
+            a.head_dim = head_dim;
+            vb::k::attention_tiled(a, 1.4426950408889634f / std::sqrt(float(head_dim)), S(stream));
+        }
         const auto h0 = std::lower_bound(t->heavy_rows.begin(), t->heavy_rows.end(), int32_t(lo));
         const auto h1 = std::lower_bound(t->heavy_rows.begin(), t->heavy_rows.end(), int32_t(lo + n));
         if (h1 > h0) {
             vb::k::AttnArgs<__half> g;
             g.row_ptr = t->row_ptr.as<int32_t>(), g.edges = t->edges.as<vb::EdgeRec>(), g.dst_lo = lo;
             g.rows = t->heavy.as<int32_t>() + (h0 - t->heavy_rows.begin()), g.n_rows = int64_t(h1 - h0);
-            g.q = a.q, g.ldq = ldq, g.k = a.k, g.v = a.v, g.ldkv = ldkv, g.xr = a.xr, g.ldxr = ldxr, g.out = a.out;
-            g.ldo = ldo, g.w_e = w_e, g.C = C, g.heads = heads, g.head_dim = head_dim;
+            g.q = static_cast<const __half*>(q), g.ldq = ldq, g.k = static_cast<const __half*>(k);
+            g.v = static_cast<const __half*>(v), g.ldkv = ldkv, g.xr = static_cast<const __half*>(xr), g.ldxr = ldxr;
+            g.out = static_cast<__half*>(out), g.ldo = ldo, g.w_e = w_e, g.C = C, g.heads = heads, g.head_dim = head_dim;
             vb::k::attention<__half>(g, S(stream));
         }
     });

@@ -47,10 +47,9 @@ int64_t env_int(const char* name, int64_t dflt) {
 // measured on C1 (B200): tiled 5.2 ms vs gather 12.4 ms on the decoder (3 edges per row, heavily
 // shared sources), equal on the processor, gather ahead on the encoder (35 edges per row)
 constexpr const char* kTiledDefault = "dec";
-// Which graphs run the tensor-core attention (fp16, head_dim 64; attention_mma.cu) over tiles of up to
-// 128 rows: VB_ATT_MMA, the same forms; it takes precedence over VB_ATT_TILED. Off by default: on the C1
-// processor graph it measured 3.68 ms against 1.57 ms for the gather kernel.
-constexpr const char* kMmaDefault = "none";
+// Which graphs run the tile-sparse tensor-core attention (fp16, head_dim 64; attention_tc.cu): VB_ATT_TC,
+// the same forms; it takes precedence over VB_ATT_TILED. Default: the processor graph.
+constexpr const char* kTcDefault = "proc";
 bool graph_listed(const char* env, const std::string& graph, const char* dflt) {
     const char* v = std::getenv(env);
     const std::string s = v && *v ? v : dflt;
@@ -66,7 +65,7 @@ bool graph_listed(const char* env, const std::string& graph, const char* dflt) {
     return false;
 }
 bool tiled_for(const std::string& graph, const char* dflt) { return graph_listed("VB_ATT_TILED", graph, dflt); }
-bool mma_for(const std::string& graph) { return graph_listed("VB_ATT_MMA", graph, kMmaDefault); }
+bool tc_for(const std::string& graph) { return graph_listed("VB_ATT_TC", graph, kTcDefault); }
 // Which graphs' gather launches visit destinations in source order (VB_ATT_ORDER, same forms).
 constexpr const char* kOrderDefault = "enc";
 
@@ -121,9 +120,10 @@ struct GraphDev {
     int max_degree = 0;
     const int32_t* rp() const { return row_ptr.as<int32_t>(); }
     const EdgeRec* ed() const { return edges.as<EdgeRec>(); }
-    // destination tiles of the shared-memory-staged attention (fp16), and the heavy rows
-    bool tiled = false, mma = false;  // mma: the tiles run the tensor-core kernel
-    DeviceBuffer tiles, srcs, tedges, heavy;
+    // destination tiles of the shared-memory-staged attention (fp16), or of the tensor-core attention
+    // (tc: TcTile descriptors in `tiles`, record blocks in `tblob`), and the heavy rows
+    bool tiled = false, tc = false;
+    DeviceBuffer tiles, srcs, tedges, heavy, tblob;
     std::vector<int32_t> tile_row0, heavy_rows;  // host copies, to pick a chunk's tiles
     // wide rows (more than kWideDeg edges, VB_ATT_WIDE_DEG; 0 disables) cut into parts of kPartEdges
     // edges (VB_ATT_PART_EDGES), run by the split kernels over a scratch of one partial record per
@@ -520,13 +520,24 @@ GraphDev Engine<T>::upload_graph(const CsrGraph& csr, const std::string& name, i
     std::vector<EdgeRec> packed = pack_edges(csr, !std::is_same<T, float>::value);
     GraphDev d;
     d.name = name;
-    const bool mma = std::is_same<T, __half>::value && k::mma_supported(C_, hd_) && mma_for(name);
-    if (mma || (std::is_same<T, __half>::value && k::tiled_supported(C_, hd_) && tiled_for(name, kTiledDefault))) {
-        TilePlan tp = mma ? make_tiles(csr, k::mma_max_src(), k::mma_max_rows(), k::mma_max_edges(), chunk_rows, true, 0, true)
-                          : make_tiles(csr, k::tiled_max_src(), k::tiled_max_rows(), k::tiled_max_edges(), chunk_rows, true);
+    const bool half = std::is_same<T, __half>::value;
+    // the tensor-core tiles restart every kTcAlignRows rows; a chunked graph needs chunks on that grid
+    const bool tc = half && k::tc_attention_supported(C_, heads_, hd_) && tc_for(name) &&
+                    (chunk_rows <= 0 || chunk_rows % kTcAlignRows == 0);
+    if (tc) {
+        const TcPlan tp = make_tc_tiles(csr, kTcAlignRows);
+        d.tiled = true, d.tc = true;
+        d.tiles = upload(tp.tiles.data(), std::max<size_t>(1, tp.tiles.size()) * sizeof(TcTile));
+        d.srcs = upload(tp.srcs.data(), std::max<size_t>(1, tp.srcs.size()) * sizeof(int32_t));
+        d.tblob = upload(tp.blob.data(), std::max<size_t>(16, tp.blob.size()));
+        d.heavy = upload(tp.heavy.data(), std::max<size_t>(1, tp.heavy.size()) * sizeof(int32_t));
+        for (const TcTile& t : tp.tiles) d.tile_row0.push_back(t.row0);
+        d.heavy_rows = tp.heavy;
+    } else if (half && k::tiled_supported(C_, hd_) && tiled_for(name, kTiledDefault)) {
+        TilePlan tp = make_tiles(csr, k::tiled_max_src(), k::tiled_max_rows(), k::tiled_max_edges(), chunk_rows, true);
         std::vector<int4> t4(tp.row0.size());
         for (size_t i = 0; i < t4.size(); ++i) t4[i] = make_int4(tp.row0[i], tp.nrows[i], tp.src0[i], tp.nsrc[i]);
-        d.tiled = true, d.mma = mma;
+        d.tiled = true;
         d.tiles = upload(t4.data(), std::max<size_t>(1, t4.size()) * sizeof(int4));
         d.srcs = upload(tp.srcs.data(), std::max<size_t>(1, tp.srcs.size()) * sizeof(int32_t));
         d.tedges = upload(tp.edges.data(), std::max<size_t>(1, tp.edges.size()) * sizeof(EdgeRec));
@@ -947,14 +958,24 @@ void Engine<T>::attention(const GraphDev& g, const Block<T>& b, int64_t lo, int6
             // tiles of rows [lo, lo + n) (tiles never straddle a decoder chunk), then the heavy rows
             const auto t0 = std::lower_bound(g.tile_row0.begin(), g.tile_row0.end(), int32_t(lo));
             const auto t1 = std::lower_bound(g.tile_row0.begin(), g.tile_row0.end(), int32_t(lo + n));
-            k::TileArgs t;
-            t.tiles = g.tiles.template as<int4>(), t.srcs = g.srcs.template as<int32_t>();
-            t.edges = g.tedges.template as<EdgeRec>(), t.row_ptr = g.rp(), t.dst_lo = lo;
-            t.tile0 = int(t0 - g.tile_row0.begin()), t.ntiles = int(t1 - t0);
-            t.q = q, t.k = kk, t.v = v, t.xr = xr, t.out = out, t.ldq = ldq, t.ldkv = ldkv, t.ldxr = ldxr, t.ldo = C_;
-            t.w_e = a.w_e, t.C = C_, t.heads = heads_, t.head_dim = hd_;
-            if (g.mma) k::attention_mma(t, 1.4426950408889634f / std::sqrt(float(hd_)), s);
-            else k::attention_tiled(t, 1.4426950408889634f / std::sqrt(float(hd_)), s);
+            if (g.tc) {
+                k::TcArgs t;
+                t.tiles = g.tiles.template as<TcTile>(), t.srcs = g.srcs.template as<int32_t>();
+                t.blob = g.tblob.template as<uint8_t>();
+                t.tile0 = int(t0 - g.tile_row0.begin()), t.ntiles = int(t1 - t0), t.dst_lo = lo;
+                t.q = q, t.k = kk, t.v = v, t.xr = xr, t.out = out, t.ldq = ldq, t.ldkv = ldkv, t.ldxr = ldxr;
+                t.ldo = C_, t.n_q_rows = n, t.n_src = g.n_src, t.w_e = a.w_e, t.C = C_, t.heads = heads_;
+                t.head_dim = hd_;
+                k::attention_tc(t, s);
+            } else {
+                k::TileArgs t;
+                t.tiles = g.tiles.template as<int4>(), t.srcs = g.srcs.template as<int32_t>();
+                t.edges = g.tedges.template as<EdgeRec>(), t.row_ptr = g.rp(), t.dst_lo = lo;
+                t.tile0 = int(t0 - g.tile_row0.begin()), t.ntiles = int(t1 - t0);
+                t.q = q, t.k = kk, t.v = v, t.xr = xr, t.out = out, t.ldq = ldq, t.ldkv = ldkv, t.ldxr = ldxr;
+                t.ldo = C_, t.w_e = a.w_e, t.C = C_, t.heads = heads_, t.head_dim = hd_;
+                k::attention_tiled(t, 1.4426950408889634f / std::sqrt(float(hd_)), s);
+            }
             const auto h0 = std::lower_bound(g.heavy_rows.begin(), g.heavy_rows.end(), int32_t(lo));
             const auto h1 = std::lower_bound(g.heavy_rows.begin(), g.heavy_rows.end(), int32_t(lo + n));
             if (h1 > h0) {

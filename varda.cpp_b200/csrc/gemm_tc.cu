@@ -817,4 +817,9 @@ int take_error() {
     return e;
 }
 
+CUtensorMap tensor_map_2d(const __half* base, int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols,
+                          CUtensorMapSwizzle swz) {
+    return make_map(base, rows, cols, ld, box_rows, box_cols, swz);
+}
+
 }  // namespace vb::tc

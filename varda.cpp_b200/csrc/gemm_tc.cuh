@@ -3,6 +3,7 @@
 // (bias, GELU, residual) applied when the accumulator is read back.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -18,5 +19,10 @@ void gemm(const k::GemmArgs<__half>& a, cudaStream_t s);
 // Reads and clears the device-side error flag set when a bounded wait inside the kernel gave up
 // (synchronises the device). Returns 0 when no wait timed out.
 int take_error();
+
+// 2-D fp16 tensor map over a row-major [rows, cols] matrix with leading dimension ld (elements):
+// box [box_rows, box_cols] with the given shared-memory swizzle; out-of-bounds loads read zeros.
+CUtensorMap tensor_map_2d(const __half* base, int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols,
+                          CUtensorMapSwizzle swz);
 
 }  // namespace vb::tc

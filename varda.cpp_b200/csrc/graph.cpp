@@ -188,4 +188,77 @@ TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges,
     return t;
 }
 
+TcPlan make_tc_tiles(const CsrGraph& g, int64_t align_rows) {
+    if (g.attr_dim > 3) fail(kUnsupported, "edge_attr_dim must be 1..3");
+    TcPlan t;
+    std::vector<int32_t> slot(size_t(std::max<int64_t>(g.n_src, 1)), -1);  // source -> slot in the open tile
+    std::vector<int32_t> open;                                             // the open tile's sources, by slot
+    int64_t row0 = -1;
+    auto half_bits = [](float v) {
+        const __half h = __float2half_rn(v);
+        uint16_t b;
+        std::memcpy(&b, &h, 2);
+        return b;
+    };
+    auto close = [&](int64_t end_row) {
+        if (row0 < 0) return;
+        const int64_t e0 = g.row_ptr[size_t(row0)], e1 = g.row_ptr[size_t(end_row)];
+        const int nrows = int(end_row - row0), ne = int(e1 - e0);
+        TcTile tile{};
+        tile.row0 = int32_t(row0), tile.nrows = nrows, tile.nsrc = int32_t(open.size());
+        tile.src_off = int32_t(t.srcs.size());
+        tile.blob_off = int32_t(t.blob.size()), tile.n_edges = ne;
+        tile.blob_bytes = int32_t(align_up(size_t(kTcEdgeOff) + 8 * size_t(ne), 16));
+        t.srcs.insert(t.srcs.end(), open.begin(), open.end());
+        while (t.srcs.size() % 4) t.srcs.push_back(open.back());
+        t.blob.resize(t.blob.size() + size_t(tile.blob_bytes), 0);
+        uint8_t* b = t.blob.data() + tile.blob_off;
+        uint16_t* off = reinterpret_cast<uint16_t*>(b);
+        uint16_t* mask = reinterpret_cast<uint16_t*>(b + kTcMaskOff);
+        for (int i = 0; i <= kTcRows; ++i)
+            off[i] = uint16_t(i <= nrows ? g.row_ptr[size_t(row0 + i)] - e0 : ne);
+        uint16_t* rec = reinterpret_cast<uint16_t*>(b + kTcEdgeOff);
+        for (int i = 0; i < nrows; ++i)
+            for (int64_t e = g.row_ptr[size_t(row0 + i)]; e < g.row_ptr[size_t(row0 + i + 1)]; ++e) {
+                const int32_t sl = slot[size_t(g.src[size_t(e)])];
+                mask[i / 16] = uint16_t(mask[i / 16] | (1u << (sl / 8)));
+                uint16_t* r = rec + 4 * (e - e0);
+                r[0] = uint16_t(sl);
+                for (int k = 0; k < 3; ++k)
+                    r[1 + k] = half_bits(k < g.attr_dim ? g.attr[size_t(e) * size_t(g.attr_dim) + size_t(k)] : 0.f);
+            }
+        t.tiles.push_back(tile);
+        for (int32_t s : open) slot[size_t(s)] = -1;
+        open.clear();
+        row0 = -1;
+    };
+    std::vector<int32_t> fresh, u;
+    for (int64_t d = 0; d < g.n_dst; ++d) {
+        if (align_rows > 0 && d % align_rows == 0) close(d);
+        const int32_t b = g.row_ptr[size_t(d)], e = g.row_ptr[size_t(d + 1)];
+        u.assign(g.src.begin() + b, g.src.begin() + e);
+        std::sort(u.begin(), u.end());
+        const bool dup = std::adjacent_find(u.begin(), u.end()) != u.end();
+        if (dup || e - b > kTcMaxEdges || int64_t(u.size()) > kTcMaxSrc) {
+            close(d);
+            t.heavy.push_back(int32_t(d));
+            continue;
+        }
+        // the row's sources not yet in the open tile, in edge order (no duplicates within the row)
+        fresh.clear();
+        for (int32_t i = b; i < e; ++i)
+            if (slot[size_t(g.src[size_t(i)])] < 0) fresh.push_back(g.src[size_t(i)]);
+        const bool fits = row0 >= 0 && open.size() + fresh.size() <= size_t(kTcMaxSrc) && d - row0 < kTcRows &&
+                          e - g.row_ptr[size_t(row0)] <= kTcMaxEdges;
+        if (!fits) {
+            close(d);
+            row0 = d;
+            fresh.assign(g.src.begin() + b, g.src.begin() + e);
+        }
+        for (int32_t s : fresh) slot[size_t(s)] = int32_t(open.size()), open.push_back(s);
+    }
+    close(g.n_dst);
+    return t;
+}
+
 }  // namespace vb

@@ -58,4 +58,33 @@ struct TilePlan {
 TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges, int64_t chunk_rows, bool round_fp16,
                     int max_row_edges = 0, bool sort_by_slot = false);
 
+// Tiles of the tensor-core edge attention (attention_tc.cu): runs of at most kTcRows consecutive
+// destination rows whose distinct sources number at most kTcMaxSrc and whose edges number at most
+// kTcMaxEdges. A tile's sources are numbered (its "slots") in order of first appearance along its
+// CSR edges, so the numbering depends only on the tile's rows, not on how the graph's nodes are
+// numbered; tiles restart at every multiple of align_rows (so a graph split into row ranges at such
+// multiples gets the same tiles). Rows with more than kTcMaxSrc distinct sources or kTcMaxEdges edges,
+// or with a source that appears twice, are "heavy": no tile covers them (the gather kernel does).
+constexpr int kTcRows = 64, kTcMaxSrc = 128, kTcMaxEdges = 1024;
+// Row alignment of the tile restarts (the multi-GPU destination split rounds its hidden ranges to it).
+constexpr int64_t kTcAlignRows = 256;
+// Per-tile record block (16-byte aligned, one bulk copy): u16 row offsets [kTcRows + 1] (edges of
+// tile row i are [off[i], off[i + 1]), relative to the tile's first edge) padded to kTcMaskOff bytes;
+// u16 masks [kTcRows / 16] (bit j of mask b: some edge of rows [16 b, 16 b + 16) has a slot in
+// [8 j, 8 j + 8)) padded to kTcEdgeOff bytes; then 8 bytes per edge {u16 slot, fp16 a0, a1, a2}.
+constexpr int kTcMaskOff = 144, kTcEdgeOff = 160;
+struct TcTile {
+    int32_t row0, nrows, nsrc, src_off;          // rows [row0, row0 + nrows); sources srcs[src_off, + nsrc)
+    int32_t blob_off, blob_bytes, n_edges, pad;  // the tile's record block: byte offset and size
+};
+static_assert(sizeof(TcTile) == 32, "tile descriptor must be 32 bytes");
+struct TcPlan {
+    std::vector<TcTile> tiles;
+    std::vector<int32_t> srcs;  // per tile, padded with its last source to a multiple of 4
+    std::vector<uint8_t> blob;  // record blocks
+    std::vector<int32_t> heavy;
+};
+// Attributes are rounded to fp16 (the plan serves the fp16 path only).
+TcPlan make_tc_tiles(const CsrGraph& g, int64_t align_rows);
+
 }  // namespace vb

@@ -157,15 +157,26 @@ int tiled_max_rows();
 int tiled_max_edges();
 // Synchronises; reads and clears the flag a timed-out wait of the tiled attention sets.
 int take_attention_error();
-// Edge attention on the tensor cores (fp16, head_dim 64; attention_mma.cu) over the same tiles, built
-// with at most mma_max_src() sources, mma_max_rows() rows and mma_max_edges() edges and every row's
-// records sorted by slot; w_e is read as fp16 values.
-void attention_mma(const TileArgs& a, float scale_log2, cudaStream_t s);
-bool mma_supported(int C, int head_dim);
-int mma_max_src();
-int mma_max_rows();
-int mma_max_edges();
-int take_mma_error();  // reads and clears the tensor-core attention's timeout flag (no synchronise)
+// Tile-sparse tensor-core edge attention (fp16, head_dim 64; attention_tc.cu) over the tiles of a
+// TcPlan (graph.h make_tc_tiles): same contract per destination row as attention(). Tiles
+// [tile0, tile0 + ntiles) of the plan; the q / x_r / out row of graph row d is d - dst_lo (q has
+// n_q_rows rows, k and v n_src rows). The plan's heavy rows are not covered (run them on attention()).
+struct TcArgs {
+    const TcTile* tiles = nullptr;
+    const int32_t* srcs = nullptr;
+    const uint8_t* blob = nullptr;
+    int tile0 = 0, ntiles = 0;
+    int64_t dst_lo = 0;
+    const __half *q = nullptr, *k = nullptr, *v = nullptr, *xr = nullptr;
+    __half* out = nullptr;
+    int64_t ldq = 0, ldkv = 0, ldxr = 0, ldo = 0;
+    int64_t n_q_rows = 0, n_src = 0;
+    const float* w_e = nullptr;  // [4, C], fp16-representable values
+    int C = 0, heads = 0, head_dim = 0;
+};
+void attention_tc(const TcArgs& a, cudaStream_t s);
+bool tc_attention_supported(int C, int heads, int head_dim);
+int take_tc_error();  // reads and clears the kernel's timeout flag (no synchronise)
 
 // ------------------------------------------------------------------ GEMM (Linear layers)
 enum Epilogue : int {

@@ -133,6 +133,15 @@ ShardPlan make_plan(const Config& c, const CsrGraph& enc, const CsrGraph& proc, 
         for (int64_t g = 0; g < G; ++g)
             wg[size_t(g)] = flop_g * kF + (dec.row_ptr[size_t(g + 1)] - dec.row_ptr[size_t(g)]) * row_bytes * kB;
         p.h_split = balanced_split(wh, world);
+        // hidden ranges start on the tensor-core attention's tile grid (every kTcAlignRows rows) when the
+        // graph is large enough for it, so each rank's processor tiles are the single GPU's tiles and
+        // the results stay bitwise independent of the GPU count
+        if (H >= 2 * kTcAlignRows * world) {
+            for (int k = 1; k < world; ++k) {
+                const int64_t r = (p.h_split[size_t(k)] + kTcAlignRows / 2) / kTcAlignRows * kTcAlignRows;
+                p.h_split[size_t(k)] = std::min(H, std::max(p.h_split[size_t(k - 1)] + kTcAlignRows, r));
+            }
+        }
         p.g_split = balanced_split(wg, world);
         p.e_split = p.h_split;
         if (enc_split) {

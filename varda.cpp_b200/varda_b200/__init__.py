@@ -382,7 +382,7 @@ def check_device():
 class Tiles:
     """Destination tiles of a CSR graph for the shared-memory-staged fp16 attention (vb_tiles_*)."""
 
-    SMEM, MMA = 0, 1  # kind: CUDA-core shared-memory tiles, or the tensor-core kernel's tiles
+    SMEM, TC = 0, 1  # kind: CUDA-core shared-memory tiles, or the tile-sparse tensor-core kernel's tiles
 
     def __init__(self, row_ptr, src, attr_csr, n_src, head_dim, kind=0):
         rp = np.ascontiguousarray(row_ptr, np.int32)

@@ -1,7 +1,7 @@
 """Kernel microbenchmarks through the C ABI (CUDA events on the launching stream, after warm-up).
 
     python -m varda_b200.kbench gemm --M 189809 --N 4096 --K 1024 --epi 1 [--engine 2] [--iters 20]
-    python -m varda_b200.kbench attention [--config c2] [--dtype fp16] [--impl tiled|gather] [--iters 20]
+    python -m varda_b200.kbench attention [--config c2] [--dtype fp16] [--impl tc,tiled,gather] [--iters 20]
 
 `attention --config c2` is BASELINE config C2, the isolated processor graph-attention block: the
 hidden graph of C1 (189,809 nodes, ~2.6M directed multi-scale edges in CSR by destination), C=1024,
@@ -70,13 +70,10 @@ def gemm(a):
                           "frac_of_burst": round(tf / pk["bf16_tflops"], 3)}))
 
 
-def c2_graph(seed=0):
+def c2_graph():
     from varda_b200 import synth
-    _, hidden, _, proc, _ = synth.c1_graph()
-    H = len(hidden)
-    rng = np.random.default_rng(seed)
-    attr = rng.uniform(0, 1, (len(proc), 3)).astype(np.float32)
-    return H, np.ascontiguousarray(proc.T), attr
+    hidden, proc, attr = synth.graph_c2()
+    return len(hidden), np.ascontiguousarray(proc.T), attr
 
 
 def attention(a):
@@ -97,22 +94,24 @@ def attention(a):
     out = torch.empty(H, C, device="cuda", dtype=T)
     s = torch.cuda.current_stream().cuda_stream
     q, k, v, xr = (qkvs[:, i * C:] for i in range(4))
-    if a.impl in ("tiled", "mma"):
-        tiles = vb.Tiles(rp, src, at, H, C // heads, kind=vb.Tiles.MMA if a.impl == "mma" else vb.Tiles.SMEM)
-        fn = lambda: tiles.attention(0, H, q, 4 * C, k, v, 4 * C, xr, 4 * C, out, C, w4, C, heads, C // heads,  # noqa
-                                     stream=s)
-    else:
-        fn = lambda: vb.attention(dt, d_rp, d_ed, 0, H, q, 4 * C, k, v, 4 * C, xr, 4 * C, out, C, w4, C, heads,  # noqa
-                                  C // heads, stream=s)
-    ms = time_launches(fn, a.iters, a.warmup)
     E = len(src)
     es = 2 if dt == vb.FP16 else 4
     byt = es * C * (3.0 * H + 2.0 * H) + 16.0 * E + 4.0 * (H + 1) + 16.0 * C
-    gbs = byt / (ms * 1e-3) / 1e9
     pk = _peaks()
-    print(json.dumps({"kernel": "attention", "impl": a.impl, "config": "c2", "dtype": a.dtype, "H": H, "E": E, "ms": round(ms, 4),
-                      "bytes": byt, "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4),
-                      "gathered_bytes": 2.0 * E * C * es}))
+    for impl in a.impl.split(","):
+        if impl in ("tiled", "tc"):
+            tiles = vb.Tiles(rp, src, at, H, C // heads, kind=vb.Tiles.TC if impl == "tc" else vb.Tiles.SMEM)
+            fn = lambda: tiles.attention(0, H, q, 4 * C, k, v, 4 * C, xr, 4 * C, out, C, w4, C, heads,  # noqa
+                                         C // heads, stream=s)
+        else:
+            fn = lambda: vb.attention(dt, d_rp, d_ed, 0, H, q, 4 * C, k, v, 4 * C, xr, 4 * C, out, C, w4, C,  # noqa
+                                      heads, C // heads, stream=s)
+        ms = time_launches(fn, a.iters, a.warmup)
+        gbs = byt / (ms * 1e-3) / 1e9
+        print(json.dumps({"kernel": "attention", "impl": impl, "config": "c2", "dtype": a.dtype, "H": H, "E": E,
+                          "ms": round(ms, 4), "bytes": byt, "gbs": round(gbs, 1),
+                          "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4), "gathered_bytes": 2.0 * E * C * es}),
+              flush=True)
 
 
 def main():
@@ -130,7 +129,7 @@ def main():
     t = sub.add_parser("attention")
     t.add_argument("--config", default="c2")
     t.add_argument("--dtype", default="fp16")
-    t.add_argument("--impl", default="tiled", choices=["tiled", "gather", "mma"])
+    t.add_argument("--impl", default="tc", help="comma-separated: tc, tiled, gather")
     t.add_argument("--iters", type=int, default=20)
     t.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
