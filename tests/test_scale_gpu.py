@@ -6,9 +6,10 @@
   key, from oracle/_ref/ref_dump), with the reference's tolerances (3e-3 fp16, 1e-5 fp32 rel_absmax),
   input keys within 1e-6. The reference's bitwise self-checks too (hook inert, graph replay == eager).
 * C2: the isolated processor block's graph (189,809 rows, 2,634,258 edges, C = 1024, 16 heads, fp16):
-  the gather, shared-memory-tiled and no-allocation split attention paths against the oracle's
-  restatement of cpu::graph_attention on 4,096 seeded rows (16 runs of 256 consecutive rows), and the
-  three paths against each other on every row. Exercises the 64-bit row offsets of the [H, 4C] buffer.
+  the tile-sparse tensor-core, gather, shared-memory-tiled and no-allocation split attention paths
+  against the oracle's restatement of cpu::graph_attention on 4,096 seeded rows (16 runs of 256
+  consecutive rows), and the paths against each other on every row. Exercises the 64-bit row offsets
+  of the [H, 4C] buffer.
 * c1: the full Varda-shaped model (G = 1,688,650) in fp16: out.y at 8,192 seeded data nodes against
   one predict_step of the reference's CPU backend on the same model and input
   (tests/golden/c1.y_sample.npz), 3e-3 rel_absmax; graph replay bitwise equal to the eager call.
@@ -99,9 +100,12 @@ def test_c2_attention_parity(c2_graph):
     d_ed = torch.from_numpy(edges).cuda()
     d_w = torch.from_numpy(w4).cuda()
     outs = {}
-    for path in ("gather", "tiled", "split"):
+    for path in ("tc", "gather", "tiled", "split"):
         o = torch.full((H, C), float("nan"), device="cuda", dtype=torch.float16)
-        if path == "gather":
+        if path == "tc":
+            tiles = vb.Tiles(rp, src, at, H, hd, kind=vb.Tiles.TC)
+            tiles.attention(0, H, q, ld, k, v, ld, xr, ld, o, C, d_w, C, heads, hd)
+        elif path == "gather":
             vb.attention(vb.FP16, d_rp, d_ed, 0, H, q, ld, k, v, ld, xr, ld, o, C, d_w, C, heads, hd)
         elif path == "tiled":
             tiles = vb.Tiles(rp, src, at, H, hd)
@@ -129,7 +133,7 @@ def test_c2_attention_parity(c2_graph):
     zero = np.where(rp[1:] == rp[:-1])[0]
     assert len(zero) == 0  # the C2 graph has in-degree 11..54
     base = outs["gather"].float()
-    for path in ("tiled", "split"):
+    for path in ("tc", "tiled", "split"):
         e = ((outs[path].float() - base).abs().max() / base.abs().max()).item()
         assert e <= TOL[vb.FP16], f"{path} vs gather on every row: {e:.3e}"
 

@@ -10,7 +10,7 @@
 * Tiled rows keep their records in stored order.
 * Tensor-core tiles: slots number a tile's sources in order of first appearance along its edges
   (padded with the last source to a multiple of 4), so the plan does not depend on how the source
-  nodes are numbered; a row with a repeated source is heavy; tiles restart at multiples of 256 rows.
+  nodes are numbered; a row with a repeated source is heavy; tiles restart at multiples of 64 rows.
 """
 import numpy as np
 import pytest
@@ -101,7 +101,7 @@ def test_tile_plan_properties(kind, graph):
             assert ts.tolist() == first, "slots in order of first appearance along the tile's edges"
             pad = srcs[s0 + ns:s0 + ((ns + 3) // 4) * 4]
             assert ns == 0 or np.all(pad == ts[-1]), "padded with the last source to a multiple of 4"
-            assert r0 // 256 == (r0 + nr - 1) // 256, "tiles restart at multiples of 256 rows"
+            assert r0 // 64 == (r0 + nr - 1) // 64, "tiles restart at multiples of 64 rows"
         else:
             assert np.all(np.diff(ts) > 0), "a tile's sources are distinct and increasing"
         for r in range(r0, r0 + nr):

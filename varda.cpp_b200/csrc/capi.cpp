@@ -384,7 +384,7 @@ void tc_plan_export(const vb::CsrGraph& g, const vb::TcPlan& tp, int32_t* tiles4
     const auto packed = vb::pack_edges(g, true);
     std::memcpy(edges, packed.data(), packed.size() * sizeof(vb::EdgeRec));
     for (const vb::TcTile& t : tp.tiles) {
-        const uint16_t* rec = reinterpret_cast<const uint16_t*>(tp.blob.data() + t.blob_off + vb::kTcEdgeOff);
+        const uint16_t* rec = reinterpret_cast<const uint16_t*>(tp.blob.data() + t.blob_off + t.edge_off);
         const int64_t e0 = g.row_ptr[size_t(t.row0)];
         for (int i = 0; i < t.n_edges; ++i) {
             const int32_t sl = rec[4 * i];

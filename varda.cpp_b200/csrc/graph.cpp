@@ -3,6 +3,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <array>
 #include <cstring>
 #include <limits>
 #include <string>
@@ -204,26 +205,69 @@ TcPlan make_tc_tiles(const CsrGraph& g, int64_t align_rows) {
         if (row0 < 0) return;
         const int64_t e0 = g.row_ptr[size_t(row0)], e1 = g.row_ptr[size_t(end_row)];
         const int nrows = int(end_row - row0), ne = int(e1 - e0);
+        // per 16-row block: the column blocks holding edges, and each (row, slot)'s edge index in its row
+        const int nb = (nrows + 15) / 16;
+        std::vector<std::vector<int>> cols(static_cast<size_t>(nb));
+        std::vector<std::array<uint8_t, 16 * kTcMaxSrc>> at(static_cast<size_t>(nb));
+        for (auto& a : at) a.fill(255);
+        for (int i = 0; i < nrows; ++i) {
+            const int64_t b = g.row_ptr[size_t(row0 + i)], e = g.row_ptr[size_t(row0 + i + 1)];
+            for (int64_t x = b; x < e; ++x) {
+                const int32_t sl = slot[size_t(g.src[size_t(x)])];
+                at[size_t(i / 16)][size_t((i % 16) * kTcMaxSrc + sl)] = uint8_t(x - b);
+            }
+        }
+        int n_chunks = 0;
+        std::vector<int> chunk0(static_cast<size_t>(nb));
+        for (int bk = 0; bk < nb; ++bk) {
+            bool used[kTcMaxSrc / 8] = {};
+            for (int r = 0; r < 16; ++r)
+                for (int sl = 0; sl < kTcMaxSrc; ++sl)
+                    if (at[size_t(bk)][size_t(r * kTcMaxSrc + sl)] != 255) used[sl / 8] = true;
+            auto& cl = cols[size_t(bk)];
+            for (int j = 0; j < kTcMaxSrc / 8; ++j)
+                if (used[j]) cl.push_back(j);
+            if (cl.size() % 2) cl.push_back(-1 - cl.back());  // an empty repeat of the last block
+            chunk0[size_t(bk)] = n_chunks;
+            n_chunks += int(cl.size() / 2);
+        }
         TcTile tile{};
         tile.row0 = int32_t(row0), tile.nrows = nrows, tile.nsrc = int32_t(open.size());
         tile.src_off = int32_t(t.srcs.size());
         tile.blob_off = int32_t(t.blob.size()), tile.n_edges = ne;
-        tile.blob_bytes = int32_t(align_up(size_t(kTcEdgeOff) + 8 * size_t(ne), 16));
+        tile.edge_off = kTcChunkOff + 256 * n_chunks;
+        tile.blob_bytes = int32_t(align_up(size_t(tile.edge_off) + 8 * size_t(ne), 16));
         t.srcs.insert(t.srcs.end(), open.begin(), open.end());
         while (t.srcs.size() % 4) t.srcs.push_back(open.back());
         t.blob.resize(t.blob.size() + size_t(tile.blob_bytes), 0);
-        uint8_t* b = t.blob.data() + tile.blob_off;
-        uint16_t* off = reinterpret_cast<uint16_t*>(b);
-        uint16_t* mask = reinterpret_cast<uint16_t*>(b + kTcMaskOff);
-        for (int i = 0; i <= kTcRows; ++i)
+        uint8_t* bl = t.blob.data() + tile.blob_off;
+        uint16_t* off = reinterpret_cast<uint16_t*>(bl);
+        for (int i = 0; i <= kTcRows + 1; ++i)
             off[i] = uint16_t(i <= nrows ? g.row_ptr[size_t(row0 + i)] - e0 : ne);
-        uint16_t* rec = reinterpret_cast<uint16_t*>(b + kTcEdgeOff);
+        for (int bk = 0; bk < nb; ++bk) {
+            uint8_t* hd = bl + kTcBlockOff + 32 * bk;
+            const auto& cl = cols[size_t(bk)];
+            hd[0] = uint8_t(cl.size() / 2), hd[1] = uint8_t(chunk0[size_t(bk)]);
+            for (size_t k = 0; k < cl.size(); ++k) hd[2 + k] = uint8_t(cl[k] >= 0 ? cl[k] : -1 - cl[k]);
+            for (size_t c = 0; c < cl.size() / 2; ++c) {
+                uint8_t* ch = bl + kTcChunkOff + 256 * (chunk0[size_t(bk)] + int(c));
+                for (int l = 0; l < 32; ++l) {
+                    const int r = l / 4, tq = l % 4;
+                    for (int h = 0; h < 2; ++h) {  // the chunk's first / second column block
+                        const int j = cl[2 * c + size_t(h)];
+                        for (int q = 0; q < 4; ++q) {
+                            const int row = r + (q >= 2 ? 8 : 0), sl = 8 * (j >= 0 ? j : 0) + 2 * tq + (q & 1);
+                            ch[8 * l + 4 * h + q] = j >= 0 ? at[size_t(bk)][size_t(row * kTcMaxSrc + sl)] : 255;
+                        }
+                    }
+                }
+            }
+        }
+        uint16_t* rec = reinterpret_cast<uint16_t*>(bl + tile.edge_off);
         for (int i = 0; i < nrows; ++i)
             for (int64_t e = g.row_ptr[size_t(row0 + i)]; e < g.row_ptr[size_t(row0 + i + 1)]; ++e) {
-                const int32_t sl = slot[size_t(g.src[size_t(e)])];
-                mask[i / 16] = uint16_t(mask[i / 16] | (1u << (sl / 8)));
                 uint16_t* r = rec + 4 * (e - e0);
-                r[0] = uint16_t(sl);
+                r[0] = uint16_t(slot[size_t(g.src[size_t(e)])]);
                 for (int k = 0; k < 3; ++k)
                     r[1 + k] = half_bits(k < g.attr_dim ? g.attr[size_t(e) * size_t(g.attr_dim) + size_t(k)] : 0.f);
             }

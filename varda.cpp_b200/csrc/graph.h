@@ -59,7 +59,7 @@ TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges,
                     int max_row_edges = 0, bool sort_by_slot = false);
 
 // Tiles of the tensor-core edge attention (attention_tc.cu): runs of at most kTcRows consecutive
-// destination rows whose distinct sources number at most kTcMaxSrc and whose edges number at most
+// destination rows whose edges reach at most kTcMaxSrc distinct sources and number at most
 // kTcMaxEdges. A tile's sources are numbered (its "slots") in order of first appearance along its
 // CSR edges, so the numbering depends only on the tile's rows, not on how the graph's nodes are
 // numbered; tiles restart at every multiple of align_rows (so a graph split into row ranges at such
@@ -67,15 +67,23 @@ TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges,
 // or with a source that appears twice, are "heavy": no tile covers them (the gather kernel does).
 constexpr int kTcRows = 64, kTcMaxSrc = 128, kTcMaxEdges = 1024;
 // Row alignment of the tile restarts (the multi-GPU destination split rounds its hidden ranges to it).
-constexpr int64_t kTcAlignRows = 256;
-// Per-tile record block (16-byte aligned, one bulk copy): u16 row offsets [kTcRows + 1] (edges of
-// tile row i are [off[i], off[i + 1]), relative to the tile's first edge) padded to kTcMaskOff bytes;
-// u16 masks [kTcRows / 16] (bit j of mask b: some edge of rows [16 b, 16 b + 16) has a slot in
-// [8 j, 8 j + 8)) padded to kTcEdgeOff bytes; then 8 bytes per edge {u16 slot, fp16 a0, a1, a2}.
-constexpr int kTcMaskOff = 144, kTcEdgeOff = 160;
+constexpr int64_t kTcAlignRows = 64;
+// Per-tile record block (16-byte aligned, one bulk copy), in this order:
+//   u16 row offsets [kTcRows + 2]: edges of tile row i are [off[i], off[i + 1]), relative to the
+//       tile's first edge (rows past the tile: empty);
+//   per 16-row block b (at kTcBlockOff + 32 b): u8 chunk count n_b, u8 chunk base (index of the block's
+//       first chunk in the tile), then 2 n_b u8 column-block indices: the block's 8-slot column blocks
+//       that hold edges, in pairs (one pair per chunk; an odd count padded with a repeat whose entries
+//       are all empty);
+//   per chunk (at kTcChunkOff + 256 c): per lane l of a warp, 8 u8 entries: for the m16n8 fragment
+//       positions lane l holds in the chunk's two column blocks ((r, 2t), (r, 2t + 1), (r + 8, 2t),
+//       (r + 8, 2t + 1) with r = l / 4, t = l % 4, first block then second), the index of that edge
+//       within its row, or 255 when (row, slot) is not an edge;
+//   edges at edge_off = kTcChunkOff + 256 n_chunks: 8 bytes each {u16 slot, fp16 a0, a1, a2}.
+constexpr int kTcBlockOff = 144, kTcChunkOff = 272, kTcMaxChunks = 4 * (kTcMaxSrc / 16);
 struct TcTile {
-    int32_t row0, nrows, nsrc, src_off;          // rows [row0, row0 + nrows); sources srcs[src_off, + nsrc)
-    int32_t blob_off, blob_bytes, n_edges, pad;  // the tile's record block: byte offset and size
+    int32_t row0, nrows, nsrc, src_off;               // rows [row0, row0 + nrows); sources srcs[src_off, + nsrc)
+    int32_t blob_off, blob_bytes, n_edges, edge_off;  // record block: byte offset, size; edge list offset
 };
 static_assert(sizeof(TcTile) == 32, "tile descriptor must be 32 bytes");
 struct TcPlan {
