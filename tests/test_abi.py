@@ -93,7 +93,7 @@ def test_load_rejects_unconsumed_tensor(tmp_path):
     (lambda c: c["architecture"]["processor"].__setitem__("kind", "gnn"), "architecture.processor.kind"),
     (lambda c: c["dims"].__setitem__("gelu_approximate", "erf2"), "gelu_approximate"),
     (lambda c: c.__setitem__("format_version", 2), "format_version"),
-    (lambda c: c["bounding"].append({"type": "softplus", "index": [0]}), "bounding type"),
+    (lambda c: c["bounding"].append({"type": "softplus", "index": [0]}), "softplus"),
     (lambda c: c["residual"].__setitem__("step", 5), "residual.step"),
 ])
 def test_load_rejects_bad_config(tmp_path, edit, msg):

@@ -1,6 +1,7 @@
-// Model configuration from the `config` metadata JSON (format v3) of a converted varda.cpp model.
-// Same fields, validation and error classes as the reference's parse_config
-// (src/varda/config.h:11-77, config.cpp:34-194); unknown kinds are rejected at load.
+// Model configuration from the `config` metadata JSON (format v3) of a converted varda.cpp model:
+// the fields of the reference's varda::Config (src/varda/config.h:11-77) that this engine uses, read
+// and validated against the format contract (the reference's docs/format.md section 1.2) by
+// config.cpp; unknown kinds and variants are rejected at load (kFormat errors).
 #pragma once
 
 #include <cstdint>
