@@ -81,12 +81,12 @@ def _load_error(path):
 
 def test_load_rejects_missing_tensor(tmp_path):
     err = _load_error(_small_model(tmp_path, mutate=lambda t: t.pop("proc.0.mlp1.weight")))
-    assert err.code == 2 and "missing tensor 'proc.0.mlp1.weight'" in str(err)
+    assert err.code == 2 and "no tensor 'proc.0.mlp1.weight'" in str(err)
 
 
 def test_load_rejects_unconsumed_tensor(tmp_path):
     err = _load_error(_small_model(tmp_path, mutate=lambda t: t.__setitem__("extra.thing", np.zeros(3, np.float32))))
-    assert err.code == 2 and "not consumed" in str(err) and "extra.thing" in str(err)
+    assert err.code == 2 and "extra.thing" in str(err)
 
 
 @pytest.mark.parametrize("edit,msg", [

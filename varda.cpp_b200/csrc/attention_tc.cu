@@ -339,26 +339,35 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
                 float o[8][4];
 #pragma unroll
                 for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-                // ---- 16-slot steps: two column blocks (ja, jb) each
+                // ---- 16-slot steps: two column blocks (ja, jb) each. The products S and the entry words of
+                // step c + 1 are issued before the weights of step c (software pipeline).
+                auto scores = [&](int c, float (&sv)[8], uint2& ent) {
+                    const int ja = bh[2 + 2 * c], jb = bh[3 + 2 * c];
+                    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        uint32_t b[4], d[4];
+                        ldsm_x4(kbase + swz(8 * ja + (lane & 7), 4 * half + (lane >> 3)), b);
+                        ldsm_x4(kbase + swz(8 * jb + (lane & 7), 4 * half + (lane >> 3)), d);
+                        mma16816(sa, qa[2 * half], b[0], b[1]);
+                        mma16816(sb, qa[2 * half], d[0], d[1]);
+                        mma16816(sa, qa[2 * half + 1], b[2], b[3]);
+                        mma16816(sb, qa[2 * half + 1], d[2], d[3]);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) sv[i] = sa[i], sv[4 + i] = sb[i];
+                    ent = *reinterpret_cast<const uint2*>(bl + kTcChunkOff + 256 * (cbase + c) + 8 * lane);
+                };
+                float svn[8];
+                uint2 entn = make_uint2(0xffffffffu, 0xffffffffu);
+                if (nch > 0) scores(0, svn, entn);
                 for (int c = 0; c < nch; ++c) {
                     const int ja = bh[2 + 2 * c], jb = bh[3 + 2 * c];
                     float sv[8];  // positions: block ja (r0: 2t, 2t + 1; r1: 2t, 2t + 1), then block jb
-                    {
-                        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                        for (int half = 0; half < 2; ++half) {
-                            uint32_t b[4], d[4];
-                            ldsm_x4(kbase + swz(8 * ja + (lane & 7), 4 * half + (lane >> 3)), b);
-                            ldsm_x4(kbase + swz(8 * jb + (lane & 7), 4 * half + (lane >> 3)), d);
-                            mma16816(sa, qa[2 * half], b[0], b[1]);
-                            mma16816(sb, qa[2 * half], d[0], d[1]);
-                            mma16816(sa, qa[2 * half + 1], b[2], b[3]);
-                            mma16816(sb, qa[2 * half + 1], d[2], d[3]);
-                        }
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) sv[i] = sa[i], sv[4 + i] = sb[i];
-                    }
-                    const uint2 ent = *reinterpret_cast<const uint2*>(bl + kTcChunkOff + 256 * (cbase + c) + 8 * lane);
+                    for (int i = 0; i < 8; ++i) sv[i] = svn[i];
+                    const uint2 ent = entn;
+                    if (c + 1 < nch) scores(c + 1, svn, entn);
                     float av[8][3];
                     float cm[2] = {-INFINITY, -INFINITY};
 #pragma unroll
@@ -376,14 +385,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
                         av[e][0] = a0, av[e][1] = a1, av[e][2] = a2, sv[e] = sc;
                         cm[rr] = fmaxf(cm[rr], sc);
                     }
-#pragma unroll
-                    for (int rr = 0; rr < 2; ++rr) {
-                        cm[rr] = fmaxf(cm[rr], __shfl_xor_sync(kFull, cm[rr], 1));
-                        cm[rr] = fmaxf(cm[rr], __shfl_xor_sync(kFull, cm[rr], 2));
-                    }
+                    // the reference maxima m are the same in the four lanes of a row's quad; they move only
+                    // when a lane's own score exceeds them by more than the slack (then over the quad)
                     if (__any_sync(kFull, cm[0] > m[0] + kSlack || cm[1] > m[1] + kSlack)) {
 #pragma unroll
                         for (int rr = 0; rr < 2; ++rr) {
+                            cm[rr] = fmaxf(cm[rr], __shfl_xor_sync(kFull, cm[rr], 1));
+                            cm[rr] = fmaxf(cm[rr], __shfl_xor_sync(kFull, cm[rr], 2));
                             const float mn = fmaxf(m[rr], cm[rr]);
                             const float corr = mn == -INFINITY ? 1.f : ex2(m[rr] - mn);
                             m[rr] = mn;
@@ -450,21 +458,17 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
                 }
                 // ---- out = T(T(O / l) + x_r), rows of this tile only
                 const float i0 = l[0] > 0.f ? 1.0f / l[0] : 0.f, i1 = l[1] > 0.f ? 1.0f / l[1] : 0.f;
+                // (T(T(o) + x_r) as one fp16 add of T(o) and x_r: the sum of two fp16 values is exact in
+                // fp32 whenever it can round differently, so both give the same fp16)
 #pragma unroll
                 for (int n = 0; n < 8; ++n) {
                     const int cc = c0 + 8 * n;
-                    if (r0 < t.nrows) {
-                        const float2 x = unpack_h2(xv0[n]);
-                        const float u = rnd<__half>(rnd<__half>(o[n][0] * i0) + x.x);
-                        const float v = rnd<__half>(rnd<__half>(o[n][1] * i0) + x.y);
-                        *reinterpret_cast<__half2*>(p.out + lr0 * p.ldo + cc) = __floats2half2_rn(u, v);
-                    }
-                    if (r1 < t.nrows) {
-                        const float2 x = unpack_h2(xv1[n]);
-                        const float u = rnd<__half>(rnd<__half>(o[n][2] * i1) + x.x);
-                        const float v = rnd<__half>(rnd<__half>(o[n][3] * i1) + x.y);
-                        *reinterpret_cast<__half2*>(p.out + lr1 * p.ldo + cc) = __floats2half2_rn(u, v);
-                    }
+                    if (r0 < t.nrows)
+                        *reinterpret_cast<__half2*>(p.out + lr0 * p.ldo + cc) =
+                            __hadd2(__floats2half2_rn(o[n][0] * i0, o[n][1] * i0), *reinterpret_cast<const __half2*>(&xv0[n]));
+                    if (r1 < t.nrows)
+                        *reinterpret_cast<__half2*>(p.out + lr1 * p.ldo + cc) =
+                            __hadd2(__floats2half2_rn(o[n][2] * i1, o[n][3] * i1), *reinterpret_cast<const __half2*>(&xv1[n]));
                 }
             }
             __syncwarp();
