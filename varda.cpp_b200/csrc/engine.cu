@@ -30,6 +30,7 @@
 #include "gemm_tc.cuh"
 #include "graph.h"
 #include "kernels.cuh"
+#include "params.h"
 #include "safetensors.h"
 #include "shard.h"
 
@@ -48,8 +49,9 @@ int64_t env_int(const char* name, int64_t dflt) {
 // shared sources), equal on the processor, gather ahead on the encoder (35 edges per row)
 constexpr const char* kTiledDefault = "dec";
 // Which graphs run the tile-sparse tensor-core attention (fp16, head_dim 64; attention_tc.cu): VB_ATT_TC,
-// the same forms; it takes precedence over VB_ATT_TILED. Default: the processor graph.
-constexpr const char* kTcDefault = "proc";
+// the same forms; it takes precedence over VB_ATT_TILED. Off by default: on the C2 block it measured
+// 1.67 ms against 1.58 ms for the gather kernel (in the C1 step 2.25 against about 2.2 ms per block).
+constexpr const char* kTcDefault = "none";
 bool graph_listed(const char* env, const std::string& graph, const char* dflt) {
     const char* v = std::getenv(env);
     const std::string s = v && *v ? v : dflt;
@@ -69,18 +71,6 @@ bool tc_for(const std::string& graph) { return graph_listed("VB_ATT_TC", graph, 
 // Which graphs' gather launches visit destinations in source order (VB_ATT_ORDER, same forms).
 constexpr const char* kOrderDefault = "enc";
 
-// f(begin, end) over [0, n) split into contiguous ranges on up to 16 host threads (one below `grain`
-// items per thread). Used for the per-element conversions of the load path, whose results do not
-// depend on the split.
-template <class F> void parallel_ranges(int64_t n, int64_t grain, F f) {
-    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-    const int nt = int(std::max<int64_t>(1, std::min<int64_t>(std::min<unsigned>(hw, 16u), n / std::max<int64_t>(grain, 1))));
-    if (nt <= 1) return f(int64_t(0), n);
-    std::vector<std::thread> ts;
-    for (int t = 0; t < nt; ++t) ts.emplace_back(f, n * t / nt, n * (t + 1) / nt);
-    for (auto& th : ts) th.join();
-}
-
 // Load-stage timer: VB_LOAD_TIMING=1 prints the seconds of each stage of a model load to stderr.
 struct LoadTimer {
     bool on = env_int("VB_LOAD_TIMING", 0) != 0;
@@ -91,26 +81,6 @@ struct LoadTimer {
         std::fprintf(stderr, "varda_b200 load: %-28s %.3f s\n", stage, std::chrono::duration<double>(now - t).count());
         t = now;
     }
-};
-
-template <class T> struct Lin {
-    DeviceBuffer w, b;
-    int64_t N = 0, K = 0, ldw = 0;
-    const T* W() const { return w.as<T>(); }
-    const T* B() const { return b.get() ? b.as<T>() : nullptr; }
-};
-
-struct Norm {
-    DeviceBuffer w, b;  // fp32 [C]; b empty when absent
-    const float* W() const { return w.as<float>(); }
-    const float* B() const { return b.get() ? b.as<float>() : nullptr; }
-};
-
-template <class T> struct Block {
-    bool mapper = false;
-    Norm ln_src, ln_dst, ln_mlp;
-    Lin<T> qkvs, qs, kv, proj, mlp1, mlp2;
-    DeviceBuffer w_e;  // fp32 [4, C]
 };
 
 struct GraphDev {
@@ -139,43 +109,7 @@ struct GraphDev {
 };
 constexpr int kWideDeg = 2048, kPartEdges = 64;
 
-template <class T> float round_op(float x) {
-    if (std::is_same<T, float>::value) return x;
-    return __half2float(__float2half_rn(x));
-}
-
 }  // namespace
-
-// The names a model file must hold, exactly (the reference consumes every tensor with take() and
-// then requires that nothing is left, model.cpp:76; names listed in config `absent` may be missing).
-void check_tensor_set(const SafeTensorsFile& f, const Config& c) {
-    std::vector<std::string> want = {"norm.mul", "norm.add", "nodes.data.attr", "nodes.hidden.attr"};
-    for (const char* g : {"enc", "proc", "dec"})
-        want.push_back(std::string("graph.") + g + ".edge_index"), want.push_back(std::string("graph.") + g + ".edge_attr");
-    auto lin = [&](const std::string& n) {
-        want.push_back(n + ".weight");
-        if (!c.is_absent(n + ".bias")) want.push_back(n + ".bias");
-    };
-    for (const char* n : {"enc.emb_src", "enc.emb_dst", "dec.emb_dst", "dec.out_proj", "dec.out_norm"}) lin(n);
-    for (const std::string& b : c.block_names) {
-        const bool mapper = b == "enc.block" || b == "dec.block";
-        for (const char* l : {"q", "k", "v", "self", "edge", "proj", "mlp1", "mlp2", "ln_dst", "ln_mlp"}) lin(b + "." + l);
-        if (mapper) lin(b + ".ln_src");
-    }
-    for (const std::string& n : want) f.peek(n);  // throws "missing tensor"
-    std::vector<std::string> extra;
-    for (const std::string& n : f.names()) {
-        if (n == "grid.latitudes" || n == "grid.longitudes") continue;
-        if (std::find(want.begin(), want.end(), n) == want.end()) extra.push_back(n);
-    }
-    if (f.has("grid.latitudes") != f.has("grid.longitudes"))
-        fail(kFormat, f.path() + ": grid.latitudes and grid.longitudes must come together");
-    if (!extra.empty()) {
-        std::string m = std::to_string(extra.size()) + " tensor(s) not consumed by the engine:";
-        for (size_t i = 0; i < extra.size() && i < 20; ++i) m += " " + extra[i];
-        fail(kFormat, f.path() + ": " + m);
-    }
-}
 
 template <class T>
 class Engine final : public Model {
@@ -221,7 +155,7 @@ public:
                  void* user, float* step_ms) override;
 
 private:
-    struct Hook;
+    struct HookSink;
     // ---- profiling (eager runs only): an event pair around every launch
     struct ProfRec {
         std::string name;
@@ -244,29 +178,26 @@ private:
             if (e->prof_) cudaEventRecord(e->prof_->back().b, s);
         }
     };
-    void ln(const T* x, const Norm& n, T* y, int64_t rows, cudaStream_t s) {
+    void ln(const T* x, const Affine& n, T* y, int64_t rows, cudaStream_t s) {
         Span sp(this, s, "layernorm", 0, double(rows) * C_ * 2 * sizeof(T));
-        k::layernorm<T>(x, C_, n.W(), n.B(), y, C_, rows, C_, eps_, s);
+        k::layernorm<T>(x, C_, n.g(), n.b(), y, C_, rows, C_, eps_, s);
     }
-    Lin<T> load_linear(SafeTensorsFile& f, const std::vector<std::string>& names, int64_t N_each, int64_t K);
-    Norm load_norm(SafeTensorsFile& f, const std::string& name);
-    Block<T> load_block(SafeTensorsFile& f, const std::string& pre, bool mapper);
     CsrGraph read_graph(SafeTensorsFile& f, const std::string& g, int64_t n_src, int64_t n_dst);
     GraphDev upload_graph(const CsrGraph& csr, const std::string& name, int64_t chunk_rows);
     DeviceBuffer upload(const void* h, size_t bytes);
     T* act(size_t elems);
     float* actf(size_t elems);
 
-    void linear(const Lin<T>& L, const T* x, int64_t ldx, T* y, int64_t ldy, int64_t M, cudaStream_t s,
+    void linear(const Dense<T>& L, const T* x, int64_t ldx, T* y, int64_t ldy, int64_t M, cudaStream_t s,
                 int epi = k::kEpiBias, const T* R = nullptr, int64_t ldr = 0);
-    void attention(const GraphDev& g, const Block<T>& b, int64_t lo, int64_t n, const T* q, int64_t ldq, const T* kk,
+    void attention(const GraphDev& g, const AttnLayer<T>& b, int64_t lo, int64_t n, const T* q, int64_t ldq, const T* kk,
                    const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out, cudaStream_t s);
-    void forward(const float* xn, float* yn, cudaStream_t s, Hook* hk);
+    void forward(const float* xn, float* yn, cudaStream_t s, HookSink* hk);
     // pieces of forward(), in its order; the pipelined host path runs them around chunked copies
-    void enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64_t n, cudaStream_t s, Hook* hk);
-    void enc_dest_pre(cudaStream_t s, Hook* hk);
-    bool middle(cudaStream_t s, Hook* hk);
-    void dec_chunk(int64_t lo, int64_t n, cudaStream_t s, Hook* hk, bool& halo_pending, float* h_emb, float* h_bo);
+    void enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64_t n, cudaStream_t s, HookSink* hk);
+    void enc_dest_pre(cudaStream_t s, HookSink* hk);
+    bool middle(cudaStream_t s, HookSink* hk);
+    void dec_chunk(int64_t lo, int64_t n, cudaStream_t s, HookSink* hk, bool& halo_pending, float* h_emb, float* h_bo);
     void output_rows(const float* xn, float* yn, int64_t lo, int64_t n, cudaStream_t s, float* pre_bound);
     cudaGraphExec_t capture(const std::function<void(cudaStream_t)>& body, cudaStream_t s);
     bool capture_graph(cudaStream_t s);
@@ -284,10 +215,10 @@ private:
     float eps_ = 0;
     bool gelu_tanh_ = false;
 
-    Lin<T> enc_emb_src_, enc_emb_dst_, dec_emb_dst_, dec_out_proj_;
-    Norm dec_out_norm_;
-    Block<T> enc_, dec_;
-    std::vector<Block<T>> proc_;
+    Dense<T> enc_emb_src_, enc_emb_dst_, dec_emb_dst_, dec_out_proj_;
+    Affine dec_out_norm_;
+    AttnLayer<T> enc_, dec_;
+    std::vector<AttnLayer<T>> proc_;
     GraphDev g_enc_, g_proc_, g_dec_;
     DeviceBuffer mul_in_, add_in_, mul_out_, add_out_, res_src_, bounds_, bidx_;
     int n_bounds_ = 0;
@@ -355,7 +286,7 @@ private:
     void predict_pipelined(const float* x, float* y);
     DeviceBuffer proc_inner_, proc_outer_;
     int64_t n_inner_ = 0, n_outer_ = 0;
-    void attention_rows(const GraphDev& g, const Block<T>& b, const DeviceBuffer& rows, int64_t n, const T* q,
+    void attention_rows(const GraphDev& g, const AttnLayer<T>& b, const DeviceBuffer& rows, int64_t n, const T* q,
                         int64_t ldq, const T* kk, const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out,
                         cudaStream_t s);
     T *xsend_ = nullptr, *xrecv_ = nullptr;
@@ -388,34 +319,39 @@ private:
 
 // ====================================================================== hook
 
+// Delivers activations to the caller's hook (eager runs only) as host fp32, contiguous. A device
+// tensor [rows, cols] (row stride ld, element type U) is converted to fp32 on the device into a staging
+// buffer in slabs of whole rows, alternating between the buffer's two halves, each slab copied to the
+// host behind its conversion on the same stream; one synchronisation at the end.
 template <class T>
-struct Engine<T>::Hook {
+struct Engine<T>::HookSink {
     Engine& e;
     HookFn fn;
     void* user;
     cudaStream_t s;
+    static constexpr int64_t kStageFloats = int64_t(1) << 24;
 
-    void host(const std::string& key, const float* d, std::vector<int64_t> shape) {
-        fn(key.c_str(), d, shape.data(), int(shape.size()), user);
+    void emit_host(const std::string& key, const float* host, std::vector<int64_t> shape) {
+        fn(key.c_str(), host, shape.data(), int(shape.size()), user);
     }
-    template <class U> void fetch(const U* d, int64_t ld, int64_t rows, int64_t cols, float* dst, int64_t r0 = 0) {
-        VB_CUDA(cudaStreamSynchronize(s));
-        const int64_t stage = int64_t(1) << 24;
-        if (!e.hook_stage_.get()) e.hook_stage_.alloc(size_t(stage) * sizeof(float));
-        const int64_t blk = std::max<int64_t>(1, stage / cols);
-        for (int64_t a = 0; a < rows; a += blk) {
-            const int64_t n = std::min(blk, rows - a);
-            k::convert_2d<U, float>(d + a * ld, ld, e.hook_stage_.as<float>(), cols, n, cols, s);
-            VB_CUDA(cudaMemcpyAsync(dst + (r0 + a) * cols, e.hook_stage_.get(), size_t(n * cols) * sizeof(float),
+    // rows [0, rows) of the device tensor into dst rows [row0, row0 + rows)
+    template <class U> void to_host(const U* d, int64_t ld, int64_t rows, int64_t cols, float* dst, int64_t row0 = 0) {
+        if (!e.hook_stage_.get()) e.hook_stage_.alloc(size_t(kStageFloats) * sizeof(float));
+        const int64_t slab = std::max<int64_t>(1, kStageFloats / 2 / std::max<int64_t>(cols, 1));
+        for (int64_t r = 0, i = 0; r < rows; r += slab, ++i) {
+            const int64_t n = std::min(slab, rows - r);
+            float* half = e.hook_stage_.as<float>() + (i & 1) * (kStageFloats / 2);
+            k::convert_2d<U, float>(d + r * ld, ld, half, cols, n, cols, s);
+            VB_CUDA(cudaMemcpyAsync(dst + (row0 + r) * cols, half, size_t(n * cols) * sizeof(float),
                                     cudaMemcpyDeviceToHost, s));
-            VB_CUDA(cudaStreamSynchronize(s));
         }
+        VB_CUDA(cudaStreamSynchronize(s));
     }
-    template <class U> void dev(const std::string& key, const U* d, int64_t ld, int64_t rows, int64_t cols,
-                                std::vector<int64_t> shape) {
-        std::vector<float> h(size_t(rows * cols));
-        fetch(d, ld, rows, cols, h.data());
-        host(key, h.data(), shape);
+    template <class U> void emit(const std::string& key, const U* d, int64_t ld, int64_t rows, int64_t cols,
+                                 std::vector<int64_t> shape) {
+        std::vector<float> host(size_t(rows * cols));
+        to_host(d, ld, rows, cols, host.data());
+        emit_host(key, host.data(), std::move(shape));
     }
 };
 
@@ -428,81 +364,6 @@ DeviceBuffer Engine<T>::upload(const void* h, size_t bytes) {
     if (bytes && h) VB_CUDA(cudaMemcpy(b.get(), h, bytes, cudaMemcpyHostToDevice));
     else if (bytes) VB_CUDA(cudaMemset(b.get(), 0, bytes));
     weight_bytes_ += bytes;
-    return b;
-}
-
-// Linear layers stacked by output rows, each `<name>.weight` F32 [N_each, K] and `<name>.bias` F32
-// [N_each] unless listed absent; stored as T with the row stride padded to a multiple of 8 elements
-// (16 bytes in fp16, the tensor-memory-access alignment), zero padded.
-template <class T>
-Lin<T> Engine<T>::load_linear(SafeTensorsFile& f, const std::vector<std::string>& names, int64_t N_each, int64_t K) {
-    Lin<T> L;
-    L.K = K;
-    L.ldw = int64_t(align_up(size_t(K), 8));
-    L.N = N_each * int64_t(names.size());
-    std::vector<T> w(size_t(L.N * L.ldw), T(0.0f)), b(size_t(L.N), T(0.0f));
-    bool any_bias = false;
-    for (size_t i = 0; i < names.size(); ++i) {
-        const TensorView& tw = f.take(names[i] + ".weight", DType::F32, {N_each, K});
-        const float* src = tw.as<float>();
-        T* dst = w.data() + size_t(int64_t(i) * N_each * L.ldw);
-        parallel_ranges(N_each, std::max<int64_t>(1, (int64_t(1) << 20) / std::max<int64_t>(K, 1)), [&](int64_t r0, int64_t r1) {
-            for (int64_t r = r0; r < r1; ++r)
-                for (int64_t c = 0; c < K; ++c) dst[size_t(r * L.ldw + c)] = T(src[r * K + c]);
-        });
-        const std::string bn = names[i] + ".bias";
-        if (!cfg_.is_absent(bn)) {
-            const TensorView& tb = f.take(bn, DType::F32, {N_each});
-            for (int64_t r = 0; r < N_each; ++r) b[size_t(int64_t(i) * N_each + r)] = T(tb.as<float>()[r]);
-            any_bias = true;
-        }
-    }
-    L.w = upload(w.data(), w.size() * sizeof(T));
-    if (any_bias) L.b = upload(b.data(), b.size() * sizeof(T));
-    return L;
-}
-
-template <class T>
-Norm Engine<T>::load_norm(SafeTensorsFile& f, const std::string& name) {
-    Norm n;
-    const TensorView& w = f.take(name + ".weight", DType::F32, {C_});
-    n.w = upload(w.data, w.nbytes);
-    if (!cfg_.is_absent(name + ".bias")) {
-        const TensorView& b = f.take(name + ".bias", DType::F32, {C_});
-        n.b = upload(b.data, b.nbytes);
-    }
-    return n;
-}
-
-template <class T>
-Block<T> Engine<T>::load_block(SafeTensorsFile& f, const std::string& pre, bool mapper) {
-    Block<T> b;
-    b.mapper = mapper;
-    if (mapper) b.ln_src = load_norm(f, pre + ".ln_src");
-    b.ln_dst = load_norm(f, pre + ".ln_dst");
-    b.ln_mlp = load_norm(f, pre + ".ln_mlp");
-    auto P = [&](const char* n) { return pre + "." + n; };
-    if (mapper) {
-        b.qs = load_linear(f, {P("q"), P("self")}, C_, C_);
-        b.kv = load_linear(f, {P("k"), P("v")}, C_, C_);
-    } else {
-        b.qkvs = load_linear(f, {P("q"), P("k"), P("v"), P("self")}, C_, C_);
-    }
-    b.proj = load_linear(f, {P("proj")}, C_, C_);
-    b.mlp1 = load_linear(f, {P("mlp1")}, mlp_, C_);
-    b.mlp2 = load_linear(f, {P("mlp2")}, C_, mlp_);
-    const int A = cfg_.edge_attr_dim;
-    const TensorView& we = f.take(P("edge") + ".weight", DType::F32, {C_, A});
-    // [4, C], attribute-major (coalesced per-lane vector loads): W_e[:, 0..2] zero padded, then b_e.
-    // fp16 mode rounds the edge Linear's weights to fp16, as autocast does.
-    std::vector<float> w4(size_t(C_) * 4, 0.0f);
-    for (int c = 0; c < C_; ++c)
-        for (int a = 0; a < A; ++a) w4[size_t(a) * C_ + c] = round_op<T>(we.as<float>()[c * A + a]);
-    if (!cfg_.is_absent(P("edge") + ".bias")) {
-        const TensorView& bv = f.take(P("edge") + ".bias", DType::F32, {C_});
-        for (int c = 0; c < C_; ++c) w4[size_t(3) * C_ + c] = round_op<T>(bv.as<float>()[c]);
-    }
-    b.w_e = upload(w4.data(), w4.size() * sizeof(float));
     return b;
 }
 
@@ -671,7 +532,7 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     if (file.metadata("varda_format") != "1")
         fail(kFormat, path + ": unsupported varda_format " + file.metadata("varda_format"));
     cfg_ = parse_config(file.metadata("config"));
-    check_tensor_set(file, cfg_);  // format errors surface before any device call
+    validate_model_file(file, cfg_);  // format errors surface before any device call
     VB_CUDA(cudaSetDevice(dev_));
     file.prefetch();
     const Config& c = cfg_;
@@ -828,14 +689,17 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
 
     lt.mark("node attributes");
     // ---- weights
-    enc_emb_src_ = load_linear(file, {"enc.emb_src"}, C_, F_);
-    enc_emb_dst_ = load_linear(file, {"enc.emb_dst"}, C_, A_node_);
-    dec_emb_dst_ = load_linear(file, {"dec.emb_dst"}, C_, F_);
-    dec_out_norm_ = load_norm(file, "dec.out_norm");
-    dec_out_proj_ = load_linear(file, {"dec.out_proj"}, V_dec_, C_);
-    enc_ = load_block(file, "enc.block", true);
-    for (int i = 0; i < n_proc_; ++i) proc_.push_back(load_block(file, "proc." + std::to_string(i), false));
-    dec_ = load_block(file, "dec.block", true);
+    {
+        ParamLoader<T> pl(file, cfg_, weight_bytes_);
+        enc_emb_src_ = pl.dense({"enc.emb_src"}, C_, F_);
+        enc_emb_dst_ = pl.dense({"enc.emb_dst"}, C_, A_node_);
+        dec_emb_dst_ = pl.dense({"dec.emb_dst"}, C_, F_);
+        dec_out_norm_ = pl.affine("dec.out_norm", C_);
+        dec_out_proj_ = pl.dense({"dec.out_proj"}, V_dec_, C_);
+        enc_ = pl.layer("enc.block", true, C_, mlp_);
+        for (int i = 0; i < n_proc_; ++i) proc_.push_back(pl.layer("proc." + std::to_string(i), false, C_, mlp_));
+        dec_ = pl.layer("dec.block", true, C_, mlp_);
+    }
     file.require_all_consumed();
 
     lt.mark("weights");
@@ -915,32 +779,32 @@ void Engine<T>::use_high_priority_stream() {
 // ====================================================================== forward
 
 template <class T>
-void Engine<T>::linear(const Lin<T>& L, const T* x, int64_t ldx, T* y, int64_t ldy, int64_t M, cudaStream_t s,
+void Engine<T>::linear(const Dense<T>& L, const T* x, int64_t ldx, T* y, int64_t ldy, int64_t M, cudaStream_t s,
                        int epi, const T* R, int64_t ldr) {
     k::GemmArgs<T> a;
-    a.A = x, a.lda = ldx, a.W = L.W(), a.ldw = L.ldw, a.bias = L.B(), a.C = y, a.ldc = ldy;
-    a.R = R, a.ldr = ldr, a.M = M, a.N = L.N, a.K = L.K, a.epi = epi, a.gelu_tanh = gelu_tanh_;
+    a.A = x, a.lda = ldx, a.W = L.w(), a.ldw = L.ld_in, a.bias = L.b(), a.C = y, a.ldc = ldy;
+    a.R = R, a.ldr = ldr, a.M = M, a.N = L.out, a.K = L.in, a.epi = epi, a.gelu_tanh = gelu_tanh_;
     if constexpr (std::is_same<T, __half>::value) {
         if (use_tc_ && tc::supported(a)) {
-            Span sp(this, s, "gemm_tc M=" + std::to_string(M) + " N=" + std::to_string(L.N) + " K=" +
-                                 std::to_string(L.K) + " epi=" + std::to_string(epi),
-                    2.0 * double(M) * double(L.N) * double(L.K), 0);
+            Span sp(this, s, "gemm_tc M=" + std::to_string(M) + " N=" + std::to_string(L.out) + " K=" +
+                                 std::to_string(L.in) + " epi=" + std::to_string(epi),
+                    2.0 * double(M) * double(L.out) * double(L.in), 0);
             tc::gemm(a, s);
             return;
         }
     }
-    Span sp(this, s, "gemm_simt M=" + std::to_string(M) + " N=" + std::to_string(L.N) + " K=" + std::to_string(L.K) +
-                         " epi=" + std::to_string(epi), 2.0 * double(M) * double(L.N) * double(L.K), 0);
+    Span sp(this, s, "gemm_simt M=" + std::to_string(M) + " N=" + std::to_string(L.out) + " K=" + std::to_string(L.in) +
+                         " epi=" + std::to_string(epi), 2.0 * double(M) * double(L.out) * double(L.in), 0);
     k::gemm_simt<T>(a, s);
 }
 
 template <class T>
-void Engine<T>::attention(const GraphDev& g, const Block<T>& b, int64_t lo, int64_t n, const T* q, int64_t ldq,
+void Engine<T>::attention(const GraphDev& g, const AttnLayer<T>& b, int64_t lo, int64_t n, const T* q, int64_t ldq,
                           const T* kk, const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out, cudaStream_t s) {
     k::AttnArgs<T> a;
     a.row_ptr = g.rp(), a.edges = g.ed(), a.dst_lo = lo, a.n_rows = n;
     a.q = q, a.ldq = ldq, a.k = kk, a.v = v, a.ldkv = ldkv, a.xr = xr, a.ldxr = ldxr, a.out = out, a.ldo = C_;
-    a.w_e = b.w_e.template as<float>(), a.C = C_, a.heads = heads_, a.head_dim = hd_;
+    a.w_e = b.edge_fold.template as<float>(), a.C = C_, a.heads = heads_, a.head_dim = hd_;
     // compulsory bytes: q, x_r, out per destination, k and v per source, one 16-byte record per
     // edge, row_ptr, the [4, C] edge weights
     double edges = 0;
@@ -1019,21 +883,21 @@ void Engine<T>::attention(const GraphDev& g, const Block<T>& b, int64_t lo, int6
 
 // The gather attention over an explicit list of rows (local ids) of graph g.
 template <class T>
-void Engine<T>::attention_rows(const GraphDev& g, const Block<T>& b, const DeviceBuffer& rows, int64_t n, const T* q,
+void Engine<T>::attention_rows(const GraphDev& g, const AttnLayer<T>& b, const DeviceBuffer& rows, int64_t n, const T* q,
                                int64_t ldq, const T* kk, const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out,
                                cudaStream_t s) {
     if (n <= 0) return;
     k::AttnArgs<T> a;
     a.row_ptr = g.rp(), a.edges = g.ed(), a.dst_lo = 0, a.n_rows = n, a.rows = rows.template as<int32_t>();
     a.q = q, a.ldq = ldq, a.k = kk, a.v = v, a.ldkv = ldkv, a.xr = xr, a.ldxr = ldxr, a.out = out, a.ldo = C_;
-    a.w_e = b.w_e.template as<float>(), a.C = C_, a.heads = heads_, a.head_dim = hd_;
+    a.w_e = b.edge_fold.template as<float>(), a.C = C_, a.heads = heads_, a.head_dim = hd_;
     k::attention<T>(a, s);
 }
 
 // Encoder source side on data rows [r0, r0 + n) of the Gx rows: assemble (the T_in input slots slot_rows
 // rows apart), emb_src, LN_src (in place), [k | v]. Row-wise, so any split of the rows gives the same bits.
 template <class T>
-void Engine<T>::enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64_t n, cudaStream_t s, Hook* hk) {
+void Engine<T>::enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64_t n, cudaStream_t s, HookSink* hk) {
     if (n <= 0) return;
     const int64_t G = Gx_, C = C_;
     {
@@ -1043,38 +907,38 @@ void Engine<T>::enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64
     }
     if (hk) {
         if (std::is_same<T, float>::value) {
-            hk->dev("enc.x_src", x_data_, ldF_, G, F_, {G, F_});
+            hk->emit("enc.x_src", x_data_, ldF_, G, F_, {G, F_});
         } else {  // the reference's x_data is fp32; the fp16 cast happens inside the Linear
             if (!hook_xsrc_.get()) hook_xsrc_.alloc(size_t(G * F_) * sizeof(float));
             k::assemble<float>(xn, d_attr_.as<float>(), T_in_, G, V_in_, A_node_, hook_xsrc_.as<float>(), F_, s);
-            hk->dev("enc.x_src", hook_xsrc_.as<float>(), F_, G, F_, {G, F_});
+            hk->emit("enc.x_src", hook_xsrc_.as<float>(), F_, G, F_, {G, F_});
         }
-        hk->host("enc.x_dst", h_attr_host_.data(), {Hl_, A_node_});
+        hk->emit_host("enc.x_dst", h_attr_host_.data(), {Hl_, A_node_});
     }
     T* emb_src = region_ + r0 * C;
     T* kv_enc = region_ + G * C + r0 * 2 * C;
     linear(enc_emb_src_, x_data_ + r0 * ldF_, ldF_, emb_src, C, n, s);
-    if (hk) hk->dev("enc.emb_src", emb_src, C, n, C, {n, C});
-    ln(emb_src, enc_.ln_src, emb_src, n, s);
-    linear(enc_.kv, emb_src, C, kv_enc, 2 * C, n, s);
+    if (hk) hk->emit("enc.emb_src", emb_src, C, n, C, {n, C});
+    ln(emb_src, enc_.norm_src, emb_src, n, s);
+    linear(enc_.proj_kv, emb_src, C, kv_enc, 2 * C, n, s);
 }
 
 // Encoder destination side before the attention (needs no input): emb_dst of the hidden attributes,
 // LN_dst, [q | self].
 template <class T>
-void Engine<T>::enc_dest_pre(cudaStream_t s, Hook* hk) {
+void Engine<T>::enc_dest_pre(cudaStream_t s, HookSink* hk) {
     const int64_t H = El_, C = C_;
     T* emb_dst = zA_;
     linear(enc_emb_dst_, h_attr_.as<T>(), ldA_, emb_dst, C, H, s);
-    if (hk) hk->dev("enc.emb_dst", emb_dst, C, H, C, {H, C});
-    ln(emb_dst, enc_.ln_dst, xh_, H, s);
-    linear(enc_.qs, xh_, C, qkvs_, 2 * C, H, s);
+    if (hk) hk->emit("enc.emb_dst", emb_dst, C, H, C, {H, C});
+    ln(emb_dst, enc_.norm_dst, xh_, H, s);
+    linear(enc_.proj_qx, xh_, C, qkvs_, 2 * C, H, s);
 }
 
 // From the encoder attention to the decoder's source side ([k | v] of LN_src(latent) and its halo).
 // Returns whether the decoder halo exchange is still in flight on the communication stream.
 template <class T>
-bool Engine<T>::middle(cudaStream_t s, Hook* hk) {
+bool Engine<T>::middle(cudaStream_t s, HookSink* hk) {
     const int64_t G = Gx_, H = Hl_, C = C_, E = El_;
     T* kv_enc = region_ + G * C;
     T* emb_dst = zA_;
@@ -1082,13 +946,13 @@ bool Engine<T>::middle(cudaStream_t s, Hook* hk) {
     // processor block) and its rows then move to their processor owners' z_enc_
     T* enc_out = emove_.on ? zB_ : z_enc_;
     attention(g_enc_, enc_, 0, E, qkvs_, 2 * C, kv_enc, kv_enc + C, 2 * C, qkvs_ + C, 2 * C, sbuf_, s);
-    linear(enc_.proj, sbuf_, C, out1_, C, E, s, k::kEpiResidual, emb_dst, C);
-    ln(out1_, enc_.ln_mlp, xh_, E, s);
-    linear(enc_.mlp1, xh_, C, hbuf_, mlp_, E, s, k::kEpiGelu);
-    linear(enc_.mlp2, hbuf_, mlp_, enc_out, C, E, s, k::kEpiResidual, out1_, C);
+    linear(enc_.proj_out, sbuf_, C, out1_, C, E, s, k::kEpiResidual, emb_dst, C);
+    ln(out1_, enc_.norm_ffn, xh_, E, s);
+    linear(enc_.ffn_up, xh_, C, hbuf_, mlp_, E, s, k::kEpiGelu);
+    linear(enc_.ffn_down, hbuf_, mlp_, enc_out, C, E, s, k::kEpiResidual, out1_, C);
     if (emove_.on) enc_redistribute(enc_out, z_enc_, s);
-    if (hk) hk->dev("enc.out", z_enc_, C, H, C, {H, C});
-    ln(z_enc_, proc_[0].ln_dst, xh_, H, s);
+    if (hk) hk->emit("enc.out", z_enc_, C, H, C, {H, C});
+    ln(z_enc_, proc_[0].norm_dst, xh_, H, s);
 
     // ---- processor; xh_ holds LN_dst of the block input
     // sharded: exchange / interior-attention overlap, except under the hook or the profiler (whose
@@ -1098,8 +962,8 @@ bool Engine<T>::middle(cudaStream_t s, Hook* hk) {
     T* z_in = z_enc_;
     T* latent = nullptr;
     for (int i = 0; i < n_proc_; ++i) {
-        const Block<T>& b = proc_[size_t(i)];
-        linear(b.qkvs, xh_, C, qkvs_, 4 * C, H, s);
+        const AttnLayer<T>& b = proc_[size_t(i)];
+        linear(b.proj_qkvx, xh_, C, qkvs_, 4 * C, H, s);
         if (overlap) {
             // K|V of remote sources on the communication stream while the interior rows run
             VB_CUDA(cudaEventRecord(ev_kv_, s));
@@ -1115,30 +979,30 @@ bool Engine<T>::middle(cudaStream_t s, Hook* hk) {
             exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, s);  // K|V of remote sources
             attention(g_proc_, b, 0, H, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C, 4 * C, sbuf_, s);
         }
-        linear(b.proj, sbuf_, C, out1_, C, H, s, k::kEpiResidual, z_in, C);
-        ln(out1_, b.ln_mlp, xh_, H, s);
-        linear(b.mlp1, xh_, C, hbuf_, mlp_, H, s, k::kEpiGelu);
+        linear(b.proj_out, sbuf_, C, out1_, C, H, s, k::kEpiResidual, z_in, C);
+        ln(out1_, b.norm_ffn, xh_, H, s);
+        linear(b.ffn_up, xh_, C, hbuf_, mlp_, H, s, k::kEpiGelu);
         T* z_out = z_in == zA_ ? zB_ : zA_;
-        linear(b.mlp2, hbuf_, mlp_, z_out, C, H, s, k::kEpiResidual, out1_, C);
-        if (hk) hk->dev("proc." + std::to_string(i) + ".out", z_out, C, H, C, {H, C});
+        linear(b.ffn_down, hbuf_, mlp_, z_out, C, H, s, k::kEpiResidual, out1_, C);
+        if (hk) hk->emit("proc." + std::to_string(i) + ".out", z_out, C, H, C, {H, C});
         if (i + 1 < n_proc_) {
-            k::layernorm<T>(z_out, C, proc_[size_t(i + 1)].ln_dst.W(), proc_[size_t(i + 1)].ln_dst.B(), xh_, C, H,
+            k::layernorm<T>(z_out, C, proc_[size_t(i + 1)].norm_dst.g(), proc_[size_t(i + 1)].norm_dst.b(), xh_, C, H,
                             C_, eps_, s);
         } else if (cfg_.latent_skip) {
             latent = z_in == z_enc_ ? sbuf_ : z_in;  // a dead buffer
             Span sp(this, s, "add_layernorm", 0, double(H) * C_ * 4 * sizeof(T));
-            k::add_layernorm<T>(z_out, z_enc_, latent, dec_.ln_src.W(), dec_.ln_src.B(), xh_, C, H, C_, eps_, s);
+            k::add_layernorm<T>(z_out, z_enc_, latent, dec_.norm_src.g(), dec_.norm_src.b(), xh_, C, H, C_, eps_, s);
         } else {
             latent = z_out;
-            ln(z_out, dec_.ln_src, xh_, H, s);
+            ln(z_out, dec_.norm_src, xh_, H, s);
         }
         z_in = z_out;
     }
-    if (hk) hk->dev("latent", latent, C, H, C, {H, C});
+    if (hk) hk->emit("latent", latent, C, H, C, {H, C});
 
     // ---- decoder, source side: [k | v] of LN_src(latent)
     T* kv_dec = qkvs_;
-    linear(dec_.kv, xh_, C, kv_dec, 2 * C, H, s);
+    linear(dec_.proj_kv, xh_, C, kv_dec, 2 * C, H, s);
     if (overlap) {  // the decoder's K|V halo flies while the first chunk's destination GEMMs run
         VB_CUDA(cudaEventRecord(ev_kv_, s));
         VB_CUDA(cudaStreamWaitEvent(cs_, ev_kv_, 0));
@@ -1153,7 +1017,7 @@ bool Engine<T>::middle(cudaStream_t s, Hook* hk) {
 // Decoder destination rows [lo, lo + n) of the own data rows (at most dec_rows_ of them, and never
 // straddling a decoder tile; the chunk buffers sit in region_), through out_proj into dec_out_.
 template <class T>
-void Engine<T>::dec_chunk(int64_t lo, int64_t n, cudaStream_t s, Hook* hk, bool& halo_pending, float* h_emb,
+void Engine<T>::dec_chunk(int64_t lo, int64_t n, cudaStream_t s, HookSink* hk, bool& halo_pending, float* h_emb,
                           float* h_bo) {
     const int64_t C = C_, R = dec_rows_;
     T* kv_dec = qkvs_;
@@ -1164,19 +1028,19 @@ void Engine<T>::dec_chunk(int64_t lo, int64_t n, cudaStream_t s, Hook* hk, bool&
     T* o1 = sb + R * C;
     T* h = o1 + R * C;
     linear(dec_emb_dst_, x_data_ + lo * ldF_, ldF_, e, C, n, s);
-    if (hk) hk->fetch(e, C, n, C, h_emb, lo);
-    ln(e, dec_.ln_dst, t, n, s);
-    linear(dec_.qs, t, C, qs, 2 * C, n, s);
+    if (hk) hk->to_host(e, C, n, C, h_emb, lo);
+    ln(e, dec_.norm_dst, t, n, s);
+    linear(dec_.proj_qx, t, C, qs, 2 * C, n, s);
     if (halo_pending) {
         VB_CUDA(cudaStreamWaitEvent(s, ev_halo_, 0));
         halo_pending = false;
     }
     attention(g_dec_, dec_, lo, n, qs, 2 * C, kv_dec, kv_dec + C, 2 * C, qs + C, 2 * C, sb, s);
-    linear(dec_.proj, sb, C, o1, C, n, s, k::kEpiResidual, e, C);
-    ln(o1, dec_.ln_mlp, t, n, s);
-    linear(dec_.mlp1, t, C, h, mlp_, n, s, k::kEpiGelu);
-    linear(dec_.mlp2, h, mlp_, sb, C, n, s, k::kEpiResidual, o1, C);
-    if (hk) hk->fetch(sb, C, n, C, h_bo, lo);
+    linear(dec_.proj_out, sb, C, o1, C, n, s, k::kEpiResidual, e, C);
+    ln(o1, dec_.norm_ffn, t, n, s);
+    linear(dec_.ffn_up, t, C, h, mlp_, n, s, k::kEpiGelu);
+    linear(dec_.ffn_down, h, mlp_, sb, C, n, s, k::kEpiResidual, o1, C);
+    if (hk) hk->to_host(sb, C, n, C, h_bo, lo);
     ln(sb, dec_out_norm_, t, n, s);
     linear(dec_out_proj_, t, C, dec_out_ + lo * ldVo_, ldVo_, n, s);
 }
@@ -1198,7 +1062,7 @@ void Engine<T>::output_rows(const float* xn, float* yn, int64_t lo, int64_t n, c
 }
 
 template <class T>
-void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
+void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, HookSink* hk) {
     const int64_t Gl = Gl_, C = C_;
     // ---- encoder: source side on all data rows (own, then the encoder's halo), destination side
     enc_source(xn, Gx_, 0, Gx_, s, hk);
@@ -1211,9 +1075,9 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
     for (int64_t lo = 0; lo < Gl; lo += dec_rows_)
         dec_chunk(lo, std::min(dec_rows_, Gl - lo), s, hk, halo_pending, h_emb.data(), h_bo.data());
     if (hk) {
-        hk->host("dec.emb_dst", h_emb.data(), {Gl, C});
-        hk->host("dec.block_out", h_bo.data(), {Gl, C});
-        hk->dev("dec.out", dec_out_, ldVo_, Gl, V_dec_, {Gl, int64_t(V_dec_)});
+        hk->emit_host("dec.emb_dst", h_emb.data(), {Gl, C});
+        hk->emit_host("dec.block_out", h_bo.data(), {Gl, C});
+        hk->emit("dec.out", dec_out_, ldVo_, Gl, V_dec_, {Gl, int64_t(V_dec_)});
     }
 
     // ---- output
@@ -1221,8 +1085,8 @@ void Engine<T>::forward(const float* xn, float* yn, cudaStream_t s, Hook* hk) {
     output_rows(xn, yn, 0, Gl, s, hk ? hook_prebound_.as<float>() : nullptr);
     if (hk) {
         const std::vector<int64_t> shp = {1, T_out_, 1, Gl, V_out_};
-        hk->dev("out.pre_bound", hook_prebound_.as<float>(), V_out_, T_out_ * Gl, V_out_, shp);
-        hk->dev("out.norm", yn, V_out_, T_out_ * Gl, V_out_, shp);
+        hk->emit("out.pre_bound", hook_prebound_.as<float>(), V_out_, T_out_ * Gl, V_out_, shp);
+        hk->emit("out.norm", yn, V_out_, T_out_ * Gl, V_out_, shp);
     }
 }
 
@@ -1346,15 +1210,15 @@ void Engine<T>::predict_step(const float* x, float* y, HookFn hook, void* user) 
     }
     VB_CUDA(cudaMemcpyAsync(x_dev_, x, size_t(in_n) * sizeof(float), cudaMemcpyHostToDevice, s));
     if (hook) {
-        Hook hk{*this, hook, user, s};
-        hk.host("in.x", x, {1, T_in_, G_, V_in_});
+        HookSink hk{*this, hook, user, s};
+        hk.emit_host("in.x", x, {1, T_in_, G_, V_in_});
         normalise(x_dev_, xn_, s);
-        hk.dev("in.x_norm", xn_, in_n, 1, in_n, {1, T_in_, 1, G_, V_in_});
+        hk.emit("in.x_norm", xn_, in_n, 1, in_n, {1, T_in_, 1, G_, V_in_});
         forward(xn_, yn_, s, &hk);
         denormalise(yn_, y_dev_, s);
         VB_CUDA(cudaMemcpyAsync(y, y_dev_, size_t(out_n) * sizeof(float), cudaMemcpyDeviceToHost, s));
         VB_CUDA(cudaStreamSynchronize(s));
-        hk.host("out.y", y, {1, T_out_, 1, G_, V_out_});
+        hk.emit_host("out.y", y, {1, T_out_, 1, G_, V_out_});
         ran_eager_ = true;
         return;
     }
