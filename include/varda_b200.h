@@ -226,7 +226,12 @@ void vb_tiles_free(vb_tiles* t);
 
 /* Gemm::linear (src/varda/cuda/gemm.h): y[M, N] = A[M, K] W[N, K]^T (+ bias), then epilogue
  * 0 = none, 1 = GELU (gelu_tanh selects the tanh form), 2 = + residual R[M, N]. engine: 0 = auto
- * (tensor cores for fp16), 1 = CUDA cores, 2 = tensor cores (fp16 only; fails if not applicable). */
+ * (tensor cores for fp16), 1 = CUDA cores, 2 = tensor cores (fp16 only; fails if not applicable).
+ * The tensor-core GEMM visits its tiles in a fixed order here (the engine's own GEMMs take their next
+ * tile from a counter of the model's). With VB_GEMM_SCHED=1 in the environment this entry point uses
+ * the dynamic order too, on a counter kept per (device, stream, thread): then a CUDA graph holding it
+ * must not run concurrently with itself or with other such launches keyed to its capture stream. Both
+ * orders give the same bits. */
 int vb_gemm(int dtype, int engine, const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* Y,
             int64_t ldy, const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int epilogue, int gelu_tanh,
             void* stream);

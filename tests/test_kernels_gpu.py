@@ -426,10 +426,10 @@ def test_gemm_cta_pair(M, N, K, lda, epi, monkeypatch):
                                        (70000, 256, 64, 0), (5000, 128, 192, 2)])
 @pytest.mark.parametrize("pair", ["1", "0"])
 def test_gemm_tile_order_bitwise(M, N, K, epi, pair, monkeypatch):
-    """Dynamic tile order (each CTA or CTA pair takes its next tile from a per-stream counter) against
-    the static order (VB_GEMM_SCHED=0): the same tiles with the same k order, so bitwise equal; repeated
-    launches (the counter is zeroed by each launch's last CTA) and launches interleaved on two streams
-    (a counter each) too."""
+    """Dynamic tile order (each CTA or CTA pair takes its next tile from a counter; through vb_gemm with
+    VB_GEMM_SCHED=1, a counter per stream) against the static order (vb_gemm's default): the same tiles
+    with the same k order, so bitwise equal; repeated launches (the counter is zeroed by each launch's
+    last CTA) and launches interleaved on two streams (a counter each) too."""
     rng = np.random.default_rng(M + N + K + epi)
     T = torch.float16
     A = dev(rounded(rng.normal(size=(M, K)), vb.FP16), T)

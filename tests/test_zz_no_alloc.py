@@ -5,8 +5,11 @@ other test in the session has used the device; it passes alone as well.
 Two calls in a row on the same inputs (the second reuses the static scratch the first wrote) must both
 match vb_attention: within 1e-5 rel_absmax in fp32 (the summation order differs), and in fp16 within
 the fp16 bar with nearly every element bitwise equal (only outputs near an fp16 rounding boundary may
-differ by one unit). Cases cover every degree class incl. zero in-degree, a destination sub-range,
-several split counts, and a graph large enough to need several scratch-sized batches.
+differ by one unit). In fp32 the output is also checked against the CPU oracle's restatement of the
+reference's graph attention, plus x_r. The device's free memory is the same before and after the
+second call (the entry point allocates nothing). Cases cover every degree class incl. zero in-degree,
+a destination sub-range, several split counts, and a graph large enough to need several scratch-sized
+batches.
 """
 import numpy as np
 import pytest
@@ -47,7 +50,7 @@ def setup(rng, C, heads, A, n_src, n_dst, dt):
     w4[3] = rounded(rng.normal(size=C) * 0.5, dt)
     edges = vb.pack_edges(src, attr, round_fp16=False)
     return dict(rp=dev(rp, torch.int32), ed=dev(edges, torch.float32), w=dev(w4, torch.float32), q=q, k=k, v=v,
-                xr=xr, ld=ld, T=T, rp_host=rp)
+                xr=xr, ld=ld, T=T, rp_host=rp, csr=(rp, src, None, attr), w4=w4, A=A)
 
 
 def run_both(g, dt, C, heads, lo, n, splits):
@@ -56,12 +59,16 @@ def run_both(g, dt, C, heads, lo, n, splits):
     vb.attention(dt, g["rp"], g["ed"], lo, n, g["q"][lo:], g["ld"], g["k"], g["v"], g["ld"], g["xr"][lo:], g["ld"],
                  ref, C, g["w"], C, heads, hd)
     outs = []
-    for _ in range(2):  # two calls in a row: the second reuses the scratch the first wrote
+    for i in range(2):  # two calls in a row: the second reuses the scratch the first wrote
         o = torch.full((n, C), float("nan"), device="cuda", dtype=g["T"])
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
         vb.attention_split_noalloc(dt, g["rp"], g["ed"], lo, n, g["q"][lo:], g["ld"], g["k"], g["v"], g["ld"],
                                    g["xr"][lo:], g["ld"], o, C, g["w"], C, heads, hd, splits)
+        torch.cuda.synchronize()
+        if i == 1:  # the first call on a device may load the module; the second must take no memory
+            assert torch.cuda.mem_get_info()[0] == free0, "the no-allocation entry point took device memory"
         outs.append(o)
-    torch.cuda.synchronize()
     return ref.float().cpu().numpy(), [o.float().cpu().numpy() for o in outs]
 
 
@@ -79,6 +86,18 @@ def check(ref, outs, dt, g, lo, n):
         xr = g["xr"][lo:lo + n].float().cpu().numpy()[:, :got.shape[1]]
         assert np.array_equal(got[zero], xr[zero]), "zero in-degree gives x_r exactly"
     assert np.array_equal(outs[0], outs[1]), "repeat calls are deterministic"
+    if dt == vb.FP32:  # the CPU oracle (the reference's graph attention restated), plus x_r
+        C = outs[0].shape[1]
+        heads = g["heads"]
+        ld = g["ld"]
+        q = g["q"].float().cpu().numpy()[:, :C]
+        k = g["k"].float().cpu().numpy()[:, :C]
+        v = g["v"].float().cpu().numpy()[:, :C]
+        xr = g["xr"].float().cpu().numpy()[:, :C]
+        we = np.ascontiguousarray(g["w4"][:g["A"]])
+        o = oracle.graph_attention(g["csr"], lo, n, q[lo:lo + n], k, v, we, g["w4"][3], heads, C // heads)
+        assert oracle.rel_absmax(outs[0], o + xr[lo:lo + n]) <= 1e-5, "against the CPU oracle"
+        del ld
 
 
 @pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])
@@ -87,6 +106,7 @@ def check(ref, outs, dt, g, lo, n):
 def test_matches_existing_entry_point(C, heads, A, splits, dt):
     rng = np.random.default_rng(C + heads + splits + dt)
     g = setup(rng, C, heads, A, 131, 97, dt)
+    g["heads"] = heads
     ref, outs = run_both(g, dt, C, heads, 0, 97, splits)
     check(ref, outs, dt, g, 0, 97)
     lo, n = 13, 51  # a destination sub-range, rows local
@@ -99,18 +119,24 @@ def test_many_batches(dt):
     """2,500 rows x 8 splits x (1024 + 80) floats: about six scratch-sized batches."""
     rng = np.random.default_rng(5 + dt)
     g = setup(rng, 1024, 16, 3, 700, 2500, dt)
+    g["heads"] = 16
     ref, outs = run_both(g, dt, 1024, 16, 0, 2500, 8)
     check(ref, outs, dt, g, 0, 2500)
 
 
 def test_rejects_what_does_not_fit():
     rp = torch.zeros(2, dtype=torch.int32, device="cuda")
-    w = torch.zeros(4, 65536, dtype=torch.float32, device="cuda")
+    ed = torch.zeros(1, 4, dtype=torch.float32, device="cuda")
+    C = 65536
+    row = torch.zeros(1, C, dtype=torch.float32, device="cuda")  # one row of q, k, v, x_r, out
+    w = torch.zeros(4, C, dtype=torch.float32, device="cuda")
     # one row: 64 splits x (65536 + 5 x 1024) floats > the 16 MiB scratch; rejected before any launch
     with pytest.raises(vb.VardaError, match="static scratch"):
-        vb.attention_split_noalloc(vb.FP32, rp, None, 0, 1, None, 65536, None, None, 65536, None, 65536, None, 65536,
-                                   w, 65536, 1024, 64, 64)
+        vb.attention_split_noalloc(vb.FP32, rp, ed, 0, 1, row, C, row, row, C, row, C, row, C, w, C, 1024, 64, 64)
     with pytest.raises(vb.VardaError, match="splits"):
-        vb.attention_split_noalloc(vb.FP32, rp, None, 0, 1, None, 256, None, None, 256, None, 256, None, 256,
-                                   w, 256, 4, 64, 0)
+        vb.attention_split_noalloc(vb.FP32, rp, ed, 0, 1, row, 256, row, row, 256, row, 256, row, 256, w, 256, 4, 64, 0)
+    with pytest.raises(vb.VardaError, match="non-null"):
+        vb.attention_split_noalloc(vb.FP32, rp, ed, 0, 1, None, 256, row, row, 256, row, 256, row, 256, w, 256, 4, 64, 2)
+    with pytest.raises(vb.VardaError, match="at least C"):
+        vb.attention_split_noalloc(vb.FP32, rp, ed, 0, 1, row, 128, row, row, 256, row, 256, row, 256, w, 256, 4, 64, 2)
     vb.check_device()

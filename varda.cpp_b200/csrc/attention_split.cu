@@ -313,6 +313,10 @@ void attention_split_noalloc(const AttnArgs<T>& a, int splits, cudaStream_t s) {
     if (a.heads < 1 || a.C != a.heads * a.head_dim) fail(kInvalidArgument, "attention_split: C != heads x head_dim");
     if (a.n_rows < 0 || a.dst_lo < 0) fail(kInvalidArgument, "attention_split: bad destination range");
     if (a.n_rows == 0) return;
+    if (!a.row_ptr || !a.edges || !a.q || !a.k || !a.v || !a.xr || !a.out || !a.w_e)
+        fail(kInvalidArgument, "attention_split: row_ptr, edges, q, k, v, x_r, out and w_e must be non-null");
+    if (a.ldq < a.C || a.ldkv < a.C || a.ldxr < a.C || a.ldo < a.C)
+        fail(kInvalidArgument, "attention_split: leading dimensions must be at least C");
     const size_t vb = 4 * sizeof(T);  // the kernels move 4 channels at a time
     if (a.ldq % 4 || a.ldkv % 4 || a.ldxr % 4 || a.ldo % 4 || !aligned(a.q, vb) || !aligned(a.k, vb) ||
         !aligned(a.v, vb) || !aligned(a.xr, vb) || !aligned(a.out, vb) || !aligned(a.edges, 16))

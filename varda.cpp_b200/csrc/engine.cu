@@ -208,6 +208,9 @@ private:
     int dev_ = 0;
     cudaStream_t stream_ = nullptr;
     bool use_tc_ = false;
+    // the dynamic tile order's counter of this model's GEMMs (all on its stream, one at a time)
+    DeviceBuffer gemm_sched_;
+    unsigned* sched_ = nullptr;
     int C_ = 0, heads_ = 0, hd_ = 0, mlp_ = 0, n_proc_ = 0, T_in_ = 0, T_out_ = 0, V_in_ = 0, V_out_ = 0, V_dec_ = 0;
     int A_node_ = 0, F_ = 0;
     int64_t ldF_ = 0, ldA_ = 0, ldVo_ = 0;
@@ -553,6 +556,11 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     const bool fp16 = !std::is_same<T, float>::value;
     use_tc_ = fp16 && opts_.gemm == 0 && env_int("VB_GEMM_SIMT", 0) == 0;
     VB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    if (env_int("VB_GEMM_SCHED", 1) != 0) {
+        gemm_sched_.alloc(2 * sizeof(unsigned));
+        VB_CUDA(cudaMemset(gemm_sched_.get(), 0, 2 * sizeof(unsigned)));
+        sched_ = gemm_sched_.as<unsigned>();
+    }
 
     // ---- normaliser, residual, bounding
     const TensorView& mul = file.take("norm.mul", DType::F32, {c.n_data_vars});
@@ -789,7 +797,7 @@ void Engine<T>::linear(const Dense<T>& L, const T* x, int64_t ldx, T* y, int64_t
             Span sp(this, s, "gemm_tc M=" + std::to_string(M) + " N=" + std::to_string(L.out) + " K=" +
                                  std::to_string(L.in) + " epi=" + std::to_string(epi),
                     2.0 * double(M) * double(L.out) * double(L.in), 0);
-            tc::gemm(a, s);
+            tc::gemm(a, s, sched_);
             return;
         }
     }

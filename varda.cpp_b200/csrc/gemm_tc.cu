@@ -697,17 +697,20 @@ CUtensorMap make_map(const __half* base, int64_t rows, int64_t cols, int64_t ld,
     return m;
 }
 
-// Per-stream tile counters for the dynamic tile order (g_sched, two words per stream: tiles handed
-// out, fetchers done; each launch leaves them zero). Launches on one stream run one after another, so a
-// counter per (device, stream) is never shared by two running launches; cudaStreamPerThread gets one
-// per thread. Static order (nullptr) when VB_GEMM_SCHED=0, when the slots are used up, or when the
-// first launch on a device comes during stream capture (the symbol lookup may load the module).
+// Per-stream tile counters for the dynamic tile order of launches that bring no counter of their own
+// (the public vb_gemm with VB_GEMM_SCHED=1): g_sched, two words per (device, stream, thread): tiles
+// handed out, fetchers done; each launch leaves them zero. Launches on one stream run one after
+// another, so such a counter is shared only by launches that run concurrently on the same stream key,
+// which a CUDA graph replayed on another stream (or twice at once) can do: the public entry point
+// therefore uses the static order unless asked. Static order (nullptr) also when the slots are used up,
+// or when the first launch on a device comes during stream capture (the symbol lookup may load the
+// module).
 constexpr int kSchedSlots = 1024, kMaxDevices = 64;
 __device__ unsigned g_sched[2 * kSchedSlots];
 
 unsigned* sched_counter(cudaStream_t s) {
     const char* e = std::getenv("VB_GEMM_SCHED");
-    if (e && *e && std::atoi(e) == 0) return nullptr;
+    if (!(e && *e && std::atoi(e) != 0)) return nullptr;
     int dev = 0;
     VB_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return nullptr;
@@ -736,7 +739,7 @@ unsigned* sched_counter(cudaStream_t s) {
 int sm_count() { return device_sm_count(); }
 
 template <int BN, int STAGES, int EPI, bool PAIR>
-void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
+void launch(const k::GemmArgs<__half>& a, cudaStream_t s, unsigned* sched) {
     using L = Layout<BN, STAGES, EPI, PAIR>;
     static std::atomic<uint64_t> configured{0};  // per instantiation and device
     once_per_device(configured, [] {
@@ -747,7 +750,7 @@ void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
     const CUtensorMap tb = make_map(a.W, a.N, a.K, a.ldw, PAIR ? BN / 2 : BN);
     // 32 x 32 sub-tiles of the output, 64-byte swizzle: the epilogue's TMA stores
     const CUtensorMap tc = make_map(a.C, a.M, a.N, a.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-    Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0, sched_counter(s)};
+    Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0, sched};
     constexpr int UM = PAIR ? 2 * BM : BM;
     const int64_t tiles = ((a.M + UM - 1) / UM) * ((a.N + BN - 1) / BN);
     if (!PAIR) {
@@ -773,17 +776,17 @@ void launch(const k::GemmArgs<__half>& a, cudaStream_t s) {
 
 // stage counts: as deep as the 227 KB of shared memory allows next to the epilogue staging
 template <int BN>
-void dispatch_epi(const k::GemmArgs<__half>& a, cudaStream_t s) {
+void dispatch_epi(const k::GemmArgs<__half>& a, cudaStream_t s, unsigned* sched) {
     constexpr int S = BN == 256 ? 4 : 6;
     // CTA pairs (cta_group::2) for N > 128 unless VB_GEMM_PAIR=0: on C1's shapes 3-8% faster than single
     // CTAs (each SM loads half of W per tile: a third less L2-to-SM traffic)
     const char* pe = std::getenv("VB_GEMM_PAIR");
     const bool pair = BN == 256 && !(pe && *pe && std::atoi(pe) == 0) && a.M >= 2 * BM;
     switch (a.epi) {
-        case k::kEpiBias: pair ? launch<BN, 6, k::kEpiBias, true>(a, s) : launch<BN, S, k::kEpiBias, false>(a, s); break;
-        case k::kEpiGelu: pair ? launch<BN, 6, k::kEpiGelu, true>(a, s) : launch<BN, S, k::kEpiGelu, false>(a, s); break;
+        case k::kEpiBias: pair ? launch<BN, 6, k::kEpiBias, true>(a, s, sched) : launch<BN, S, k::kEpiBias, false>(a, s, sched); break;
+        case k::kEpiGelu: pair ? launch<BN, 6, k::kEpiGelu, true>(a, s, sched) : launch<BN, S, k::kEpiGelu, false>(a, s, sched); break;
         case k::kEpiResidual:
-            pair ? launch<BN, 6, k::kEpiResidual, true>(a, s) : launch<BN, S, k::kEpiResidual, false>(a, s);
+            pair ? launch<BN, 6, k::kEpiResidual, true>(a, s, sched) : launch<BN, S, k::kEpiResidual, false>(a, s, sched);
             break;
         default: fail(kInvalidArgument, "gemm: unknown epilogue");
     }
@@ -803,10 +806,12 @@ bool supported(const k::GemmArgs<__half>& a) {
     return true;
 }
 
-void gemm(const k::GemmArgs<__half>& a, cudaStream_t s) {
+void gemm(const k::GemmArgs<__half>& a, cudaStream_t s) { gemm(a, s, sched_counter(s)); }
+
+void gemm(const k::GemmArgs<__half>& a, cudaStream_t s, unsigned* sched) {
     if (!supported(a)) fail(kInvalidArgument, "tensor-core gemm: unsupported operand alignment");
-    if (a.N <= 128) dispatch_epi<128>(a, s);
-    else dispatch_epi<256>(a, s);
+    if (a.N <= 128) dispatch_epi<128>(a, s, sched);
+    else dispatch_epi<256>(a, s, sched);
 }
 
 int take_error() {

@@ -14,8 +14,13 @@ namespace vb::tc {
 // True when the operands meet the tensor-memory-access rules: 16-byte aligned base pointers and
 // row strides (multiples of 8 fp16 elements).
 bool supported(const k::GemmArgs<__half>& a);
-// Enqueues the GEMM on s (no allocation, no synchronisation; capturable).
+// Enqueues the GEMM on s (no allocation, no synchronisation; capturable). Static tile order, or with
+// VB_GEMM_SCHED=1 the dynamic order on a counter kept per (device, stream, thread).
 void gemm(const k::GemmArgs<__half>& a, cudaStream_t s);
+// The same with the dynamic tile order on the caller's counter: two unsigned words in device memory,
+// zero before the first launch and left zero by each launch; launches that may run at the same time
+// must not share one. nullptr: the static order. Both orders give the same bits.
+void gemm(const k::GemmArgs<__half>& a, cudaStream_t s, unsigned* sched);
 // Reads and clears the device-side error flag set when a bounded wait inside the kernel gave up
 // (synchronises the device). Returns 0 when no wait timed out.
 int take_error();
