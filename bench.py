@@ -1,7 +1,7 @@
 """Benchmark: ms per fp16 predict_step at the Varda shape, plus edge-attention
 HBM GB/s, on N B200s of one node.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c0|c3|c4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c0|c2|c3|c4]
 
 Prints one JSON line (rank 0). `value` is the device-resident time of one predict_step (the model's
 own input/output buffers, CUDA-graph replay, CUDA events on the model's stream, max over ranks);
@@ -11,6 +11,14 @@ D2H of y inside the timed region; the library overlaps them with the compute in 
 edges gather, mostly L2 hits), both from one eager pass with a CUDA event pair around every launch
 (vb_profile_forward). `cpu_baseline` is the reference's own CPU fp32 backend
 (oracle/_ref/ref_dump, built from the reference's sources) timed on this host on a bounded sample.
+
+--workload c2 is the isolated processor block (the C1 hidden graph, 189,809 rows,
+2.63M edges with U[0,1) attributes, C=1024, fp16, N(0,1) node features) through vb_processor_block:
+`value` = device ms per block run (LN_dst + the block, K runs on the same input, sharded runs exchanging
+the K|V halo every run), `e2e` = the same with the host fp32 features copied in and the output copied
+back every run. Its `cpu_baseline` / reference arm is the reference CPU backend's time per processor
+block: ref_dump on models with 3 and with 1 block over the same 1/8 sample of the graph, half the
+difference, scaled by the row count (C2_SAMPLE_FACTOR).
 
 --workload c4 is the 24-step autoregressive rollout of C1: K rollout steps through
 vb_rollout (CUDA graph per step, forcings replayed from the host, every step's output copied back to
@@ -92,6 +100,27 @@ def reference_cpu(steps, warmup, threads=0):
     rec = json.loads(r.stdout.strip().splitlines()[-1])
     times = rec["steps_s"][warmup:]
     return times, rec["threads"], SAMPLE_FACTOR
+
+
+def reference_cpu_c2(steps, warmup):
+    """The reference's CPU fp32 backend per processor block of C2: ref_dump on the c2s1 and c2s3 models
+    (1 and 3 processor blocks over the first 1/8 of the C2 graph's rows with the edges among them; the
+    encoder, decoder and I/O identical in both), half the per-step difference, scaled by the row count
+    (the block's GEMMs, which dominate it on the CPU, are linear in rows)."""
+    if not os.path.exists(REF_DUMP):
+        raise FileNotFoundError(f"{REF_DUMP} missing (make -C oracle with the reference sources)")
+    from varda_b200 import safetensors as st
+    recs = {}
+    for name in ("c2s1", "c2s3"):
+        mp, xp = model_paths(name)
+        r = subprocess.run([REF_DUMP, "--model", mp, "--input", xp, "--steps", str(warmup + steps)],
+                           capture_output=True, text=True, check=True)
+        recs[name] = json.loads(r.stdout.strip().splitlines()[-1])
+    hs = int(json.loads(st.read(model_paths("c2s1")[0])[1]["config"])["dims"]["n_hidden_nodes"])
+    f = 189_809 / hs
+    t1, t3 = recs["c2s1"]["steps_s"][warmup:], recs["c2s3"]["steps_s"][warmup:]
+    times = [(b - a) / 2 * f for a, b in zip(t1, t3)]
+    return times, recs["c2s1"]["threads"], hs
 
 
 # ------------------------------------------------------------------ clocks
@@ -265,6 +294,64 @@ def run_rollout(args, rank, world, local_rank):
                 n_launch_timed=vb.launch_count() - n_launch0)
 
 
+def run_c2(args, rank, world, local_rank):
+    """C2: the isolated processor block through vb_processor_block on this rank's hidden rows."""
+    import torch
+    import varda_b200 as vb
+    from varda_b200 import synth
+
+    m, mp, xp, dist, load_s = load_model(args, rank, world, local_rank)
+    rows = m.hidden_hi - m.hidden_lo
+    z = synth.c2_features(m.H, m.C)[m.hidden_lo:m.hidden_hi]
+    zin = torch.from_numpy(np.ascontiguousarray(z)).pin_memory().numpy()
+    zout = torch.empty((rows, m.C), dtype=torch.float32).pin_memory().numpy()
+    stream = torch.cuda.ExternalStream(m.stream(), device=f"cuda:{local_rank}")
+    # the timed runs are short: the clock sampler runs from before the warm-up through the e2e runs
+    clk = Clocks(local_rank)
+    time.sleep(0.5)
+    for _ in range(args.warmup):
+        m.processor_block(0, zin, zout)
+    assert np.isfinite(zout).all(), "processor block output not finite"
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    n_launch0 = vb.launch_count()
+    _, total_ms = m.processor_block(0, None, None, repeats=args.steps)
+    ms = total_ms / args.steps
+    n_launch = vb.launch_count() - n_launch0
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        m.processor_block(0, zin, zout)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    clocks = clk.stop()
+    clocks["window"] = "warm-up through the e2e runs"
+    prof = m.profile_block(0)
+    vb.check_device()
+    if dist:
+        t = torch.tensor([ms, e2e_ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    return dict(m=m, ms=ms, e2e_ms=e2e_ms, clocks=clocks, prof=prof, load_s=load_s, h2d=rows * m.C * 4,
+                d2h=rows * m.C * 4, launches=n_launch / args.steps, dist=dist, n_launch_timed=n_launch,
+                rows=rows)
+
+
+def halo_ms_per_rank(prof, dist):
+    """Milliseconds each rank spent in the halo records (pack, NCCL exchange including the wait for
+    the slowest peer, unpack) of its profiled pass; rank 0 gets the list."""
+    own = round(sum(r["ms"] for r in prof if r["name"].startswith("halo")), 3)
+    if not dist:
+        return [own]
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, own)
+    return out
+
+
 TRAFFIC = os.path.join(HERE, "profiles", "c1_traffic.json")
 
 
@@ -334,7 +421,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c1", choices=["c1", "c0", "c3", "c4"])
+    ap.add_argument("--workload", default="c1", choices=["c1", "c0", "c2", "c3", "c4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-out", default=None, help="write the per-launch profile records (JSON) here")
     args = ap.parse_args()
@@ -359,7 +446,28 @@ def main():
         config["workload"] = (f"C4: {args.steps}-step autoregressive rollout of C1 in fp16 (CUDA graph per step, "
                               "synthetic sin/cos forcings replayed from the host, outputs streamed back)")
         metric = "ms/rollout step fp16 at Varda shape"
+    if args.workload == "c2":
+        config["workload"] = ("C2: one isolated processor block, fp16 (LN_dst + q|k|v|self GEMM + edge attention + "
+                              "proj/residual + LN + MLP), H=189,809 hidden rows, 2,561,682 edges (in-degree 11-54), "
+                              "U[0,1) edge attributes, C=1024, 16 heads of 64, N(0,1) node features")
+        metric = "ms/processor block fp16 at C2 shape"
 
+    if args.impl == "reference" and args.workload == "c2":
+        if rank != 0:
+            return
+        times, threads, hs = reference_cpu_c2(args.steps, args.warmup)
+        v = statistics.median(times) * 1000
+        line = {"impl": "reference", "metric": metric, "value": round(v, 2), "unit": "ms", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 2), "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+                "config": config,
+                "cpu_baseline": {"value": round(v, 2), "unit": "ms", "cores": threads, "kind": "reference",
+                                 "sample": f"reference CPU fp32 backend (oracle/_ref/ref_dump) on 1/8 of the C2 rows "
+                                           f"({hs} rows): (3-block step - 1-block step) / 2, x {189809 / hs:.3f}; "
+                                           f"median of {len(times)}"},
+                "e2e": {"value": round(v, 2), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if args.impl == "reference":
         if rank != 0:
             return
@@ -382,8 +490,11 @@ def main():
         args.workload = "c1"  # the rollout runs the C1 model
         r = run_rollout(args, rank, world, local_rank)
         args.workload = "c4"
+    elif args.workload == "c2":
+        r = run_c2(args, rank, world, local_rank)
     else:
         r = run_ours(args, rank, world, local_rank)
+    halo = halo_ms_per_rank(r["prof"], r["dist"]) if world > 1 else None
     roof, edge, shares, prof_total = summarise(r["prof"], pk, src)
     if edge is not None and world == 1:
         try:  # secondary figure: never in the way of the bench line
@@ -396,6 +507,14 @@ def main():
         with open(args.profile_out, "w") as fh:
             json.dump(r["prof"], fh, indent=0)
     cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "c2":
+        try:
+            times, threads, hs = reference_cpu_c2(2, 1)
+            cpu = {"value": round(statistics.median(times) * 1000, 1), "unit": "ms", "cores": threads,
+                   "kind": "reference", "sample": f"reference CPU fp32 backend (oracle/_ref/ref_dump) per processor "
+                   f"block on 1/8 of the C2 rows ({hs}): (3-block - 1-block step) / 2, scaled by rows"}
+        except Exception as e:
+            cpu = {"value": None, "unit": "ms", "error": str(e)[:200]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("c1", "c4"):
         try:
             times, threads, f = reference_cpu(2, 1)
@@ -417,6 +536,10 @@ def main():
                 "kernel_shares": shares, "profiled_forward_ms": round(prof_total, 3), "load_s": round(r["load_s"], 1)}
         if "step_ms" in r:
             line["rollout"] = {"step_ms": r["step_ms"], "wall_s": round(r["wall_s"], 3)}
+        if halo is not None:
+            line["halo_ms_per_rank"] = halo
+        if args.workload == "c2":
+            line["gpu_launches"] = int(round(r["launches"] * args.steps))
         print(json.dumps(line), flush=True)
     if r["dist"]:
         r["dist"].barrier()

@@ -94,6 +94,8 @@ int vb_rollout(vb_model* m, const float* x0, int n_steps, const float* forcings,
  * T_out G V_out (cuda/cuda_backend.h:34-35). */
 int vb_sizes(const vb_model* m, int64_t out8[8]);
 int vb_data_range(const vb_model* m, int64_t* lo, int64_t* hi);
+/* This rank's hidden-node range [lo, hi): the processor's destination rows (all of [0, H) on one GPU). */
+int vb_hidden_range(const vb_model* m, int64_t* lo, int64_t* hi);
 /* Element counts of the device tensors of this rank: x/xn (T_in, G_local, V_in) and yn/y
  * (T_out, own data rows, V_out); on one GPU input_numel / output_numel (cuda_backend.h:34-35). On a
  * sharded model G_local = own data rows followed by the encoder's halo rows: the caller fills the own
@@ -130,6 +132,20 @@ int vb_check_device(void);
  * the length it needs (call again with a larger buffer if that exceeds len). Synchronises. */
 int64_t vb_launch_count(void);
 int64_t vb_profile_forward(vb_model* m, char* buf, size_t len);
+
+/* The isolated processor block (the benchmark's C2 workload; the reference runs it only inside
+ * predict_step: CpuBackend::processor, source_side then destination_side per block,
+ * src/varda/cpu/backend_cpu.cpp:400-415, and the processor loop of src/varda/cuda/backend_cuda.cu:
+ * 571-590 on the GPU): LN_dst then processor block `block`, `repeats` times on the same input, this
+ * rank's hidden rows (vb_hidden_range). z_in: host fp32 [own hidden rows, C], or NULL to keep the
+ * previous call's input (a forward pass in between overwrites it); z_out: host fp32 [own hidden rows,
+ * C] receiving the block's output, or NULL. device_ms (may be NULL): device time of the runs, CUDA
+ * events on the model's stream, the copies excluded. On a sharded model every run exchanges the K|V
+ * halo: all ranks call it together. Synchronises. vb_profile_processor_block: one such run with an
+ * event pair around every launch, records as vb_profile_forward. No reference counterpart as entry
+ * points (benchmark and test instruments). */
+int vb_processor_block(vb_model* m, int block, const float* z_in, float* z_out, int repeats, float* device_ms);
+int64_t vb_profile_processor_block(vb_model* m, int block, char* buf, size_t len);
 
 /* The destination partition vb_load_sharded uses for `rank` of `world` on this model file, computed
  * on the host only (no GPU): JSON with the hidden/data ranges of every rank (and the encoder's hidden

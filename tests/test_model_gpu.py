@@ -194,3 +194,36 @@ def test_wide_rows_by_parts(name, dt, seeded_model, monkeypatch):
     y = vb.Model.load(mp, precision=dt).predict_step(x)
     vb.check_device()
     assert oracle.rel_absmax(y, golden(name)["out.y"]) <= TOL[dt]
+
+
+@pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])
+@pytest.mark.parametrize("name", ["t256", "t1024", "c0"])
+def test_processor_block_entry(name, dt, seeded_model):
+    """vb_processor_block (the isolated C2 block) on a block's input from a hooked forward pass gives
+    that block's output bitwise (the same kernels on the same rows), and the oracle's within the
+    contract tolerance; repeats run on the same input; a NULL z_in keeps the previous input."""
+    mp, xp = seeded_model(name)
+    x = np.array(st.read(xp)[0]["in.x"])
+    m = vb.Model.load(mp, precision=dt)
+    acts = {}
+    m.predict_step(x, hook=lambda k, a: acts.__setitem__(k, a))
+    want = oracle_acts(name, mp, x)
+    assert (m.hidden_lo, m.hidden_hi) == (0, m.H)
+    prev = "enc.out"
+    for i in range(m.n_proc):
+        z, ms = m.processor_block(i, acts[prev], True, repeats=2)
+        assert ms > 0
+        key = f"proc.{i}.out"
+        assert np.array_equal(z, acts[key]), f"{key}: the block entry point differs from the forward pass"
+        assert oracle.rel_absmax(z, want[key]) <= TOL[dt], key
+        prev = key
+    z2, _ = m.processor_block(m.n_proc - 1, None, True)
+    assert np.array_equal(z2, z), "a NULL z_in keeps the previous call's input"
+    rec = m.profile_block(0)
+    assert any(r["name"] == "attention proc" for r in rec) and any(r["name"].startswith("gemm") for r in rec)
+    vb.check_device()
+    with pytest.raises(vb.VardaError):
+        m.processor_block(m.n_proc, None, None)
+    with pytest.raises(vb.VardaError):
+        m.processor_block(0, None, None, repeats=0)
+    m.free()

@@ -1,5 +1,6 @@
 """Multi-GPU destination partition on B200s (skipped with fewer than 2 visible GPUs): one process per
-GPU, NCCL halo exchange; every rank's output rows must be bitwise equal to the single-GPU result
+GPU, NCCL halo exchange; every rank's output rows (of predict_step, and of the isolated processor
+block vb_processor_block with its K|V halo exchange) must be bitwise equal to the single-GPU result
 (the partition keeps every destination's edge order and every GEMM row's arithmetic, and, on graphs of
 at least 128 hidden rows per GPU, the tensor-core attention's tiles), with and without the encoder
 split. On smaller graphs the hidden ranges are not on the tiles' 64-row grid, so those models run the
@@ -36,9 +37,15 @@ def _worker(rank, world, mp, xp, dtype, uid_path, out_dir):
         y = np.full(m.output_shape, np.nan, np.float32)
         m.predict_step(x, y)
         ys.append(y[:, :, :, m.data_lo:m.data_hi].copy())
+    zb, _ = m.processor_block(0, _block_input(m)[m.hidden_lo:m.hidden_hi], True)  # the isolated block (C2)
     vb.check_device()
-    np.savez(os.path.join(out_dir, f"r{rank}.npz"), y0=ys[0], y1=ys[1], y2=ys[2], lo=m.data_lo, hi=m.data_hi)
+    np.savez(os.path.join(out_dir, f"r{rank}.npz"), y0=ys[0], y1=ys[1], y2=ys[2], lo=m.data_lo, hi=m.data_hi,
+             zb=zb, hlo=m.hidden_lo, hhi=m.hidden_hi)
     m.free()
+
+
+def _block_input(m):
+    return np.random.default_rng(5).standard_normal((m.H, m.C), dtype=np.float32)
 
 
 def _single(mp, xp, dtype, out):
@@ -48,6 +55,7 @@ def _single(mp, xp, dtype, out):
     m = vb.Model.load(mp, precision=dtype)
     y = m.predict_step(np.array(st.read(xp)[0]["in.x"]))
     np.save(out, y)
+    np.save(out + ".block.npy", m.processor_block(0, _block_input(m), True)[0])
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -74,16 +82,20 @@ def test_sharded_equals_single_gpu(name, enc_split, dtype, seeded_model, tmp_pat
     p.join(300)
     assert p.exitcode == 0
     y1 = np.load(tmp_path / "single.npy")
+    zb1 = np.load(str(tmp_path / "single.npy") + ".block.npy")
     tmp.start_processes(_worker, args=(world, mp, xp, dtype, str(tmp_path / "uid"), str(tmp_path)), nprocs=world,
                         join=True, start_method="spawn")
-    covered = 0
+    covered = hidden = 0
     for r in range(world):
         z = np.load(tmp_path / f"r{r}.npz")
         lo, hi = int(z["lo"]), int(z["hi"])
         covered += hi - lo
         for k in ("y0", "y1", "y2"):
             assert np.array_equal(z[k], y1[:, :, :, lo:hi]), f"rank {r} {k} differs from one GPU"
-    assert covered == y1.shape[3]
+        hlo, hhi = int(z["hlo"]), int(z["hhi"])
+        hidden += hhi - hlo
+        assert np.array_equal(z["zb"], zb1[hlo:hhi]), f"rank {r}: the isolated block differs from one GPU"
+    assert covered == y1.shape[3] and hidden == zb1.shape[0]
 
 
 def _rollout_worker(rank, world, mp, xp, fp, dtype, uid_path, out_dir):

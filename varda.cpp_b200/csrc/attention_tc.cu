@@ -37,6 +37,7 @@
 // Every mbarrier wait is bounded (4 s of %globaltimer): on timeout the CTA sets the device error flag
 // (read by take_attention_error), stops, and the producers drain their own copies before returning.
 #include <cmath>
+#include <cstdlib>
 #include <string>
 
 #include "common.h"
@@ -97,14 +98,16 @@ __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait; false on timeout (flags raised) or when another warp of the CTA aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+// Bounded wait (limit_ns of %globaltimer); false on timeout (flags raised) or when another warp of the
+// CTA aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag,
+                                          unsigned long long limit_ns) {
     if (mbar_test(b, parity)) return true;
     const uint64_t t0 = now_ns();
     for (;;) {
         if (mbar_test(b, parity)) return true;
         if (*abort_flag) return false;
-        if (now_ns() - t0 > kTimeoutNs) {
+        if (now_ns() - t0 > limit_ns) {
             *abort_flag = 1;
             atomicExch(&g_tc_error, 1);
             return false;
@@ -178,6 +181,8 @@ struct TcParams {
     const float* w_e;  // [4, C] fp32 (fp16-representable values)
     int C, heads;
     float scale_log2;
+    unsigned long long wait_ns;  // limit of every wait (kTimeoutNs; shorter in the failure-path test)
+    int withhold;                // failure-path test only: CTA 0 leaves its first head stage unfilled
 };
 
 __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParams p) {
@@ -227,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
         for (int ti = blockIdx.x; ti < p.ntiles && ok; ti += gridDim.x, ++tc) {
             const TcTile t = p.tiles[p.tile0 + ti];
             const int tb = tc & 1;
-            ok = __all_sync(kFull, mbar_wait(&empty_t[tb], ((tc >> 1) & 1) ^ 1, abort_flag));
+            ok = __all_sync(kFull, mbar_wait(&empty_t[tb], ((tc >> 1) & 1) ^ 1, abort_flag, p.wait_ns));
             if (!ok) break;
             if (pl == 0) {
                 mbar_expect_tx(&full_t[tb], uint32_t(t.blob_bytes));
@@ -245,10 +250,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
             const int64_t qrow = int64_t(t.row0) - p.dst_lo;
             for (int h = 0; h < heads; ++h, ++hc) {
                 const int s = int(hc % kStages);
-                ok = __all_sync(kFull, mbar_wait(&empty_h[s], uint32_t(((hc / kStages) & 1) ^ 1), abort_flag));
+                ok = __all_sync(kFull, mbar_wait(&empty_h[s], uint32_t(((hc / kStages) & 1) ^ 1), abort_flag, p.wait_ns));
                 if (!ok) break;
                 const uint32_t st = smem_u32(sm + kOffStage + s * kStageBytes);
                 const int col = h * kHD + pch * 8;
+                if (p.withhold && blockIdx.x == 0 && hc == 0) continue;  // no copies, no arrival: the wait runs out
 #pragma unroll
                 for (int i = 0; i < kRounds; ++i) {
                     if (srow[i] < 0) continue;
@@ -279,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
     int tc = 0;
     for (int ti = blockIdx.x; ti < p.ntiles; ti += gridDim.x, ++tc) {
         const int tb = tc & 1;
-        if (!__all_sync(kFull, mbar_wait(&full_t[tb], uint32_t((tc >> 1) & 1), abort_flag))) return;
+        if (!__all_sync(kFull, mbar_wait(&full_t[tb], uint32_t((tc >> 1) & 1), abort_flag, p.wait_ns))) return;
         const TcTile t = p.tiles[p.tile0 + ti];
         const uint8_t* bl = blobs + tb * kBlobMax;
         const uint16_t* roff = reinterpret_cast<const uint16_t*>(bl);
@@ -287,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
         const int nb = (t.nrows + 15) >> 4;
         for (int h = 0; h < heads; ++h, ++hc) {
             const int s = int(hc % kStages);
-            if (!__all_sync(kFull, mbar_wait(&full_h[s], uint32_t((hc / kStages) & 1), abort_flag))) return;
+            if (!__all_sync(kFull, mbar_wait(&full_h[s], uint32_t((hc / kStages) & 1), abort_flag, p.wait_ns))) return;
             const uint32_t kbase = smem_u32(sm + kOffStage + s * kStageBytes);
             const uint32_t vbase = kbase + kKVBytes, qbase = kbase + 2 * kKVBytes;
             const uint32_t wbase = smem_u32(wext + h * 1024);
@@ -503,6 +509,12 @@ void attention_tc(const TcArgs& a, cudaStream_t s) {
     p.ldq = a.ldq, p.ldkv = a.ldkv, p.ldxr = a.ldxr, p.ldo = a.ldo, p.n_q_rows = a.n_q_rows;
     p.w_e = a.w_e, p.C = a.C, p.heads = a.heads;
     p.scale_log2 = 1.4426950408889634f / std::sqrt(float(a.head_dim));
+    // failure-path test hooks (host-side, no fault): VB_DEBUG_WAIT_NS shortens every wait's limit and
+    // VB_DEBUG_TC_WITHHOLD=1 makes CTA 0 skip its first stage's copies, so its consumers' wait runs out
+    const char* wn = std::getenv("VB_DEBUG_WAIT_NS");
+    const char* wh = std::getenv("VB_DEBUG_TC_WITHHOLD");
+    p.wait_ns = wn && *wn ? std::strtoull(wn, nullptr, 10) : kTimeoutNs;
+    p.withhold = wh && *wh && std::atoi(wh) != 0;
     static std::atomic<uint64_t> configured{0};
     once_per_device(configured, [] {
         VB_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

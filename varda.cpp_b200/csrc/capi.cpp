@@ -146,6 +146,20 @@ int vb_data_range(const vb_model* m, int64_t* lo, int64_t* hi) {
     });
 }
 
+int vb_hidden_range(const vb_model* m, int64_t* lo, int64_t* hi) {
+    return guard([&] {
+        need(m, "model"), need(lo, "lo"), need(hi, "hi");
+        m->m->hidden_range(lo, hi);
+    });
+}
+
+int vb_processor_block(vb_model* m, int block, const float* z_in, float* z_out, int repeats, float* device_ms) {
+    return guard([&] {
+        need(m, "model");
+        m->m->processor_block(block, z_in, z_out, repeats, device_ms);
+    });
+}
+
 int vb_io_numel(const vb_model* m, int64_t* in, int64_t* out) {
     return guard([&] {
         need(m, "model"), need(in, "in"), need(out, "out");
@@ -237,6 +251,21 @@ int64_t vb_profile_forward(vb_model* m, char* buf, size_t len) {
     const int rc = guard([&] {
         need(m, "model");
         s = m->m->profile_forward();
+    });
+    if (rc != VB_OK) return -rc;
+    if (buf && len) {
+        const size_t n = std::min(len - 1, s.size());
+        std::memcpy(buf, s.data(), n);
+        buf[n] = 0;
+    }
+    return int64_t(s.size() + 1);
+}
+
+int64_t vb_profile_processor_block(vb_model* m, int block, char* buf, size_t len) {
+    std::string s;
+    const int rc = guard([&] {
+        need(m, "model");
+        s = m->m->profile_block(block);
     });
     if (rc != VB_OK) return -rc;
     if (buf && len) {

@@ -150,7 +150,11 @@ public:
         o[0] = T_in_, o[1] = G_, o[2] = V_in_, o[3] = T_out_, o[4] = V_out_, o[5] = H_, o[6] = C_, o[7] = n_proc_;
     }
     void data_range(int64_t* lo, int64_t* hi) const override { *lo = plan_.g_lo, *hi = plan_.g_hi; }
+    void hidden_range(int64_t* lo, int64_t* hi) const override { *lo = plan_.h_lo, *hi = plan_.h_hi; }
+    void processor_block(int block, const float* z_in, float* z_out, int repeats, float* device_ms) override;
     std::string profile_forward() override;
+    std::string profile_block(int block) override;
+    template <class F> std::string profiled(F body);
     void rollout(const float* x0, int n_steps, const float* forcings, float* y, bool constants_oldest, StepFn cb,
                  void* user, float* step_ms) override;
 
@@ -197,6 +201,10 @@ private:
     void enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64_t n, cudaStream_t s, HookSink* hk);
     void enc_dest_pre(cudaStream_t s, HookSink* hk);
     bool middle(cudaStream_t s, HookSink* hk);
+    void proc_block(int i, const T* z_in, T* z_out, bool overlap, cudaStream_t s);
+    // processor_block(): fp32 [H, C] host-copy staging and the events around its runs
+    DeviceBuffer blk_stage_;
+    cudaEvent_t blk_ev_[2] = {nullptr, nullptr};
     void dec_chunk(int64_t lo, int64_t n, cudaStream_t s, HookSink* hk, bool& halo_pending, float* h_emb, float* h_bo);
     void output_rows(const float* xn, float* yn, int64_t lo, int64_t n, cudaStream_t s, float* pre_bound);
     cudaGraphExec_t capture(const std::function<void(cudaStream_t)>& body, cudaStream_t s);
@@ -768,6 +776,8 @@ Engine<T>::~Engine() {
     if (cs_) cudaStreamSynchronize(cs_), cudaStreamDestroy(cs_);
     if (ev_kv_) cudaEventDestroy(ev_kv_);
     if (ev_halo_) cudaEventDestroy(ev_halo_);
+    for (cudaEvent_t e : blk_ev_)
+        if (e) cudaEventDestroy(e);
     comm_.reset();
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -943,6 +953,69 @@ void Engine<T>::enc_dest_pre(cudaStream_t s, HookSink* hk) {
     linear(enc_.proj_qx, xh_, C, qkvs_, 2 * C, H, s);
 }
 
+// Processor block i on this rank's hidden rows: xh_ holds LN_dst(z_in); z_out = the block's output.
+template <class T>
+void Engine<T>::proc_block(int i, const T* z_in, T* z_out, bool overlap, cudaStream_t s) {
+    const int64_t H = Hl_, C = C_;
+    const AttnLayer<T>& b = proc_[size_t(i)];
+    linear(b.proj_qkvx, xh_, C, qkvs_, 4 * C, H, s);
+    if (overlap) {
+        // K|V of remote sources on the communication stream while the interior rows run
+        VB_CUDA(cudaEventRecord(ev_kv_, s));
+        VB_CUDA(cudaStreamWaitEvent(cs_, ev_kv_, 0));
+        exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, cs_);
+        VB_CUDA(cudaEventRecord(ev_halo_, cs_));
+        attention_rows(g_proc_, b, proc_inner_, n_inner_, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C,
+                       4 * C, sbuf_, s);
+        VB_CUDA(cudaStreamWaitEvent(s, ev_halo_, 0));
+        attention_rows(g_proc_, b, proc_outer_, n_outer_, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C,
+                       4 * C, sbuf_, s);
+    } else {
+        exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, s);  // K|V of remote sources
+        attention(g_proc_, b, 0, H, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C, 4 * C, sbuf_, s);
+    }
+    linear(b.proj_out, sbuf_, C, out1_, C, H, s, k::kEpiResidual, z_in, C);
+    ln(out1_, b.norm_ffn, xh_, H, s);
+    linear(b.ffn_up, xh_, C, hbuf_, mlp_, H, s, k::kEpiGelu);
+    linear(b.ffn_down, hbuf_, mlp_, z_out, C, H, s, k::kEpiResidual, out1_, C);
+}
+
+// The isolated processor block (the benchmark's C2 workload): LN_dst then block `i`, `repeats` times on
+// the same input, on this rank's hidden rows (sharded: with the K|V halo exchange of every run).
+// z_in / z_out: host fp32 [own hidden rows, C]; a null z_in keeps the previous call's input, a null
+// z_out skips the read-back. device_ms: the device time of the runs (CUDA events on the model's stream
+// around them, the copies excluded). The block buffers are zA_ (input) and zB_ (output), which only a
+// forward pass otherwise uses.
+template <class T>
+void Engine<T>::processor_block(int i, const float* z_in, float* z_out, int repeats, float* device_ms) {
+    if (i < 0 || i >= n_proc_) fail(kInvalidArgument, "processor_block: no such block");
+    if (repeats < 1) fail(kInvalidArgument, "processor_block: repeats must be >= 1");
+    VB_CUDA(cudaSetDevice(dev_));
+    cudaStream_t s = stream_;
+    const int64_t H = Hl_, C = C_;
+    if (!blk_stage_.get()) blk_stage_ = DeviceBuffer(size_t(std::max<int64_t>(H * C, 1)) * sizeof(float));
+    float* stage = blk_stage_.as<float>();
+    if (z_in) {
+        VB_CUDA(cudaMemcpyAsync(stage, z_in, size_t(H * C) * sizeof(float), cudaMemcpyHostToDevice, s));
+        k::convert_2d<float, T>(stage, C, zA_, C, H, C, s);
+    }
+    const bool overlap = plan_.world > 1 && cs_ && !prof_ && !g_proc_.tiled && !g_proc_.wide &&
+                         env_int("VB_SHARD_OVERLAP", 1) != 0;
+    if (!blk_ev_[0]) VB_CUDA(cudaEventCreate(&blk_ev_[0])), VB_CUDA(cudaEventCreate(&blk_ev_[1]));
+    VB_CUDA(cudaEventRecord(blk_ev_[0], s));
+    for (int r = 0; r < repeats; ++r) {
+        ln(zA_, proc_[size_t(i)].norm_dst, xh_, H, s);
+        proc_block(i, zA_, zB_, overlap, s);
+    }
+    VB_CUDA(cudaEventRecord(blk_ev_[1], s));
+    if (z_out) {
+        k::convert_2d<T, float>(zB_, C, stage, C, H, C, s);
+        VB_CUDA(cudaMemcpyAsync(z_out, stage, size_t(H * C) * sizeof(float), cudaMemcpyDeviceToHost, s));
+    }
+    VB_CUDA(cudaStreamSynchronize(s));
+    if (device_ms) VB_CUDA(cudaEventElapsedTime(device_ms, blk_ev_[0], blk_ev_[1]));
+}
+
 // From the encoder attention to the decoder's source side ([k | v] of LN_src(latent) and its halo).
 // Returns whether the decoder halo exchange is still in flight on the communication stream.
 template <class T>
@@ -970,28 +1043,8 @@ bool Engine<T>::middle(cudaStream_t s, HookSink* hk) {
     T* z_in = z_enc_;
     T* latent = nullptr;
     for (int i = 0; i < n_proc_; ++i) {
-        const AttnLayer<T>& b = proc_[size_t(i)];
-        linear(b.proj_qkvx, xh_, C, qkvs_, 4 * C, H, s);
-        if (overlap) {
-            // K|V of remote sources on the communication stream while the interior rows run
-            VB_CUDA(cudaEventRecord(ev_kv_, s));
-            VB_CUDA(cudaStreamWaitEvent(cs_, ev_kv_, 0));
-            exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, cs_);
-            VB_CUDA(cudaEventRecord(ev_halo_, cs_));
-            attention_rows(g_proc_, b, proc_inner_, n_inner_, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C,
-                           qkvs_ + 3 * C, 4 * C, sbuf_, s);
-            VB_CUDA(cudaStreamWaitEvent(s, ev_halo_, 0));
-            attention_rows(g_proc_, b, proc_outer_, n_outer_, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C,
-                           qkvs_ + 3 * C, 4 * C, sbuf_, s);
-        } else {
-            exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, s);  // K|V of remote sources
-            attention(g_proc_, b, 0, H, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C, 4 * C, sbuf_, s);
-        }
-        linear(b.proj_out, sbuf_, C, out1_, C, H, s, k::kEpiResidual, z_in, C);
-        ln(out1_, b.norm_ffn, xh_, H, s);
-        linear(b.ffn_up, xh_, C, hbuf_, mlp_, H, s, k::kEpiGelu);
         T* z_out = z_in == zA_ ? zB_ : zA_;
-        linear(b.ffn_down, hbuf_, mlp_, z_out, C, H, s, k::kEpiResidual, out1_, C);
+        proc_block(i, z_in, z_out, overlap, s);
         if (hk) hk->emit("proc." + std::to_string(i) + ".out", z_out, C, H, C, {H, C});
         if (i + 1 < n_proc_) {
             k::layernorm<T>(z_out, C, proc_[size_t(i + 1)].norm_dst.g(), proc_[size_t(i + 1)].norm_dst.b(), xh_, C, H,
@@ -1115,6 +1168,9 @@ cudaGraphExec_t Engine<T>::capture(const std::function<void(cudaStream_t)>& body
     VB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     std::string err;
     try {
+        // failure-path test hook (host side): VB_DEBUG_CAPTURE_FAIL=1 fails every capture as a throwing
+        // launch inside it would, so the caller's fallback to eager runs is exercised
+        if (env_int("VB_DEBUG_CAPTURE_FAIL", 0) != 0) fail(kInternal, "capture failure injected (VB_DEBUG_CAPTURE_FAIL)");
         body(s);
     } catch (const std::exception& e) {
         err = e.what();
@@ -1533,13 +1589,27 @@ void Engine<T>::rollout(const float* x0, int n, const float* forcings, float* y,
 
 template <class T>
 std::string Engine<T>::profile_forward() {
+    return profiled([&] {
+        normalise(x_dev_, xn_, stream_);
+        forward(xn_, yn_, stream_, nullptr);
+    });
+}
+
+template <class T>
+std::string Engine<T>::profile_block(int block) {
+    return profiled([&] { processor_block(block, nullptr, nullptr, 1, nullptr); });
+}
+
+// Runs body() eagerly with an event pair around every launch; the records as a JSON array.
+template <class T>
+template <class F>
+std::string Engine<T>::profiled(F body) {
     VB_CUDA(cudaSetDevice(dev_));
     std::vector<ProfRec> recs;
     prof_ = &recs;
     std::string out = "[";
     try {
-        normalise(x_dev_, xn_, stream_);
-        forward(xn_, yn_, stream_, nullptr);
+        body();
         VB_CUDA(cudaStreamSynchronize(stream_));
     } catch (...) {
         prof_ = nullptr;

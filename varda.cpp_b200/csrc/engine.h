@@ -52,10 +52,19 @@ public:
     virtual void sizes(int64_t out[8]) const = 0;
     // multi-GPU: this rank's data-node range [lo, hi)
     virtual void data_range(int64_t* lo, int64_t* hi) const = 0;
+    // multi-GPU: this rank's hidden-node range [lo, hi) (the processor's destination rows)
+    virtual void hidden_range(int64_t* lo, int64_t* hi) const = 0;
+    // The isolated processor block: LN_dst then processor block `block`, `repeats` times on the same
+    // input, this rank's hidden rows (sharded: the K|V halo exchange every run, a collective). z_in /
+    // z_out host fp32 [own hidden rows, C] or null (keep the previous call's input / no read-back);
+    // device_ms: device time of the runs. Synchronises.
+    virtual void processor_block(int block, const float* z_in, float* z_out, int repeats, float* device_ms) = 0;
     // One eager forward_normalised on the internal buffers with a CUDA event pair around every
     // launch; returns a JSON array of {"name", "ms", "flop", "bytes"} records (algorithmic FLOPs
     // of the GEMMs, compulsory bytes of the bandwidth-bound kernels). Synchronises.
     virtual std::string profile_forward() = 0;
+    // The same for one run of processor_block(block) on the current block input.
+    virtual std::string profile_block(int block) = 0;
     // Device-resident autoregressive rollout with replayed forcings (include/varda_b200.h vb_rollout):
     // x0 (1, T_in, G, V_in) and forcings (n_steps - 1, G, F) full host arrays; y (n_steps, G, V_out)
     // receives this rank's rows when not null; cb gets each step's rows when not null; step_ms

@@ -60,6 +60,9 @@ def _load_lib():
         "vb_launch_count": ([], I64),
         "vb_shard_plan": ([ctypes.c_char_p, I, I, ctypes.c_char_p, SZ], I64),
         "vb_profile_forward": ([P, ctypes.c_char_p, SZ], I64),
+        "vb_hidden_range": ([P, P, P], I),
+        "vb_processor_block": ([P, I, P, P, I, P], I),
+        "vb_profile_processor_block": ([P, I, ctypes.c_char_p, SZ], I64),
         "vb_build_csr": ([P, I64, P, I, I64, I64, P, P, P, P], I),
         "vb_pack_edges": ([P, P, I, I64, I, P], I),
         "vb_attention": ([I, P, P, I64, I64, P, I64, P, P, I64, P, I64, P, I64, P, I, I, I, P], I),
@@ -149,6 +152,8 @@ class Model:
         lo, hi = ctypes.c_int64(), ctypes.c_int64()
         check(lib.vb_data_range(self._h, ctypes.byref(lo), ctypes.byref(hi)))
         self.data_lo, self.data_hi = lo.value, hi.value
+        check(lib.vb_hidden_range(self._h, ctypes.byref(lo), ctypes.byref(hi)))
+        self.hidden_lo, self.hidden_hi = lo.value, hi.value
         i, o = ctypes.c_int64(), ctypes.c_int64()
         check(lib.vb_io_numel(self._h, ctypes.byref(i), ctypes.byref(o)))
         self.device_input_numel, self.device_output_numel = i.value, o.value
@@ -272,15 +277,31 @@ class Model:
     def profile(self):
         """One eager forward with a CUDA event pair around every launch: list of
         {"name", "ms", "flop", "bytes"} records."""
-        import json
-        n = lib.vb_profile_forward(self._h, None, 0)
-        if n < 0:
-            check(-n)
-        buf = ctypes.create_string_buffer(int(n) + 1024)
-        n = lib.vb_profile_forward(self._h, buf, len(buf))
-        if n < 0:
-            check(-n)
-        return json.loads(buf.value.decode())
+        return _records(lambda buf, n: lib.vb_profile_forward(self._h, buf, n))
+
+    def processor_block(self, block, z_in=None, z_out=None, repeats=1):
+        """The isolated processor block (vb_processor_block): LN_dst then block `block`, `repeats` times on
+        the same input, this rank's hidden rows [hidden_lo, hidden_hi). z_in (rows, C) fp32 or None
+        (keep the previous call's input); z_out: an array to fill, True for a new one, or None. Returns
+        (z_out, device_ms)."""
+        rows = self.hidden_hi - self.hidden_lo
+        zi = None
+        if z_in is not None:
+            zi = np.ascontiguousarray(z_in, dtype=np.float32)
+            if zi.size != rows * self.C:
+                raise ValueError(f"z_in has {zi.size} elements, expected ({rows}, {self.C})")
+        if z_out is True:
+            z_out = np.empty((rows, self.C), np.float32)
+        elif z_out is not None:
+            _check_out(z_out, rows * self.C, "z_out")
+        ms = ctypes.c_float()
+        check(lib.vb_processor_block(self._h, block, _ptr(zi), _ptr(z_out), repeats, ctypes.byref(ms)))
+        return z_out, ms.value
+
+    def profile_block(self, block):
+        """One run of processor_block(block) on the current block input with a CUDA event pair around
+        every launch: records as profile()."""
+        return _records(lambda buf, n: lib.vb_profile_processor_block(self._h, block, buf, n))
 
     @property
     def weight_bytes(self):
@@ -289,6 +310,18 @@ class Model:
     @property
     def activation_bytes(self):
         return lib.vb_activation_bytes(self._h)
+
+
+def _records(call):
+    import json
+    n = call(None, 0)
+    if n < 0:
+        check(-n)
+    buf = ctypes.create_string_buffer(int(n) + 1024)
+    n = call(buf, len(buf))
+    if n < 0:
+        check(-n)
+    return json.loads(buf.value.decode())
 
 
 # ---------------------------------------------------------------- kernel-level wrappers

@@ -233,8 +233,8 @@ def _processor_edges(hidden, und, knn_extra):
     H = len(hidden)
     nb = knn(hidden, hidden, knn_extra + 1)[:, 1:]
     kn = np.stack([nb.ravel(), np.repeat(np.arange(H), knn_extra)], 1)
-    kn = np.stack([np.minimum(kn[:, 0], kn[:, 1]), np.maximum(kn[:, 0], kn[:, 1])], 1)
-    und = np.unique(np.concatenate([und, kn]), axis=0)
+    pairs = np.concatenate([und, kn])  # as (lo, hi): each undirected edge once, whichever list it came from
+    und = np.unique(np.stack([pairs.min(1), pairs.max(1)], 1), axis=0)
     return np.concatenate([und, und[:, ::-1]])
 
 
@@ -533,18 +533,55 @@ def sha256_file(path, chunk=1 << 24):
 
 
 C1_SAMPLE_FACTOR = 64
+C2_SAMPLE_FACTOR = 8
+
+
+def fibonacci_sphere(n):
+    """n nearly uniform unit vectors (the Fibonacci lattice)."""
+    i = np.arange(n) + 0.5
+    z = 1 - 2 * i / n
+    phi = i * np.pi * (3 - 5 ** 0.5)
+    r = np.sqrt(1 - z * z)
+    return np.stack([r * np.cos(phi), r * np.sin(phi), z], 1)
+
+
+def config_c2(seed=2, n_proc=1, sample=1, G=4096):
+    """c2: the isolated processor block (C2) as a complete model file. Hidden nodes and processor graph
+    of graph_c2 (edge attributes U[0, 1) from `seed`), C=1024, 16 heads of 64, mlp 4096, `n_proc`
+    processor blocks. The data grid only completes the file: G Fibonacci-lattice nodes, each sending to
+    its 4 nearest hidden nodes and receiving from its 3 nearest. With sample > 1 the hidden nodes are
+    the first 1/sample of graph_c2's (Morton order, so a compact region) with the edges among them: the
+    bounded sample the reference CPU backend is timed on."""
+    hidden, proc, attr = graph_c2(seed=seed)
+    if sample > 1:
+        Hs = len(hidden) // sample
+        keep = (proc[:, 0] < Hs) & (proc[:, 1] < Hs)
+        hidden, proc, attr = hidden[:Hs], proc[keep], attr[keep]
+    data = fibonacci_sphere(G)
+    data = data[morton_order(data)]
+
+    def srt(e):
+        return e[np.lexsort((e[:, 0], e[:, 1]))]
+
+    enc = srt(np.stack([np.repeat(np.arange(G), 4), knn(hidden, data, 4).ravel()], 1))
+    dec = srt(np.stack([knn(hidden, data, 3).ravel(), np.repeat(np.arange(G), 3)], 1))
+    v = _vars(8, 8, 8, 8)
+    cfg, t, x = make_model(seed=seed, C=1024, heads=16, mlp=4096, n_proc=n_proc, T=2, data_pos=data,
+                           hidden_pos=hidden, enc=enc, proc=proc, dec=dec, A=4, Ae=3,
+                           uuid=f"b200-c2-p{n_proc}-s{sample}", **v)
+    t["graph.proc.edge_attr"] = attr
+    return cfg, t, x
+
+
+def c2_features(rows, C=1024, seed=2):
+    """C2's node features: N(0, 1) float32 [rows, C] from `seed`."""
+    return np.random.default_rng(seed + 1000).standard_normal((rows, C), dtype=np.float32)
 
 
 def config_c1_sample(factor=C1_SAMPLE_FACTOR):
     """c1s: C1's architecture on 1/factor of its nodes, with the same per-node edge counts."""
     G, H = 1_688_650 // factor, 189_809 // factor
-
-    def fib(n):
-        i = np.arange(n) + 0.5
-        z = 1 - 2 * i / n
-        phi = i * np.pi * (3 - 5 ** 0.5)
-        r = np.sqrt(1 - z * z)
-        return np.stack([r * np.cos(phi), r * np.sin(phi), z], 1)
+    fib = fibonacci_sphere
 
     data, hidden = fib(G), fib(H)
     enc = np.stack([np.repeat(np.arange(G), 4), knn(hidden, data, 4).ravel()], 1)
@@ -572,6 +609,10 @@ def generate(name, out_dir, **kw):
         cfg, t, x = config_c1(T_out=6, **kw)
     elif name == "c1s":
         cfg, t, x = config_c1_sample(**kw)
+    elif name == "c2":
+        cfg, t, x = config_c2(**kw)
+    elif name in ("c2s1", "c2s3"):  # the CPU baseline's sample: 1 and 3 processor blocks
+        cfg, t, x = config_c2(n_proc=int(name[-1]), sample=C2_SAMPLE_FACTOR, **kw)
     else:
         cfg, t, x = config_test(name)
     write_model(mp, cfg, t)
