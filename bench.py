@@ -352,7 +352,7 @@ def halo_ms_per_rank(prof, dist):
     return out
 
 
-TRAFFIC = os.path.join(HERE, "profiles", "c1_traffic.json")
+TRAFFIC = os.path.join(HERE, "profiles", "traffic.json")
 
 
 def proc_gathered_bytes(workload, C):
@@ -363,18 +363,33 @@ def proc_gathered_bytes(workload, C):
     return int(st.read(mp)[0]["graph.proc.edge_index"].shape[1]) * 2 * int(C) * 2
 
 
-def traffic_for(kind):
-    """DRAM bytes (read + write) per launch of a kernel class of the C1 step, from the committed ncu
-    launch-list capture summarised in profiles/c1_traffic.json (None when absent)."""
+def traffic_for(kind, records):
+    """DRAM bytes (read + write) per launch of a kernel class, averaged over the class's launches in
+    `records`, from the single-kernel ncu captures in profiles/traffic.json scaled to each launch as its
+    `method` says; (None, None) when a launch has no capture to scale."""
     if not os.path.exists(TRAFFIC):
         return None, None
     d = json.load(open(TRAFFIC))
-    rec = d.get("per_launch", {}).get(kind)
-    return (rec, d.get("source")) if rec is not None else (None, None)
+    ent = d.get(kind)
+    if ent is None or not records:
+        return None, None
+    total = 0.0
+    if kind == "gemm_tc":
+        for r in records:
+            f = dict(kv.split("=") for kv in r["name"].split(" ")[1:])
+            sh = ent["shapes"].get(f"N={f['N']} K={f['K']} epi={f['epi']}")
+            if sh is None:
+                return None, None
+            M, N = int(f["M"]), int(f["N"])
+            total += sh["weight"] + (sh["read"] - sh["weight"]) * M / ent["M"] + M * N * 2
+    else:
+        for r in records:
+            total += (ent["read"] + ent["write"]) * r["bytes"] / ent["compulsory"]
+    return int(total / len(records)), f"{ent.get('capture')} ({ent['method']})"
 
 
 def summarise(prof, pk, src):
-    by = {}
+    by, recs = {}, {}
     for r in prof:
         cls = r["name"].split(" ")[0]
         if r["name"].startswith("attention"):
@@ -384,32 +399,35 @@ def summarise(prof, pk, src):
         d["flop"] += r["flop"]
         d["bytes"] += r["bytes"]
         d["n"] += 1
+        recs.setdefault(cls, []).append(r)
     total = sum(d["ms"] for d in by.values())
     # the dominant compute kernel class (halo_* records of a sharded run are communication and waits)
     dom = max((k for k in by if not k.startswith("halo")), key=lambda k: by[k]["ms"])
     d = by[dom]
+    tr, tr_src = traffic_for(dom, recs.get(dom))
     if d["flop"] > 0:
         ach = d["flop"] / (d["ms"] * 1e-3) / 1e12
         peak = pk["bf16_tflops_sustained"]
         roof = {"kernel": dom, "bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(ach / peak, 4), "traffic": traffic_for(dom)[0], "launches_per_step": d["n"],
+                "frac": round(ach / peak, 4), "traffic": tr, "launches_per_step": d["n"],
                 "share": round(d["ms"] / total, 4), "peak_source": f"{src} (sustained bf16, kernel inside a long step)",
-                "traffic_source": traffic_for(dom)[1], "flop_per_launch": d["flop"] / d["n"]}
+                "traffic_source": tr_src, "flop_per_launch": d["flop"] / d["n"]}
     else:
         ach = d["bytes"] / (d["ms"] * 1e-3) / 1e9
         peak = pk["hbm_gbs"]
         roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(ach / peak, 4), "traffic": traffic_for(dom)[0], "launches_per_step": d["n"],
-                "share": round(d["ms"] / total, 4), "peak_source": src, "traffic_source": traffic_for(dom)[1]}
+                "frac": round(ach / peak, 4), "traffic": tr, "launches_per_step": d["n"],
+                "share": round(d["ms"] / total, 4), "peak_source": src, "traffic_source": tr_src}
     att = by.get("attention proc")
     edge = None
     if att:
         per = att["ms"] / att["n"]
         gbs = att["bytes"] / (att["ms"] * 1e-3) / 1e9
+        atr, atr_src = traffic_for("attention proc", recs.get("attention proc"))
         edge = {"kernel": "attention proc", "bound": "hbm", "ms_per_launch": round(per, 4),
                 "bytes_per_launch": att["bytes"] / att["n"], "achieved": round(gbs, 1), "peak": pk["hbm_gbs"],
-                "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": traffic_for("attention proc")[0],
-                "peak_source": src, "traffic_source": traffic_for("attention proc")[1]}
+                "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": atr,
+                "peak_source": src, "traffic_source": atr_src}
     shares = {k: {"ms": round(v["ms"], 3), "share": round(v["ms"] / total, 4), "launches": v["n"]}
               for k, v in sorted(by.items(), key=lambda kv: -kv[1]["ms"])}
     return roof, edge, shares, total

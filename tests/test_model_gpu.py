@@ -177,6 +177,10 @@ def test_attention_tc_choice(name, tc, chunk, seeded_model, monkeypatch):
     y = vb.Model.load(mp, precision=vb.FP16).predict_step(x)
     vb.check_device()
     assert oracle.rel_absmax(y, golden(name)["out.y"]) <= TOL[vb.FP16]
+    if tc != "none":  # the dynamic tile order (default) and the static one give the same bits
+        monkeypatch.setenv("VB_ATT_SCHED", "0")
+        y0 = vb.Model.load(mp, precision=vb.FP16).predict_step(x)
+        assert np.array_equal(y0, y)
 
 
 @pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])

@@ -183,6 +183,7 @@ struct TcParams {
     float scale_log2;
     unsigned long long wait_ns;  // limit of every wait (kTimeoutNs; shorter in the failure-path test)
     int withhold;                // failure-path test only: CTA 0 leaves its first head stage unfilled
+    unsigned* sched;             // dynamic tile order: [tiles handed out, CTAs done], zero between launches; or null
 };
 
 __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParams p) {
@@ -196,13 +197,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
     uint64_t* empty_h = bar + kStages;  // [kStages]
     uint64_t* full_t = bar + 2 * kStages;
     uint64_t* empty_t = bar + 2 * kStages + 2;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 2 * kStages + 4);
+    uint64_t* tready = bar + 2 * kStages + 4;  // the tile index of record-block buffer b is in tidx[b]
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 2 * kStages + 6);
+    volatile int* tidx = abort_flag + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // ---- set-up: barriers, zeroed stages (every slot holds finite values), the edge weights as fp16 rows
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) mbar_init(&full_h[s], 32 * kProducers), mbar_init(&empty_h[s], kConsumers);
-        for (int s = 0; s < 2; ++s) mbar_init(&full_t[s], 1), mbar_init(&empty_t[s], kConsumers);
+        for (int s = 0; s < 2; ++s)
+            mbar_init(&full_t[s], 1), mbar_init(&empty_t[s], kConsumers), mbar_init(&tready[s], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -227,18 +231,34 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
         constexpr int kRounds = kTcMaxSrc / kRows;
         uint32_t hc = 0;
         int tc = 0;
-        int blob_round[2] = {-1, -1};  // per record-block buffer: the round of its last copy issued
+        // per record-block buffer: the round of its barrier's last phase (a copy, or the end marker)
+        int blob_round[2] = {-1, -1};
         bool ok = true;
-        for (int ti = blockIdx.x; ti < p.ntiles && ok; ti += gridDim.x, ++tc) {
-            const TcTile t = p.tiles[p.tile0 + ti];
+        // Tile order: static (tile blockIdx.x + i gridDim.x), or dynamic (p.sched): the first tile is
+        // blockIdx.x, each further one gridDim.x + the next index of the launch's counter, fetched by
+        // producer thread 0 and published to the other producers (tready) and the consumers (full_t).
+        for (tc = 0; ok; ++tc) {
             const int tb = tc & 1;
             ok = __all_sync(kFull, mbar_wait(&empty_t[tb], ((tc >> 1) & 1) ^ 1, abort_flag, p.wait_ns));
             if (!ok) break;
             if (pl == 0) {
+                tidx[tb] = tc == 0 || !p.sched ? int(blockIdx.x + tc * gridDim.x)
+                                                : int(gridDim.x + atomicAdd(p.sched, 1u));
+                mbar_arrive(&tready[tb]);
+            }
+            ok = __all_sync(kFull, mbar_wait(&tready[tb], uint32_t((tc >> 1) & 1), abort_flag, p.wait_ns));
+            if (!ok) break;
+            const int ti = tidx[tb];
+            blob_round[tb] = tc >> 1;  // the last phase of this buffer's barrier that anything completes
+            if (ti >= p.ntiles) {  // no more tiles: the consumers read the index past the end and stop
+                if (pl == 0) mbar_arrive(&full_t[tb]);
+                break;
+            }
+            const TcTile t = p.tiles[p.tile0 + ti];
+            if (pl == 0) {
                 mbar_expect_tx(&full_t[tb], uint32_t(t.blob_bytes));
                 bulk_g2s(blobs + tb * kBlobMax, p.blob + t.blob_off, uint32_t(t.blob_bytes), &full_t[tb]);
             }
-            blob_round[tb] = tc >> 1;
             // this lane's source rows of the tile (rows prow + kRows i), -1 past the tile's sources
             int srow[kRounds];
 #pragma unroll
@@ -273,9 +293,17 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
         }
         // drain: every copy of this thread has landed before the CTA may exit
         asm volatile("cp.async.wait_all;" ::: "memory");
-        if (pl == 0)
+        if (pl == 0) {
             for (int b = 0; b < 2; ++b)
                 if (blob_round[b] >= 0) mbar_drain(&full_t[b], uint32_t(blob_round[b] & 1));
+            if (p.sched) {  // the last CTA to finish zeroes the counter for the next launch
+                __threadfence();
+                if (atomicAdd(p.sched + 1, 1u) == gridDim.x - 1) {
+                    atomicExch(p.sched, 0u);
+                    atomicExch(p.sched + 1, 0u);
+                }
+            }
+        }
         return;
     }
 
@@ -283,9 +311,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
     const int g = lane >> 2, t4 = lane & 3;  // fragment coordinates: row group, column pair
     uint32_t hc = 0;
     int tc = 0;
-    for (int ti = blockIdx.x; ti < p.ntiles; ti += gridDim.x, ++tc) {
+    for (;; ++tc) {
         const int tb = tc & 1;
         if (!__all_sync(kFull, mbar_wait(&full_t[tb], uint32_t((tc >> 1) & 1), abort_flag, p.wait_ns))) return;
+        const int ti = tidx[tb];
+        if (ti >= p.ntiles) return;
         const TcTile t = p.tiles[p.tile0 + ti];
         const uint8_t* bl = blobs + tb * kBlobMax;
         const uint16_t* roff = reinterpret_cast<const uint16_t*>(bl);
@@ -382,9 +412,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
                         const uint32_t idx = ((e < 4 ? ent.x : ent.y) >> (8 * (e & 3))) & 0xffu;
                         float a0 = 0.f, a1 = 0.f, a2 = 0.f, sc = -INFINITY;
                         if (idx != 0xffu) {
-                            const uint2 rec = recs[ro[rr] + int(idx)];
-                            const float2 a01 = unpack_h2(rec.x >> 16 | (rec.y << 16));
-                            a0 = a01.x, a1 = a01.y, a2 = __half2float(__ushort_as_half(uint16_t(rec.y >> 16)));
+                            const uint2 rec = recs[ro[rr] + int(idx)];  // {a0, a1 | a2, slot}
+                            const float2 a01 = unpack_h2(rec.x);
+                            a0 = a01.x, a1 = a01.y, a2 = __half2float(__ushort_as_half(uint16_t(rec.y & 0xffffu)));
                             sc = fmaf(sv[e], p.scale_log2,
                                       fmaf(qv[rr][0], a0, fmaf(qv[rr][1], a1, fmaf(qv[rr][2], a2, qv[rr][3]))));
                         }
@@ -515,6 +545,7 @@ void attention_tc(const TcArgs& a, cudaStream_t s) {
     const char* wh = std::getenv("VB_DEBUG_TC_WITHHOLD");
     p.wait_ns = wn && *wn ? std::strtoull(wn, nullptr, 10) : kTimeoutNs;
     p.withhold = wh && *wh && std::atoi(wh) != 0;
+    p.sched = a.sched;
     static std::atomic<uint64_t> configured{0};
     once_per_device(configured, [] {
         VB_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

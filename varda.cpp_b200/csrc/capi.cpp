@@ -402,8 +402,9 @@ vb::CsrGraph host_csr(const int32_t* row_ptr, const int32_t* src, const float* a
     return g;
 }
 
-// The tensor-core tiles' CSR-order records in the vb_tile_plan form {a0, a1, a2, slot (int bits)}
-// (heavy rows: their source), and each tile's {row0, nrows, src_off, nsrc}.
+// The tensor-core tiles' CSR-order records in the vb_tile_plan form {a0, a1, a2, slot (int bits)}, read
+// back from the tiles' record blocks (heavy rows: the packed record with their source), and each tile's
+// {row0, nrows, src_off, nsrc}.
 void tc_plan_export(const vb::CsrGraph& g, const vb::TcPlan& tp, int32_t* tiles4, float* edges) {
     if (tiles4)
         for (size_t i = 0; i < tp.tiles.size(); ++i)
@@ -416,7 +417,8 @@ void tc_plan_export(const vb::CsrGraph& g, const vb::TcPlan& tp, int32_t* tiles4
         const uint16_t* rec = reinterpret_cast<const uint16_t*>(tp.blob.data() + t.blob_off + t.edge_off);
         const int64_t e0 = g.row_ptr[size_t(t.row0)];
         for (int i = 0; i < t.n_edges; ++i) {
-            const int32_t sl = rec[4 * i];
+            for (int k = 0; k < 3; ++k) edges[4 * (e0 + i) + k] = __half2float(__ushort_as_half(rec[4 * i + k]));
+            const int32_t sl = rec[4 * i + 3];
             std::memcpy(edges + 4 * (e0 + i) + 3, &sl, 4);
         }
     }

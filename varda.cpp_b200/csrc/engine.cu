@@ -216,9 +216,11 @@ private:
     int dev_ = 0;
     cudaStream_t stream_ = nullptr;
     bool use_tc_ = false;
-    // the dynamic tile order's counter of this model's GEMMs (all on its stream, one at a time)
+    // the dynamic tile order's counters of this model's GEMMs and tensor-core attention launches (all on
+    // its stream, one at a time): words 0-1 and 2-3 of gemm_sched_
     DeviceBuffer gemm_sched_;
     unsigned* sched_ = nullptr;
+    unsigned* att_sched_ = nullptr;
     int C_ = 0, heads_ = 0, hd_ = 0, mlp_ = 0, n_proc_ = 0, T_in_ = 0, T_out_ = 0, V_in_ = 0, V_out_ = 0, V_dec_ = 0;
     int A_node_ = 0, F_ = 0;
     int64_t ldF_ = 0, ldA_ = 0, ldVo_ = 0;
@@ -564,11 +566,10 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     const bool fp16 = !std::is_same<T, float>::value;
     use_tc_ = fp16 && opts_.gemm == 0 && env_int("VB_GEMM_SIMT", 0) == 0;
     VB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
-    if (env_int("VB_GEMM_SCHED", 1) != 0) {
-        gemm_sched_.alloc(2 * sizeof(unsigned));
-        VB_CUDA(cudaMemset(gemm_sched_.get(), 0, 2 * sizeof(unsigned)));
-        sched_ = gemm_sched_.as<unsigned>();
-    }
+    gemm_sched_.alloc(4 * sizeof(unsigned));
+    VB_CUDA(cudaMemset(gemm_sched_.get(), 0, 4 * sizeof(unsigned)));
+    if (env_int("VB_GEMM_SCHED", 1) != 0) sched_ = gemm_sched_.as<unsigned>();
+    if (env_int("VB_ATT_SCHED", 1) != 0) att_sched_ = gemm_sched_.as<unsigned>() + 2;
 
     // ---- normaliser, residual, bounding
     const TensorView& mul = file.take("norm.mul", DType::F32, {c.n_data_vars});
@@ -847,7 +848,7 @@ void Engine<T>::attention(const GraphDev& g, const AttnLayer<T>& b, int64_t lo, 
                 t.tile0 = int(t0 - g.tile_row0.begin()), t.ntiles = int(t1 - t0), t.dst_lo = lo;
                 t.q = q, t.k = kk, t.v = v, t.xr = xr, t.out = out, t.ldq = ldq, t.ldkv = ldkv, t.ldxr = ldxr;
                 t.ldo = C_, t.n_q_rows = n, t.n_src = g.n_src, t.w_e = a.w_e, t.C = C_, t.heads = heads_;
-                t.head_dim = hd_;
+                t.head_dim = hd_, t.sched = att_sched_;
                 k::attention_tc(t, s);
             } else {
                 k::TileArgs t;

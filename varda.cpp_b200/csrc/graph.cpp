@@ -267,9 +267,9 @@ TcPlan make_tc_tiles(const CsrGraph& g, int64_t align_rows) {
         for (int i = 0; i < nrows; ++i)
             for (int64_t e = g.row_ptr[size_t(row0 + i)]; e < g.row_ptr[size_t(row0 + i + 1)]; ++e) {
                 uint16_t* r = rec + 4 * (e - e0);
-                r[0] = uint16_t(slot[size_t(g.src[size_t(e)])]);
                 for (int k = 0; k < 3; ++k)
-                    r[1 + k] = half_bits(k < g.attr_dim ? g.attr[size_t(e) * size_t(g.attr_dim) + size_t(k)] : 0.f);
+                    r[k] = half_bits(k < g.attr_dim ? g.attr[size_t(e) * size_t(g.attr_dim) + size_t(k)] : 0.f);
+                r[3] = uint16_t(slot[size_t(g.src[size_t(e)])]);
             }
         t.tiles.push_back(tile);
         for (int32_t s : open) slot[size_t(s)] = -1;

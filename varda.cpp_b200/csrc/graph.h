@@ -79,7 +79,8 @@ constexpr int64_t kTcAlignRows = 64;
 //       positions lane l holds in the chunk's two column blocks ((r, 2t), (r, 2t + 1), (r + 8, 2t),
 //       (r + 8, 2t + 1) with r = l / 4, t = l % 4, first block then second), the index of that edge
 //       within its row, or 255 when (row, slot) is not an edge;
-//   edges at edge_off = kTcChunkOff + 256 n_chunks: 8 bytes each {u16 slot, fp16 a0, a1, a2}.
+//   edges at edge_off = kTcChunkOff + 256 n_chunks: 8 bytes each {fp16 a0, a1, a2, u16 slot} (a0, a1
+//   one aligned fp16 pair).
 constexpr int kTcBlockOff = 144, kTcChunkOff = 272, kTcMaxChunks = 4 * (kTcMaxSrc / 16);
 struct TcTile {
     int32_t row0, nrows, nsrc, src_off;               // rows [row0, row0 + nrows); sources srcs[src_off, + nsrc)

@@ -173,6 +173,9 @@ struct TcArgs {
     int64_t n_q_rows = 0, n_src = 0;
     const float* w_e = nullptr;  // [4, C], fp16-representable values
     int C = 0, heads = 0, head_dim = 0;
+    // dynamic tile order: two zeroed words the launch leaves zero (one counter per stream: launches that
+    // share it must not run concurrently); null: static order (tile b + i x grid for CTA b)
+    unsigned* sched = nullptr;
 };
 void attention_tc(const TcArgs& a, cudaStream_t s);
 bool tc_attention_supported(int C, int heads, int head_dim);
