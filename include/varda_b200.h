@@ -217,7 +217,8 @@ int vb_tiles_create(const int32_t* row_ptr, const int32_t* src, const float* att
                     int64_t n_dst, int head_dim, vb_tiles** out);
 /* The same with the tile kind: VB_TILES_SMEM (the shared-memory-staged CUDA-core kernel the engine runs
  * on the decoder graph, as vb_tiles_create) or VB_TILES_TC (the tile-sparse tensor-core kernel, which
- * the engine runs where VB_ATT_TC names the graph: tiles of up to 64 consecutive rows reaching at most
+ * the engine runs on the processor graph, or where VB_ATT_TC names a graph: tiles of up to 64 consecutive
+ * rows reaching at most
  * 128 distinct sources, restarting every 64 rows; per 16-row block and head q.k and the value sums as
  * tensor-core products over the 8-column blocks that hold edges; head_dim 64 and at most 32 heads; rows
  * with a repeated source or more than 128 sources run on the gather kernel). vb_attention_tiled runs

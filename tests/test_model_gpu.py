@@ -165,7 +165,7 @@ def test_attention_kernel_choice(name, tiled, chunk, seeded_model, monkeypatch):
 @pytest.mark.parametrize("tc,chunk", [("all", ""), ("proc", ""), ("dec", "256"), ("dec", "32"), ("none", "")])
 @pytest.mark.parametrize("name", ["t1024", "t768", "t384i"])
 def test_attention_tc_choice(name, tc, chunk, seeded_model, monkeypatch):
-    """The engine with the tile-sparse tensor-core attention (VB_ATT_TC; off by default)
+    """The engine with the tile-sparse tensor-core attention (VB_ATT_TC; default: the processor graph)
     on each graph of the head_dim-64 models, with decoder chunks on the tiles' 256-row grid and off it
     (then the decoder keeps the shared-memory kernel): the fp16 parity bar against the reference's
     goldens for every choice."""

@@ -49,9 +49,11 @@ int64_t env_int(const char* name, int64_t dflt) {
 // shared sources), equal on the processor, gather ahead on the encoder (35 edges per row)
 constexpr const char* kTiledDefault = "dec";
 // Which graphs run the tile-sparse tensor-core attention (fp16, head_dim 64; attention_tc.cu): VB_ATT_TC,
-// the same forms; it takes precedence over VB_ATT_TILED. Off by default: on the C2 block it measured
-// 1.67 ms against 1.58 ms for the gather kernel (in the C1 step 2.25 against about 2.2 ms per block).
-constexpr const char* kTcDefault = "none";
+// the same forms; it takes precedence over VB_ATT_TILED. Default: the processor graph, where it measured
+// 1.25 ms per C2 block against 1.57 ms for the gather kernel (1.66 against 2.16 ms per block inside the
+// C1 step, 167.9 against 173.8 ms per step). A graph whose tiles would not restart on the 64-row grid
+// of a decoder chunk keeps its other kernel.
+constexpr const char* kTcDefault = "proc";
 bool graph_listed(const char* env, const std::string& graph, const char* dflt) {
     const char* v = std::getenv(env);
     const std::string s = v && *v ? v : dflt;
