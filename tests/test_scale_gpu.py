@@ -5,7 +5,7 @@
   reference CPU backend's own values (tests/golden/c1s.sampled.npz: seeded rows and columns of every
   key, from oracle/_ref/ref_dump), with the reference's tolerances (3e-3 fp16, 1e-5 fp32 rel_absmax),
   input keys within 1e-6. The reference's bitwise self-checks too (hook inert, graph replay == eager).
-* C2: the isolated processor block's graph (189,809 rows, 2,634,258 edges, C = 1024, 16 heads, fp16):
+* C2: the isolated processor block's graph (189,809 rows, 2,561,682 edges, C = 1024, 16 heads, fp16):
   the tile-sparse tensor-core, gather, shared-memory-tiled and no-allocation split attention paths
   against the oracle's restatement of cpu::graph_attention on 4,096 seeded rows (16 runs of 256
   consecutive rows), and the paths against each other on every row. Exercises the 64-bit row offsets
@@ -85,7 +85,7 @@ def test_c2_attention_parity(c2_graph):
     H, rp, src, at = c2_graph
     C, heads = 1024, 16
     hd = C // heads
-    assert rp[-1] == 2_634_258 and H == 189_809
+    assert rp[-1] == 2_561_682 and H == 189_809
     rng = np.random.default_rng(22)
     qkvs = rng.standard_normal((H, 4 * C), dtype=np.float32).astype(np.float16)
     we = (rng.standard_normal((C, 3)) / np.sqrt(3)).astype(np.float16).astype(np.float32)

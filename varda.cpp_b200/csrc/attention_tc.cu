@@ -30,8 +30,8 @@
 //              on B200 four warps of them gather scattered 128-byte rows at about 22 bytes per clock per
 //              SM, against 12 for TMA row gathers), completing on the stage's mbarrier, into a 4-deep
 //              ring of head stages laid out with the 128-byte swizzle (full / empty mbarriers).
-//   consumers  a tile of nb row blocks has nb x heads tasks (head-major); task i goes to warp i % 8, so
-//              the warps work on several heads at once. Per task: x_r read ahead; Q fragments; qe = Q
+//   consumers  a tile of nb row blocks has nb x heads tasks (head-major); the warps take a stage's tasks
+//              from its counter as they reach it, so they spread over the stages in the ring. Per task: x_r read ahead; Q fragments; qe = Q
 //              W_ext (the edge weights as 8 extra columns: per row <W_e^T q, a>, <q, b_e>); per 16-slot
 //              step the scores, the online weights and O += P V; the W_e / b_e terms; out.
 // Every mbarrier wait is bounded (4 s of %globaltimer): on timeout the CTA sets the device error flag
@@ -54,10 +54,17 @@ constexpr int kHD = 64;  // head_dim
 constexpr int kStages = 4;  // head stages
 constexpr int kConsumers = 8, kProducers = 4;
 constexpr int kThreads = 32 * (kConsumers + kProducers);
+// per-thread registers after the split: the launch gives every thread 168 (65536 / 384, rounded down to
+// a multiple of 8); one producer warpgroup at kProducerRegs and two consumer warpgroups at kConsumerRegs
+// use exactly the CTA's 384 x 168
+constexpr int kLaunchRegs = 168, kProducerRegs = 56, kConsumerRegs = 224;
+static_assert(kConsumers == 8 && kProducers == 4, "the register split assumes 2 consumer and 1 producer warpgroups");
+static_assert(32 * (kProducers * kProducerRegs + kConsumers * kConsumerRegs) <= kThreads * kLaunchRegs,
+              "register split over the CTA's registers");
 constexpr int kKVBytes = kTcMaxSrc * kHD * 2;  // 16 KB
 constexpr int kQBytes = kTcRows * kHD * 2;     // 8 KB
 constexpr int kStageBytes = 2 * kKVBytes + kQBytes;
-constexpr int kBlobMax = kTcChunkOff + 256 * kTcMaxChunks + 8 * kTcMaxEdges;
+constexpr int kBlobMax = kTcMaskOff + 32 * kTcMaxChunks;  // the part of a record block staged in shared memory
 constexpr int kMaxHeads = 32;
 constexpr unsigned long long kTimeoutNs = 4000000000ull;
 constexpr float kSlack = 8.0f;  // log2 headroom of the weights over their reference maximum
@@ -67,7 +74,7 @@ constexpr int kOffStage = 0;
 constexpr int kOffWext = kOffStage + kStages * kStageBytes;           // [heads][8 x 64] fp16, 1 KB each
 constexpr int kOffBlob(int heads) { return kOffWext + heads * 1024; }  // 2 record blocks
 constexpr int kOffBar(int heads) { return kOffBlob(heads) + 2 * kBlobMax; }
-constexpr int kSmemBytes(int heads) { return kOffBar(heads) + 128 + 1024; }  // + barriers + alignment slack
+constexpr int kSmemBytes(int heads) { return kOffBar(heads) + 256 + 1024; }  // + barriers + alignment slack
 static_assert(kSmemBytes(kMaxHeads) <= 232448, "shared memory budget");
 
 __device__ int g_tc_error = 0;
@@ -200,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
     uint64_t* tready = bar + 2 * kStages + 4;  // the tile index of record-block buffer b is in tidx[b]
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 2 * kStages + 6);
     volatile int* tidx = abort_flag + 1;
+    int* tgrab = const_cast<int*>(abort_flag) + 3;  // [kStages] task counters of the head stages
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // ---- set-up: barriers, zeroed stages (every slot holds finite values), the edge weights as fp16 rows
@@ -208,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
         for (int s = 0; s < 2; ++s)
             mbar_init(&full_t[s], 1), mbar_init(&empty_t[s], kConsumers), mbar_init(&tready[s], 1);
         *abort_flag = 0;
+        for (int s = 0; s < kStages; ++s) tgrab[s] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     for (int i = threadIdx.x; i < kStages * kStageBytes / 16; i += blockDim.x)
@@ -225,6 +234,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
 
     if (warp >= kConsumers) {
         // ================================================================ producers
+        // registers: the producer warpgroup gives back to the consumers' (kProducerRegs + 2 x
+        // kConsumerRegs = 3 x the 168 of the launch: the split adds up to what the CTA holds)
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
         const int pl = threadIdx.x - 32 * kConsumers;  // 0 .. 32 kProducers - 1
         const int prow = pl >> 3, pch = pl & 7;        // 16 rows x 8 chunks of 16 bytes per round
         constexpr int kRows = 4 * kProducers;          // rows per round
@@ -256,8 +268,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
             }
             const TcTile t = p.tiles[p.tile0 + ti];
             if (pl == 0) {
-                mbar_expect_tx(&full_t[tb], uint32_t(t.blob_bytes));
-                bulk_g2s(blobs + tb * kBlobMax, p.blob + t.blob_off, uint32_t(t.blob_bytes), &full_t[tb]);
+                // the tile's block heads and position masks (its attributes stay in global memory)
+                mbar_expect_tx(&full_t[tb], uint32_t(t.attr_off));
+                bulk_g2s(blobs + tb * kBlobMax, p.blob + t.blob_off, uint32_t(t.attr_off), &full_t[tb]);
             }
             // this lane's source rows of the tile (rows prow + kRows i), -1 past the tile's sources
             int srow[kRounds];
@@ -308,9 +321,17 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
     }
 
     // ==================================================================== consumers
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
     const int g = lane >> 2, t4 = lane & 3;  // fragment coordinates: row group, column pair
     uint32_t hc = 0;
     int tc = 0;
+    // The tasks of a head stage (its 16-row blocks) go to whichever consumer warps reach the stage first:
+    // each grabs block indices from the stage's counter until one is past the tile's blocks. Every warp
+    // makes exactly one failed grab per stage, so the counter of slot s advances by nb + kConsumers per
+    // use and each warp tracks the slot's base itself (no reset).
+    int gbase[kStages];
+#pragma unroll
+    for (int i = 0; i < kStages; ++i) gbase[i] = 0;
     for (;; ++tc) {
         const int tb = tc & 1;
         if (!__all_sync(kFull, mbar_wait(&full_t[tb], uint32_t((tc >> 1) & 1), abort_flag, p.wait_ns))) return;
@@ -318,8 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
         if (ti >= p.ntiles) return;
         const TcTile t = p.tiles[p.tile0 + ti];
         const uint8_t* bl = blobs + tb * kBlobMax;
-        const uint16_t* roff = reinterpret_cast<const uint16_t*>(bl);
-        const uint2* recs = reinterpret_cast<const uint2*>(bl + t.edge_off);
+        const uint8_t* attr = p.blob + t.blob_off + t.attr_off;  // per-position attributes (global)
         const int nb = (t.nrows + 15) >> 4;
         for (int h = 0; h < heads; ++h, ++hc) {
             const int s = int(hc % kStages);
@@ -327,8 +347,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
             const uint32_t kbase = smem_u32(sm + kOffStage + s * kStageBytes);
             const uint32_t vbase = kbase + kKVBytes, qbase = kbase + 2 * kKVBytes;
             const uint32_t wbase = smem_u32(wext + h * 1024);
-            for (int rb = 0; rb < nb; ++rb) {
-                if ((h * nb + rb) % kConsumers != warp) continue;
+            int base = 0;
+#pragma unroll
+            for (int i = 0; i < kStages; ++i) base = i == s ? gbase[i] : base;
+            for (;;) {
+                int rb = 0;
+                if (lane == 0) rb = atomicAdd(&tgrab[s], 1);
+                rb = __shfl_sync(kFull, rb, 0) - base;
+                if (rb >= nb) break;
                 const uint8_t* bh = bl + kTcBlockOff + 32 * rb;
                 const int nch = bh[0], cbase = bh[1];
                 // ---- x_r of this lane's output elements, read now so the loads overlap the products (the
@@ -369,15 +395,24 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
                         qv[rr][3] = __shfl_sync(kFull, ce[2 * rr + 1], la + 1) * p.scale_log2;
                     }
                 }
-                const int ro[2] = {roff[r0], roff[r1]};
-                float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-                float pa[2][3] = {{0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}};
+                float m[2] = {-INFINITY, -INFINITY};
+                // l and pa as two partial sums (even / odd slot column) updated by paired fp32 operations
+                float2 l2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                float2 pa2[2][3];
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) pa2[rr][0] = pa2[rr][1] = pa2[rr][2] = make_float2(0.f, 0.f);
+                float2 qv2[2][4];
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) qv2[rr][k] = make_float2(qv[rr][k], qv[rr][k]);
+                const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
                 float o[8][4];
 #pragma unroll
                 for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-                // ---- 16-slot steps: two column blocks (ja, jb) each. The products S and the entry words of
-                // step c + 1 are issued before the weights of step c (software pipeline).
-                auto scores = [&](int c, float (&sv)[8], uint2& ent) {
+                // ---- 16-slot steps: two column blocks (ja, jb) each. The products S, the position mask and
+                // the attribute words of step c + 1 are issued before the weights of step c (software pipeline).
+                auto scores = [&](int c, float (&sv)[8], uint4 (&at)[3], uint32_t& mk) {
                     const int ja = bh[2 + 2 * c], jb = bh[3 + 2 * c];
                     float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -392,34 +427,45 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
                     }
 #pragma unroll
                     for (int i = 0; i < 4; ++i) sv[i] = sa[i], sv[4 + i] = sb[i];
-                    ent = *reinterpret_cast<const uint2*>(bl + kTcChunkOff + 256 * (cbase + c) + 8 * lane);
+                    const uint4* ap = reinterpret_cast<const uint4*>(attr + kTcChunkAttr * (cbase + c)) + 3 * lane;
+                    at[0] = __ldg(ap), at[1] = __ldg(ap + 1), at[2] = __ldg(ap + 2);
+                    mk = bl[kTcMaskOff + 32 * (cbase + c) + lane];
                 };
                 float svn[8];
-                uint2 entn = make_uint2(0xffffffffu, 0xffffffffu);
-                if (nch > 0) scores(0, svn, entn);
+                uint4 atn[3] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+                uint32_t mkn = 0u;
+                if (nch > 0) scores(0, svn, atn, mkn);
                 for (int c = 0; c < nch; ++c) {
                     const int ja = bh[2 + 2 * c], jb = bh[3 + 2 * c];
-                    float sv[8];  // positions: block ja (r0: 2t, 2t + 1; r1: 2t, 2t + 1), then block jb
+                    // positions e = 4 k + 2 h + i: column block k (ja, jb), row r0 + 8 h, slot column 2 t4 + i;
+                    // pair q = e / 2 = (block k, row h) holds columns 2 t4, 2 t4 + 1
+                    float sv[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) sv[i] = svn[i];
-                    const uint2 ent = entn;
-                    if (c + 1 < nch) scores(c + 1, svn, entn);
-                    float av[8][3];
+                    float2 av[4][3], sp[4];
+                    {
+                        const uint32_t aw[12] = {atn[0].x, atn[0].y, atn[0].z, atn[0].w, atn[1].x, atn[1].y,
+                                                 atn[1].z, atn[1].w, atn[2].x, atn[2].y, atn[2].z, atn[2].w};
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+#pragma unroll
+                            for (int k = 0; k < 3; ++k) av[q][k] = unpack_h2(aw[3 * q + k]);
+                    }
+                    const uint32_t mk = mkn;
+                    if (c + 1 < nch) scores(c + 1, svn, atn, mkn);
                     float cm[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int rr = (e >> 1) & 1;  // row r0 or r1
-                        const uint32_t idx = ((e < 4 ? ent.x : ent.y) >> (8 * (e & 3))) & 0xffu;
-                        float a0 = 0.f, a1 = 0.f, a2 = 0.f, sc = -INFINITY;
-                        if (idx != 0xffu) {
-                            const uint2 rec = recs[ro[rr] + int(idx)];  // {a0, a1 | a2, slot}
-                            const float2 a01 = unpack_h2(rec.x);
-                            a0 = a01.x, a1 = a01.y, a2 = __half2float(__ushort_as_half(uint16_t(rec.y & 0xffffu)));
-                            sc = fmaf(sv[e], p.scale_log2,
-                                      fmaf(qv[rr][0], a0, fmaf(qv[rr][1], a1, fmaf(qv[rr][2], a2, qv[rr][3]))));
-                        }
-                        av[e][0] = a0, av[e][1] = a1, av[e][2] = a2, sv[e] = sc;
-                        cm[rr] = fmaxf(cm[rr], sc);
+                    for (int q = 0; q < 4; ++q) {
+                        const int rr = q & 1;
+                        // s = S / sqrt(d) + <W_e^T q, a> + <q, b_e> in the log2 domain, in the reference's order
+                        float2 tt = __ffma2_rn(qv2[rr][2], av[q][2], qv2[rr][3]);
+                        tt = __ffma2_rn(qv2[rr][1], av[q][1], tt);
+                        tt = __ffma2_rn(qv2[rr][0], av[q][0], tt);
+                        float2 sc = __ffma2_rn(make_float2(sv[2 * q], sv[2 * q + 1]), scale2, tt);
+                        sc.x = (mk >> (2 * q)) & 1u ? sc.x : -INFINITY;
+                        sc.y = (mk >> (2 * q + 1)) & 1u ? sc.y : -INFINITY;
+                        sp[q] = sc;
+                        cm[rr] = fmaxf(cm[rr], fmaxf(sc.x, sc.y));
                     }
                     // the reference maxima m are the same in the four lanes of a row's quad; they move only
                     // when a lane's own score exceeds them by more than the slack (then over the quad)
@@ -431,24 +477,26 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
                             const float mn = fmaxf(m[rr], cm[rr]);
                             const float corr = mn == -INFINITY ? 1.f : ex2(m[rr] - mn);
                             m[rr] = mn;
-                            l[rr] *= corr, pa[rr][0] *= corr, pa[rr][1] *= corr, pa[rr][2] *= corr;
+                            const float2 c2 = make_float2(corr, corr);
+                            l2[rr] = __fmul2_rn(l2[rr], c2);
+                            pa2[rr][0] = __fmul2_rn(pa2[rr][0], c2), pa2[rr][1] = __fmul2_rn(pa2[rr][1], c2);
+                            pa2[rr][2] = __fmul2_rn(pa2[rr][2], c2);
 #pragma unroll
                             for (int n = 0; n < 8; ++n) o[n][2 * rr] *= corr, o[n][2 * rr + 1] *= corr;
                         }
                     }
                     const float mu[2] = {m[0] == -INFINITY ? 0.f : m[0], m[1] == -INFINITY ? 0.f : m[1]};
-                    float w[8];
+                    uint32_t a[4];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int rr = (e >> 1) & 1;
-                        w[e] = ex2(sv[e] - mu[rr]);
-                        l[rr] += w[e];
-                        pa[rr][0] = fmaf(w[e], av[e][0], pa[rr][0]);
-                        pa[rr][1] = fmaf(w[e], av[e][1], pa[rr][1]);
-                        pa[rr][2] = fmaf(w[e], av[e][2], pa[rr][2]);
+                    for (int q = 0; q < 4; ++q) {
+                        const int rr = q & 1;
+                        const float2 d = __fadd2_rn(sp[q], make_float2(-mu[rr], -mu[rr]));
+                        const float2 w = make_float2(ex2(d.x), ex2(d.y));
+                        l2[rr] = __fadd2_rn(l2[rr], w);
+#pragma unroll
+                        for (int k = 0; k < 3; ++k) pa2[rr][k] = __ffma2_rn(w, av[q][k], pa2[rr][k]);
+                        a[q] = pack_h2(w.x, w.y);
                     }
-                    const uint32_t a[4] = {pack_h2(w[0], w[1]), pack_h2(w[2], w[3]), pack_h2(w[4], w[5]),
-                                           pack_h2(w[6], w[7])};
                     const int vr = 8 * (((lane >> 3) & 1) ? jb : ja) + (lane & 7);
 #pragma unroll
                     for (int n = 0; n < 8; n += 2) {
@@ -457,6 +505,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
                         mma16816(o[n], a, b[0], b[1]);
                         mma16816(o[n + 1], a, b[2], b[3]);
                     }
+                }
+                float l[2], pa[2][3];
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    l[rr] = l2[rr].x + l2[rr].y;
+#pragma unroll
+                    for (int k = 0; k < 3; ++k) pa[rr][k] = pa2[rr][k].x + pa2[rr][k].y;
                 }
 #pragma unroll
                 for (int rr = 0; rr < 2; ++rr) {
@@ -507,6 +562,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParam
                             __hadd2(__floats2half2_rn(o[n][2] * i1, o[n][3] * i1), *reinterpret_cast<const __half2*>(&xv1[n]));
                 }
             }
+#pragma unroll
+            for (int i = 0; i < kStages; ++i) gbase[i] += i == s ? nb + kConsumers : 0;
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty_h[s]);
         }

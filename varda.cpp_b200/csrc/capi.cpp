@@ -402,8 +402,10 @@ vb::CsrGraph host_csr(const int32_t* row_ptr, const int32_t* src, const float* a
     return g;
 }
 
-// The tensor-core tiles' CSR-order records in the vb_tile_plan form {a0, a1, a2, slot (int bits)}, read
-// back from the tiles' record blocks (heavy rows: the packed record with their source), and each tile's
+// The tensor-core tiles' edges in the vb_tile_plan form {a0, a1, a2, slot (int bits)} in CSR order, decoded
+// back from the tiles' record blocks (every masked fragment position of every chunk names its row and
+// slot; the edge is the row's edge from that slot's source); a tiled edge no position names keeps
+// NaN attributes and slot -1. Heavy rows: the packed record with their source. And each tile's
 // {row0, nrows, src_off, nsrc}.
 void tc_plan_export(const vb::CsrGraph& g, const vb::TcPlan& tp, int32_t* tiles4, float* edges) {
     if (tiles4)
@@ -413,13 +415,35 @@ void tc_plan_export(const vb::CsrGraph& g, const vb::TcPlan& tp, int32_t* tiles4
     if (!edges) return;
     const auto packed = vb::pack_edges(g, true);
     std::memcpy(edges, packed.data(), packed.size() * sizeof(vb::EdgeRec));
+    const int32_t none = -1;
+    for (const vb::TcTile& t : tp.tiles)
+        for (int64_t x = g.row_ptr[size_t(t.row0)]; x < g.row_ptr[size_t(t.row0 + t.nrows)]; ++x) {
+            for (int k = 0; k < 3; ++k) edges[4 * x + k] = NAN;
+            std::memcpy(edges + 4 * x + 3, &none, 4);
+        }
     for (const vb::TcTile& t : tp.tiles) {
-        const uint16_t* rec = reinterpret_cast<const uint16_t*>(tp.blob.data() + t.blob_off + t.edge_off);
-        const int64_t e0 = g.row_ptr[size_t(t.row0)];
-        for (int i = 0; i < t.n_edges; ++i) {
-            for (int k = 0; k < 3; ++k) edges[4 * (e0 + i) + k] = __half2float(__ushort_as_half(rec[4 * i + k]));
-            const int32_t sl = rec[4 * i + 3];
-            std::memcpy(edges + 4 * (e0 + i) + 3, &sl, 4);
+        const uint8_t* bl = tp.blob.data() + t.blob_off;
+        for (int bk = 0; bk < (t.nrows + 15) / 16; ++bk) {
+            const uint8_t* hd = bl + vb::kTcBlockOff + 32 * bk;
+            for (int c = 0; c < hd[0]; ++c) {
+                const int ci = hd[1] + c;
+                const uint16_t* attr =
+                    reinterpret_cast<const uint16_t*>(bl + t.attr_off + size_t(vb::kTcChunkAttr) * size_t(ci));
+                for (int l = 0; l < 32; ++l)
+                    for (int e = 0; e < 8; ++e) {
+                        if (!((bl[vb::kTcMaskOff + 32 * ci + l] >> e) & 1)) continue;
+                        const int row = 16 * bk + l / 4 + 8 * ((e >> 1) & 1);
+                        const int32_t sl = 8 * hd[2 + 2 * c + (e >> 2)] + 2 * (l % 4) + (e & 1);
+                        if (row >= t.nrows || sl >= t.nsrc) vb::fail(vb::kInternal, "tile plan: a masked position is outside its tile");
+                        const int32_t source = tp.srcs[size_t(t.src_off + sl)];
+                        int64_t x = g.row_ptr[size_t(t.row0 + row)];
+                        while (x < g.row_ptr[size_t(t.row0 + row + 1)] && g.src[size_t(x)] != source) ++x;
+                        if (x == g.row_ptr[size_t(t.row0 + row + 1)]) vb::fail(vb::kInternal, "tile plan: a masked position is not an edge");
+                        for (int k = 0; k < 3; ++k)
+                            edges[4 * x + k] = __half2float(__ushort_as_half(attr[24 * l + 2 * (3 * (e >> 1) + k) + (e & 1)]));
+                        std::memcpy(edges + 4 * x + 3, &sl, 4);
+                    }
+            }
         }
     }
 }

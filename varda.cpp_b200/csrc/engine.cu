@@ -301,6 +301,12 @@ private:
     void predict_pipelined(const float* x, float* y);
     DeviceBuffer proc_inner_, proc_outer_;
     int64_t n_inner_ = 0, n_outer_ = 0;
+    // the same split for the tensor-core processor attention: its tiles reordered, those with no remote
+    // source first (n_tc_inner_ of them); its heavy rows by the row split
+    DeviceBuffer proc_tc_tiles_, proc_heavy_inner_, proc_heavy_outer_;
+    int n_tc_inner_ = 0, n_tc_tiles_ = 0;
+    int64_t n_heavy_inner_ = 0, n_heavy_outer_ = 0;
+    void proc_attention_part(const AttnLayer<T>& b, bool boundary, cudaStream_t s);
     void attention_rows(const GraphDev& g, const AttnLayer<T>& b, const DeviceBuffer& rows, int64_t n, const T* q,
                         int64_t ldq, const T* kk, const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out,
                         cudaStream_t s);
@@ -663,6 +669,24 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         n_inner_ = int64_t(inner.size()), n_outer_ = int64_t(outer.size());
         proc_inner_ = upload(inner.data(), std::max<size_t>(1, inner.size()) * sizeof(int32_t));
         proc_outer_ = upload(outer.data(), std::max<size_t>(1, outer.size()) * sizeof(int32_t));
+        if (g_proc_.tc) {
+            const TcPlan tp = make_tc_tiles(pg, kTcAlignRows);  // the same tiles upload_graph built
+            std::vector<TcTile> in_t, out_t;
+            for (const TcTile& t : tp.tiles) {
+                bool remote = false;
+                for (int i = 0; i < t.nsrc && !remote; ++i) remote = tp.srcs[size_t(t.src_off + i)] >= Hl_;
+                (remote ? out_t : in_t).push_back(t);
+            }
+            n_tc_inner_ = int(in_t.size()), n_tc_tiles_ = int(tp.tiles.size());
+            in_t.insert(in_t.end(), out_t.begin(), out_t.end());
+            proc_tc_tiles_ = upload(in_t.data(), std::max<size_t>(1, in_t.size()) * sizeof(TcTile));
+            std::vector<int32_t> hin, hout;
+            for (int32_t r : tp.heavy)
+                (std::binary_search(inner.begin(), inner.end(), r) ? hin : hout).push_back(r);
+            n_heavy_inner_ = int64_t(hin.size()), n_heavy_outer_ = int64_t(hout.size());
+            proc_heavy_inner_ = upload(hin.data(), std::max<size_t>(1, hin.size()) * sizeof(int32_t));
+            proc_heavy_outer_ = upload(hout.data(), std::max<size_t>(1, hout.size()) * sizeof(int32_t));
+        }
     }
     // pipelined host I/O: decoder chunks of ~Gl / VB_IO_CHUNKS rows (the memory cap's chunks if set),
     // input chunks of ~Gl / (2 VB_IO_CHUNKS) own rows; the decoder tiles respect the chunk boundaries. On C1
@@ -902,6 +926,35 @@ void Engine<T>::attention(const GraphDev& g, const AttnLayer<T>& b, int64_t lo, 
     k::attention<T>(a, s);
 }
 
+// The processor attention of the rows with no remote source (boundary false) or of the others: the
+// tensor-core kernel over the interior or boundary tiles (and the heavy rows among those rows on the
+// gather kernel), or the gather kernel over the row list.
+template <class T>
+void Engine<T>::proc_attention_part(const AttnLayer<T>& b, bool boundary, cudaStream_t s) {
+    const int64_t C = C_, H = Hl_;
+    const T *q = qkvs_, *kk = qkvs_ + C, *v = qkvs_ + 2 * C, *xr = qkvs_ + 3 * C;
+    if constexpr (std::is_same<T, __half>::value) {
+        if (g_proc_.tc) {
+            const int t0 = boundary ? n_tc_inner_ : 0, t1 = boundary ? n_tc_tiles_ : n_tc_inner_;
+            if (t1 > t0) {
+                k::TcArgs t;
+                t.tiles = proc_tc_tiles_.template as<TcTile>(), t.srcs = g_proc_.srcs.template as<int32_t>();
+                t.blob = g_proc_.tblob.template as<uint8_t>();
+                t.tile0 = t0, t.ntiles = t1 - t0, t.dst_lo = 0;
+                t.q = q, t.k = kk, t.v = v, t.xr = xr, t.out = sbuf_, t.ldq = 4 * C, t.ldkv = 4 * C, t.ldxr = 4 * C;
+                t.ldo = C, t.n_q_rows = H, t.n_src = g_proc_.n_src, t.w_e = b.edge_fold.template as<float>();
+                t.C = int(C), t.heads = heads_, t.head_dim = hd_, t.sched = att_sched_;
+                k::attention_tc(t, s);
+            }
+            attention_rows(g_proc_, b, boundary ? proc_heavy_outer_ : proc_heavy_inner_,
+                           boundary ? n_heavy_outer_ : n_heavy_inner_, q, 4 * C, kk, v, 4 * C, xr, 4 * C, sbuf_, s);
+            return;
+        }
+    }
+    attention_rows(g_proc_, b, boundary ? proc_outer_ : proc_inner_, boundary ? n_outer_ : n_inner_, q, 4 * C, kk, v,
+                   4 * C, xr, 4 * C, sbuf_, s);
+}
+
 // The gather attention over an explicit list of rows (local ids) of graph g.
 template <class T>
 void Engine<T>::attention_rows(const GraphDev& g, const AttnLayer<T>& b, const DeviceBuffer& rows, int64_t n, const T* q,
@@ -968,11 +1021,9 @@ void Engine<T>::proc_block(int i, const T* z_in, T* z_out, bool overlap, cudaStr
         VB_CUDA(cudaStreamWaitEvent(cs_, ev_kv_, 0));
         exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, cs_);
         VB_CUDA(cudaEventRecord(ev_halo_, cs_));
-        attention_rows(g_proc_, b, proc_inner_, n_inner_, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C,
-                       4 * C, sbuf_, s);
+        proc_attention_part(b, false, s);
         VB_CUDA(cudaStreamWaitEvent(s, ev_halo_, 0));
-        attention_rows(g_proc_, b, proc_outer_, n_outer_, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C,
-                       4 * C, sbuf_, s);
+        proc_attention_part(b, true, s);
     } else {
         exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, s);  // K|V of remote sources
         attention(g_proc_, b, 0, H, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C, 4 * C, sbuf_, s);
@@ -1002,7 +1053,7 @@ void Engine<T>::processor_block(int i, const float* z_in, float* z_out, int repe
         VB_CUDA(cudaMemcpyAsync(stage, z_in, size_t(H * C) * sizeof(float), cudaMemcpyHostToDevice, s));
         k::convert_2d<float, T>(stage, C, zA_, C, H, C, s);
     }
-    const bool overlap = plan_.world > 1 && cs_ && !prof_ && !g_proc_.tiled && !g_proc_.wide &&
+    const bool overlap = plan_.world > 1 && cs_ && !prof_ && (!g_proc_.tiled || g_proc_.tc) && !g_proc_.wide &&
                          env_int("VB_SHARD_OVERLAP", 1) != 0;
     if (!blk_ev_[0]) VB_CUDA(cudaEventCreate(&blk_ev_[0])), VB_CUDA(cudaEventCreate(&blk_ev_[1]));
     VB_CUDA(cudaEventRecord(blk_ev_[0], s));
@@ -1040,8 +1091,8 @@ bool Engine<T>::middle(cudaStream_t s, HookSink* hk) {
 
     // ---- processor; xh_ holds LN_dst of the block input
     // sharded: exchange / interior-attention overlap, except under the hook or the profiler (whose
-    // per-launch records stay serial) and when the processor runs the tiled or split kernels
-    const bool overlap = plan_.world > 1 && cs_ && !hk && !prof_ && !g_proc_.tiled && !g_proc_.wide &&
+    // per-launch records stay serial) and when the processor runs the shared-memory tiled or split kernels
+    const bool overlap = plan_.world > 1 && cs_ && !hk && !prof_ && (!g_proc_.tiled || g_proc_.tc) && !g_proc_.wide &&
                          env_int("VB_SHARD_OVERLAP", 1) != 0;
     T* z_in = z_enc_;
     T* latent = nullptr;

@@ -235,42 +235,37 @@ TcPlan make_tc_tiles(const CsrGraph& g, int64_t align_rows) {
         tile.row0 = int32_t(row0), tile.nrows = nrows, tile.nsrc = int32_t(open.size());
         tile.src_off = int32_t(t.srcs.size());
         tile.blob_off = int32_t(t.blob.size()), tile.n_edges = ne;
-        tile.edge_off = kTcChunkOff + 256 * n_chunks;
-        tile.blob_bytes = int32_t(align_up(size_t(tile.edge_off) + 8 * size_t(ne), 16));
+        tile.attr_off = kTcMaskOff + 32 * n_chunks;
+        tile.blob_bytes = tile.attr_off + kTcChunkAttr * n_chunks;
         t.srcs.insert(t.srcs.end(), open.begin(), open.end());
         while (t.srcs.size() % 4) t.srcs.push_back(open.back());
         t.blob.resize(t.blob.size() + size_t(tile.blob_bytes), 0);
         uint8_t* bl = t.blob.data() + tile.blob_off;
-        uint16_t* off = reinterpret_cast<uint16_t*>(bl);
-        for (int i = 0; i <= kTcRows + 1; ++i)
-            off[i] = uint16_t(i <= nrows ? g.row_ptr[size_t(row0 + i)] - e0 : ne);
         for (int bk = 0; bk < nb; ++bk) {
             uint8_t* hd = bl + kTcBlockOff + 32 * bk;
             const auto& cl = cols[size_t(bk)];
             hd[0] = uint8_t(cl.size() / 2), hd[1] = uint8_t(chunk0[size_t(bk)]);
             for (size_t k = 0; k < cl.size(); ++k) hd[2 + k] = uint8_t(cl[k] >= 0 ? cl[k] : -1 - cl[k]);
             for (size_t c = 0; c < cl.size() / 2; ++c) {
-                uint8_t* ch = bl + kTcChunkOff + 256 * (chunk0[size_t(bk)] + int(c));
+                const int ci = chunk0[size_t(bk)] + int(c);
+                uint8_t* mask = bl + kTcMaskOff + 32 * ci;
+                uint16_t* attr = reinterpret_cast<uint16_t*>(bl + tile.attr_off + size_t(kTcChunkAttr) * size_t(ci));
                 for (int l = 0; l < 32; ++l) {
                     const int r = l / 4, tq = l % 4;
-                    for (int h = 0; h < 2; ++h) {  // the chunk's first / second column block
-                        const int j = cl[2 * c + size_t(h)];
-                        for (int q = 0; q < 4; ++q) {
-                            const int row = r + (q >= 2 ? 8 : 0), sl = 8 * (j >= 0 ? j : 0) + 2 * tq + (q & 1);
-                            ch[8 * l + 4 * h + q] = j >= 0 ? at[size_t(bk)][size_t(row * kTcMaxSrc + sl)] : 255;
-                        }
+                    for (int e = 0; e < 8; ++e) {
+                        const int j = cl[2 * c + size_t(e >> 2)];  // column block (negative: the padding)
+                        const int row = r + 8 * ((e >> 1) & 1), sl = 8 * (j >= 0 ? j : 0) + 2 * tq + (e & 1);
+                        const int idx = j >= 0 ? at[size_t(bk)][size_t(row * kTcMaxSrc + sl)] : 255;
+                        if (idx == 255) continue;
+                        mask[l] = uint8_t(mask[l] | (1u << e));
+                        const int64_t x = g.row_ptr[size_t(row0 + 16 * bk + row)] + idx;  // the edge
+                        for (int k = 0; k < 3; ++k)  // word 3 (e / 2) + k, half e % 2
+                            attr[24 * l + 2 * (3 * (e >> 1) + k) + (e & 1)] =
+                                half_bits(k < g.attr_dim ? g.attr[size_t(x) * size_t(g.attr_dim) + size_t(k)] : 0.f);
                     }
                 }
             }
         }
-        uint16_t* rec = reinterpret_cast<uint16_t*>(bl + tile.edge_off);
-        for (int i = 0; i < nrows; ++i)
-            for (int64_t e = g.row_ptr[size_t(row0 + i)]; e < g.row_ptr[size_t(row0 + i + 1)]; ++e) {
-                uint16_t* r = rec + 4 * (e - e0);
-                for (int k = 0; k < 3; ++k)
-                    r[k] = half_bits(k < g.attr_dim ? g.attr[size_t(e) * size_t(g.attr_dim) + size_t(k)] : 0.f);
-                r[3] = uint16_t(slot[size_t(g.src[size_t(e)])]);
-            }
         t.tiles.push_back(tile);
         for (int32_t s : open) slot[size_t(s)] = -1;
         open.clear();

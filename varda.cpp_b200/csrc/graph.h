@@ -68,23 +68,24 @@ TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges,
 constexpr int kTcRows = 64, kTcMaxSrc = 128, kTcMaxEdges = 1024;
 // Row alignment of the tile restarts (the multi-GPU destination split rounds its hidden ranges to it).
 constexpr int64_t kTcAlignRows = 64;
-// Per-tile record block (16-byte aligned, one bulk copy), in this order:
-//   u16 row offsets [kTcRows + 2]: edges of tile row i are [off[i], off[i + 1]), relative to the
-//       tile's first edge (rows past the tile: empty);
+// Per-tile record block (16-byte aligned), in this order:
 //   per 16-row block b (at kTcBlockOff + 32 b): u8 chunk count n_b, u8 chunk base (index of the block's
 //       first chunk in the tile), then 2 n_b u8 column-block indices: the block's 8-slot column blocks
-//       that hold edges, in pairs (one pair per chunk; an odd count padded with a repeat whose entries
-//       are all empty);
-//   per chunk (at kTcChunkOff + 256 c): per lane l of a warp, 8 u8 entries: for the m16n8 fragment
-//       positions lane l holds in the chunk's two column blocks ((r, 2t), (r, 2t + 1), (r + 8, 2t),
-//       (r + 8, 2t + 1) with r = l / 4, t = l % 4, first block then second), the index of that edge
-//       within its row, or 255 when (row, slot) is not an edge;
-//   edges at edge_off = kTcChunkOff + 256 n_chunks: 8 bytes each {fp16 a0, a1, a2, u16 slot} (a0, a1
-//   one aligned fp16 pair).
-constexpr int kTcBlockOff = 144, kTcChunkOff = 272, kTcMaxChunks = 4 * (kTcMaxSrc / 16);
+//       that hold edges, in pairs (one pair per chunk; an odd count padded with a repeat that holds no
+//       edge);
+//   per chunk c (at kTcMaskOff + 32 c): per lane l of a warp one u8 mask: bit e set when fragment
+//       position e of lane l in the chunk is an edge. Lane l = 4 r + t holds positions
+//       e = 4 k + 2 h + i: column block k of the chunk (first, second), row r + 8 h of the block, slot
+//       column 2 t + i of the column block;
+//   at attr_off = kTcMaskOff + 32 n_chunks, per chunk 1536 bytes: per lane 48 bytes, for each pair
+//       p = e / 2 of positions (same row, adjacent columns) three fp16x2 words (a0, a1, a2) x
+//       (position 2p, position 2p + 1), zero where there is no edge.
+// The head and masks ([0, attr_off)) are what the kernel stages in shared memory; the attributes it
+// reads from global memory, one coalesced 48-byte run per lane and chunk.
+constexpr int kTcBlockOff = 0, kTcMaskOff = 128, kTcChunkAttr = 1536, kTcMaxChunks = 4 * (kTcMaxSrc / 16);
 struct TcTile {
     int32_t row0, nrows, nsrc, src_off;               // rows [row0, row0 + nrows); sources srcs[src_off, + nsrc)
-    int32_t blob_off, blob_bytes, n_edges, edge_off;  // record block: byte offset, size; edge list offset
+    int32_t blob_off, blob_bytes, n_edges, attr_off;  // record block: byte offset, size; attributes offset
 };
 static_assert(sizeof(TcTile) == 32, "tile descriptor must be 32 bytes");
 struct TcPlan {
