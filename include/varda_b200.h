@@ -149,7 +149,7 @@ int64_t vb_profile_processor_block(vb_model* m, int block, char* buf, size_t len
 
 /* The destination partition vb_load_sharded uses for `rank` of `world` on this model file, computed
  * on the host only (no GPU): JSON with the hidden/data ranges of every rank (and the encoder's hidden
- * ranges with the row moves after the encoder; they equal the hidden ranges unless VB_SHARD_ENC=1),
+ * ranges with the row moves after the encoder; they equal the hidden ranges when VB_SHARD_ENC=0),
  * this rank's halos (global ids), its send lists per peer, and its local CSR graphs (sources in local
  * ids). Same length convention as vb_profile_forward; a negative return is minus the error class. No
  * reference counterpart (the reference runs on one GPU). */

@@ -62,7 +62,7 @@ def _single(mp, xp, dtype, out):
 @pytest.mark.parametrize("name,enc_split", [("c0", 0), ("t256", 0), ("c0", 1), ("t1024", 1), ("c1s", 0), ("c1s", 1)])
 @pytest.mark.parametrize("dtype", [0, 1])
 def test_sharded_equals_single_gpu(name, enc_split, dtype, seeded_model, tmp_path, monkeypatch):
-    """enc_split: the encoder on its own hidden ranges (VB_SHARD_ENC=1), its output rows moved to their
+    """enc_split: the encoder on its own hidden ranges (VB_SHARD_ENC=1, the default), its output rows moved to their
     processor owners; c0 and t1024 move rows between ranks at 2-4 GPUs. c1s (C1's widths, 2,965 hidden
     rows) runs its processor on the tensor-core attention (fp16)."""
     import torch.multiprocessing as tmp
@@ -133,12 +133,14 @@ def _rollout_single(mp, xp, fp, dtype, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("enc_split", [0, 1])
 @pytest.mark.parametrize("dtype", [0, 1])
-def test_sharded_rollout_equals_single_gpu(dtype, seeded_model, tmp_path):
+def test_sharded_rollout_equals_single_gpu(dtype, enc_split, seeded_model, tmp_path, monkeypatch):
     """The rollout's per-step exchange of the encoder-halo rows' outputs: every rank's rows of every
-    step bitwise equal to the single-GPU rollout."""
+    step bitwise equal to the single-GPU rollout, with and without the encoder's own split."""
     import torch.multiprocessing as tmp
     from conftest import rollout_golden
+    monkeypatch.setenv("VB_SHARD_ENC", str(enc_split))
     mp, xp = seeded_model("t256r")
     fp = str(tmp_path / "f.npy")
     np.save(fp, rollout_golden("t256r")["forcings"])

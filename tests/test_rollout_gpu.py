@@ -17,9 +17,26 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 MODELS = ["t256r", "t128r"]
-# rel_absmax per step against the reference CPU fp32 rollout. One step is the predict_step bar
-# (1e-5 fp32, 3e-3 fp16); the autoregressive feedback lets differences grow over the 4 steps.
-TOL = {vb.FP32: 1e-4, vb.FP16: 2e-2}
+# rel_absmax against the reference CPU fp32 rollout: step 0 is a predict_step and has its bar (1e-5
+# fp32, 3e-3 fp16); later steps feed the outputs back (step_bars).
+STEP0 = {vb.FP32: 1e-5, vb.FP16: 3e-3}
+
+
+def step_bars(mp, x, f, n, oldest, step0):
+    """Per-step bars from the model's own error growth, measured on the CPU oracle: g_k = the relative
+    difference at step k between two oracle rollouts whose inputs differ by a seeded relative perturbation
+    of size step0, divided by that difference at step 0 (for the synthetic models here g_k stays within
+    0.77-1.08 over 4 steps). Each step adds at most one predict_step's error (step0), and the error added
+    at step j has grown by g_(s-j) by step s, so bar_s = step0 x sum_(k<=s) max(1, g_k). Nothing here
+    depends on the B200 path."""
+    om = oracle.OracleModel(mp)
+    base = oracle.rollout(om, x, n, f, oldest)
+    rng = np.random.default_rng(123)
+    xq = (x * (1.0 + step0 * rng.uniform(-1.0, 1.0, x.shape))).astype(np.float32)
+    pert = oracle.rollout(om, xq, n, f, oldest)
+    e = [oracle.rel_absmax(pert[s], base[s]) for s in range(n)]
+    g = [max(1.0, v / e[0]) for v in e]
+    return [step0 * sum(g[:s + 1]) for s in range(n)], g
 
 
 def bits(a):
@@ -78,7 +95,8 @@ def test_rollout_parity_and_host_loop_bitwise(name, dt, oldest, seeded_model):
     assert (ms > 0).all()
     ref = gold["y_oldest" if oldest else "y_newest"]
     errs = [oracle.rel_absmax(y[s], ref[s]) for s in range(n)]
-    assert max(errs) <= TOL[dt], errs
+    bars, growth = step_bars(mp, x, f, n, oldest, STEP0[dt])
+    assert all(e <= b for e, b in zip(errs, bars)), f"per-step errors {errs} against bars {bars} (growth {growth})"
     # device loop == host loop on the same backend, bitwise
     host = oracle.rollout(HostLoop(m, oracle.OracleModel(mp).cfg), x, n, f, oldest)
     assert np.array_equal(bits(y), bits(host))
