@@ -231,4 +231,3 @@ def test_processor_block_entry(name, dt, seeded_model):
     with pytest.raises(vb.VardaError):
         m.processor_block(0, None, None, repeats=0)
     m.free()
-

@@ -551,6 +551,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         };
+        // 32 bias values from col0 as fp16 pairs (zero where absent), the same for every lane
+        auto load_bias = [&](int col0, uint32_t(&bh)[16]) {
+            if (p.bias && col0 + 32 <= p.N) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p.bias + col0) + q);
+                    bh[4 * q] = u.x, bh[4 * q + 1] = u.y, bh[4 * q + 2] = u.z, bh[4 * q + 3] = u.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c0 = col0 + 2 * i;
+                    const uint32_t lo = (p.bias && c0 < p.N) ? __half_as_ushort(p.bias[c0]) : 0u;
+                    const uint32_t hi = (p.bias && c0 + 1 < p.N) ? __half_as_ushort(p.bias[c0 + 1]) : 0u;
+                    bh[i] = lo | (hi << 16);
+                }
+            }
+        };
         // the leader's tempty barriers, which both CTAs' epilogue warps release
         const uint32_t te0 = PAIR ? mapa(smem_u32(&tempty[0]), 0) : 0u, te1 = PAIR ? mapa(smem_u32(&tempty[1]), 0) : 0u;
         auto release = [&](int ab) {
@@ -569,9 +587,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int mb = tile / n_n, nb = tile - mb * n_n;
             const int row0 = mb * UM + int(rank) * BM + lg * 32;
             const int colh = nb * BN + half * (BN / 2);
-            // the first chunk's residual loads fly while the accumulator is being computed
-            uint32_t resa[16], resb[16];
+            // the first chunk's residual and bias loads fly while the accumulator is being computed
+            uint32_t resa[16], resb[16], bia[16], bib[16];
             if (EPI == k::kEpiResidual) load_res(row0 + lane, colh, resa);
+            load_bias(colh, bia);
             if (!mbar_wait(&tfull[ab], ap, abort_flag)) break;
             fence_after();
             const uint32_t taddr = tmem + (uint32_t(lg * 32) << 16) + uint32_t(ab * BN + half * (BN / 2));
@@ -591,22 +610,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (c + 1 < kChunks) tmem_ld32_async(taddr + uint32_t((c + 1) * 32), nxt);
                 const int col0 = colh + c * 32;
                 if (EPI == k::kEpiResidual && c + 1 < kChunks) load_res(row0 + lane, col0 + 32, rnxt);
-                uint32_t bh[16];  // bias, fp16 pairs (zero where absent)
-                if (p.bias && col0 + 32 <= p.N) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const uint4 u = __ldg(reinterpret_cast<const uint4*>(p.bias + col0) + q);
-                        bh[4 * q] = u.x, bh[4 * q + 1] = u.y, bh[4 * q + 2] = u.z, bh[4 * q + 3] = u.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int c0 = col0 + 2 * i;
-                        const uint32_t lo = (p.bias && c0 < p.N) ? __half_as_ushort(p.bias[c0]) : 0u;
-                        const uint32_t hi = (p.bias && c0 + 1 < p.N) ? __half_as_ushort(p.bias[c0 + 1]) : 0u;
-                        bh[i] = lo | (hi << 16);
-                    }
-                }
+                uint32_t(&bh)[16] = (c & 1) ? bib : bia;  // this chunk's bias; the next one's in flight
+                if (c + 1 < kChunks) load_bias(col0 + 32, (c & 1) ? bia : bib);
                 uint32_t o[16];  // the output sub-row, fp16 pairs
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
