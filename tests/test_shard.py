@@ -31,7 +31,7 @@ def rows(lo, hi):
 
 @pytest.mark.parametrize("enc_split", [False, True])
 @pytest.mark.parametrize("name", ["t256", "c0"])
-@pytest.mark.parametrize("world", [1, 2, 3, 4])
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
 def test_plan_consistency(name, world, enc_split, seeded_model, monkeypatch):
     mp, _ = seeded_model(name)
     monkeypatch.setenv("VB_SHARD_ENC", "1" if enc_split else "0")
