@@ -1,6 +1,6 @@
 """Kernel microbenchmarks through the C ABI (CUDA events on the launching stream, after warm-up).
 
-    python -m varda_b200.kbench gemm --M 189809 --N 4096 --K 1024 --epi 1 [--engine 2] [--iters 20]
+    python -m varda_b200.kbench gemm --M 189809 --N 4096 --K 1024 --epi 1 [--engine 2] [--iters 20] [--library]
     python -m varda_b200.kbench attention [--config c2] [--dtype fp16] [--impl tc,tiled,gather] [--iters 20]
 
 `attention --config c2` is BASELINE config C2, the isolated processor graph-attention block: the
@@ -56,6 +56,11 @@ def gemm(a):
     s = torch.cuda.current_stream().cuda_stream
     fn = lambda: vb.gemm(vb.FP16, a.engine, A, a.K, W, a.K, b, Y, a.N, R, a.N, a.M, a.N, a.K, a.epi, stream=s)  # noqa
     pk = _peaks()
+    if a.library:  # the library GEMM (cuBLAS through torch.matmul, fp16, no fused epilogue) on the same shape
+        ms = time_launches(lambda: torch.matmul(A, W.t(), out=Y), a.iters, a.warmup)
+        tf = 2.0 * a.M * a.N * a.K / (ms * 1e-3) / 1e12
+        print(json.dumps({"kernel": "library matmul (cuBLAS)", "M": a.M, "N": a.N, "K": a.K, "ms": round(ms, 4),
+                          "tflops": round(tf, 1), "frac_of_burst": round(tf / pk["bf16_tflops"], 3)}))
     # --modes: comma-separated CTA-pair / tile-order settings timed one after another in this process
     # (pair|single)_(dyn|static) -> VB_GEMM_PAIR, VB_GEMM_SCHED; default: the library's defaults
     for mode in (a.modes.split(",") if a.modes else [""]):
@@ -126,6 +131,7 @@ def main():
     g.add_argument("--iters", type=int, default=20)
     g.add_argument("--warmup", type=int, default=3)
     g.add_argument("--modes", default="", help="e.g. pair_dyn,pair_static,single_dyn,single_static")
+    g.add_argument("--library", action="store_true", help="also time cuBLAS (torch.matmul) on the shape")
     t = sub.add_parser("attention")
     t.add_argument("--config", default="c2")
     t.add_argument("--dtype", default="fp16")
