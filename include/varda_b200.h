@@ -228,7 +228,8 @@ enum { VB_TILES_SMEM = 0, VB_TILES_TC = 1 };
  * counts[1] source entries, counts[2] heavy rows (left to the gather kernel); then, where the arrays
  * are non-null and sized by a first call: tiles4 [tiles][4] = {row0, nrows, src0, nsrc}, srcs (a tile's
  * slot s being srcs[src0 + s]: for VB_TILES_SMEM each tile's distinct sources in increasing order, for
- * VB_TILES_TC in order of first appearance along the tile's edges, padded with the last one to a
+ * VB_TILES_TC ordered by the first and then the last 16-row block of the tile that reads them, then by
+ * first appearance along the tile's edges, padded with the last one to a
  * multiple of 4), heavy (rows), edges [E][4] (the CSR-order records {a0, a1, a2, slot or, for heavy
  * rows, source (int bits)}, attributes rounded to fp16). */
 int vb_tile_plan(const int32_t* row_ptr, const int32_t* src, const float* attr_csr, int A, int64_t n_src,

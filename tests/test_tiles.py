@@ -8,8 +8,9 @@
   sources and their stored order.
 * Attributes are rounded to fp16.
 * Tiled rows keep their records in stored order.
-* Tensor-core tiles: slots number a tile's sources in order of first appearance along its edges
-  (padded with the last source to a multiple of 4), so the plan does not depend on how the source
+* Tensor-core tiles: slots number a tile's sources by the first, then the last 16-row block of the tile
+  that reads them, then by first appearance along its edges (padded with the last source to a
+  multiple of 4), so the plan does not depend on how the source
   nodes are numbered; a row with a repeated source is heavy; tiles restart at multiples of 64 rows.
 """
 import numpy as np
@@ -98,7 +99,13 @@ def test_tile_plan_properties(kind, graph):
         if kind == vb.Tiles.TC:
             assert len(np.unique(ts)) == ns, "a tile's sources are distinct"
             first = list(dict.fromkeys(src[rp[r0]:rp[r0 + nr]].tolist()))
-            assert ts.tolist() == first, "slots in order of first appearance along the tile's edges"
+            fb, lb = {}, {}
+            for i in range(nr):
+                for s_ in src[rp[r0 + i]:rp[r0 + i + 1]].tolist():
+                    fb.setdefault(s_, i // 16)
+                    lb[s_] = i // 16
+            want_order = sorted(first, key=lambda s_: (fb[s_], lb[s_]))  # stable: first appearance breaks ties
+            assert ts.tolist() == want_order, "slots by first block, last block, first appearance"
             pad = srcs[s0 + ns:s0 + ((ns + 3) // 4) * 4]
             assert ns == 0 or np.all(pad == ts[-1]), "padded with the last source to a multiple of 4"
             assert r0 // 64 == (r0 + nr - 1) // 64, "tiles restart at multiples of 64 rows"

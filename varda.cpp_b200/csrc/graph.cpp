@@ -205,8 +205,30 @@ TcPlan make_tc_tiles(const CsrGraph& g, int64_t align_rows) {
         if (row0 < 0) return;
         const int64_t e0 = g.row_ptr[size_t(row0)], e1 = g.row_ptr[size_t(end_row)];
         const int nrows = int(end_row - row0), ne = int(e1 - e0);
-        // per 16-row block: the column blocks holding edges, and each (row, slot)'s edge index in its row
         const int nb = (nrows + 15) / 16;
+        // slot order: by the first 16-row block that reads the source, then by the last one, then by first
+        // appearance (stable), so each block's private sources come first in its range and the sources it
+        // shares with the next blocks sit next to theirs: a block's edges fall into fewer 8-slot column
+        // blocks (4.4 per block on the C2 graph against 5.2 in plain first-appearance order). The order
+        // depends only on the tile's rows and edges, not on how the graph's nodes are numbered.
+        {
+            std::vector<int> fb(open.size(), nb), lb(open.size(), -1);
+            for (int i = 0; i < nrows; ++i)
+                for (int64_t x = g.row_ptr[size_t(row0 + i)]; x < g.row_ptr[size_t(row0 + i + 1)]; ++x) {
+                    const size_t k = size_t(slot[size_t(g.src[size_t(x)])]);
+                    fb[k] = std::min(fb[k], i / 16), lb[k] = std::max(lb[k], i / 16);
+                }
+            std::vector<int32_t> ord(open.size());
+            for (size_t k = 0; k < ord.size(); ++k) ord[k] = int32_t(k);
+            std::stable_sort(ord.begin(), ord.end(), [&](int32_t x, int32_t y) {
+                return fb[size_t(x)] != fb[size_t(y)] ? fb[size_t(x)] < fb[size_t(y)] : lb[size_t(x)] < lb[size_t(y)];
+            });
+            std::vector<int32_t> sorted(open.size());
+            for (size_t k = 0; k < ord.size(); ++k) sorted[k] = open[size_t(ord[k])];
+            open.swap(sorted);
+            for (size_t k = 0; k < open.size(); ++k) slot[size_t(open[k])] = int32_t(k);
+        }
+        // per 16-row block: the column blocks holding edges, and each (row, slot)'s edge index in its row
         std::vector<std::vector<int>> cols(static_cast<size_t>(nb));
         std::vector<std::array<uint8_t, 16 * kTcMaxSrc>> at(static_cast<size_t>(nb));
         for (auto& a : at) a.fill(255);
