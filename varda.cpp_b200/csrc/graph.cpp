@@ -311,6 +311,19 @@ TcPlan make_tc_tiles(const CsrGraph& g, int64_t align_rows) {
             if (slot[size_t(g.src[size_t(i)])] < 0) fresh.push_back(g.src[size_t(i)]);
         const bool fits = row0 >= 0 && open.size() + fresh.size() <= size_t(kTcMaxSrc) && d - row0 < kTcRows &&
                           e - g.row_ptr[size_t(row0)] <= kTcMaxEdges;
+        if (!fits && row0 >= 0 && d - row0 > 16 && (d - row0) % 16) {
+            // end the tile at its last whole 16-row block (the kernel's unit of work) and take the rows
+            // after it again into the next tile: fewer, fuller blocks (C2: 11,866 blocks against 14,686)
+            const int64_t end = row0 + (d - row0) / 16 * 16;
+            for (int32_t s : open) slot[size_t(s)] = -1;
+            open.clear();
+            for (int64_t x = g.row_ptr[size_t(row0)]; x < g.row_ptr[size_t(end)]; ++x)
+                if (slot[size_t(g.src[size_t(x)])] < 0)
+                    slot[size_t(g.src[size_t(x)])] = int32_t(open.size()), open.push_back(g.src[size_t(x)]);
+            close(end);
+            d = end - 1;  // the loop goes on at row `end`
+            continue;
+        }
         if (!fits) {
             close(d);
             row0 = d;

@@ -60,7 +60,8 @@ TilePlan make_tiles(const CsrGraph& g, int max_src, int max_rows, int max_edges,
 
 // Tiles of the tensor-core edge attention (attention_tc.cu): runs of at most kTcRows consecutive
 // destination rows whose edges reach at most kTcMaxSrc distinct sources and number at most
-// kTcMaxEdges. A tile's sources are numbered (its "slots") by the first 16-row block of the tile that
+// kTcMaxEdges, grown greedily; a tile that a limit cuts after more than 16 rows ends at its last whole
+// 16-row block (the kernel's unit of work). A tile's sources are numbered (its "slots") by the first 16-row block of the tile that
 // reads them, then by the last one, then by first appearance along the tile's CSR edges, so the
 // numbering depends only on the tile's rows, not on how the graph's nodes are numbered; tiles restart at every multiple of align_rows (so a graph split into row ranges at such
 // multiples gets the same tiles). Rows with more than kTcMaxSrc distinct sources or kTcMaxEdges edges,
