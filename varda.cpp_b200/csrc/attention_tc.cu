@@ -28,12 +28,14 @@
 //   producers  per tile: the record block by one bulk copy (cp.async.bulk); per head: K_h and V_h rows
 //              of the tile's sources and the tile's Q_h rows by 16-byte asynchronous copies (cp.async:
 //              on B200 four warps of them gather scattered 128-byte rows at about 22 bytes per clock per
-//              SM, against 12 for TMA row gathers), completing on the stage's mbarrier, into a 4-deep
-//              ring of head stages laid out with the 128-byte swizzle (full / empty mbarriers).
+//              SM, against 12 for TMA row gathers), completing on the stage's mbarrier, into a 5-deep
+//              (more than 16 heads: 4-deep) ring of head stages laid out with the 128-byte swizzle
+//              (full / empty mbarriers).
 //   consumers  a tile of nb row blocks has nb x heads tasks (head-major); the warps take a stage's tasks
-//              from its counter as they reach it, so they spread over the stages in the ring. Per task: x_r read ahead; Q fragments; qe = Q
-//              W_ext (the edge weights as 8 extra columns: per row <W_e^T q, a>, <q, b_e>); per 16-slot
-//              step the scores, the online weights and O += P V; the W_e / b_e terms; out.
+//              from its counter as they reach it, so they spread over the stages in the ring. Per task:
+//              x_r read ahead; Q fragments; qe = Q W_ext (the edge weights as 8 extra columns: per row
+//              <W_e^T q, a>, <q, b_e>); per 16-slot step the scores, the online weights and O += P V;
+//              the W_e / b_e terms; out.
 // Every mbarrier wait is bounded (4 s of %globaltimer): on timeout the CTA sets the device error flag
 // (read by take_attention_error), stops, and the producers drain their own copies before returning.
 #include <cmath>
@@ -51,7 +53,8 @@ using namespace vb::d;
 namespace {
 
 constexpr int kHD = 64;  // head_dim
-constexpr int kStages = 4;  // head stages
+// head stages in the ring: 5 where the shared memory holds them (heads <= 16: 200 KB of stages + the
+// edge weights), else 4 (5 measured 1.067 against 1.107 ms on C2)
 constexpr int kConsumers = 8, kProducers = 4;
 constexpr int kThreads = 32 * (kConsumers + kProducers);
 // per-thread registers after the split: the launch gives every thread 168 (65536 / 384, rounded down to
@@ -71,11 +74,13 @@ constexpr float kSlack = 8.0f;  // log2 headroom of the weights over their refer
 
 // shared memory layout (dynamic, 1024-byte aligned base)
 constexpr int kOffStage = 0;
-constexpr int kOffWext = kOffStage + kStages * kStageBytes;           // [heads][8 x 64] fp16, 1 KB each
-constexpr int kOffBlob(int heads) { return kOffWext + heads * 1024; }  // 2 record blocks
-constexpr int kOffBar(int heads) { return kOffBlob(heads) + 2 * kBlobMax; }
-constexpr int kSmemBytes(int heads) { return kOffBar(heads) + 256 + 1024; }  // + barriers + alignment slack
-static_assert(kSmemBytes(kMaxHeads) <= 232448, "shared memory budget");
+constexpr int kSmemLimit = 232448;
+constexpr int kOffWext(int st) { return kOffStage + st * kStageBytes; }                 // [heads][8 x 64] fp16, 1 KB each
+constexpr int kOffBlob(int st, int heads) { return kOffWext(st) + heads * 1024; }  // 2 record blocks
+constexpr int kOffBar(int st, int heads) { return kOffBlob(st, heads) + 2 * kBlobMax; }
+constexpr int kSmemBytes(int st, int heads) { return kOffBar(st, heads) + 256 + 1024; }  // + barriers + slack
+static_assert(kSmemBytes(4, kMaxHeads) <= kSmemLimit && kSmemBytes(5, 16) <= kSmemLimit, "shared memory budget");
+constexpr int stages_for(int heads) { return kSmemBytes(5, heads) <= kSmemLimit ? 5 : 4; }
 
 __device__ int g_tc_error = 0;
 
@@ -193,13 +198,14 @@ struct TcParams {
     unsigned* sched;             // dynamic tile order: [tiles handed out, CTAs done], zero between launches; or null
 };
 
+template <int kStages>
 __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int heads = p.heads;
-    uint8_t* wext = sm + kOffWext;
-    uint8_t* blobs = sm + kOffBlob(heads);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar(heads));
+    uint8_t* wext = sm + kOffWext(kStages);
+    uint8_t* blobs = sm + kOffBlob(kStages, heads);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar(kStages, heads));
     uint64_t* full_h = bar;             // [kStages]
     uint64_t* empty_h = bar + kStages;  // [kStages]
     uint64_t* full_t = bar + 2 * kStages;
@@ -605,11 +611,14 @@ void attention_tc(const TcArgs& a, cudaStream_t s) {
     p.sched = a.sched;
     static std::atomic<uint64_t> configured{0};
     once_per_device(configured, [] {
-        VB_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kSmemBytes(kMaxHeads)));
+        VB_CUDA(cudaFuncSetAttribute(attention_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemBytes(4, kMaxHeads)));
+        VB_CUDA(cudaFuncSetAttribute(attention_tc_kernel<5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemLimit));
     });
     const int grid = std::min(a.ntiles, device_sm_count());
-    attention_tc_kernel<<<grid, kThreads, kSmemBytes(a.heads), s>>>(p);
+    if (stages_for(a.heads) == 5) attention_tc_kernel<5><<<grid, kThreads, kSmemBytes(5, a.heads), s>>>(p);
+    else attention_tc_kernel<4><<<grid, kThreads, kSmemBytes(4, a.heads), s>>>(p);
     VB_LAUNCH();
 }
 
