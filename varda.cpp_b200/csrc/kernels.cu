@@ -18,30 +18,34 @@ unsigned grid_for(int64_t n, int per_block) {
     return unsigned(std::max<int64_t>(1, std::min<int64_t>(b, 148 * 16 * 64)));
 }
 
+// Element-wise kernels index with I: 32-bit where the launch's elements fit (the integer division of the
+// row / column split is several times cheaper than in 64 bits), else 64-bit.
+template <class I>
 __global__ void normalise_kernel(const float* __restrict__ x, const float* __restrict__ mul,
-                                 const float* __restrict__ add, float* __restrict__ xn, int64_t n, int V) {
-    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
-        const int v = int(i % V);
+                                 const float* __restrict__ add, float* __restrict__ xn, I n, int V) {
+    for (I i = I(blockIdx.x) * I(blockDim.x) + I(threadIdx.x); i < n; i += I(gridDim.x) * I(blockDim.x)) {
+        const int v = int(i % I(V));
         xn[i] = __fadd_rn(__fmul_rn(x[i], __ldg(mul + v)), __ldg(add + v));
     }
 }
 
+template <class I>
 __global__ void denormalise_kernel(const float* __restrict__ yn, const float* __restrict__ add,
-                                   const float* __restrict__ mul, float* __restrict__ y, int64_t n, int V) {
-    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
-        const int v = int(i % V);
+                                   const float* __restrict__ mul, float* __restrict__ y, I n, int V) {
+    for (I i = I(blockIdx.x) * I(blockDim.x) + I(threadIdx.x); i < n; i += I(gridDim.x) * I(blockDim.x)) {
+        const int v = int(i % I(V));
         y[i] = __fdiv_rn(__fsub_rn(yn[i], __ldg(add + v)), __ldg(mul + v));
     }
 }
 
-template <class T>
+template <class T, class I>
 __global__ void assemble_kernel(const float* __restrict__ xn, const float* __restrict__ attr, int T_in, int64_t G,
                                 int V, int A, T* __restrict__ out, int64_t ld, int64_t slot_rows) {
-    const int64_t n = G * ld;
+    const I n = I(G * ld), ldi = I(ld);
     const int TV = T_in * V;
-    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
-        const int64_t g = i / ld;
-        const int f = int(i - g * ld);
+    for (I i = I(blockIdx.x) * I(blockDim.x) + I(threadIdx.x); i < n; i += I(gridDim.x) * I(blockDim.x)) {
+        const int64_t g = int64_t(i / ldi);
+        const int f = int(i - I(g) * ldi);
         float val = 0.0f;
         if (f < TV) {
             const int t = f / V, v = f - t * V;
@@ -236,15 +240,20 @@ __global__ void __launch_bounds__(256) output_kernel(OutputArgs a) {
 
 }  // namespace
 
+// elements per launch that 32-bit indices cover (a grid-stride step stays below 2^31 too)
+constexpr int64_t kIdx32 = (int64_t(1) << 31) - int64_t(148) * 16 * 64 * 256;
+
 void normalise(const float* x, const float* mul, const float* add, float* xn, int64_t n, int V, cudaStream_t s) {
     if (n <= 0) return;
-    normalise_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, mul, add, xn, n, V);
+    if (n < kIdx32) normalise_kernel<int32_t><<<grid_for(n, 256), 256, 0, s>>>(x, mul, add, xn, int32_t(n), V);
+    else normalise_kernel<int64_t><<<grid_for(n, 256), 256, 0, s>>>(x, mul, add, xn, n, V);
     VB_LAUNCH();
 }
 
 void denormalise(const float* yn, const float* add, const float* mul, float* y, int64_t n, int V, cudaStream_t s) {
     if (n <= 0) return;
-    denormalise_kernel<<<grid_for(n, 256), 256, 0, s>>>(yn, add, mul, y, n, V);
+    if (n < kIdx32) denormalise_kernel<int32_t><<<grid_for(n, 256), 256, 0, s>>>(yn, add, mul, y, int32_t(n), V);
+    else denormalise_kernel<int64_t><<<grid_for(n, 256), 256, 0, s>>>(yn, add, mul, y, n, V);
     VB_LAUNCH();
 }
 
@@ -252,8 +261,12 @@ template <class T>
 void assemble(const float* xn, const float* attr, int T_in, int64_t G, int V, int A, T* out, int64_t ld,
               cudaStream_t s, int64_t slot_rows) {
     if (G <= 0) return;
-    assemble_kernel<T><<<grid_for(G * ld, 256), 256, 0, s>>>(xn, attr, T_in, G, V, A, out, ld,
-                                                            slot_rows > 0 ? slot_rows : G);
+    if (G * ld < kIdx32)
+        assemble_kernel<T, int32_t><<<grid_for(G * ld, 256), 256, 0, s>>>(xn, attr, T_in, G, V, A, out, ld,
+                                                                         slot_rows > 0 ? slot_rows : G);
+    else
+        assemble_kernel<T, int64_t><<<grid_for(G * ld, 256), 256, 0, s>>>(xn, attr, T_in, G, V, A, out, ld,
+                                                                         slot_rows > 0 ? slot_rows : G);
     VB_LAUNCH();
 }
 
