@@ -79,6 +79,8 @@ constexpr int kOffWext(int st) { return kOffStage + st * kStageBytes; }         
 constexpr int kOffBlob(int st, int heads) { return kOffWext(st) + heads * 1024; }  // 2 record blocks
 constexpr int kOffBar(int st, int heads) { return kOffBlob(st, heads) + 2 * kBlobMax; }
 constexpr int kSmemBytes(int st, int heads) { return kOffBar(st, heads) + 256 + 1024; }  // + barriers + slack
+// the 256-byte barrier area: 2 st + 6 mbarriers, then the abort flag, 2 tile indices and st task counters
+static_assert((2 * 5 + 6) * 8 + 4 * (1 + 2 + 5) <= 256, "barrier area");
 static_assert(kSmemBytes(4, kMaxHeads) <= kSmemLimit && kSmemBytes(5, 16) <= kSmemLimit, "shared memory budget");
 constexpr int stages_for(int heads) { return kSmemBytes(5, heads) <= kSmemLimit ? 5 : 4; }
 
