@@ -1,4 +1,4 @@
-"""Benchmark: ms per fp16 predict_step at the Varda shape, plus edge-attention
+"""Benchmark: ms per fp16 predict_step at the Varda shape (the benchmark's config C1), plus edge-attention
 HBM GB/s, on N B200s of one node.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c0|c2|c3|c4]
@@ -12,7 +12,7 @@ edges gather, mostly L2 hits), both from one eager pass with a CUDA event pair a
 (vb_profile_forward). `cpu_baseline` is the reference's own CPU fp32 backend
 (oracle/_ref/ref_dump, built from the reference's sources) timed on this host on a bounded sample.
 
---workload c2 is the isolated processor block (the C1 hidden graph, 189,809 rows,
+--workload c2 is the isolated processor block (the benchmark's config C2: the C1 hidden graph, 189,809 rows,
 2.63M edges with U[0,1) attributes, C=1024, fp16, N(0,1) node features) through vb_processor_block:
 `value` = device ms per block run (LN_dst + the block, K runs on the same input, sharded runs exchanging
 the K|V halo every run), `e2e` = the same with the host fp32 features copied in and the output copied
@@ -20,7 +20,7 @@ back every run. Its `cpu_baseline` / reference arm is the reference CPU backend'
 block: ref_dump on models with 3 and with 1 block over the same 1/8 sample of the graph, half the
 difference, scaled by the row count (C2_SAMPLE_FACTOR).
 
---workload c4 is the 24-step autoregressive rollout of C1: K rollout steps through
+--workload c4 is the 24-step autoregressive rollout of C1 (the benchmark's config C4): K rollout steps through
 vb_rollout (CUDA graph per step, forcings replayed from the host, every step's output copied back to
 pinned host memory), `value` = device ms per rollout step, `e2e` = wall time of the whole rollout call
 per step.

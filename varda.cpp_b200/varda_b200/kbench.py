@@ -3,7 +3,7 @@
     python -m varda_b200.kbench gemm --M 189809 --N 4096 --K 1024 --epi 1 [--engine 2] [--iters 20] [--library]
     python -m varda_b200.kbench attention [--config c2] [--dtype fp16] [--impl tc,tiled,gather] [--iters 20]
 
-`attention --config c2` is BASELINE config C2, the isolated processor graph-attention block: the
+`attention --config c2` is the benchmark's config C2, the isolated processor graph-attention block: the
 hidden graph of C1 (189,809 nodes, ~2.6M directed multi-scale edges in CSR by destination), C=1024,
 16 heads of 64, 3-dim edge attributes uniform[0,1], node features N(0,1), seeded. q, k, v and x_r
 are column slices of one [H, 4C] buffer as in the processor block. Reported: ms per launch, and the
