@@ -58,3 +58,37 @@ def test_gathered_bytes_of_the_processor_attention(tmp_path, monkeypatch):
     """E_proc * 2C * 2 bytes: one fp16 K|V row per processor edge (C0: 20,460 edges, C = 128)."""
     monkeypatch.setattr(bench, "CACHE", str(tmp_path))
     assert bench.proc_gathered_bytes("c0", 128) == 20460 * 2 * 128 * 2
+
+
+def test_traffic_scales_the_captures_to_each_launch():
+    """profiles/traffic.json: a GEMM launch of M rows gets the capture's weight bytes once, its reads per
+    row times M and its output once; a shape without a capture its algorithmic bytes; the processor
+    attention the capture's traffic in proportion to the launch's compulsory bytes."""
+    import json
+    d = json.load(open(bench.TRAFFIC))
+    sh = d["gemm_tc"]["shapes"]["N=4096 K=1024 epi=0"]
+    m0 = d["gemm_tc"]["M"]
+    rec = {"name": "gemm_tc M=65536 N=4096 K=1024 epi=0", "ms": 1.0, "flop": 1.0, "bytes": 0.0}
+    t, src = bench.traffic_for("gemm_tc", [rec])
+    assert t == int(sh["weight"] + (sh["read"] - sh["weight"]) * 65536 / m0 + 65536 * 4096 * 2)
+    assert "gemm_tc_dram" in src
+    other = {"name": "gemm_tc M=100 N=1024 K=4 epi=0", "ms": 1.0, "flop": 1.0, "bytes": 0.0}
+    t2, _ = bench.traffic_for("gemm_tc", [other])
+    assert t2 == 2 * (100 * 4 + 1024 * 4 + 100 * 1024)
+    a = d["attention proc"]
+    att = {"name": "attention proc", "ms": 1.0, "flop": 0.0, "bytes": a["compulsory"] / 2}
+    t3, _ = bench.traffic_for("attention proc", [att])
+    assert t3 == int((a["read"] + a["write"]) / 2)
+    assert bench.traffic_for("layernorm", [att]) == (None, None)
+
+
+def test_reference_env_names_an_openblas_core_type(monkeypatch):
+    monkeypatch.delenv("OPENBLAS_CORETYPE", raising=False)
+    env = bench.ref_env()
+    flags = open("/proc/cpuinfo").read() if os.path.exists("/proc/cpuinfo") else ""
+    if " avx512f" in flags:
+        assert env["OPENBLAS_CORETYPE"] == "SkylakeX"
+    elif " avx2" in flags:
+        assert env["OPENBLAS_CORETYPE"] == "Haswell"
+    monkeypatch.setenv("OPENBLAS_CORETYPE", "Zen")
+    assert bench.ref_env()["OPENBLAS_CORETYPE"] == "Zen", "a caller's choice is kept"
