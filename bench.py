@@ -404,7 +404,7 @@ def traffic_for(kind, records):
     total = 0.0
     if kind == "gemm_tc":
         for r in records:
-            f = dict(kv.split("=") for kv in r["name"].split(" ")[1:])
+            f = dict(kv.split("=") for kv in r["name"].split(" ")[1:] if "=" in kv)  # ("+ln": LayerNorm folded in)
             sh = ent["shapes"].get(f"N={f['N']} K={f['K']} epi={f['epi']}")
             M, N, K = int(f["M"]), int(f["N"]), int(f["K"])
             if sh is None:  # a shape without a capture (the K = 4 embeddings): its algorithmic bytes

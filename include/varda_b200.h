@@ -254,6 +254,27 @@ int vb_gemm(int dtype, int engine, const void* A, int64_t lda, const void* W, in
             int64_t ldy, const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int epilogue, int gelu_tanh,
             void* stream);
 
+/* LayerNorm fused into the GEMMs around it (fp16, tensor cores; no reference counterpart: the
+ * reference runs kernels.h:49-59 as separate launches). A LayerNorm's statistics travel as segment
+ * records: per row and per run of vb_ln_segment_width(N) output columns, {mean, M2} (two floats) of
+ * the fp16 values stored there.
+ * vb_gemm_ln: vb_gemm's tensor-core GEMM (epilogue 0, 1 or 2) that also
+ *   st_out != NULL (epilogue 0 or 2): writes the output rows' records, [M, N / width] float pairs;
+ *   st_in != NULL (epilogue 0 or 1): computes y = LN(A) W^T + b for W, bias folded by
+ *     vb_fold_layernorm, from A's rows' records st_in ([M, nseg_in] pairs of segw_in columns,
+ *     nseg_in <= 16) and the fold's column sums colsum.
+ * vb_fold_layernorm: folds LN weight g and bias be (be may be NULL) into the Linear after it, in place:
+ *   W[n, k] = T(W[n, k] g[k]), bias[n] = T(bias[n] + sum_k be[k] W[n, k]) (bias not NULL: zeros for
+ *   a Linear without one), colsum[n] = sum_k W[n, k] after the fold (fp32).
+ * vb_row_seg_stats: the records of rows of x (C columns, segments of segw) as a GEMM epilogue writes them. */
+int vb_ln_segment_width(int64_t N);
+int vb_gemm_ln(const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* Y, int64_t ldy,
+               const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int epilogue, int gelu_tanh, float* st_out,
+               const float* st_in, const float* colsum, int nseg_in, int segw_in, float eps, void* stream);
+int vb_fold_layernorm(void* W, int64_t ldw, int64_t N, int K, const float* g, const float* be, void* bias,
+                      float* colsum, void* stream);
+int vb_row_seg_stats(const void* x, int64_t ldx, int64_t rows, int C, int segw, float* st, void* stream);
+
 /* layernorm / add_layernorm (src/varda/cuda/kernels.h:49-59); b may be NULL. */
 int vb_layernorm(int dtype, const void* x, int64_t ldx, const float* w, const float* b, void* y, int64_t ldy,
                  int64_t rows, int C, float eps, void* stream);

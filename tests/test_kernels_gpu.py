@@ -189,6 +189,98 @@ def test_gemm_tensor_core_matches_cuda_core():
     assert torch.equal(Y2, Y3)
 
 
+def seg_records_reference(y, segw):
+    """float64 {mean, M2} of every run of segw columns of every row of y."""
+    M, N = y.shape
+    s = y.astype(np.float64).reshape(M, N // segw, segw)
+    m = s.mean(2)
+    return np.stack([m, ((s - m[..., None]) ** 2).sum(2)], -1)
+
+
+@pytest.mark.parametrize("M,N,K,epi", [(1000, 1024, 1024, 2), (700, 384, 256, 0), (333, 128, 512, 2),
+                                       (2000, 1024, 184, 0), (513, 2048, 1024, 2), (300, 256, 64, 0)])
+def test_gemm_ln_records(M, N, K, epi):
+    """LayerNorm records written by the GEMM epilogue (vb_gemm_ln st_out): the output is bitwise the
+    plain GEMM's, each record is the float64 {mean, M2} of its fp16 segment within fp32 rounding (rows
+    with a mean of several standard deviations), and row_seg_stats of the stored output gives the
+    same bits (the engine uses it for rows no GEMM produced)."""
+    rng = np.random.default_rng(M + N + K)
+    A = dev(rng.normal(size=(M, K)), torch.float16)
+    W = dev(rng.normal(size=(N, K)) / math.sqrt(K), torch.float16)
+    b = dev(rng.normal(size=N) * 0.2 + 4.0, torch.float16)
+    R = dev(rng.normal(size=(M, N)) + rng.normal(size=(M, 1)) * 3, torch.float16)
+    segw = vb.ln_segment_width(N)
+    assert segw == (64 if N <= 128 else 128)
+    Y0 = torch.empty((M, N), device="cuda", dtype=torch.float16)
+    Y1 = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float16)
+    st1 = torch.full((M, N // segw, 2), float("nan"), device="cuda", dtype=torch.float32)
+    st2 = torch.full_like(st1, float("nan"))
+    Rp = R if epi == 2 else None
+    vb.gemm(vb.FP16, 2, A, K, W, K, b, Y0, N, Rp, N, M, N, K, epi)
+    vb.gemm_ln(A, K, W, K, b, Y1, N, Rp, N, M, N, K, epi, st_out=st1)
+    vb.row_seg_stats(Y1, N, M, N, segw, st2)
+    torch.cuda.synchronize()
+    vb.check_device()
+    assert torch.equal(Y0, Y1), "writing the records must not change the output"
+    assert torch.equal(st1, st2), "epilogue records and row_seg_stats must agree bitwise"
+    got = st1.cpu().numpy().astype(np.float64)
+    ref = seg_records_reference(Y1.float().cpu().numpy(), segw)
+    scale = np.abs(ref[..., 0]).max() + np.sqrt(ref[..., 1].max() / segw)
+    assert np.abs(got[..., 0] - ref[..., 0]).max() <= 1e-6 * scale
+    assert np.all(np.abs(got[..., 1] - ref[..., 1]) <= 1e-4 * ref[..., 1] + 1e-6 * segw * scale ** 2)
+    with pytest.raises(vb.VardaError):  # GELU epilogues write no records
+        vb.gemm_ln(A, K, W, K, b, Y1, N, None, N, M, N, K, 1, st_out=st1)
+
+
+@pytest.mark.parametrize("M,N,C,epi,shift", [(1000, 4096, 1024, 0, 0.0), (1000, 4096, 1024, 1, 3.0),
+                                             (777, 2048, 384, 0, 8.0), (500, 80, 1024, 0, 1.0),
+                                             (300, 512, 128, 1, 0.0), (1200, 1024, 2048, 0, 2.0)])
+def test_gemm_ln_fold(M, N, C, epi, shift):
+    """A LayerNorm folded into the Linear after it: vb_fold_layernorm on (W, b) with the LN's weight and
+    bias, then vb_gemm_ln on the raw rows and their records (row_seg_stats): against float64
+    LN(x) W^T + b (GELU: exact erf) at the fp16 tolerance, and against the unfused fp16 path (LN kernel,
+    then the GEMM) at the same bar; rows whose mean is `shift` standard deviations off zero, where the
+    fold's two terms cancel the most."""
+    rng = np.random.default_rng(M + N + C)
+    x = rounded(rng.normal(size=(M, C)) * 1.5 + shift * 1.5 * rng.uniform(0.5, 1.0, size=(M, 1)), vb.FP16)
+    g = rng.uniform(0.5, 1.5, C).astype(np.float32)
+    be = (rng.normal(size=C) * 0.3).astype(np.float32)
+    W = rounded(rng.normal(size=(N, C)) / math.sqrt(C), vb.FP16)
+    b = rounded(rng.normal(size=N) * 0.2, vb.FP16)
+    segw = vb.ln_segment_width(C)
+    dx, dg, dbe = dev(x, torch.float16), dev(g, torch.float32), dev(be, torch.float32)
+    ldy = (N + 7) // 8 * 8
+    # unfused: LN kernel then the GEMM
+    t = torch.empty((M, C), device="cuda", dtype=torch.float16)
+    Y0 = torch.zeros((M, ldy), device="cuda", dtype=torch.float16)
+    vb.layernorm(vb.FP16, dx, C, dg, dbe, t, C, M, C, 1e-5)
+    vb.gemm(vb.FP16, 2, t, C, dev(W, torch.float16), C, dev(b, torch.float16), Y0, ldy, None, ldy, M, N, C, epi)
+    # folded
+    Wf, bf = dev(W, torch.float16), dev(b, torch.float16)
+    cs = torch.empty(N, device="cuda", dtype=torch.float32)
+    st = torch.empty((M, C // segw, 2), device="cuda", dtype=torch.float32)
+    vb.fold_layernorm(Wf, C, N, C, dg, dbe, bf, cs)
+    vb.row_seg_stats(dx, C, M, C, segw, st)
+    Y = torch.full((M, ldy), float("nan"), device="cuda", dtype=torch.float16)
+    vb.gemm_ln(dx, C, Wf, C, bf, Y, ldy, None, 0, M, N, C, epi, st_in=st, colsum=cs, nseg_in=C // segw,
+               segw_in=segw, eps=1e-5)
+    torch.cuda.synchronize()
+    vb.check_device()
+    xd = x.astype(np.float64)
+    m = xd.mean(1, keepdims=True)
+    ln = (xd - m) / np.sqrt(((xd - m) ** 2).mean(1, keepdims=True) + 1e-5) * g + be
+    ref = gemm_reference(ln, W, b, None, epi, False, True)
+    got = Y.float().cpu().numpy()[:, :N]
+    assert oracle.rel_absmax(got, ref) <= 2e-3
+    assert oracle.rel_absmax(got, Y0.float().cpu().numpy()[:, :N]) <= 2e-3
+    # the folded weights and sums
+    Wg = (W.astype(np.float32) * g).astype(np.float16)  # fp32 product, rounded once to fp16
+    assert np.array_equal(Wf.cpu().numpy(), Wg)
+    assert np.allclose(cs.cpu().numpy(), Wg.astype(np.float64).sum(1), rtol=1e-5, atol=1e-5)
+    bref = b.astype(np.float64) + W.astype(np.float64) @ be.astype(np.float64)
+    assert np.allclose(bf.float().cpu().numpy(), bref, rtol=2e-3, atol=2e-3)
+
+
 @pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])
 @pytest.mark.parametrize("C", [128, 256, 384, 768, 1024, 2048])
 def test_layernorm(C, dt):

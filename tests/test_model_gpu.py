@@ -183,6 +183,67 @@ def test_attention_tc_choice(name, tc, chunk, seeded_model, monkeypatch):
         assert np.array_equal(y0, y)
 
 
+@pytest.mark.parametrize("name", ["t256", "t1024", "c0", "t128", "t2048"])
+def test_layernorm_fold(name, seeded_model, monkeypatch, tmp_path):
+    """fp16 folds LayerNorms into the Linear after them: the producing GEMM's epilogue writes per-row
+    segment statistics, the next GEMM runs on the raw rows with W' = T(W g), and its epilogue forms
+    rstd (x W'^T) - rstd mean colsum + b'. VB_LN_FOLD=1 (default) folds every LN but ln_mlp (whose GELU
+    GEMM keeps its LN kernel), 2 folds all of them, 0 none. Checked: the LayerNorm launches each mode
+    leaves; every mode meets the contract tolerance against the oracle on every key; and on a copy of
+    the model whose embedding biases are shifted by +16 (every LN input row then has a mean of about 16
+    standard deviations, where the fold's two terms cancel most, and fp16 storage of the rows themselves
+    costs accuracy in every mode) the folded runs are no further from the oracle than the unfolded one,
+    up to the tolerance."""
+    mp, xp = seeded_model(name)
+    x = np.array(st.read(xp)[0]["in.x"])
+    ref = oracle_acts(name, mp, x)
+
+    def run(path, mode):
+        monkeypatch.setenv("VB_LN_FOLD", mode)
+        m = vb.Model.load(path, precision=vb.FP16)
+        acts = {}
+        m.predict_step(x, hook=lambda k, a: acts.__setitem__(k, a))
+        names = [r["name"] for r in m.profile()]
+        n_proc = m.n_proc
+        vb.check_device()
+        m.free()
+        return acts, names, n_proc
+
+    runs = {}
+    for mode in ("0", "1", "2"):
+        acts, names, n_proc = run(mp, mode)
+        runs[mode] = acts
+        n_ln = sum(n == "layernorm" for n in names)
+        n_add = sum(n == "add_layernorm" for n in names)
+        assert n_add <= 1
+        if mode == "0":
+            assert n_ln >= n_proc + 2 and not any(n.endswith("+ln") for n in names)
+        else:  # mode 1 keeps ln_mlp of the encoder, every processor block and the decoder
+            assert n_ln == {"1": n_proc + 2, "2": 0}[mode], (mode, n_ln, names)
+            assert any(n.endswith("+ln") for n in names)
+        for k, r in ref.items():
+            tol = 1e-6 if k in EXACT else TOL[vb.FP16]
+            assert oracle.rel_absmax(acts[k], r) <= tol, (mode, k)
+
+    if name not in ("t256", "t1024"):
+        return
+    tensors, meta = st.read(mp)
+    shifted = {k: np.array(v) for k, v in tensors.items()}
+    for k in ("enc.emb_src.bias", "enc.emb_dst.bias", "dec.emb_dst.bias"):
+        if k in shifted:
+            shifted[k] = (shifted[k] + 16.0).astype(shifted[k].dtype)
+    sp = str(tmp_path / f"{name}_shifted.safetensors")
+    st.write(sp, shifted, meta)
+    sref = {}
+    oracle.OracleModel(sp).predict_step(x, lambda k, a: sref.__setitem__(k, a))
+    plain = run(sp, "0")[0]
+    for mode in ("1", "2"):
+        folded = run(sp, mode)[0]
+        for k in plain:
+            ef, ep = oracle.rel_absmax(folded[k], sref[k]), oracle.rel_absmax(plain[k], sref[k])
+            assert ef <= max(TOL[vb.FP16], 1.5 * ep), f"mode {mode} {k}: folded {ef:.3e}, unfolded {ep:.3e}"
+
+
 @pytest.mark.parametrize("dt", [vb.FP32, vb.FP16])
 @pytest.mark.parametrize("name", ["t256", "t512", "c0"])
 def test_wide_rows_by_parts(name, dt, seeded_model, monkeypatch):

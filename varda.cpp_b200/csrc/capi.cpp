@@ -601,6 +601,39 @@ int vb_gemm(int dtype, int engine, const void* A, int64_t lda, const void* W, in
     });
 }
 
+int vb_ln_segment_width(int64_t N) { return vb::tc::stats_segw(N); }
+
+int vb_gemm_ln(const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* Y, int64_t ldy,
+               const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int epilogue, int gelu_tanh, float* st_out,
+               const float* st_in, const float* colsum, int nseg_in, int segw_in, float eps, void* stream) {
+    return guard([&] {
+        if (epilogue < 0 || epilogue > 2) vb::fail(vb::kInvalidArgument, "epilogue");
+        vb::k::GemmArgs<__half> a;
+        a.A = static_cast<const __half*>(A), a.lda = lda, a.W = static_cast<const __half*>(W), a.ldw = ldw;
+        a.bias = static_cast<const __half*>(bias), a.C = static_cast<__half*>(Y), a.ldc = ldy;
+        a.R = static_cast<const __half*>(R), a.ldr = ldr, a.M = M, a.N = N, a.K = K, a.epi = epilogue;
+        a.gelu_tanh = gelu_tanh != 0;
+        a.st_out = reinterpret_cast<float2*>(st_out), a.st_in = reinterpret_cast<const float2*>(st_in);
+        a.colsum = colsum, a.nseg_in = nseg_in, a.segw_in = segw_in, a.eps = eps;
+        if (!vb::tc::supported(a)) vb::fail(vb::kUnsupported, "gemm_ln: operands or LayerNorm arguments not supported");
+        vb::tc::gemm(a, S(stream));
+    });
+}
+
+int vb_fold_layernorm(void* W, int64_t ldw, int64_t N, int K, const float* g, const float* be, void* bias,
+                      float* colsum, void* stream) {
+    return guard([&] {
+        if (!W || !g || !bias || !colsum || K < 1 || ldw < K) vb::fail(vb::kInvalidArgument, "fold_layernorm");
+        vb::k::fold_layernorm(static_cast<__half*>(W), ldw, N, K, g, be, static_cast<__half*>(bias), colsum, S(stream));
+    });
+}
+
+int vb_row_seg_stats(const void* x, int64_t ldx, int64_t rows, int C, int segw, float* st, void* stream) {
+    return guard([&] {
+        vb::k::row_seg_stats(static_cast<const __half*>(x), ldx, rows, C, segw, reinterpret_cast<float2*>(st), S(stream));
+    });
+}
+
 int vb_layernorm(int dtype, const void* x, int64_t ldx, const float* w, const float* b, void* y, int64_t ldy,
                  int64_t rows, int C, float eps, void* stream) {
     return guard([&] {

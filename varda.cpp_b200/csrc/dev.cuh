@@ -90,6 +90,46 @@ __device__ __forceinline__ float warp_sum(float x) {
     return x;
 }
 
+// LayerNorm statistics of a row kept as segment records. A segment is a run of segw consecutive
+// columns (the column half one GEMM epilogue warp writes); its record is {mean, M2} (M2 the sum of
+// squared deviations from the segment mean) of the fp16 values stored there, accumulated in column
+// order with the even and the odd columns in separate fp32 lanes, relative to the segment's first
+// value k (no cancellation for rows with a large mean). The GEMM epilogue and row_seg_stats use these
+// same functions in the same order, so a record does not depend on which kernel made it.
+__device__ __forceinline__ void seg_add(float2& s1, float2& s2, float k, float2 v) {
+    const float2 dv = __fadd2_rn(v, make_float2(-k, -k));
+    s1 = __fadd2_rn(s1, dv);
+    s2 = __ffma2_rn(dv, dv, s2);
+}
+__device__ __forceinline__ float2 seg_record(float2 s1, float2 s2, float k, float n) {
+    const float a = __fadd_rn(s1.x, s1.y), q = __fadd_rn(s2.x, s2.y);
+    const float m = __fdiv_rn(a, n);
+    return make_float2(__fadd_rn(k, m), __fmaf_rn(-a, m, q));  // mean = k + a / n, M2 = q - a^2 / n
+}
+// A row's mean and 1 / sqrt(var + eps) from its nseg <= kMax records (segments of segw columns,
+// C = nseg segw; record i at rec[i stride]), all loads issued first: the mean of the segment means, then
+// M2 = sum of (M2_s + segw (mean_s - mean)^2) in segment order, var = M2 / C.
+template <int kMax>
+__device__ __forceinline__ float2 ln_from_records(const float2* rec, int stride, int nseg, float segw, float eps) {
+    float2 r[kMax];
+#pragma unroll
+    for (int i = 0; i < kMax; ++i) r[i] = i < nseg ? __ldg(rec + i * stride) : make_float2(0.0f, 0.0f);
+    float ms = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMax; ++i)
+        if (i < nseg) ms = __fadd_rn(ms, r[i].x);
+    const float mean = __fdiv_rn(ms, float(nseg));
+    float m2 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMax; ++i)
+        if (i < nseg) {
+            const float dm = __fadd_rn(r[i].x, -mean);
+            m2 = __fadd_rn(m2, __fmaf_rn(__fmul_rn(segw, dm), dm, r[i].y));
+        }
+    const float var = __fdiv_rn(m2, __fmul_rn(segw, float(nseg)));
+    return make_float2(mean, 1.0f / sqrtf(var + eps));
+}
+
 // GELU, torch's formulas in fp32: exact x/2 (1 + erf(x / sqrt 2)), or the tanh form.
 __device__ __forceinline__ float gelu(float x, bool tanh_approx) {
     if (!tanh_approx) return x * 0.5f * (1.0f + erff(x * 0.70710678118654752440f));

@@ -194,8 +194,21 @@ private:
     T* act(size_t elems);
     float* actf(size_t elems);
 
+    // st_out: write the output rows' LayerNorm segment records there; st_in: L has a LayerNorm folded in
+    // and x's rows have their records there (both only with fold_)
     void linear(const Dense<T>& L, const T* x, int64_t ldx, T* y, int64_t ldy, int64_t M, cudaStream_t s,
-                int epi = k::kEpiBias, const T* R = nullptr, int64_t ldr = 0);
+                int epi = k::kEpiBias, const T* R = nullptr, int64_t ldr = 0, float2* st_out = nullptr,
+                const float2* st_in = nullptr);
+    // y = L(LN(x)) for x [M, C]: when L has the LN folded in, L on x and x's records st; else the LN
+    // kernel into xh (which may be x), then L
+    void ln_linear(const Affine& n, const Dense<T>& L, const T* x, const float2* st, T* xh, T* y, int64_t ldy,
+                   int64_t M, cudaStream_t s, int epi = k::kEpiBias) {
+        if (L.cs()) return linear(L, x, C_, y, ldy, M, s, epi, nullptr, 0, nullptr, st);
+        ln(x, n, xh, M, s);
+        linear(L, xh, C_, y, ldy, M, s, epi);
+    }
+    // the records of rows [0, rows) of x when no GEMM epilogue wrote them
+    void row_stats(const T* x, int64_t rows, float2* st, cudaStream_t s);
     void attention(const GraphDev& g, const AttnLayer<T>& b, int64_t lo, int64_t n, const T* q, int64_t ldq, const T* kk,
                    const T* v, int64_t ldkv, const T* xr, int64_t ldxr, T* out, cudaStream_t s);
     void forward(const float* xn, float* yn, cudaStream_t s, HookSink* hk);
@@ -218,6 +231,16 @@ private:
     int dev_ = 0;
     cudaStream_t stream_ = nullptr;
     bool use_tc_ = false;
+    // LayerNorm folded into the Linear after it (fp16 tensor-core path): an LN's statistics are segment
+    // records of its input rows, written by the epilogue of the GEMM that produced them (or by
+    // row_stats), and the Linear's weights carry the LN's affine parameters. VB_LN_FOLD: 1 (default) the
+    // LNs before the bias-epilogue Linears (ln_src, ln_dst, out_norm); 2 also ln_mlp, whose GELU GEMM's
+    // epilogue bounds it already (its fold measured slower than the LN kernel it removes); 0 none.
+    // stA_: the records of a block's input (and of the decoder's emb_dst and block output), stB_: of its
+    // out1 (fold_mlp_); nseg_ records of segw_ columns per row.
+    bool fold_ = false, fold_mlp_ = false;
+    float2 *stA_ = nullptr, *stB_ = nullptr;
+    int nseg_ = 0, segw_ = 0;
     // the dynamic tile order's counters of this model's GEMMs and tensor-core attention launches (all on
     // its stream, one at a time): words 0-1 and 2-3 of gemm_sched_
     DeviceBuffer gemm_sched_;
@@ -744,6 +767,37 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
         dec_ = pl.layer("dec.block", true, C_, mlp_);
     }
     file.require_all_consumed();
+    {
+        const int lnf = use_tc_ ? env_int("VB_LN_FOLD", 1) : 0;
+        fold_ = lnf != 0, fold_mlp_ = lnf >= 2;
+    }
+    if constexpr (std::is_same<T, __half>::value) {
+        if (fold_) {
+            segw_ = tc::stats_segw(C_), nseg_ = C_ / segw_;
+            auto fold = [&](Dense<T>& L, const Affine& n) {
+                if (!L.bias.get()) {
+                    L.bias.alloc(size_t(L.out) * sizeof(T));
+                    VB_CUDA(cudaMemset(L.bias.get(), 0, size_t(L.out) * sizeof(T)));
+                }
+                L.colsum.alloc(size_t(L.out) * sizeof(float));
+                weight_bytes_ += size_t(L.out) * sizeof(float);
+                k::fold_layernorm(L.weight.template as<__half>(), L.ld_in, L.out, int(L.in), n.g(), n.b(),
+                                  L.bias.template as<__half>(), L.colsum.template as<float>(), stream_);
+            };
+            fold(enc_.proj_kv, enc_.norm_src);
+            fold(enc_.proj_qx, enc_.norm_dst);
+            for (AttnLayer<T>& b : proc_) fold(b.proj_qkvx, b.norm_dst);
+            if (!cfg_.latent_skip) fold(dec_.proj_kv, dec_.norm_src);  // else LN(latent + skip) by add_layernorm
+            fold(dec_.proj_qx, dec_.norm_dst);
+            fold(dec_out_proj_, dec_out_norm_);
+            if (fold_mlp_) {
+                fold(enc_.ffn_up, enc_.norm_ffn);
+                for (AttnLayer<T>& b : proc_) fold(b.ffn_up, b.norm_ffn);
+                fold(dec_.ffn_up, dec_.norm_ffn);
+            }
+            VB_CUDA(cudaStreamSynchronize(stream_));
+        }
+    }
 
     lt.mark("weights");
     // ---- activations (this rank's rows)
@@ -765,6 +819,11 @@ Engine<T>::Engine(const std::string& path, const Options& o) : opts_(o) {
     sbuf_ = act(size_t(Hm * C_));
     out1_ = act(size_t(Hm * C_));
     hbuf_ = act(size_t(Hm * mlp_));
+    if (fold_) {  // records of the encoder's source rows, the hidden rows or a decoder chunk
+        const int64_t rows = std::max({Gx_, Hm, dec_rows_});
+        stA_ = reinterpret_cast<float2*>(actf(size_t(rows * nseg_ * 2)));
+        if (fold_mlp_) stB_ = reinterpret_cast<float2*>(actf(size_t(rows * nseg_ * 2)));
+    }
     // Shared region: the encoder's source side ([Gx, C] embedding + [Gx, 2C] k|v), then the decoder's
     // destination chunks (6C + mlp per row). All own data rows in one chunk unless limited.
     const int64_t enc_elems = Gx_ * 3 * C_;
@@ -825,22 +884,39 @@ void Engine<T>::use_high_priority_stream() {
 
 template <class T>
 void Engine<T>::linear(const Dense<T>& L, const T* x, int64_t ldx, T* y, int64_t ldy, int64_t M, cudaStream_t s,
-                       int epi, const T* R, int64_t ldr) {
+                       int epi, const T* R, int64_t ldr, float2* st_out, const float2* st_in) {
+    if (M <= 0) return;
     k::GemmArgs<T> a;
     a.A = x, a.lda = ldx, a.W = L.w(), a.ldw = L.ld_in, a.bias = L.b(), a.C = y, a.ldc = ldy;
     a.R = R, a.ldr = ldr, a.M = M, a.N = L.out, a.K = L.in, a.epi = epi, a.gelu_tanh = gelu_tanh_;
+    if (fold_) {
+        a.st_out = st_out;
+        if (st_in) a.st_in = st_in, a.colsum = L.cs(), a.nseg_in = nseg_, a.segw_in = segw_, a.eps = eps_;
+        if (bool(st_in) != bool(L.cs())) fail(kInternal, "linear: LayerNorm fold mismatch");
+    }
     if constexpr (std::is_same<T, __half>::value) {
         if (use_tc_ && tc::supported(a)) {
             Span sp(this, s, "gemm_tc M=" + std::to_string(M) + " N=" + std::to_string(L.out) + " K=" +
-                                 std::to_string(L.in) + " epi=" + std::to_string(epi),
+                                 std::to_string(L.in) + " epi=" + std::to_string(epi) + (a.st_in ? " +ln" : ""),
                     2.0 * double(M) * double(L.out) * double(L.in), 0);
             tc::gemm(a, s, sched_);
             return;
         }
     }
+    if (a.st_in || a.st_out) fail(kInternal, "linear: LayerNorm fusion needs the tensor-core GEMM");
     Span sp(this, s, "gemm_simt M=" + std::to_string(M) + " N=" + std::to_string(L.out) + " K=" + std::to_string(L.in) +
                          " epi=" + std::to_string(epi), 2.0 * double(M) * double(L.out) * double(L.in), 0);
     k::gemm_simt<T>(a, s);
+}
+
+template <class T>
+void Engine<T>::row_stats(const T* x, int64_t rows, float2* st, cudaStream_t s) {
+    if constexpr (std::is_same<T, __half>::value) {
+        Span sp(this, s, "ln_stats", 0, double(rows) * (C_ * sizeof(T) + nseg_ * sizeof(float2)));
+        k::row_seg_stats(x, C_, rows, C_, segw_, st, s);
+    } else {
+        fail(kInternal, "row_stats: fp16 only");
+    }
 }
 
 template <class T>
@@ -991,10 +1067,10 @@ void Engine<T>::enc_source(const float* xn, int64_t slot_rows, int64_t r0, int64
     }
     T* emb_src = region_ + r0 * C;
     T* kv_enc = region_ + G * C + r0 * 2 * C;
-    linear(enc_emb_src_, x_data_ + r0 * ldF_, ldF_, emb_src, C, n, s);
+    float2* st = fold_ ? stA_ + r0 * nseg_ : nullptr;
+    linear(enc_emb_src_, x_data_ + r0 * ldF_, ldF_, emb_src, C, n, s, k::kEpiBias, nullptr, 0, st);
     if (hk) hk->emit("enc.emb_src", emb_src, C, n, C, {n, C});
-    ln(emb_src, enc_.norm_src, emb_src, n, s);
-    linear(enc_.proj_kv, emb_src, C, kv_enc, 2 * C, n, s);
+    ln_linear(enc_.norm_src, enc_.proj_kv, emb_src, st, emb_src, kv_enc, 2 * C, n, s);
 }
 
 // Encoder destination side before the attention (needs no input): emb_dst of the hidden attributes,
@@ -1003,18 +1079,19 @@ template <class T>
 void Engine<T>::enc_dest_pre(cudaStream_t s, HookSink* hk) {
     const int64_t H = El_, C = C_;
     T* emb_dst = zA_;
-    linear(enc_emb_dst_, h_attr_.as<T>(), ldA_, emb_dst, C, H, s);
+    linear(enc_emb_dst_, h_attr_.as<T>(), ldA_, emb_dst, C, H, s, k::kEpiBias, nullptr, 0, stA_);
     if (hk) hk->emit("enc.emb_dst", emb_dst, C, H, C, {H, C});
-    ln(emb_dst, enc_.norm_dst, xh_, H, s);
-    linear(enc_.proj_qx, xh_, C, qkvs_, 2 * C, H, s);
+    ln_linear(enc_.norm_dst, enc_.proj_qx, emb_dst, stA_, xh_, qkvs_, 2 * C, H, s);
 }
 
-// Processor block i on this rank's hidden rows: xh_ holds LN_dst(z_in); z_out = the block's output.
+// Processor block i on this rank's hidden rows: xh_ holds LN_dst(z_in) (with fold_: stA_ holds z_in's
+// records); z_out = the block's output (with fold_ its records into stA_).
 template <class T>
 void Engine<T>::proc_block(int i, const T* z_in, T* z_out, bool overlap, cudaStream_t s) {
     const int64_t H = Hl_, C = C_;
     const AttnLayer<T>& b = proc_[size_t(i)];
-    linear(b.proj_qkvx, xh_, C, qkvs_, 4 * C, H, s);
+    if (fold_) linear(b.proj_qkvx, z_in, C, qkvs_, 4 * C, H, s, k::kEpiBias, nullptr, 0, nullptr, stA_);
+    else linear(b.proj_qkvx, xh_, C, qkvs_, 4 * C, H, s);
     if (overlap) {
         // K|V of remote sources on the communication stream while the interior rows run
         VB_CUDA(cudaEventRecord(ev_kv_, s));
@@ -1028,10 +1105,9 @@ void Engine<T>::proc_block(int i, const T* z_in, T* z_out, bool overlap, cudaStr
         exchange(xp_, qkvs_ + C, 4 * C, qkvs_ + H * 4 * C + C, 4 * C, false, s);  // K|V of remote sources
         attention(g_proc_, b, 0, H, qkvs_, 4 * C, qkvs_ + C, qkvs_ + 2 * C, 4 * C, qkvs_ + 3 * C, 4 * C, sbuf_, s);
     }
-    linear(b.proj_out, sbuf_, C, out1_, C, H, s, k::kEpiResidual, z_in, C);
-    ln(out1_, b.norm_ffn, xh_, H, s);
-    linear(b.ffn_up, xh_, C, hbuf_, mlp_, H, s, k::kEpiGelu);
-    linear(b.ffn_down, hbuf_, mlp_, z_out, C, H, s, k::kEpiResidual, out1_, C);
+    linear(b.proj_out, sbuf_, C, out1_, C, H, s, k::kEpiResidual, z_in, C, fold_mlp_ ? stB_ : nullptr);
+    ln_linear(b.norm_ffn, b.ffn_up, out1_, stB_, xh_, hbuf_, mlp_, H, s, k::kEpiGelu);
+    linear(b.ffn_down, hbuf_, mlp_, z_out, C, H, s, k::kEpiResidual, out1_, C, stA_);
 }
 
 // The isolated processor block (the benchmark's C2 workload): LN_dst then block `i`, `repeats` times on
@@ -1058,7 +1134,8 @@ void Engine<T>::processor_block(int i, const float* z_in, float* z_out, int repe
     if (!blk_ev_[0]) VB_CUDA(cudaEventCreate(&blk_ev_[0])), VB_CUDA(cudaEventCreate(&blk_ev_[1]));
     VB_CUDA(cudaEventRecord(blk_ev_[0], s));
     for (int r = 0; r < repeats; ++r) {
-        ln(zA_, proc_[size_t(i)].norm_dst, xh_, H, s);
+        if (fold_) row_stats(zA_, H, stA_, s);
+        else ln(zA_, proc_[size_t(i)].norm_dst, xh_, H, s);
         proc_block(i, zA_, zB_, overlap, s);
     }
     VB_CUDA(cudaEventRecord(blk_ev_[1], s));
@@ -1081,13 +1158,15 @@ bool Engine<T>::middle(cudaStream_t s, HookSink* hk) {
     // processor block) and its rows then move to their processor owners' z_enc_
     T* enc_out = emove_.on ? zB_ : z_enc_;
     attention(g_enc_, enc_, 0, E, qkvs_, 2 * C, kv_enc, kv_enc + C, 2 * C, qkvs_ + C, 2 * C, sbuf_, s);
-    linear(enc_.proj_out, sbuf_, C, out1_, C, E, s, k::kEpiResidual, emb_dst, C);
-    ln(out1_, enc_.norm_ffn, xh_, E, s);
-    linear(enc_.ffn_up, xh_, C, hbuf_, mlp_, E, s, k::kEpiGelu);
-    linear(enc_.ffn_down, hbuf_, mlp_, enc_out, C, E, s, k::kEpiResidual, out1_, C);
-    if (emove_.on) enc_redistribute(enc_out, z_enc_, s);
+    linear(enc_.proj_out, sbuf_, C, out1_, C, E, s, k::kEpiResidual, emb_dst, C, fold_mlp_ ? stB_ : nullptr);
+    ln_linear(enc_.norm_ffn, enc_.ffn_up, out1_, stB_, xh_, hbuf_, mlp_, E, s, k::kEpiGelu);
+    linear(enc_.ffn_down, hbuf_, mlp_, enc_out, C, E, s, k::kEpiResidual, out1_, C, emove_.on ? nullptr : stA_);
+    if (emove_.on) {
+        enc_redistribute(enc_out, z_enc_, s);
+        if (fold_) row_stats(z_enc_, H, stA_, s);  // the same records the epilogue would have written
+    }
     if (hk) hk->emit("enc.out", z_enc_, C, H, C, {H, C});
-    ln(z_enc_, proc_[0].norm_dst, xh_, H, s);
+    if (!fold_) ln(z_enc_, proc_[0].norm_dst, xh_, H, s);
 
     // ---- processor; xh_ holds LN_dst of the block input
     // sharded: exchange / interior-attention overlap, except under the hook or the profiler (whose
@@ -1101,15 +1180,16 @@ bool Engine<T>::middle(cudaStream_t s, HookSink* hk) {
         proc_block(i, z_in, z_out, overlap, s);
         if (hk) hk->emit("proc." + std::to_string(i) + ".out", z_out, C, H, C, {H, C});
         if (i + 1 < n_proc_) {
-            k::layernorm<T>(z_out, C, proc_[size_t(i + 1)].norm_dst.g(), proc_[size_t(i + 1)].norm_dst.b(), xh_, C, H,
-                            C_, eps_, s);
+            if (!fold_)  // (fold_: stA_ holds z_out's records)
+                k::layernorm<T>(z_out, C, proc_[size_t(i + 1)].norm_dst.g(), proc_[size_t(i + 1)].norm_dst.b(), xh_, C,
+                                H, C_, eps_, s);
         } else if (cfg_.latent_skip) {
             latent = z_in == z_enc_ ? sbuf_ : z_in;  // a dead buffer
             Span sp(this, s, "add_layernorm", 0, double(H) * C_ * 4 * sizeof(T));
             k::add_layernorm<T>(z_out, z_enc_, latent, dec_.norm_src.g(), dec_.norm_src.b(), xh_, C, H, C_, eps_, s);
         } else {
             latent = z_out;
-            ln(z_out, dec_.norm_src, xh_, H, s);
+            if (!fold_) ln(z_out, dec_.norm_src, xh_, H, s);
         }
         z_in = z_out;
     }
@@ -1117,7 +1197,8 @@ bool Engine<T>::middle(cudaStream_t s, HookSink* hk) {
 
     // ---- decoder, source side: [k | v] of LN_src(latent)
     T* kv_dec = qkvs_;
-    linear(dec_.proj_kv, xh_, C, kv_dec, 2 * C, H, s);
+    if (fold_ && !cfg_.latent_skip) linear(dec_.proj_kv, latent, C, kv_dec, 2 * C, H, s, k::kEpiBias, nullptr, 0, nullptr, stA_);
+    else linear(dec_.proj_kv, xh_, C, kv_dec, 2 * C, H, s);
     if (overlap) {  // the decoder's K|V halo flies while the first chunk's destination GEMMs run
         VB_CUDA(cudaEventRecord(ev_kv_, s));
         VB_CUDA(cudaStreamWaitEvent(cs_, ev_kv_, 0));
@@ -1142,22 +1223,19 @@ void Engine<T>::dec_chunk(int64_t lo, int64_t n, cudaStream_t s, HookSink* hk, b
     T* sb = qs + R * 2 * C;
     T* o1 = sb + R * C;
     T* h = o1 + R * C;
-    linear(dec_emb_dst_, x_data_ + lo * ldF_, ldF_, e, C, n, s);
+    linear(dec_emb_dst_, x_data_ + lo * ldF_, ldF_, e, C, n, s, k::kEpiBias, nullptr, 0, stA_);
     if (hk) hk->to_host(e, C, n, C, h_emb, lo);
-    ln(e, dec_.norm_dst, t, n, s);
-    linear(dec_.proj_qx, t, C, qs, 2 * C, n, s);
+    ln_linear(dec_.norm_dst, dec_.proj_qx, e, stA_, t, qs, 2 * C, n, s);
     if (halo_pending) {
         VB_CUDA(cudaStreamWaitEvent(s, ev_halo_, 0));
         halo_pending = false;
     }
     attention(g_dec_, dec_, lo, n, qs, 2 * C, kv_dec, kv_dec + C, 2 * C, qs + C, 2 * C, sb, s);
-    linear(dec_.proj_out, sb, C, o1, C, n, s, k::kEpiResidual, e, C);
-    ln(o1, dec_.norm_ffn, t, n, s);
-    linear(dec_.ffn_up, t, C, h, mlp_, n, s, k::kEpiGelu);
-    linear(dec_.ffn_down, h, mlp_, sb, C, n, s, k::kEpiResidual, o1, C);
+    linear(dec_.proj_out, sb, C, o1, C, n, s, k::kEpiResidual, e, C, fold_mlp_ ? stB_ : nullptr);
+    ln_linear(dec_.norm_ffn, dec_.ffn_up, o1, stB_, t, h, mlp_, n, s, k::kEpiGelu);
+    linear(dec_.ffn_down, h, mlp_, sb, C, n, s, k::kEpiResidual, o1, C, stA_);
     if (hk) hk->to_host(sb, C, n, C, h_bo, lo);
-    ln(sb, dec_out_norm_, t, n, s);
-    linear(dec_out_proj_, t, C, dec_out_ + lo * ldVo_, ldVo_, n, s);
+    ln_linear(dec_out_norm_, dec_out_proj_, sb, stA_, t, dec_out_ + lo * ldVo_, ldVo_, n, s);
 }
 
 // Output rows [lo, lo + n) of the own data rows: per step t, fp32 cast + residual + bounding into yn

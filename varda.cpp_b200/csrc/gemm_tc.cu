@@ -47,7 +47,10 @@ namespace {
 
 using vb::d::from_f;
 using vb::d::gelu;
+using vb::d::ln_from_records;
 using vb::d::rnd;
+using vb::d::seg_add;
+using vb::d::seg_record;
 using vb::d::to_f;
 
 constexpr int BM = 128, BK = 64;
@@ -69,7 +72,19 @@ struct Params {
     int epi;
     int gelu_tanh;
     unsigned* sched;  // dynamic tile order: [tiles handed out, fetchers done], zero between launches; or null
+    // LayerNorm fusion: the output rows' segment records (kLnStats), or A's records and the folded
+    // weights' column sums (kLnFold)
+    float2* st_out;
+    int nseg_out;
+    const float2* st_in;
+    const float* colsum;
+    int nseg_in;
+    float segw_in, eps;
 };
+// LN template argument of the kernel: no LayerNorm work, write the output's segment records, or apply
+// the LayerNorm of A folded into the weights.
+constexpr int kLnNone = 0, kLnStats = 1, kLnFold = 2;
+constexpr int kMaxSegs = 16;  // records per row a folded GEMM reads (C <= 2048)
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
 __device__ __forceinline__ uint64_t now_ns() {
@@ -332,7 +347,7 @@ __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.a
 // tensor map (chunk index XOR bits 1-2 of the row): conflict-free 16-byte accesses by 32 lanes.
 __device__ __forceinline__ int sw64(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
 
-template <int BN, int STAGES, int EPI, bool PAIR>
+template <int BN, int STAGES, int EPI, bool PAIR, int LN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, Params p) {
@@ -569,6 +584,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         };
+        // 32 fp32 column sums of the folded weights from col0 (kLnFold; zero out of bounds)
+        auto load_colsum = [&](int col0, float(&cs)[32]) {
+            if (col0 + 32 <= p.N) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 u = __ldg(reinterpret_cast<const float4*>(p.colsum + col0) + q);
+                    cs[4 * q] = u.x, cs[4 * q + 1] = u.y, cs[4 * q + 2] = u.z, cs[4 * q + 3] = u.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) cs[i] = col0 + i < p.N ? p.colsum[col0 + i] : 0.0f;
+            }
+        };
         // the leader's tempty barriers, which both CTAs' epilogue warps release
         const uint32_t te0 = PAIR ? mapa(smem_u32(&tempty[0]), 0) : 0u, te1 = PAIR ? mapa(smem_u32(&tempty[1]), 0) : 0u;
         auto release = [&](int ab) {
@@ -589,8 +617,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int colh = nb * BN + half * (BN / 2);
             // the first chunk's residual and bias loads fly while the accumulator is being computed
             uint32_t resa[16], resb[16], bia[16], bib[16];
+            float cs[32];  // kLnFold: this chunk's column sums (the next chunk's loaded once o is formed)
+            // kLnFold: y = rstd acc + (-rstd mean) colsum + b' for this lane's row (its records read
+            // while the accumulator is being computed)
+            float rstd = 0.0f, nm = 0.0f;
+            if (LN == kLnFold && row0 + lane < p.M) {
+                const float2 mr = ln_from_records<kMaxSegs>(p.st_in + int64_t(row0 + lane) * p.nseg_in, 1, p.nseg_in,
+                                                            p.segw_in, p.eps);
+                rstd = mr.y, nm = __fmul_rn(-mr.y, mr.x);
+            }
             if (EPI == k::kEpiResidual) load_res(row0 + lane, colh, resa);
             load_bias(colh, bia);
+            if (LN == kLnFold) load_colsum(colh, cs);
+            // kLnStats: this half row's segment record, from its first stored value
+            float2 s1 = make_float2(0.0f, 0.0f), s2 = make_float2(0.0f, 0.0f);
+            float kshift = 0.0f;
             if (!mbar_wait(&tfull[ab], ap, abort_flag)) break;
             fence_after();
             const uint32_t taddr = tmem + (uint32_t(lg * 32) << 16) + uint32_t(ab * BN + half * (BN / 2));
@@ -610,13 +651,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (c + 1 < kChunks) tmem_ld32_async(taddr + uint32_t((c + 1) * 32), nxt);
                 const int col0 = colh + c * 32;
                 if (EPI == k::kEpiResidual && c + 1 < kChunks) load_res(row0 + lane, col0 + 32, rnxt);
-                uint32_t(&bh)[16] = (c & 1) ? bib : bia;  // this chunk's bias; the next one's in flight
-                if (c + 1 < kChunks) load_bias(col0 + 32, (c & 1) ? bia : bib);
+                // this chunk's bias; the next one's in flight (kLnFold: one buffer, reloaded with the column
+                // sums once o is formed, for registers)
+                uint32_t(&bh)[16] = (LN == kLnFold || !(c & 1)) ? bia : bib;
+                if (LN != kLnFold && c + 1 < kChunks) load_bias(col0 + 32, (c & 1) ? bia : bib);
                 uint32_t o[16];  // the output sub-row, fp16 pairs
+                if (LN == kLnFold) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float2 x = add_h2(bh[i], make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])));
-                    o[i] = pack_h2(x);  // T(acc + b)
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 acc = make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1]));
+                        const float2 t = __ffma2_rn(acc, make_float2(rstd, rstd),
+                                                    __fmul2_rn(make_float2(cs[2 * i], cs[2 * i + 1]), make_float2(nm, nm)));
+                        o[i] = pack_h2(add_h2(bh[i], t));  // T(LN(x) W^T + b)
+                    }
+                    if (c + 1 < kChunks) load_colsum(col0 + 32, cs), load_bias(col0 + 32, bia);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 x = add_h2(bh[i], make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])));
+                        o[i] = pack_h2(x);  // T(acc + b)
+                    }
                 }
                 if (EPI == k::kEpiGelu) {
                     if (p.gelu_tanh) {
@@ -633,6 +687,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (EPI == k::kEpiResidual) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) o[i] = pack_h2(add_h2(rcur[i], unpack_h2(o[i])));  // T(T(acc+b)+r)
+                }
+                if (LN == kLnStats) {  // over the stored (rounded) values
+                    if (c == 0) kshift = unpack_h2(o[0]).x;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) seg_add(s1, s2, kshift, unpack_h2(o[i]));
                 }
                 if (c + 1 < kChunks) {
                     tmem_wait32(nxt);
@@ -658,6 +717,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++n_out;
             }
             if (!released) release(ab);
+            if (LN == kLnStats && row0 + lane < p.M && colh < p.N)  // (a half past N has no segment)
+                p.st_out[int64_t(row0 + lane) * p.nseg_out + colh / (BN / 2)] = seg_record(s1, s2, kshift, float(BN / 2));
             if (!ok) break;
         }
         if (lane == 0) bulk_wait_all();  // every TMA store has finished before the CTA exits
@@ -743,24 +804,25 @@ unsigned* sched_counter(cudaStream_t s) {
 
 int sm_count() { return device_sm_count(); }
 
-template <int BN, int STAGES, int EPI, bool PAIR>
+template <int BN, int STAGES, int EPI, bool PAIR, int LN>
 void launch(const k::GemmArgs<__half>& a, cudaStream_t s, unsigned* sched) {
     using L = Layout<BN, STAGES, EPI, PAIR>;
     static std::atomic<uint64_t> configured{0};  // per instantiation and device
     once_per_device(configured, [] {
-        VB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, EPI, PAIR>,
+        VB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, EPI, PAIR, LN>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem));
     });
     const CUtensorMap ta = make_map(a.A, a.M, a.K, a.lda, BM);
     const CUtensorMap tb = make_map(a.W, a.N, a.K, a.ldw, PAIR ? BN / 2 : BN);
     // 32 x 32 sub-tiles of the output, 64-byte swizzle: the epilogue's TMA stores
     const CUtensorMap tc = make_map(a.C, a.M, a.N, a.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-    Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0, sched};
+    Params p{a.bias, a.C, a.ldc, a.R, a.ldr, int(a.M), int(a.N), int(a.K), a.epi, a.gelu_tanh ? 1 : 0, sched,
+             a.st_out, int(a.N / (BN / 2)), a.st_in, a.colsum, a.nseg_in, float(a.segw_in), a.eps};
     constexpr int UM = PAIR ? 2 * BM : BM;
     const int64_t tiles = ((a.M + UM - 1) / UM) * ((a.N + BN - 1) / BN);
     if (!PAIR) {
         const int grid = int(std::min<int64_t>(tiles, sm_count()));
-        gemm_tc_kernel<BN, STAGES, EPI, PAIR><<<grid, kThreads, L::kSmem, s>>>(ta, tb, tc, p);
+        gemm_tc_kernel<BN, STAGES, EPI, PAIR, LN><<<grid, kThreads, L::kSmem, s>>>(ta, tb, tc, p);
         VB_LAUNCH();
         return;
     }
@@ -775,24 +837,43 @@ void launch(const k::GemmArgs<__half>& a, cudaStream_t s, unsigned* sched) {
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr, cfg.numAttrs = 1;
-    VB_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, STAGES, EPI, PAIR>, ta, tb, tc, p));
+    VB_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, STAGES, EPI, PAIR, LN>, ta, tb, tc, p));
     ++launch_counter();
 }
 
+// the LayerNorm variant: records written by bias and residual epilogues, the fold applied by bias and
+// GELU epilogues (supported() rejects the other combinations)
+template <int BN, int STAGES, int EPI, bool PAIR>
+void dispatch_ln(const k::GemmArgs<__half>& a, cudaStream_t s, unsigned* sched) {
+    if constexpr (EPI != k::kEpiResidual) {
+        if (a.st_in) return launch<BN, STAGES, EPI, PAIR, kLnFold>(a, s, sched);
+    }
+    if constexpr (EPI != k::kEpiGelu) {
+        if (a.st_out) return launch<BN, STAGES, EPI, PAIR, kLnStats>(a, s, sched);
+    }
+    launch<BN, STAGES, EPI, PAIR, kLnNone>(a, s, sched);
+}
+
 // stage counts: as deep as the 227 KB of shared memory allows next to the epilogue staging
+template <int BN, int EPI>
+void dispatch_pair(const k::GemmArgs<__half>& a, cudaStream_t s, unsigned* sched) {
+    if constexpr (BN == 256) {
+        // CTA pairs (cta_group::2) for N > 128 unless VB_GEMM_PAIR=0: on C1's shapes 3-8% faster than
+        // single CTAs (each SM loads half of W per tile: a third less L2-to-SM traffic)
+        const char* pe = std::getenv("VB_GEMM_PAIR");
+        if (!(pe && *pe && std::atoi(pe) == 0) && a.M >= 2 * BM) return dispatch_ln<BN, 6, EPI, true>(a, s, sched);
+        return dispatch_ln<BN, 4, EPI, false>(a, s, sched);
+    } else {
+        return dispatch_ln<BN, 6, EPI, false>(a, s, sched);
+    }
+}
+
 template <int BN>
 void dispatch_epi(const k::GemmArgs<__half>& a, cudaStream_t s, unsigned* sched) {
-    constexpr int S = BN == 256 ? 4 : 6;
-    // CTA pairs (cta_group::2) for N > 128 unless VB_GEMM_PAIR=0: on C1's shapes 3-8% faster than single
-    // CTAs (each SM loads half of W per tile: a third less L2-to-SM traffic)
-    const char* pe = std::getenv("VB_GEMM_PAIR");
-    const bool pair = BN == 256 && !(pe && *pe && std::atoi(pe) == 0) && a.M >= 2 * BM;
     switch (a.epi) {
-        case k::kEpiBias: pair ? launch<BN, 6, k::kEpiBias, true>(a, s, sched) : launch<BN, S, k::kEpiBias, false>(a, s, sched); break;
-        case k::kEpiGelu: pair ? launch<BN, 6, k::kEpiGelu, true>(a, s, sched) : launch<BN, S, k::kEpiGelu, false>(a, s, sched); break;
-        case k::kEpiResidual:
-            pair ? launch<BN, 6, k::kEpiResidual, true>(a, s, sched) : launch<BN, S, k::kEpiResidual, false>(a, s, sched);
-            break;
+        case k::kEpiBias: dispatch_pair<BN, k::kEpiBias>(a, s, sched); break;
+        case k::kEpiGelu: dispatch_pair<BN, k::kEpiGelu>(a, s, sched); break;
+        case k::kEpiResidual: dispatch_pair<BN, k::kEpiResidual>(a, s, sched); break;
         default: fail(kInvalidArgument, "gemm: unknown epilogue");
     }
 }
@@ -808,6 +889,13 @@ bool supported(const k::GemmArgs<__half>& a) {
     if (!aligned16(a.A) || !aligned16(a.W) || !aligned16(a.C)) return false;
     if (a.bias && !aligned16(a.bias)) return false;
     if (a.epi == k::kEpiResidual && (!a.R || a.ldr % 8 || !aligned16(a.R))) return false;
+    // LayerNorm fusion: records of whole segments, from bias / residual epilogues; the fold with its
+    // column sums and bias, at most kMaxSegs records per row, in bias / GELU epilogues
+    if (a.st_out && (a.epi == k::kEpiGelu || a.N % stats_segw(a.N) || !aligned16(a.st_out))) return false;
+    if (a.st_in && (a.st_out || a.epi == k::kEpiResidual || !a.colsum || !a.bias || a.nseg_in < 1 ||
+                    a.nseg_in > kMaxSegs || a.segw_in < 1 || !aligned16(a.colsum) ||
+                    (reinterpret_cast<uintptr_t>(a.st_in) & 7)))
+        return false;
     return true;
 }
 

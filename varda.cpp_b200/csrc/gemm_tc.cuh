@@ -14,6 +14,9 @@ namespace vb::tc {
 // True when the operands meet the tensor-memory-access rules: 16-byte aligned base pointers and
 // row strides (multiples of 8 fp16 elements).
 bool supported(const k::GemmArgs<__half>& a);
+// Width of the LayerNorm segment records a GEMM with N output columns writes (st_out): one column
+// half of its output tile, 64 for N <= 128, else 128.
+inline int stats_segw(int64_t N) { return N <= 128 ? 64 : 128; }
 // Enqueues the GEMM on s (no allocation, no synchronisation; capturable). Static tile order, or with
 // VB_GEMM_SCHED=1 the dynamic order on a counter kept per (device, stream, thread).
 void gemm(const k::GemmArgs<__half>& a, cudaStream_t s);

@@ -215,6 +215,49 @@ __global__ void __launch_bounds__(256) add_layernorm_kernel(const T* a, const T*
     for (int i = 0; i < NV; ++i) Vec<T, 4>::store(ln + r * ld + (lane + 32 * i) * 4, v[i]);
 }
 
+// One warp per output row n of W: b'[n] += sum_k be[k] W[n, k] (fp32, the original weights), then
+// W[n, k] = T(W[n, k] g[k]) in place and colsum[n] = sum of the rounded values.
+__global__ void __launch_bounds__(256) fold_ln_kernel(__half* W, int64_t ldw, int64_t N, int K, const float* __restrict__ g,
+                                                      const float* __restrict__ be, __half* b, float* colsum) {
+    const int lane = threadIdx.x & 31;
+    const int64_t n = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (n >= N) return;
+    __half* w = W + n * ldw;
+    float c = 0.0f, sw = 0.0f;
+    for (int k = lane; k < K; k += 32) {
+        const float wv = __half2float(w[k]);
+        if (be) c = __fmaf_rn(be[k], wv, c);
+        const __half wg = __float2half_rn(__fmul_rn(wv, g[k]));
+        w[k] = wg;
+        sw = __fadd_rn(sw, __half2float(wg));
+    }
+    c = warp_sum(c);
+    sw = warp_sum(sw);
+    if (lane == 0) {
+        colsum[n] = sw;
+        b[n] = __float2half_rn(__fadd_rn(__half2float(b[n]), c));
+    }
+}
+
+// One thread per (row, segment), the segment's columns in the order the GEMM epilogue takes them.
+__global__ void __launch_bounds__(256) row_seg_stats_kernel(const __half* x, int64_t ldx, int64_t rows, int nseg,
+                                                            int segw, float2* st) {
+    const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= rows * nseg) return;
+    const int64_t r = t / nseg;
+    const int sg = int(t - r * nseg);
+    const __half* p = x + r * ldx + int64_t(sg) * segw;
+    const float k0 = __half2float(p[0]);
+    float2 s1 = make_float2(0.0f, 0.0f), s2 = make_float2(0.0f, 0.0f);
+    for (int j = 0; j < segw; j += 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p + j);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) seg_add(s1, s2, k0, __half22float2(h[q]));
+    }
+    st[t] = seg_record(s1, s2, k0, float(segw));
+}
+
 // One warp per output row (step t, data node g). The row is staged in shared memory; the
 // boundings then run in config order with the lanes spread over each bounding's index list.
 template <class T>
@@ -401,6 +444,22 @@ void add_layernorm(const T* a, const T* r, T* out1, const float* w, const float*
 #define VB_ALN(NV) add_layernorm_kernel<T, NV><<<grid, 256, 0, s>>>(a, r, out1, w, b, ln, ld, rows, eps)
     VB_NV_SWITCH(C, VB_ALN, "add_layernorm")
 #undef VB_ALN
+    VB_LAUNCH();
+}
+
+void fold_layernorm(__half* W, int64_t ldw, int64_t N, int K, const float* g, const float* be, __half* b,
+                    float* colsum, cudaStream_t s) {
+    if (N <= 0) return;
+    fold_ln_kernel<<<unsigned((N + 7) / 8), 256, 0, s>>>(W, ldw, N, K, g, be, b, colsum);
+    VB_LAUNCH();
+}
+
+void row_seg_stats(const __half* x, int64_t ldx, int64_t rows, int C, int segw, float2* st, cudaStream_t s) {
+    if (rows <= 0) return;
+    if (segw < 8 || segw % 8 || C % segw || ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15))
+        fail(kInvalidArgument, "row_seg_stats: segments must be whole 16-byte runs");
+    const int nseg = C / segw;
+    row_seg_stats_kernel<<<unsigned((rows * nseg + 255) / 256), 256, 0, s>>>(x, ldx, rows, nseg, segw, st);
     VB_LAUNCH();
 }
 

@@ -84,6 +84,17 @@ void layernorm(const T* x, int64_t ldx, const float* w, const float* b, T* y, in
 template <class T>
 void add_layernorm(const T* a, const T* r, T* out1, const float* w, const float* b, T* ln, int64_t ld, int64_t rows,
                    int C, float eps, cudaStream_t s);
+// LayerNorm folded into the next Linear (fp16 tensor-core path). For y = LN(x) W^T + b with LN's
+// weight g and bias be: W'[n, k] = T(W[n, k] g[k]), colsum[n] = sum_k W'[n, k] (fp32),
+// b'[n] = T(b[n] + sum_k be[k] W[n, k]); then y = rstd (x W'^T) - rstd mean colsum + b', rstd and mean
+// of each x row coming from its segment records (dev.cuh). In place on W (ldw) and b (N, allocated);
+// one warp per output row, fixed reduction order.
+void fold_layernorm(__half* W, int64_t ldw, int64_t N, int K, const float* g, const float* be, __half* b,
+                    float* colsum, cudaStream_t s);
+// The segment records of rows [0, rows) of x (C columns, segments of segw; C a multiple of segw): the
+// same values as the producing GEMM epilogue's (for rows that no GEMM produced: the processor block
+// entry point, rows moved between ranks). st: [rows, C / segw] float2.
+void row_seg_stats(const __half* x, int64_t ldx, int64_t rows, int C, int segw, float2* st, cudaStream_t s);
 
 // ------------------------------------------------------------------ graph attention
 template <class T> struct AttnArgs {
@@ -200,6 +211,12 @@ template <class T> struct GemmArgs {
     int64_t M = 0, N = 0, K = 0;
     int epi = kEpiBias;
     bool gelu_tanh = false;
+    // LayerNorm fusion (fp16 tensor-core path, N a multiple of the segment width stats_segw(N)):
+    float2* st_out = nullptr;        // write the output rows' segment records, [M, N / stats_segw(N)]
+    const float2* st_in = nullptr;   // A's rows' segment records, [M, nseg_in]: y = LN(A) W^T + b, W and b
+    const float* colsum = nullptr;   //   folded by fold_layernorm (bias, GELU epilogues)
+    int nseg_in = 0, segw_in = 0;
+    float eps = 0.0f;
 };
 // CUDA-core GEMM with fp32 accumulation (true fp32 FMA in fp32 mode).
 template <class T> void gemm_simt(const GemmArgs<T>& a, cudaStream_t s);

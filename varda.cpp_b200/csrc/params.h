@@ -31,9 +31,11 @@ namespace vb {
 
 template <class T> struct Dense {
     DeviceBuffer weight, bias;
+    DeviceBuffer colsum;  // fp32 [out]: set when a LayerNorm is folded into the weights (fold_layernorm)
     int64_t out = 0, in = 0, ld_in = 0;
     const T* w() const { return weight.as<T>(); }
     const T* b() const { return bias.get() ? bias.as<T>() : nullptr; }
+    const float* cs() const { return colsum.get() ? colsum.as<float>() : nullptr; }
 };
 
 struct Affine {

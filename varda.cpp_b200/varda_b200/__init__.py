@@ -68,6 +68,10 @@ def _load_lib():
         "vb_attention": ([I, P, P, I64, I64, P, I64, P, P, I64, P, I64, P, I64, P, I, I, I, P], I),
         "vb_gemm": ([I, I, P, I64, P, I64, P, P, I64, P, I64, I64, I64, I64, I, I, P], I),
         "vb_layernorm": ([I, P, I64, P, P, P, I64, I64, I, F, P], I),
+        "vb_ln_segment_width": ([I64], I),
+        "vb_gemm_ln": ([P, I64, P, I64, P, P, I64, P, I64, I64, I64, I64, I, I, P, P, P, I, I, F, P], I),
+        "vb_fold_layernorm": ([P, I64, I64, I, P, P, P, P, P], I),
+        "vb_row_seg_stats": ([P, I64, I64, I, I, P, P], I),
         "vb_add_layernorm": ([I, P, P, P, P, P, P, I64, I64, I, F, P], I),
         "vb_rollout": ([P, P, I, P, P, I, P, P, P], I),
         "vb_attention_rows": ([I, P, P, P, I64, P, I64, P, P, I64, P, I64, P, I64, P, I, I, I, P], I),
@@ -368,6 +372,26 @@ def attention_split_noalloc(dtype, row_ptr, edges, dst_lo, n_rows, q, ldq, k, v,
 def gemm(dtype, engine, A, lda, W, ldw, bias, Y, ldy, R, ldr, M, N, K, epilogue=0, gelu_tanh=False, stream=None):
     check(lib.vb_gemm(dtype, engine, _ptr(A), lda, _ptr(W), ldw, _ptr(bias), _ptr(Y), ldy, _ptr(R), ldr, M, N, K,
                       epilogue, int(gelu_tanh), stream))
+
+
+def gemm_ln(A, lda, W, ldw, bias, Y, ldy, R, ldr, M, N, K, epilogue=0, gelu_tanh=False, st_out=None, st_in=None,
+            colsum=None, nseg_in=0, segw_in=0, eps=0.0, stream=None):
+    """vb_gemm_ln: the fp16 tensor-core GEMM with LayerNorm records written (st_out) or an LN folded in
+    (st_in, colsum)."""
+    check(lib.vb_gemm_ln(_ptr(A), lda, _ptr(W), ldw, _ptr(bias), _ptr(Y), ldy, _ptr(R), ldr, M, N, K, epilogue,
+                         int(gelu_tanh), _ptr(st_out), _ptr(st_in), _ptr(colsum), nseg_in, segw_in, eps, stream))
+
+
+def fold_layernorm(W, ldw, N, K, g, be, bias, colsum, stream=None):
+    check(lib.vb_fold_layernorm(_ptr(W), ldw, N, K, _ptr(g), _ptr(be), _ptr(bias), _ptr(colsum), stream))
+
+
+def row_seg_stats(x, ldx, rows, C, segw, st, stream=None):
+    check(lib.vb_row_seg_stats(_ptr(x), ldx, rows, C, segw, _ptr(st), stream))
+
+
+def ln_segment_width(N):
+    return lib.vb_ln_segment_width(N)
 
 
 def layernorm(dtype, x, ldx, w, b, y, ldy, rows, C, eps, stream=None):

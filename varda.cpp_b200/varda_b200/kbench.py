@@ -55,6 +55,18 @@ def gemm(a):
     Y = torch.empty(a.M, a.N, device="cuda", dtype=torch.float16)
     s = torch.cuda.current_stream().cuda_stream
     fn = lambda: vb.gemm(vb.FP16, a.engine, A, a.K, W, a.K, b, Y, a.N, R, a.N, a.M, a.N, a.K, a.epi, stream=s)  # noqa
+    if a.ln == "stats":  # + the output rows' LayerNorm records
+        st = torch.empty(a.M, a.N // vb.ln_segment_width(a.N), 2, device="cuda")
+        fn = lambda: vb.gemm_ln(A, a.K, W, a.K, b, Y, a.N, R, a.N, a.M, a.N, a.K, a.epi, st_out=st, stream=s)  # noqa
+    elif a.ln == "fold":  # a LayerNorm over A's rows folded into W and b
+        segw = vb.ln_segment_width(a.K)
+        st = torch.empty(a.M, a.K // segw, 2, device="cuda")
+        cs = torch.empty(a.N, device="cuda")
+        ones = torch.ones(a.K, device="cuda")
+        vb.fold_layernorm(W, a.K, a.N, a.K, ones, None, b, cs, stream=s)
+        vb.row_seg_stats(A, a.K, a.M, a.K, segw, st, stream=s)
+        fn = lambda: vb.gemm_ln(A, a.K, W, a.K, b, Y, a.N, None, 0, a.M, a.N, a.K, a.epi, st_in=st, colsum=cs,  # noqa
+                                nseg_in=a.K // segw, segw_in=segw, eps=1e-5, stream=s)
     pk = _peaks()
     if a.library:  # the library GEMM (cuBLAS through torch.matmul, fp16, no fused epilogue) on the same shape
         ms = time_launches(lambda: torch.matmul(A, W.t(), out=Y), a.iters, a.warmup)
@@ -70,8 +82,8 @@ def gemm(a):
             os.environ["VB_GEMM_SCHED"] = "1" if order == "dyn" else "0"
         ms = time_launches(fn, a.iters, a.warmup)
         tf = 2.0 * a.M * a.N * a.K / (ms * 1e-3) / 1e12
-        print(json.dumps({"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "engine": a.engine,
-                          "mode": mode or "default", "ms": round(ms, 4), "tflops": round(tf, 1),
+        print(json.dumps({"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "ln": a.ln,
+                          "engine": a.engine, "mode": mode or "default", "ms": round(ms, 4), "tflops": round(tf, 1),
                           "frac_of_burst": round(tf / pk["bf16_tflops"], 3)}))
 
 
@@ -132,6 +144,8 @@ def main():
     g.add_argument("--warmup", type=int, default=3)
     g.add_argument("--modes", default="", help="e.g. pair_dyn,pair_static,single_dyn,single_static")
     g.add_argument("--library", action="store_true", help="also time cuBLAS (torch.matmul) on the shape")
+    g.add_argument("--ln", default="none", choices=["none", "stats", "fold"],
+                   help="LayerNorm fusion: write the output's records, or apply an LN of A folded into W")
     t = sub.add_parser("attention")
     t.add_argument("--config", default="c2")
     t.add_argument("--dtype", default="fp16")
