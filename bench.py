@@ -151,6 +151,16 @@ class Clocks:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
              "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
 
+    def start_region(self, timeout=5.0):
+        """Waits (outside the timed region) until nvidia-smi, which takes a moment to start, has written
+        a row, and marks where the region's rows begin: a region of a few hundred ms is then sampled too."""
+        t0 = time.time()
+        while time.time() - t0 < timeout and os.path.getsize(self.f.name) == 0:
+            time.sleep(0.02)
+        self.f.flush()
+        with open(self.f.name) as f:
+            self.skip = sum(1 for l in f if l.strip())
+
     def stop(self):
         self.p.terminate()
         try:
@@ -159,6 +169,9 @@ class Clocks:
             self.p.kill()
         self.f.seek(0)
         rows = [l.split(",") for l in self.f.read().strip().splitlines() if l.strip()]
+        skip = getattr(self, "skip", 0)
+        if len(rows) > skip:  # the rows taken before the region (kept only if the region got none)
+            rows = rows[skip:]
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -225,10 +238,11 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         if i == 0:
             log(f"bench: first graph step (capture + run) {time.perf_counter() - t0:.3f} s")
+    clk = Clocks(local_rank)
+    clk.start_region()
     if dist:
         dist.barrier()
     n_launch0 = vb.launch_count()
-    clk = Clocks(local_rank)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     ev0.record(stream)
@@ -295,10 +309,11 @@ def run_rollout(args, rank, world, local_rank):
 
     m.rollout(x, args.warmup, f[:max(args.warmup - 1, 0)], keep=False, on_step=on_step)
     torch.cuda.synchronize()
+    clk = Clocks(local_rank)
+    clk.start_region()
     if dist:
         dist.barrier()
     n_launch0 = vb.launch_count()
-    clk = Clocks(local_rank)
     sums.clear()
     t0 = time.perf_counter()
     _, step_ms = m.rollout(x, n, f[:n - 1], keep=False, on_step=on_step)
@@ -336,6 +351,7 @@ def run_c2(args, rank, world, local_rank):
     stream = torch.cuda.ExternalStream(m.stream(), device=f"cuda:{local_rank}")
     # the timed runs are short: the clock sampler runs from before the warm-up through the e2e runs
     clk = Clocks(local_rank)
+    clk.start_region()
     time.sleep(0.5)
     for _ in range(args.warmup):
         m.processor_block(0, zin, zout)
