@@ -92,3 +92,38 @@ def test_reference_env_names_an_openblas_core_type(monkeypatch):
         assert env["OPENBLAS_CORETYPE"] == "Haswell"
     monkeypatch.setenv("OPENBLAS_CORETYPE", "Zen")
     assert bench.ref_env()["OPENBLAS_CORETYPE"] == "Zen", "a caller's choice is kept"
+
+
+class _FakeSmi:
+    """Stands in for the nvidia-smi sampler process: writes rows into its stdout file on demand."""
+    def __init__(self, args, stdout=None, stderr=None):
+        self.out = stdout
+
+    def row(self, mhz, cap="Not Active"):
+        self.out.write(f"0, {mhz}, 1965, 900.0, 0x0, Not Active, Not Active, Not Active, {cap}\n")
+        self.out.flush()
+
+    def terminate(self):
+        pass
+
+    def wait(self, timeout=None):
+        return 0
+
+
+def test_clock_sampler_keeps_the_timed_region_rows(monkeypatch):
+    """Clocks.start_region waits for the sampler's first row and drops the rows taken before the timed
+    region; with no row inside the region the earlier ones are kept (a median of something)."""
+    monkeypatch.setattr(bench.subprocess, "Popen", _FakeSmi)
+    c = bench.Clocks(0)
+    c.p.row(1965)  # idle, before the region
+    c.start_region()
+    assert c.skip == 1
+    c.p.row(1400, "Active")
+    c.p.row(1420, "Active")
+    r = c.stop()
+    assert r["samples"] == 2 and r["sm_mhz"] == 1410 and r["reasons"] == ["sw_power_cap"]
+    c = bench.Clocks(0)
+    c.p.row(1900)
+    c.start_region()
+    r = c.stop()
+    assert r["samples"] == 1 and r["sm_mhz"] == 1900
