@@ -14,6 +14,10 @@
 //                       registers one chunk ahead), the 32 x 32 fp16 sub-tile staged in
 //                       64-byte-swizzled shared memory and written by one TMA bulk tensor store;
 //                       the accumulator goes back to the MMA warp once its last chunk is loaded.
+// LayerNorm variants of the epilogue (template argument LN): kLnStats also accumulates, per row and per
+// column half, the {mean, M2} record of the values it stores (the next LayerNorm's statistics); kLnFold
+// applies a LayerNorm of A folded into W and the bias: y = rstd acc - rstd mean colsum + b', rstd and
+// mean from A's row records (kernels.cuh fold_layernorm / row_seg_stats, dev.cuh for the arithmetic).
 // Two accumulators (2 x BN TMEM columns) let the epilogue of tile i overlap the main loop of
 // tile i + 1. With N > 128 the CTAs run in clusters of two (cta_group::2): the pair computes a
 // 256-row tile with one MMA stream issued by the leader, each CTA loading its own 128 rows of A and

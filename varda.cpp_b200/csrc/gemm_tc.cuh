@@ -1,6 +1,7 @@
 // Tensor-core GEMM for sm_100a (tcgen05 + TMEM + TMA): y[M, N] = A[M, K] W[N, K]^T with fp16
 // operands, fp32 accumulation in tensor memory, and the fused epilogues of kernels.cuh
-// (bias, GELU, residual) applied when the accumulator is read back.
+// (bias, GELU, residual; LayerNorm records written or a folded LayerNorm applied) applied when the
+// accumulator is read back.
 #pragma once
 
 #include <cuda.h>
