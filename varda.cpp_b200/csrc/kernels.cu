@@ -258,49 +258,75 @@ __global__ void __launch_bounds__(256) row_seg_stats_kernel(const __half* x, int
     st[t] = seg_record(s1, s2, k0, float(segw));
 }
 
-// One warp per output row (step t, data node g). The row is staged in shared memory; the
-// boundings then run in config order with the lanes spread over each bounding's index list.
-template <class T>
+// One warp per R consecutive output rows (step t, data nodes g0 .. g0 + R - 1), staged in shared
+// memory: the R rows' loads of each column stripe are issued together; the boundings then run in config
+// order with the lanes spread over each bounding's index list, row by row. Every element sees the same
+// operations in the same order whatever R is.
+template <class T, int R>
 __global__ void __launch_bounds__(256) output_kernel(OutputArgs a) {
     extern __shared__ float sm[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int64_t g = int64_t(blockIdx.x) * (blockDim.x >> 5) + wid;
-    if (g >= a.G) return;
-    const int t = blockIdx.y;
-    float* row = sm + wid * a.V_out;
-    const T* dec = static_cast<const T*>(a.dec) + g * a.ld_dec + int64_t(t) * a.V_out;
-    const int64_t orow = int64_t(t) * (a.y_slot > 0 ? a.y_slot : a.G) + g;
-    for (int v = lane; v < a.V_out; v += 32) {
-        float val = to_f<T>(dec[v]);
+    const int64_t g0 = (int64_t(blockIdx.x) * (blockDim.x >> 5) + wid) * R;
+    if (g0 >= a.G) return;
+    const int nr = int(a.G - g0 < R ? a.G - g0 : R);
+    const int t = blockIdx.y, V = a.V_out;
+    float* rows = sm + wid * R * V;
+    const T* dec = static_cast<const T*>(a.dec) + g0 * a.ld_dec + int64_t(t) * V;
+    const int64_t orow0 = int64_t(t) * (a.y_slot > 0 ? a.y_slot : a.G) + g0;
+    for (int v = lane; v < V; v += 32) {
         const int rs = a.res_src[v];
-        if (rs >= 0) val = __fadd_rn(val, a.xn_step[g * a.V_in + rs]);
-        row[v] = val;
-        if (a.pre_bound) a.pre_bound[orow * a.V_out + v] = val;
+        float val[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            if (r < nr) {
+                val[r] = to_f<T>(dec[r * a.ld_dec + v]);
+                if (rs >= 0) val[r] = __fadd_rn(val[r], a.xn_step[(g0 + r) * a.V_in + rs]);
+            }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            if (r < nr) {
+                rows[r * V + v] = val[r];
+                if (a.pre_bound) a.pre_bound[(orow0 + r) * V + v] = val[r];
+            }
     }
     __syncwarp();
     for (int bi = 0; bi < a.n_bounds; ++bi) {
         const BoundDev bd = a.bounds[bi];
         const int* idx = a.bidx + bd.idx_off;
         for (int j = lane; j < bd.n; j += 32) {
-            const float x = row[idx[j]];
-            if (bd.type == 0) {
-                row[idx[j]] = (x > 0.0f || x != x) ? x : 0.0f;  // relu, NaN propagates
-            } else {
-                // std::min(std::max(x, lo), hi) of the CPU reference, NaN propagating
-                const float m = (x < bd.lo) ? bd.lo : x;
-                row[idx[j]] = (bd.hi < m) ? bd.hi : m;
-            }
+            const int iv = idx[j];
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                if (r < nr) {
+                    const float x = rows[r * V + iv];
+                    if (bd.type == 0) {
+                        rows[r * V + iv] = (x > 0.0f || x != x) ? x : 0.0f;  // relu, NaN propagates
+                    } else {
+                        // std::min(std::max(x, lo), hi) of the CPU reference, NaN propagating
+                        const float m = (x < bd.lo) ? bd.lo : x;
+                        rows[r * V + iv] = (bd.hi < m) ? bd.hi : m;
+                    }
+                }
         }
         __syncwarp();
         if (bd.type == 2) {
             // y[idx] *= y[total] (already bounded); index and total lists are disjoint (checked at load)
             const int* tot = a.bidx + bd.tot_off;
-            for (int j = lane; j < bd.n; j += 32) row[idx[j]] = __fmul_rn(row[idx[j]], row[tot[bd.n_tot == 1 ? 0 : j]]);
+            for (int j = lane; j < bd.n; j += 32) {
+                const int iv = idx[j], it = tot[bd.n_tot == 1 ? 0 : j];
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    if (r < nr) rows[r * V + iv] = __fmul_rn(rows[r * V + iv], rows[r * V + it]);
+            }
             __syncwarp();
         }
     }
-    float* y = a.y + orow * a.V_out;
-    for (int v = lane; v < a.V_out; v += 32) y[v] = row[v];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+        if (r < nr) {
+            float* y = a.y + (orow0 + r) * V;
+            for (int v = lane; v < V; v += 32) y[v] = rows[r * V + v];
+        }
 }
 
 [[noreturn]] void bad_c(int C, const char* what) {
@@ -467,9 +493,13 @@ template <class T>
 void output_assemble(const OutputArgs& a, cudaStream_t s) {
     if (a.G <= 0 || a.T_out <= 0) return;
     if (a.T_out > 65535) fail(kUnsupported, "output_assemble: T_out > 65535");
-    const size_t smem = size_t(8) * a.V_out * sizeof(float);
-    if (smem > 48 * 1024) fail(kUnsupported, "output_assemble: too many output variables");
-    output_kernel<T><<<dim3(unsigned((a.G + 7) / 8), unsigned(a.T_out)), 256, smem, s>>>(a);
+    // four rows per warp while their staging fits the default 48 KB of shared memory, else one
+    const size_t smem4 = size_t(8) * 4 * a.V_out * sizeof(float), smem1 = size_t(8) * a.V_out * sizeof(float);
+    if (smem1 > 48 * 1024) fail(kUnsupported, "output_assemble: too many output variables");
+    if (smem4 <= 48 * 1024)
+        output_kernel<T, 4><<<dim3(unsigned((a.G + 31) / 32), unsigned(a.T_out)), 256, smem4, s>>>(a);
+    else
+        output_kernel<T, 1><<<dim3(unsigned((a.G + 7) / 8), unsigned(a.T_out)), 256, smem1, s>>>(a);
     VB_LAUNCH();
 }
 
